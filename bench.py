@@ -1,0 +1,488 @@
+"""Benchmark of the MoE decode hot path (Qwen3-30B-A3B shape, Q4 experts).
+
+A step is one decode step's MoE work: the MoE FFN of all 48 layers for B
+tokens (router -> dispatch -> gate/up -> SwiGLU -> down -> combine per layer,
+layers in sequence on one stream, as decode runs them). The metric is tokens
+per second through that step (B / step time); the whole 15.4 GB Q4 store is
+resident in HBM and every step streams each layer's active experts, so the
+working set is far above the 126 MB L2 and no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
+    python bench.py --impl reference ...   # the reference's CPU path, same metric
+
+Output: one JSON line on rank 0 (see the keys below). Multi-GPU (torchrun)
+runs one independent replica per GPU (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPE = dict(d=2048, E=128, k=8, m=768, norm=1, L=48)
+METRIC = "Qwen3-30B-A3B-shape Q4 MoE decode tok/s (48 MoE layers per step)"
+
+
+def rec_bytes(d, m):
+    return 3 * (m * d // 2 + m * d // 32)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.p, self.path = gpu, None, None
+
+    def __enter__(self):
+        try:
+            out = ROOT / "gpurun_out"
+            out.mkdir(exist_ok=True)
+            self.path = out / f"clocks_gpu{self.gpu}.csv"
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.path or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+def dist_init():
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(ws, v: float) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_store(moe, want_host_layers: int):
+    """Quantise seeded N(0,0.02) weights on the device into every layer; keep a
+    host copy (reference record layout) of the first `want_host_layers`."""
+    import torch
+    from joule_b200 import synth
+    from joule_b200.native import get_dll
+    cfg = moe.cfg
+    E, d, m = cfg.E, cfg.d, cfg.intermediate
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(1)
+    host = []
+    L = get_dll()
+    for l in range(cfg.L):
+        gw = synth.router_bf16(E, d, gen, dev)
+        ws = [torch.randn(E, m, d, generator=gen, device=dev) * 0.02,
+              torch.randn(E, m, d, generator=gen, device=dev) * 0.02,
+              torch.randn(E, d, m, generator=gen, device=dev) * 0.02]
+        if l < want_host_layers:
+            # reference-layout records on the device, then a host copy
+            pk = [[None] * E for _ in range(3)]
+            sc = [[None] * E for _ in range(3)]
+            for p in range(3):
+                n = m * d
+                spk = torch.empty(E, n // 2, dtype=torch.uint8, device=dev)
+                ssc = torch.empty(E, n // 64, dtype=torch.int16, device=dev)
+                for e in range(E):
+                    rc = L.jl_q4_quantize(ws[p][e].data_ptr(), n, ssc[e].data_ptr(), spk[e].data_ptr(),
+                                          torch.cuda.current_stream().cuda_stream)
+                    assert rc == 0
+                hp, hs = spk.cpu().numpy(), ssc.cpu().numpy().view(np.uint16)
+                for e in range(E):
+                    pk[p][e], sc[p][e] = hp[e], hs[e]
+            gwh = gw.cpu().numpy().view(np.uint16)
+            moe.upload_layer(l, gwh, pk, sc)
+            host.append((gwh, pk, sc))
+        else:
+            moe.quantize_layer(l, gw, *ws)
+        del ws
+    torch.cuda.synchronize()
+    return host
+
+
+def routing_unions(moe, xs, B):
+    import torch
+    U = []
+    out = torch.empty(B, moe.cfg.d, device="cuda")
+    for l in range(moe.cfg.L):
+        moe.forward(l, xs[l, :B], out)
+        U.append(moe.debug_routing(B)["U"])
+    moe.check()
+    return U
+
+
+def time_batch(moe, xs, outs, B, steps, warmup, ws):
+    """Device-resident timing: one CUDA graph per timed step (48 layers), with
+    phase events around every layer's kernels."""
+    import torch
+    L = moe.cfg.L
+    stream = torch.cuda.Stream()
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(L)]
+          for _ in range(steps)]
+    lib = moe._L
+    graphs = []
+    with torch.cuda.stream(stream):
+        for l in range(L):        # eager warm-up (sets kernel attributes outside capture)
+            moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
+        stream.synchronize()
+        for s in range(steps):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for l in range(L):
+                    import ctypes
+                    arr = (ctypes.c_void_p * 5)(*[e.cuda_event for e in ev[s][l]])
+                    lib.jl_moe_set_phase_events(moe.h, arr, 5)
+                    moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
+            graphs.append(g)
+        lib.jl_moe_set_phase_events(moe.h, None, 0)
+        for _ in range(warmup):
+            graphs[0].replay()
+        stream.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for g in graphs:
+        g.replay()
+    t1.record(stream)
+    t1.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    phase = np.zeros(4)
+    for s in range(steps):
+        for l in range(L):
+            e = ev[s][l]
+            for i in range(4):
+                phase[i] += e[i].elapsed_time(e[i + 1])
+    moe.check()
+    del graphs
+    return total_ms, phase / (steps * L)   # ms per layer-launch of each phase
+
+
+def e2e_dropin(host, B, steps, warmup, seed=11):
+    """jl_layer_ffn_batch (the reference-facing C-ABI call, host buffers): one
+    call per layer, each copying x in and out. Layers cycle over the host
+    layers kept (all 48 when memory allows)."""
+    import ctypes
+    from joule_b200.moe import layer_ffn_batch
+    from joule_b200.native import KernelCfg, KernelW
+    d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    nl = len(host)
+    cfg = KernelCfg(L=nl, d=d, E=E, topk=k, intermediate=m, norm_topk_prob=SHAPE["norm"])
+    gate = np.ascontiguousarray(np.stack([h[0] for h in host]))
+    keep = []
+    W = KernelW()
+    W.gate_w = gate.ctypes.data
+    for p in range(3):
+        pk = (ctypes.c_void_p * (nl * E))(*[host[l][1][p][e].ctypes.data for l in range(nl) for e in range(E)])
+        sc = (ctypes.c_void_p * (nl * E))(*[host[l][2][p][e].ctypes.data for l in range(nl) for e in range(E)])
+        keep += [pk, sc]
+        W.expert_pk[p] = ctypes.cast(pk, ctypes.c_void_p)
+        W.expert_sc[p] = ctypes.cast(sc, ctypes.c_void_p)
+    rng = np.random.default_rng(seed)
+    xs = rng.standard_normal((L, B, d)).astype(np.float32)
+    out = np.empty((B, d), np.float32)
+    for _ in range(max(warmup, 1)):
+        for l in range(L):
+            layer_ffn_batch(cfg, W, l % nl, xs[l], B, out)
+    t = time.perf_counter()
+    for _ in range(steps):
+        for l in range(L):
+            layer_ffn_batch(cfg, W, l % nl, xs[l], B, out)
+    dt = (time.perf_counter() - t) / steps
+    return dict(value=B / dt, unit="tok/s", h2d_bytes_per_step=L * B * d * 4,
+                d2h_bytes_per_step=L * B * d * 4, ms_per_step=dt * 1e3,
+                api="jl_layer_ffn_batch (host x/out, one call per layer)",
+                host_layers=nl), keep
+
+
+def cpu_baseline_ref(host_layer, B, budget_s=12.0):
+    """The reference's layer_ffn_batch (oracle/_ref) on this host's cores, one
+    layer (bounded sample), extrapolated to the 48-layer step."""
+    from oracle import ref
+    from oracle.layer import Q4Layer
+    if not ref.available():
+        return None
+    gwh, pk, sc = host_layer
+    d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    lay = Q4Layer(d, E, k, m, SHAPE["norm"], gwh, sc, pk)
+    R = ref.RefLayer(lay)
+    ncores = os.cpu_count() or 1
+    nthreads = max(1, min(16, ncores - 1))
+    R.L.spin_pool_init(nthreads)
+    x = np.random.default_rng(5).standard_normal((B, d)).astype(np.float32)
+    R.ffn(x)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and reps < 200:
+        R.ffn(x)
+        reps += 1
+    t_layer = (time.perf_counter() - t0) / reps
+    R.L.spin_pool_shutdown()
+    cores = 1 if B == 1 else nthreads + 1
+    return dict(value=B / (t_layer * L), unit="tok/s", cores=cores, kind="reference",
+                sample=f"1 Qwen3-shape layer x {reps} calls at B={B} (16-token chunks), "
+                       f"{t_layer * 1e3:.2f} ms/layer, x48 layers",
+                threads_note="B=1 runs on one thread by the reference's design "
+                             "(decode_kernel.c:1495-1497)" if B == 1 else
+                             f"spin_pool_init({nthreads}) + main thread",
+                cpu=cpu_model())
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
+def run_ours(a):
+    import torch
+    from joule_b200.moe import MoELayers, make_cfg
+    ws, rank, local = dist_init()
+    d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    sweep = sorted(set(int(b) for b in a.sweep.split(",")) | {a.batch})
+    Bmax = max(sweep)
+    moe = MoELayers(make_cfg(L, d, E, k, m, SHAPE["norm"]), Bmax)
+    host_layers = L if (a.e2e and rank == 0) else (1 if rank == 0 else 0)
+    t = time.time()
+    host = build_store(moe, host_layers)
+    setup_s = time.time() - t
+    gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+    xs = torch.randn(L, Bmax, d, generator=gen, device="cuda")
+    outs = torch.empty_like(xs)
+    hbm, peak_kind = peaks()
+    per_b = {}
+    head = None
+    clocks = None
+    # the headline batch runs last, with the clocks sampled over its timed region
+    for B in [b for b in sweep if b != a.batch] + [a.batch]:
+        U = routing_unions(moe, xs, B)
+        if B == a.batch:
+            with Clocks(local) as clk:
+                total_ms, phase = time_batch(moe, xs, outs, B, a.steps, a.warmup, ws)
+            clocks = clk.summary()
+        else:
+            total_ms, phase = time_batch(moe, xs, outs, B, a.steps, a.warmup, ws)
+        total_ms = max_over_ranks(ws, total_ms)
+        ms_step = total_ms / a.steps
+        layer_bytes = [u * rec_bytes(d, m) + E * d * 2 + 2 * B * d * 4 for u in U]
+        gu_bytes = [u * 2 * (m * d // 2 + m * d // 32) + B * d * 4 + B * k * m * 4 for u in U]
+        rec = dict(
+            tok_s=ws * B * a.steps / (total_ms / 1e3), ms_per_step=ms_step,
+            us_per_layer=ms_step * 1e3 / L, mean_U=float(np.mean(U)),
+            layer_gbs=sum(layer_bytes) / (ms_step / 1e3) / 1e9,
+            phase_us=dict(router=phase[0] * 1e3, gateup=phase[1] * 1e3, down=phase[2] * 1e3,
+                          combine=phase[3] * 1e3),
+            gateup_gbs=float(np.mean(gu_bytes)) / (phase[1] / 1e3) / 1e9,
+            gateup_bytes_per_launch=float(np.mean(gu_bytes)))
+        rec["layer_frac_of_hbm"] = rec["layer_gbs"] / hbm
+        per_b[str(B)] = rec
+        if B == a.batch:
+            head = rec
+    line = dict(metric=METRIC, value=head["tok_s"], unit="tok/s", n_gpus=ws, steps=a.steps,
+                warmup=a.warmup, ms_per_step=head["ms_per_step"], higher_is_better=True,
+                scaling="weak", vs_baseline=None, dtype="f32 (Q4 weights, fp32 accumulate)",
+                data="synthetic: seeded N(0,0.02) weights quantised to the reference Q4 format, "
+                     "x ~ N(0,1)",
+                config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
+                            batch=a.batch, layers=L, d=d, E=E, topk=k, intermediate=m,
+                            norm_topk_prob=1, path="exact (CUDA-core FP32, reference order)",
+                            l2="not flushed: each step streams >= 1 GB of distinct expert weights "
+                               "(store 15.4 GB) vs 126 MB L2",
+                            parallelism=f"replicas x{ws}" if ws > 1 else "single GPU",
+                            store_setup_s=round(setup_s, 1)),
+                per_batch=per_b)
+    line["roofline"] = dict(bound="hbm", kernel="k_gateup_exact (gate+up rows of the union experts)",
+                            achieved=head["gateup_gbs"], peak=hbm, unit="GB/s",
+                            frac=head["gateup_gbs"] / hbm, peak_kind=peak_kind,
+                            traffic=traffic_from_profiles(), layer_gbs=head["layer_gbs"],
+                            layer_frac=head["layer_gbs"] / hbm)
+    line["clocks"] = clocks
+    line["gpu_launches"] = launches_per_step(a.batch) * a.steps
+    if rank == 0 and a.e2e:
+        e2e, keep = e2e_dropin(host, a.batch, max(2, a.steps // 4), 1)
+        line["e2e"] = e2e
+    if rank == 0 and a.cpu:
+        line["cpu_baseline"] = cpu_baseline_ref(host[0], a.batch)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def launches_per_step(B):
+    # per layer: router (+topk, dispatch when B > 8), gate/up, down, combine
+    return SHAPE["L"] * (4 if B <= 8 else 6)
+
+
+def traffic_from_profiles():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("k_gateup_exact_bytes_per_launch"):
+            return float(line.split("=")[1].split()[0])
+    return None
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU path on this host's cores
+
+def run_reference(a):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import layer as olayer
+    from oracle import ref
+    if not ref.available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libjoule_ref.so not built (needs the reference sources)"}))
+        return
+    d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    nl = a.ref_layers
+    t = time.time()
+    lays = [olayer.make_layer(d, E, k, m, SHAPE["norm"], seed_router=10 + i, seed_experts=20 + i)
+            for i in range(nl)]
+    setup = time.time() - t
+    ncores = os.cpu_count() or 1
+    nthreads = max(1, min(16, ncores - 1))
+    R = [ref.RefLayer(lay) for lay in lays]
+    R[0].L.spin_pool_init(nthreads)
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((a.batch, d)).astype(np.float32)
+    for _ in range(a.warmup):
+        for r in R:
+            r.ffn(x)
+    times = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        for r in R:
+            r.ffn(x)
+        times.append(time.perf_counter() - t0)
+    R[0].L.spin_pool_shutdown()
+    t_layer = float(np.mean(times)) / nl
+    step = t_layer * L
+    val = a.batch / step
+    cores = 1 if a.batch == 1 else nthreads + 1
+    line = dict(metric=METRIC, value=val, unit="tok/s", n_gpus=ws, steps=a.steps, warmup=a.warmup,
+                ms_per_step=step * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None,
+                dtype="f32 (Q4 weights, fp32 accumulate)", impl="reference",
+                data="synthetic: seeded N(0,0.02) weights in the reference Q4 format, x ~ N(0,1)",
+                config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
+                            batch=a.batch, layers=L, d=d, E=E, topk=k, intermediate=m,
+                            norm_topk_prob=1, store_setup_s=round(setup, 1)),
+                cpu_baseline=dict(value=val, unit="tok/s", cores=cores, kind="reference",
+                                  sample=f"each step = {nl} distinct Qwen3-shape layers through the "
+                                         f"reference's layer_ffn_batch (B>16 as 16-token calls), "
+                                         f"time x{L}/{nl}",
+                                  cpu=cpu_model(), threads=nthreads),
+                e2e=dict(value=val, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--sweep", default="1,8,32,64")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-layers", type=int, default=2)
+    ap.add_argument("--no-e2e", dest="e2e", action="store_false")
+    ap.add_argument("--no-cpu", dest="cpu", action="store_false")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,211 @@
+/* joule_moe.h — C ABI of the B200 (sm_100a) MoE decode hot path.
+ *
+ * One MoE FFN layer at decode: router softmax/top-k -> token-to-expert
+ * dispatch -> grouped per-expert gate/up -> SwiGLU -> down over the Q4 expert
+ * store -> weighted combine. This library replaces the reference's CPU DLL
+ * for that path; every entry point below names the reference interface it
+ * replaces (paths relative to the reference project root).
+ *
+ * Conventions
+ *  - Plain C types only. `stream` is a cudaStream_t passed as void*
+ *    (NULL = the legacy default stream).
+ *  - Every function returns an int status: JL_OK (0) or a negative JL_ERR_*.
+ *    The reference's functions return void and clamp silently
+ *    (decode_kernel.c:1522); here a bad argument is an error instead.
+ *  - Pointers documented "device" must be CUDA device (or managed) memory;
+ *    "host" pointers are ordinary CPU memory.
+ *  - A jl_moe handle is not reentrant: calls on one handle must be issued
+ *    from one host thread at a time (the reference serialises its global
+ *    workspace the same way, session_manager.py:78-87). Different handles
+ *    are independent.
+ */
+#ifndef JOULE_MOE_H
+#define JOULE_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JL_OK 0
+#define JL_ERR_INVALID (-1)  /* bad argument or unsupported shape */
+#define JL_ERR_OOM (-2)      /* device or pinned-host allocation failed */
+#define JL_ERR_CUDA (-3)     /* a CUDA runtime call failed */
+#define JL_ERR_TIMEOUT (-4)  /* a bounded device-side wait ran out */
+#define JL_ERR_CAPACITY (-5) /* B (or B*topk) above the handle's capacity */
+#define JL_ERR_NOT_READY (-6)/* layer weights not uploaded yet */
+#define JL_ERR_DEVICE (-7)   /* a kernel reported a bad index / state */
+
+/* Same field order and types as the reference's KernelCfg
+ * (decode_kernel.c:269-286, decoder3.py:35-46): a caller's existing struct
+ * can be passed unchanged. Only d, E, topk, intermediate, norm_topk_prob
+ * and L are read by this library. */
+typedef struct {
+    int L, d, n_heads, n_kv, hd, E, topk, V;
+    float eps;
+    int maxT;
+    int intermediate;
+    int qk_norm_type;
+    int bias_qkv;
+    int norm_topk_prob;
+    int expert_i8;
+    int expert_bf16;
+} KernelCfg;
+
+/* Same layout as the reference's KernelW (decode_kernel.c:288-325,
+ * decoder3.py:49-69). Only gate_w ([L, E, d] bf16) and the Q4 pointer tables
+ * expert_pk[p][l*E+e] / expert_sc[p][l*E+e] (p = gate, up, down; the tables
+ * built by decoder3.py:329-367) are read, and only as HOST memory. */
+typedef struct {
+    const unsigned short* embed;
+    const unsigned short* lm_head;
+    const unsigned short* final_norm;
+    const unsigned short* norm1;
+    const unsigned short* norm2;
+    const unsigned short* wq;
+    const unsigned short* wk;
+    const unsigned short* wv;
+    const unsigned short* wo;
+    const float* bq;
+    const float* bk;
+    const float* bv;
+    const unsigned short* qn;
+    const unsigned short* kn;
+    const unsigned short* gate_w;
+    const unsigned short* w1;
+    const unsigned short* w2;
+    const unsigned short* w3;
+    const unsigned char* wq_i8;
+    const float* wq_i8s;
+    const unsigned char* wk_i8;
+    const float* wk_i8s;
+    const unsigned char* wv_i8;
+    const float* wv_i8s;
+    const unsigned char* wo_i8;
+    const float* wo_i8s;
+    const unsigned char* lm_i8;
+    const float* lm_i8s;
+    const unsigned char* const* expert_pk[3];
+    const unsigned short* const* expert_sc[3];
+    const float* cos;
+    const float* sin;
+    int use_i8;
+} KernelW;
+
+/* ------------------------------------------------------------------ */
+/* Q4 GEMV / GEMM over the reference's record layout (device pointers). */
+
+/* out[m] = dequant(packed, scales)[m, d] @ x[d].
+ * Replaces q4_gemv_f32 (src/jouleai/native/quant_gemv.c:35-57, bound by
+ * kernel.py:24-44 and backend.py:92-103). packed: [m, d/2] u8, scales:
+ * [m, d/group] fp16 bits, x: [d] fp32, out: [m] fp32 — all device memory.
+ * group must be 64 and d a multiple of 64. The sum follows the reference's
+ * AVX2 row dot exactly (decode_kernel.c:770-858), so the result is
+ * bit-identical to expert_ffn.c's q4_gemv_f32 built for AVX2. */
+int jl_q4_gemv_f32(float* out, const float* x, const unsigned char* packed,
+                   const unsigned short* scales, int m, int d, int group,
+                   void* stream);
+
+/* out[T, m] = X[T, d] @ dequant(W)^T. Replaces q4_gemm_f32
+ * (src/jouleai/native/expert_ffn.c:200-215, bound by kernel.py:47-62 and
+ * backend.py:119-129). Device pointers; same arithmetic as jl_q4_gemv_f32. */
+int jl_q4_gemm_f32(float* out, const float* X, int T,
+                   const unsigned char* packed, const unsigned short* scales,
+                   int m, int d, int group, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Q4 store: on-device quantiser and repack. */
+
+/* Quantise n fp32 values (device) into the reference's Q4 record format:
+ * scales [ceil(n/64)] fp16 bits and packed [ceil(n/64)*32] u8 (device).
+ * Bit-identical to _quantize_tensor (src/jouleai/storage/q4_store.py:40-55),
+ * which convert_experts_q4 (q4_store.py:125-166) applies per expert tensor. */
+int jl_q4_quantize(const float* x, long long n, unsigned short* scales,
+                   unsigned char* packed, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* The MoE layer. */
+
+typedef struct jl_moe jl_moe;
+
+/* Create a handle for one model's MoE layers on the current device.
+ * Reads cfg->L, d, E, topk, intermediate, norm_topk_prob. max_tokens is the
+ * largest B one forward call may pass (no BMAX=16 clamp as in
+ * decode_kernel.c:1522). Allocates the HBM expert store for all L layers and
+ * the workspace. Replaces the expert part of NativeDecoder.__init__ /
+ * _load_experts (decoder3.py:86-163, 329-367) and ws_init
+ * (decode_kernel.c:382-424). */
+int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out);
+int jl_moe_destroy(jl_moe* h);
+
+/* Upload layer l: router rows gate_w [E, d] bf16 and, for each part p in
+ * (gate, up, down) and expert e, the Q4 record pk[p*E+e] / sc[p*E+e] in the
+ * reference layout (the pointers decoder3.py:355-361 builds). Pointers may
+ * be host or device memory (`src_on_device`). The records are repacked into
+ * the device tile layout on `stream`; host sources are staged through a
+ * pinned buffer. */
+int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_w,
+                        const unsigned char* const* pk,
+                        const unsigned short* const* sc, int src_on_device,
+                        void* stream);
+
+/* Quantise and upload layer l from fp32 weights already on the device:
+ * gate_w [E, d] bf16; w_gate/w_up [E, m, d] and w_down [E, d, m] fp32. The
+ * store then holds exactly what convert_experts_q4 would have written. */
+int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
+                          const float* w_gate, const float* w_up,
+                          const float* w_down, void* stream);
+
+/* Path selection for jl_moe_forward. */
+#define JL_PATH_AUTO 0  /* exact for B <= 8, tensor-core beyond */
+#define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order */
+#define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
+int jl_moe_set_path(jl_moe* h, int path);
+
+/* One MoE FFN layer: out[B, d] = MoE(x[B, d]) for layer l (device fp32).
+ * Replaces layer_ffn_batch (decode_kernel.c:1387-1508) as called from
+ * decode_layers_batch[_argmax] (decode_kernel.c:1535, 1577). top/tw
+ * (nullable, device) receive the router's top-k ids [B, topk] int32 and
+ * weights [B, topk] fp32. Enqueued on `stream`; returns after launch. */
+int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out,
+                   int* top, float* tw, void* stream);
+
+/* Debug / parity: copies (device) the router logits [B, E], the union
+ * experts sel [U], offsets uh [U+1] and the slot map uidx/uw [B*topk] built
+ * by the last jl_moe_forward (decode_kernel.c:1424-1485). *U_out (host)
+ * receives U. Synchronises `stream`. */
+int jl_moe_debug_routing(jl_moe* h, int B, float* logits, int* sel, int* uh,
+                         int* uidx, float* uw, int* U_out, void* stream);
+
+/* Read and clear the handle's device error word (bounded waits that ran
+ * out, bad expert ids). Synchronises `stream`. Returns JL_OK or the error. */
+int jl_moe_check(jl_moe* h, void* stream);
+
+/* Host-buffer drop-in for layer_ffn_batch(c, W, l, x, B, out)
+ * (decode_kernel.c:1387): x and out are HOST fp32 [B, d]. On first use of a
+ * (c, W) pair the L layers of W's expert tables are uploaded to a cached
+ * handle; each call copies x to the device, runs jl_moe_forward and copies
+ * out back (synchronous). */
+int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l,
+                       const float* x, int B, float* out);
+
+/* Phase timing: when n > 0, each jl_moe_forward records events[0] before the
+ * router, events[1] after it, events[2] after gate/up+SwiGLU, events[3]
+ * after down and events[4] after the combine (n <= 5 records the first n),
+ * on the forward's stream. events are cudaEvent_t handles; n = 0 turns it
+ * off. No counterpart in the reference (its profiling is wall-clock,
+ * batch_bench.py:58-68). */
+int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n);
+
+/* Bytes of device memory the handle holds (store + workspace). */
+long long jl_moe_device_bytes(const jl_moe* h);
+
+/* Library version string, e.g. "joule_b200 0.1 sm_100a". */
+const char* jl_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

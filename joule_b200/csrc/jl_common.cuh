@@ -1,0 +1,185 @@
+// Shared device helpers for the sm_100a MoE kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "joule_moe.h"
+
+#define JL_CUDA(call)                                   \
+    do {                                                \
+        cudaError_t _e = (call);                        \
+        if (_e != cudaSuccess) return JL_ERR_CUDA;      \
+    } while (0)
+
+#define JL_LAUNCH_CHECK()                                   \
+    do {                                                    \
+        if (cudaGetLastError() != cudaSuccess) return JL_ERR_CUDA; \
+    } while (0)
+
+namespace jl {
+
+constexpr int kGroup = 64;        // Q4 group (q4_store.py:23)
+constexpr int kGroupBytes = 32;   // packed bytes per group
+constexpr int kTileRows = 32;     // rows per device tile
+constexpr int kTileBytes = kTileRows * kGroupBytes;  // 1024
+
+// Device error codes written into a handle's error word.
+constexpr int kErrTimeout = 1;
+constexpr int kErrBadExpert = 2;
+constexpr int kErrCapacity = 4;
+
+// ---------------------------------------------------------------------------
+// Exact scalar conversions and the reference's expf_fast.
+
+// bf16 bits -> fp32 (decode_kernel.c:47-53): the bits are the top half.
+__device__ __forceinline__ float bf16_to_f32(uint32_t h) {
+    return __uint_as_float(h << 16);
+}
+
+// fp16 bits -> fp32, exactly as decode_kernel.c:64-85 (subnormals
+// normalised, inf/NaN payload kept).
+__device__ __forceinline__ float fp16_to_f32(uint32_t h) {
+    const uint32_t sign = (h & 0x8000u) << 16;
+    const uint32_t ex = (h >> 10) & 0x1Fu;
+    const uint32_t man = h & 0x3FFu;
+    if (ex == 0u) {
+        // man * 2^-24 is exact in fp32 for man < 1024
+        const float v = __fmul_rn(__uint2float_rn(man), 5.9604644775390625e-8f);
+        return __uint_as_float(__float_as_uint(v) | sign);
+    }
+    if (ex == 31u) return __uint_as_float(sign | 0x7F800000u | (man << 13));
+    return __uint_as_float(sign | ((ex + 112u) << 23) | (man << 13));
+}
+
+// The reference's own expf approximation (decode_kernel.c:94-108), with every
+// product and sum rounded separately as in its C source.
+__device__ __forceinline__ float expf_fast(float v) {
+    if (v < -17.0f) return 0.0f;
+    if (v > 88.0f) v = 88.0f;
+    const float y = __fmul_rn(v, 1.4426950408889634f);
+    const int k = __float2int_rz(__fadd_rn(y, y >= 0.0f ? 0.5f : -0.5f));
+    const float f = __fsub_rn(y, __int2float_rn(k));
+    float p = 0.0013330f;
+    p = __fadd_rn(0.0096181f, __fmul_rn(f, p));
+    p = __fadd_rn(0.0555041f, __fmul_rn(f, p));
+    p = __fadd_rn(0.2402265f, __fmul_rn(f, p));
+    p = __fadd_rn(0.6931472f, __fmul_rn(f, p));
+    p = __fadd_rn(1.0f, __fmul_rn(f, p));
+    int kk = k + 127;
+    if (kk < 0) return 0.0f;
+    if (kk > 254) kk = 254;
+    return __fmul_rn(p, __uint_as_float((uint32_t)kk << 23));
+}
+
+// silu(g) * u as the reference writes it: (g / (1 + expf_fast(-g))) * u.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float den = __fadd_rn(1.0f, expf_fast(-g));
+    return __fmul_rn(__fdiv_rn(g, den), u);
+}
+
+// Horizontal sum of an 8-lane AVX accumulator in the reference's order
+// (decode_kernel.c:843-846): ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)).
+__device__ __forceinline__ float hsum8(const float (&l)[8]) {
+    const float s0 = __fadd_rn(l[0], l[4]), s1 = __fadd_rn(l[1], l[5]);
+    const float s2 = __fadd_rn(l[2], l[6]), s3 = __fadd_rn(l[3], l[7]);
+    return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+}
+
+// Eight Q4 values of one 32-bit word as exact floats (nib - 8). Element j of
+// the word is nibble j (bits 4j..4j+3): byte j/2, low nibble first
+// (q4_store.py:53). Each nibble is OR-ed into the mantissa of 2^23 at its own
+// bit position and rescaled by an exact FMA, so no shift is needed for the
+// low five nibbles.
+__device__ __forceinline__ void dequant8(uint32_t w, float (&a)[8]) {
+    const uint32_t M = 0x4B000000u;  // 2^23
+    a[0] = __fadd_rn(__uint_as_float((w & 0x0000000Fu) | M), -8388616.0f);
+    a[1] = __fmaf_rn(__uint_as_float((w & 0x000000F0u) | M), 0.0625f, -524296.0f);
+    a[2] = __fmaf_rn(__uint_as_float((w & 0x00000F00u) | M), 0.00390625f, -32776.0f);
+    a[3] = __fmaf_rn(__uint_as_float((w & 0x0000F000u) | M), 0.000244140625f, -2056.0f);
+    a[4] = __fmaf_rn(__uint_as_float((w & 0x000F0000u) | M), 1.52587890625e-05f, -136.0f);
+    const uint32_t h = w >> 12;  // nibbles 5..7 -> bits 8..19
+    a[5] = __fmaf_rn(__uint_as_float((h & 0x00000F00u) | M), 0.00390625f, -32776.0f);
+    a[6] = __fmaf_rn(__uint_as_float((h & 0x0000F000u) | M), 0.000244140625f, -2056.0f);
+    a[7] = __fmaf_rn(__uint_as_float((h & 0x000F0000u) | M), 1.52587890625e-05f, -136.0f);
+}
+
+// ---------------------------------------------------------------------------
+// Bounded waits, mbarriers and 1-D bulk copies (TMA, no multicast).
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of an mbarrier with a time bound. On timeout the
+// error word gets kErrTimeout and false is returned.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (err) atomicOr(err, kErrTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Global -> shared bulk copy completing on `bar` (bytes % 16 == 0, both
+// addresses 16-byte aligned). Source is this GPU's own memory; no multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace jl

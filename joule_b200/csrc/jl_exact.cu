@@ -1,0 +1,315 @@
+// Expert FFN on CUDA cores in the reference's FP32 arithmetic order
+// (ffn_expert_worker Q4 branch, decode_kernel.c:1365-1384, with the row dot
+// q4_row_dot_B, decode_kernel.c:770-858), so the layer output is
+// bit-identical to the reference's for the same inputs.
+//
+// Work decomposition: a (row, 64-value group) product p = hsum8(...) * scale
+// is independent of every other; only the per-row sum over groups is a
+// sequential chain. Each block stages one 32-row block of an expert's
+// matrices with 1-D bulk copies (one mbarrier per warp), every thread
+// computes p for its row of a tile (lane = row), and one warp then runs the
+// per-row chains from shared memory. Tokens routed to the expert are staged
+// in shared memory and read as warp-uniform broadcasts.
+#include "jl_common.cuh"
+#include "jl_internal.h"
+
+namespace jl {
+
+constexpr int kGuWarps = 8;    // gate/up block: warps 0-3 gate, 4-7 up
+constexpr int kGuTok = 2;      // tokens per pass (gate/up)
+constexpr int kDnWarps = 4;
+constexpr int kDnTok = 4;      // tokens per pass (down)
+
+// p for NT tokens of one tile row: q0/q1 = the row's 32 bytes, xs = token
+// rows (stride `xstride`) starting at this group's first column.
+template <int NT>
+__device__ __forceinline__ void tile_row_products(uint4 q0, uint4 q1, float s, const float* xs,
+                                                  int xstride, float (&p)[NT]) {
+    const uint32_t wq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    float lane[NT][8];
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) lane[t][j] = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        float a[8];
+        dequant8(wq[w], a);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float4 x0 = *reinterpret_cast<const float4*>(xs + t * xstride + w * 8);
+            const float4 x1 = *reinterpret_cast<const float4*>(xs + t * xstride + w * 8 + 4);
+            lane[t][0] = __fmaf_rn(a[0], x0.x, lane[t][0]);
+            lane[t][1] = __fmaf_rn(a[1], x0.y, lane[t][1]);
+            lane[t][2] = __fmaf_rn(a[2], x0.z, lane[t][2]);
+            lane[t][3] = __fmaf_rn(a[3], x0.w, lane[t][3]);
+            lane[t][4] = __fmaf_rn(a[4], x1.x, lane[t][4]);
+            lane[t][5] = __fmaf_rn(a[5], x1.y, lane[t][5]);
+            lane[t][6] = __fmaf_rn(a[6], x1.z, lane[t][6]);
+            lane[t][7] = __fmaf_rn(a[7], x1.w, lane[t][7]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++) p[t] = __fmul_rn(hsum8(lane[t]), s);
+}
+
+// Products for every tile a warp owns, for `nt` (<= NTMAX) tokens.
+// Tiles are [g_lo, g_hi) of part `pi` (smem tile index pi*ng + g).
+template <int NTMAX>
+__device__ __forceinline__ void warp_tiles(const uint8_t* w_s, const uint16_t* sc_s,
+                                           const float* x_s, int xstride, float* p_s, int pi,
+                                           int ng, int g_lo, int g_hi, int nt) {
+    const int lane = threadIdx.x & 31;
+    for (int g = g_lo; g < g_hi; g++) {
+        const int ti = pi * ng + g;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(w_s + (size_t)ti * kTileBytes + lane * 16);
+        const uint4 q1 =
+            *reinterpret_cast<const uint4*>(w_s + (size_t)ti * kTileBytes + 512 + lane * 16);
+        const float s = fp16_to_f32(sc_s[ti * kTileRows + lane]);
+        const float* xg = x_s + g * kGroup;
+        // p_s layout: [(pi*NTMAX + t)*ng + g][32]
+        if (nt == 1) {
+            float p[1];
+            tile_row_products<1>(q0, q1, s, xg, xstride, p);
+            p_s[((pi * NTMAX + 0) * ng + g) * 32 + lane] = p[0];
+        } else if (NTMAX >= 2 && nt == 2) {
+            float p[2];
+            tile_row_products<2>(q0, q1, s, xg, xstride, p);
+#pragma unroll
+            for (int t = 0; t < 2; t++) p_s[((pi * NTMAX + t) * ng + g) * 32 + lane] = p[t];
+        } else if (NTMAX >= 3 && nt == 3) {
+            float p[3];
+            tile_row_products<3>(q0, q1, s, xg, xstride, p);
+#pragma unroll
+            for (int t = 0; t < 3; t++) p_s[((pi * NTMAX + t) * ng + g) * 32 + lane] = p[t];
+        } else if (NTMAX >= 4) {
+            float p[4];
+            tile_row_products<4>(q0, q1, s, xg, xstride, p);
+#pragma unroll
+            for (int t = 0; t < 4; t++) p_s[((pi * NTMAX + t) * ng + g) * 32 + lane] = p[t];
+        }
+    }
+}
+
+// Issue this warp's bulk copies (tiles + scales) on its own mbarrier.
+__device__ __forceinline__ void warp_stage(uint8_t* w_dst, uint16_t* sc_dst, const uint8_t* w_src,
+                                           const uint16_t* sc_src, int ntiles, uint64_t* bar) {
+    if ((threadIdx.x & 31) == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+        if (ntiles > 0) {
+            const uint32_t tb = (uint32_t)ntiles * kTileBytes, sb = (uint32_t)ntiles * kTileRows * 2;
+            mbar_expect_tx(bar, tb + sb);
+            bulk_g2s(w_dst, w_src, tb, bar);
+            bulk_g2s(sc_dst, sc_src, sb, bar);
+        } else {
+            mbar_arrive(bar);
+        }
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// gate/up + SwiGLU. grid = (m/32 row blocks, max union size); block (rb, u)
+// handles rows 32rb..32rb+31 of expert sel[u]'s gate and up for all of its
+// tokens and writes act[slot][row] = silu(g) * u.
+__global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
+    const uint8_t* __restrict__ store_l, jl_layout L, int k, const float* __restrict__ x,
+    jl_ws ws) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int d = L.d, m = L.m, ng = d / kGroup;
+    const int rb = blockIdx.x, u = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* w_s = smem;                                                   // [2*ng] tiles
+    uint16_t* sc_s = reinterpret_cast<uint16_t*>(w_s + (size_t)2 * ng * kTileBytes);  // [2*ng*32]
+    float* x_s = reinterpret_cast<float*>(sc_s + 2 * ng * kTileRows);     // [kGuTok, d]
+    float* p_s = x_s + kGuTok * d;                                         // [2, kGuTok, ng, 32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + 2 * kGuTok * ng * 32);
+    griddep_wait();
+    if (u >= *ws.U) return;
+    const int e = ws.sel[u];
+    const int s0 = ws.uh[u], n = ws.uh[u + 1] - s0;
+    const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
+    const int pi = warp >> 2, q = warp & 3;
+    const int g_lo = q * ng / 4, g_hi = (q + 1) * ng / 4;
+    {
+        const size_t t0 = (size_t)rb * ng + g_lo;
+        warp_stage(w_s + (size_t)(pi * ng + g_lo) * kTileBytes, sc_s + (pi * ng + g_lo) * kTileRows,
+                   rec + L.tiles_off(pi) + t0 * kTileBytes,
+                   reinterpret_cast<const uint16_t*>(rec + L.scales_off(pi)) + t0 * kTileRows,
+                   g_hi - g_lo, &bars[warp]);
+    }
+    bool ok = true;
+    for (int c0 = 0; c0 < n; c0 += kGuTok) {
+        const int nt = min(kGuTok, n - c0);
+        for (int i = threadIdx.x; i < nt * d / 4; i += blockDim.x) {
+            const int t = i / (d / 4), c = i % (d / 4);
+            const int b = ws.uidx[s0 + c0 + t] / k;
+            reinterpret_cast<float4*>(x_s + t * d)[c] =
+                reinterpret_cast<const float4*>(x + (size_t)b * d)[c];
+        }
+        __syncthreads();
+        if (c0 == 0) ok = mbar_wait_bounded(&bars[warp], 0, ws.err);
+        if (ok) warp_tiles<kGuTok>(w_s, sc_s, x_s, d, p_s, pi, ng, g_lo, g_hi, nt);
+        __syncthreads();
+        if (warp == 0) {
+            for (int t = 0; t < nt; t++) {
+                float ga = 0.0f, ua = 0.0f;
+                const float* pg = p_s + (size_t)((0 * kGuTok + t) * ng) * 32 + lane;
+                const float* pu = p_s + (size_t)((1 * kGuTok + t) * ng) * 32 + lane;
+                for (int g = 0; g < ng; g++) {
+                    ga = __fadd_rn(ga, pg[g * 32]);
+                    ua = __fadd_rn(ua, pu[g * 32]);
+                }
+                const int slot = ws.uidx[s0 + c0 + t];
+                ws.act[(size_t)slot * m + rb * kTileRows + lane] = silu_mul(ga, ua);
+            }
+        }
+        __syncthreads();
+    }
+    if (n == 0) mbar_wait_bounded(&bars[warp], 0, ws.err);  // never leave copies in flight
+}
+
+// ---------------------------------------------------------------------------
+// down. grid = (d/32 row blocks, max union size); block (rb, u) handles rows
+// 32rb..32rb+31 of expert sel[u]'s down matrix for all of its tokens and
+// writes y[slot][row] = 0 + w * dacc (the reference's `ye += uw * dacc`
+// onto a zeroed ye).
+__global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __restrict__ store_l,
+                                                              jl_layout L, jl_ws ws) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int d = L.d, m = L.m, ng = m / kGroup;
+    const int rb = blockIdx.x, u = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* w_s = smem;
+    uint16_t* sc_s = reinterpret_cast<uint16_t*>(w_s + (size_t)ng * kTileBytes);
+    float* a_s = reinterpret_cast<float*>(sc_s + ng * kTileRows);  // [kDnTok, m]
+    float* p_s = a_s + kDnTok * m;                                 // [kDnTok, ng, 32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kDnTok * ng * 32);
+    griddep_wait();
+    if (u >= *ws.U) return;
+    const int e = ws.sel[u];
+    const int s0 = ws.uh[u], n = ws.uh[u + 1] - s0;
+    const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
+    const int g_lo = warp * ng / kDnWarps, g_hi = (warp + 1) * ng / kDnWarps;
+    {
+        const size_t t0 = (size_t)rb * ng + g_lo;
+        warp_stage(w_s + (size_t)g_lo * kTileBytes, sc_s + g_lo * kTileRows,
+                   rec + L.tiles_off(2) + t0 * kTileBytes,
+                   reinterpret_cast<const uint16_t*>(rec + L.scales_off(2)) + t0 * kTileRows,
+                   g_hi - g_lo, &bars[warp]);
+    }
+    bool ok = true;
+    for (int c0 = 0; c0 < n; c0 += kDnTok) {
+        const int nt = min(kDnTok, n - c0);
+        for (int i = threadIdx.x; i < nt * m / 4; i += blockDim.x) {
+            const int t = i / (m / 4), c = i % (m / 4);
+            const int slot = ws.uidx[s0 + c0 + t];
+            reinterpret_cast<float4*>(a_s + t * m)[c] =
+                reinterpret_cast<const float4*>(ws.act + (size_t)slot * m)[c];
+        }
+        __syncthreads();
+        if (c0 == 0) ok = mbar_wait_bounded(&bars[warp], 0, ws.err);
+        if (ok) warp_tiles<kDnTok>(w_s, sc_s, a_s, m, p_s, 0, ng, g_lo, g_hi, nt);
+        __syncthreads();
+        if (warp == 0) {
+            for (int t = 0; t < nt; t++) {
+                float acc = 0.0f;
+                const float* pp = p_s + (size_t)(t * ng) * 32 + lane;
+                for (int g = 0; g < ng; g++) acc = __fadd_rn(acc, pp[g * 32]);
+                const int pos = s0 + c0 + t;
+                const int slot = ws.uidx[pos];
+                ws.y[(size_t)slot * d + rb * kTileRows + lane] =
+                    __fadd_rn(0.0f, __fmul_rn(ws.uw[pos], acc));
+            }
+        }
+        __syncthreads();
+    }
+    if (n == 0) mbar_wait_bounded(&bars[warp], 0, ws.err);
+}
+
+// ---------------------------------------------------------------------------
+// Combine (decode_kernel.c:1490-1507): out[b] = 0 + y of b's experts in union
+// order (experts b did not choose contribute +0 in the reference, which
+// leaves every nonzero partial sum unchanged). Also copies top/tw out.
+__global__ void k_combine(int B, int k, int d, jl_ws ws, float* __restrict__ out,
+                          int* __restrict__ top, float* __restrict__ tw) {
+    griddep_wait();
+    const int b = blockIdx.y;
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (c < d) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < k; j++) {
+            const int slot = ws.comb[b * k + j];
+            const float4 v = *reinterpret_cast<const float4*>(ws.y + (size_t)slot * d + c);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        *reinterpret_cast<float4*>(out + (size_t)b * d + c) = acc;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < k) {
+        if (top) top[b * k + threadIdx.x] = ws.top[b * k + threadIdx.x];
+        if (tw) tw[b * k + threadIdx.x] = ws.tw[b * k + threadIdx.x];
+    }
+}
+
+size_t gateup_smem(int d) {
+    const int ng = d / kGroup;
+    return (size_t)2 * ng * kTileBytes + (size_t)2 * ng * kTileRows * 2 + (size_t)kGuTok * d * 4 +
+           (size_t)2 * kGuTok * ng * 32 * 4 + kGuWarps * 8;
+}
+size_t down_smem(int m) {
+    const int ng = m / kGroup;
+    return (size_t)ng * kTileBytes + (size_t)ng * kTileRows * 2 + (size_t)kDnTok * m * 4 +
+           (size_t)kDnTok * ng * 32 * 4 + kDnWarps * 8;
+}
+
+}  // namespace jl
+
+static int exact_attrs() {
+    using namespace jl;
+    static bool attr = false;
+    if (!attr) {
+        JL_CUDA(cudaFuncSetAttribute(k_gateup_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        JL_CUDA(cudaFuncSetAttribute(k_down_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        attr = true;
+    }
+    return JL_OK;
+}
+
+int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
+                           cudaStream_t s) {
+    using namespace jl;
+    const int umax = std::min(h->E, B * h->k);
+    const size_t gsm = gateup_smem(h->d);
+    if (gsm > 220 * 1024) return JL_ERR_INVALID;
+    int rc = exact_attrs();
+    if (rc) return rc;
+    k_gateup_exact<<<dim3(h->m / kTileRows, umax), kGuWarps * 32, gsm, s>>>(store_l, h->lay, h->k,
+                                                                            x, h->ws);
+    JL_LAUNCH_CHECK();
+    return JL_OK;
+}
+
+int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s) {
+    using namespace jl;
+    const int umax = std::min(h->E, B * h->k);
+    const size_t dsm = down_smem(h->m);
+    if (dsm > 220 * 1024) return JL_ERR_INVALID;
+    int rc = exact_attrs();
+    if (rc) return rc;
+    k_down_exact<<<dim3(h->d / kTileRows, umax), kDnWarps * 32, dsm, s>>>(store_l, h->lay, h->ws);
+    JL_LAUNCH_CHECK();
+    return JL_OK;
+}
+
+int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s) {
+    using namespace jl;
+    const int tpb = 128;
+    dim3 grid((h->d / 4 + tpb - 1) / tpb, B);
+    k_combine<<<grid, tpb, 0, s>>>(B, h->k, h->d, h->ws, out, top, tw);
+    JL_LAUNCH_CHECK();
+    return JL_OK;
+}

@@ -1,0 +1,87 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "joule_moe.h"
+
+// Device tile layout of one part matrix W[R, C] (R % 32 == 0, C % 64 == 0):
+// tiles (rb, g) for row block rb < R/32 and group g < C/64, tile index
+// rb*(C/64) + g, 1024 bytes each: [half h][row t][16 B] = bytes 16h..16h+15
+// of row (32 rb + t)'s group g. Scales: fp16 at (rb*(C/64) + g)*32 + t.
+// A warp reading one tile (lane t = row t) issues two fully coalesced
+// 512-byte loads and one 64-byte scale load.
+//
+// One expert record (per layer, per expert; record bytes identical to the
+// reference's three Q4 records, q4_store.py:150-158):
+//   [gate tiles m*d/2][up tiles m*d/2][down tiles d*m/2]
+//   [gate scales m*d/32][up scales m*d/32][down scales d*m/32]
+struct jl_layout {
+    int d, m, E;
+    size_t part_tiles;    // m*d/2 (every part has m*d values)
+    size_t part_scales;   // m*d/32 bytes
+    size_t rec_bytes;     // 3*(part_tiles + part_scales)
+    __host__ __device__ size_t tiles_off(int p) const { return (size_t)p * part_tiles; }
+    __host__ __device__ size_t scales_off(int p) const {
+        return 3 * part_tiles + (size_t)p * part_scales;
+    }
+};
+
+// Device workspace of one handle (all device pointers).
+struct jl_ws {
+    float* logits;   // [Bmax, E]
+    int* top;        // [Bmax, k]
+    float* tw;       // [Bmax, k]
+    int* U;          // [1] union size
+    int* sel;        // [E] union position -> expert
+    int* uh;         // [E+1] union position -> first index into uidx/uw
+    int* uidx;       // [Bmax*k] slots grouped by union position (slot order inside)
+    float* uw;       // [Bmax*k] routing weight of uidx[i]
+    int* comb;       // [Bmax*k] per token, its slots in union order
+    int* slot_pos;   // [Bmax*k] slot -> index into uidx
+    float* act;      // [Bmax*k, m] SwiGLU output per slot
+    float* y;        // [Bmax*k, d] weighted expert output per slot
+    int* counter;    // [1] last-block counter of the router kernel
+    int* err;        // [1] device error word (jl::kErr* bits)
+};
+
+struct jl_moe {
+    int device;
+    int L, d, E, k, m, norm;
+    int max_tokens;
+    int path;
+    jl_layout lay;
+    unsigned short* gate_w;   // [L, E, d] bf16
+    uint8_t* store;           // [L, E] records
+    unsigned char* uploaded;  // host flags [L]
+    jl_ws ws;
+    void* ws_base;
+    size_t ws_bytes;
+    size_t store_bytes;
+    int last_B;
+    cudaEvent_t phase_ev[5];  // optional phase timing events
+    int n_phase_ev;
+    // host staging for uploads from host memory
+    void* pinned;
+    size_t pinned_bytes;
+    uint8_t* dev_stage;       // device staging for one expert's reference records
+    size_t dev_stage_bytes;
+};
+
+// ---- launchers (return JL_OK or JL_ERR_*) --------------------------------
+
+// jl_store.cu
+int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int R, int C,
+                          uint8_t* tiles, uint16_t* scales, cudaStream_t s);
+
+// jl_router.cu: logits + (small B) top-k + dispatch; (large B) separate kernels.
+int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float* x, int B,
+                    cudaStream_t s);
+
+// jl_exact.cu: CUDA-core expert FFN in the reference's arithmetic order.
+int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
+                           cudaStream_t s);
+int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
+int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s);

@@ -1,0 +1,348 @@
+// Handle, store upload and the layer forward of the C ABI (joule_moe.h).
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "jl_common.cuh"
+#include "jl_internal.h"
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int check_shape(const KernelCfg* c) {
+    if (!c) return JL_ERR_INVALID;
+    if (c->L < 1 || c->d < 64 || c->E < 1 || c->topk < 1 || c->intermediate < 64)
+        return JL_ERR_INVALID;
+    if (c->d % 64 || c->intermediate % 64) return JL_ERR_INVALID;  // whole Q4 groups
+    if (c->E > 256 || c->topk > 16 || c->topk > c->E) return JL_ERR_INVALID;
+    if (c->expert_i8 || c->expert_bf16) return JL_ERR_INVALID;       // Q4 store only
+    return JL_OK;
+}
+
+struct ws_plan {
+    size_t off[14];
+    size_t total;
+};
+
+ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
+    const size_t S = (size_t)Bmax * k;
+    const size_t sizes[14] = {
+        (size_t)Bmax * E * 4,  // logits
+        S * 4,                 // top
+        S * 4,                 // tw
+        16,                    // U
+        (size_t)E * 4,         // sel
+        ((size_t)E + 1) * 4,   // uh
+        S * 4,                 // uidx
+        S * 4,                 // uw
+        S * 4,                 // comb
+        S * 4,                 // slot_pos
+        S * m * 4,             // act
+        S * d * 4,             // y
+        16,                    // counter
+        16,                    // err
+    };
+    ws_plan p;
+    size_t o = 0;
+    for (int i = 0; i < 14; i++) {
+        p.off[i] = o;
+        o = align_up(o + sizes[i], 256);
+    }
+    p.total = o;
+    return p;
+}
+
+}  // namespace
+
+extern "C" const char* jl_version(void) { return "joule_b200 0.1 sm_100a"; }
+
+extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out) {
+    if (!out) return JL_ERR_INVALID;
+    *out = nullptr;
+    int rc = check_shape(cfg);
+    if (rc) return rc;
+    if (max_tokens < 1 || (long long)max_tokens * cfg->topk > (1 << 24)) return JL_ERR_INVALID;
+    jl_moe* h = new (std::nothrow) jl_moe();
+    if (!h) return JL_ERR_OOM;
+    memset(h, 0, sizeof(*h));
+    if (cudaGetDevice(&h->device) != cudaSuccess) {
+        delete h;
+        return JL_ERR_CUDA;
+    }
+    h->L = cfg->L;
+    h->d = cfg->d;
+    h->E = cfg->E;
+    h->k = cfg->topk;
+    h->m = cfg->intermediate;
+    h->norm = cfg->norm_topk_prob ? 1 : 0;
+    h->max_tokens = max_tokens;
+    h->path = JL_PATH_AUTO;
+    h->lay.d = h->d;
+    h->lay.m = h->m;
+    h->lay.E = h->E;
+    h->lay.part_tiles = (size_t)h->m * h->d / 2;
+    h->lay.part_scales = (size_t)h->m * h->d / 32;
+    h->lay.rec_bytes = 3 * (h->lay.part_tiles + h->lay.part_scales);
+    h->store_bytes = (size_t)h->L * h->E * h->lay.rec_bytes;
+    const ws_plan wp = plan_ws(max_tokens, h->E, h->k, h->d, h->m);
+    h->ws_bytes = wp.total;
+    h->dev_stage_bytes = h->lay.rec_bytes;
+    h->uploaded = (unsigned char*)calloc(h->L, 1);
+    const size_t gw = (size_t)h->L * h->E * h->d * 2;
+    if (!h->uploaded || cudaMalloc(&h->gate_w, gw) != cudaSuccess ||
+        cudaMalloc(&h->store, h->store_bytes) != cudaSuccess ||
+        cudaMalloc(&h->ws_base, h->ws_bytes) != cudaSuccess ||
+        cudaMalloc(&h->dev_stage, h->dev_stage_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        jl_moe_destroy(h);
+        return JL_ERR_OOM;
+    }
+    uint8_t* b = (uint8_t*)h->ws_base;
+    h->ws.logits = (float*)(b + wp.off[0]);
+    h->ws.top = (int*)(b + wp.off[1]);
+    h->ws.tw = (float*)(b + wp.off[2]);
+    h->ws.U = (int*)(b + wp.off[3]);
+    h->ws.sel = (int*)(b + wp.off[4]);
+    h->ws.uh = (int*)(b + wp.off[5]);
+    h->ws.uidx = (int*)(b + wp.off[6]);
+    h->ws.uw = (float*)(b + wp.off[7]);
+    h->ws.comb = (int*)(b + wp.off[8]);
+    h->ws.slot_pos = (int*)(b + wp.off[9]);
+    h->ws.act = (float*)(b + wp.off[10]);
+    h->ws.y = (float*)(b + wp.off[11]);
+    h->ws.counter = (int*)(b + wp.off[12]);
+    h->ws.err = (int*)(b + wp.off[13]);
+    if (cudaMemset(h->ws_base, 0, h->ws_bytes) != cudaSuccess ||
+        cudaMemset(h->gate_w, 0, gw) != cudaSuccess) {
+        jl_moe_destroy(h);
+        return JL_ERR_CUDA;
+    }
+    *out = h;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_destroy(jl_moe* h) {
+    if (!h) return JL_OK;
+    if (h->gate_w) cudaFree(h->gate_w);
+    if (h->store) cudaFree(h->store);
+    if (h->ws_base) cudaFree(h->ws_base);
+    if (h->dev_stage) cudaFree(h->dev_stage);
+    if (h->pinned) cudaFreeHost(h->pinned);
+    free(h->uploaded);
+    delete h;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_set_path(jl_moe* h, int path) {
+    if (!h || path < JL_PATH_AUTO || path > JL_PATH_TC) return JL_ERR_INVALID;
+    if (path == JL_PATH_TC) return JL_ERR_INVALID;  // tensor-core path not built in this library
+    h->path = path;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n) {
+    if (!h || n < 0 || n > 5 || (n > 0 && !events)) return JL_ERR_INVALID;
+    for (int i = 0; i < n; i++) h->phase_ev[i] = (cudaEvent_t)events[i];
+    h->n_phase_ev = n;
+    return JL_OK;
+}
+
+extern "C" long long jl_moe_device_bytes(const jl_moe* h) {
+    if (!h) return 0;
+    return (long long)(h->store_bytes + h->ws_bytes + (size_t)h->L * h->E * h->d * 2 +
+                       h->dev_stage_bytes);
+}
+
+static int part_rows(const jl_moe* h, int p) { return p < 2 ? h->m : h->d; }
+static int part_cols(const jl_moe* h, int p) { return p < 2 ? h->d : h->m; }
+
+extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_w,
+                                   const unsigned char* const* pk, const unsigned short* const* sc,
+                                   int src_on_device, void* stream) {
+    if (!h || l < 0 || l >= h->L || !gate_w || !pk || !sc) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t gw = (size_t)h->E * h->d * 2;
+    JL_CUDA(cudaMemcpyAsync(h->gate_w + (size_t)l * h->E * h->d, gate_w, gw,
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    for (int e = 0; e < h->E; e++) {
+        uint8_t* rec = store_l + (size_t)e * h->lay.rec_bytes;
+        for (int p = 0; p < 3; p++) {
+            const unsigned char* src_pk = pk[p * h->E + e];
+            const unsigned short* src_sc = sc[p * h->E + e];
+            if (!src_pk || !src_sc) return JL_ERR_INVALID;
+            const int R = part_rows(h, p), C = part_cols(h, p);
+            const size_t pkb = (size_t)R * C / 2, scb = (size_t)R * C / 32;
+            uint8_t* st_pk = h->dev_stage;
+            uint16_t* st_sc = (uint16_t*)(h->dev_stage + pkb);
+            JL_CUDA(cudaMemcpyAsync(st_pk, src_pk, pkb, kind, s));
+            JL_CUDA(cudaMemcpyAsync(st_sc, src_sc, scb, kind, s));
+            int rc = jl_launch_repack_part(st_pk, st_sc, R, C, rec + h->lay.tiles_off(p),
+                                           (uint16_t*)(rec + h->lay.scales_off(p)), s);
+            if (rc) return rc;
+        }
+    }
+    JL_CUDA(cudaStreamSynchronize(s));
+    h->uploaded[l] = 1;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
+                                     const float* w_gate, const float* w_up, const float* w_down,
+                                     void* stream) {
+    if (!h || l < 0 || l >= h->L || !gate_w || !w_gate || !w_up || !w_down) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    JL_CUDA(cudaMemcpyAsync(h->gate_w + (size_t)l * h->E * h->d, gate_w, (size_t)h->E * h->d * 2,
+                            cudaMemcpyDeviceToDevice, s));
+    uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    const float* src[3] = {w_gate, w_up, w_down};
+    const size_t numel = (size_t)h->m * h->d;
+    for (int e = 0; e < h->E; e++) {
+        uint8_t* rec = store_l + (size_t)e * h->lay.rec_bytes;
+        for (int p = 0; p < 3; p++) {
+            uint8_t* st_pk = h->dev_stage;
+            uint16_t* st_sc = (uint16_t*)(h->dev_stage + numel / 2);
+            int rc = jl_q4_quantize(src[p] + (size_t)e * numel, (long long)numel, st_sc, st_pk, s);
+            if (rc) return rc;
+            rc = jl_launch_repack_part(st_pk, st_sc, part_rows(h, p), part_cols(h, p),
+                                       rec + h->lay.tiles_off(p),
+                                       (uint16_t*)(rec + h->lay.scales_off(p)), s);
+            if (rc) return rc;
+        }
+    }
+    JL_CUDA(cudaStreamSynchronize(s));
+    h->uploaded[l] = 1;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out, int* top,
+                              float* tw, void* stream) {
+    if (!h || !x || !out || l < 0 || l >= h->L || B < 1) return JL_ERR_INVALID;
+    if (B > h->max_tokens) return JL_ERR_CAPACITY;
+    if (!h->uploaded[l]) return JL_ERR_NOT_READY;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
+        return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    const unsigned short* gw = h->gate_w + (size_t)l * h->E * h->d;
+    const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    auto mark = [&](int i) -> int {
+        if (i < h->n_phase_ev && cudaEventRecord(h->phase_ev[i], s) != cudaSuccess)
+            return JL_ERR_CUDA;
+        return JL_OK;
+    };
+    int rc = mark(0);
+    if (!rc) rc = jl_launch_route(h, gw, x, B, s);
+    if (!rc) rc = mark(1);
+    if (!rc) rc = jl_launch_gateup_exact(h, store_l, x, B, s);
+    if (!rc) rc = mark(2);
+    if (!rc) rc = jl_launch_down_exact(h, store_l, B, s);
+    if (!rc) rc = mark(3);
+    if (!rc) rc = jl_launch_combine(h, B, out, top, tw, s);
+    if (!rc) rc = mark(4);
+    if (rc) return rc;
+    h->last_B = B;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_debug_routing(jl_moe* h, int B, float* logits, int* sel, int* uh, int* uidx,
+                                    float* uw, int* U_out, void* stream) {
+    if (!h || B < 1 || B > h->max_tokens) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    int U = 0;
+    JL_CUDA(cudaMemcpyAsync(&U, h->ws.U, sizeof(int), cudaMemcpyDeviceToHost, s));
+    JL_CUDA(cudaStreamSynchronize(s));
+    if (U < 0 || U > h->E) return JL_ERR_DEVICE;
+    const size_t S = (size_t)B * h->k;
+    if (logits)
+        JL_CUDA(cudaMemcpyAsync(logits, h->ws.logits, (size_t)B * h->E * 4, cudaMemcpyDeviceToDevice, s));
+    if (sel) JL_CUDA(cudaMemcpyAsync(sel, h->ws.sel, (size_t)U * 4, cudaMemcpyDeviceToDevice, s));
+    if (uh) JL_CUDA(cudaMemcpyAsync(uh, h->ws.uh, (size_t)(U + 1) * 4, cudaMemcpyDeviceToDevice, s));
+    if (uidx) JL_CUDA(cudaMemcpyAsync(uidx, h->ws.uidx, S * 4, cudaMemcpyDeviceToDevice, s));
+    if (uw) JL_CUDA(cudaMemcpyAsync(uw, h->ws.uw, S * 4, cudaMemcpyDeviceToDevice, s));
+    JL_CUDA(cudaStreamSynchronize(s));
+    if (U_out) *U_out = U;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_check(jl_moe* h, void* stream) {
+    if (!h) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    int err = 0;
+    JL_CUDA(cudaMemcpyAsync(&err, h->ws.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    JL_CUDA(cudaStreamSynchronize(s));
+    if (err) JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
+    JL_CUDA(cudaStreamSynchronize(s));
+    if (err & jl::kErrTimeout) return JL_ERR_TIMEOUT;
+    if (err) return JL_ERR_DEVICE;
+    return JL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Host-buffer drop-in for layer_ffn_batch: one cached handle per (cfg, W).
+
+namespace {
+struct dropin {
+    KernelCfg cfg;
+    const void* key_gate;
+    const void* key_pk;
+    jl_moe* h;
+    float* xd;
+    float* od;
+    int cap;
+};
+std::mutex g_dropin_mu;
+std::vector<dropin> g_dropins;
+}  // namespace
+
+extern "C" int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l, const float* x,
+                                  int B, float* out) {
+    if (!c || !W || !x || !out || B < 1 || l < 0 || l >= c->L) return JL_ERR_INVALID;
+    if (!W->gate_w || !W->expert_pk[0] || !W->expert_sc[0]) return JL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_dropin_mu);
+    dropin* ent = nullptr;
+    for (auto& e : g_dropins)
+        if (e.key_gate == W->gate_w && e.key_pk == W->expert_pk[0] && !memcmp(&e.cfg, c, sizeof(*c)))
+            ent = &e;
+    if (!ent) {
+        dropin e{};
+        e.cfg = *c;
+        e.key_gate = W->gate_w;
+        e.key_pk = W->expert_pk[0];
+        e.cap = std::max(B, 64);
+        int rc = jl_moe_create(c, e.cap, &e.h);
+        if (rc) return rc;
+        std::vector<const unsigned char*> pk(3 * c->E);
+        std::vector<const unsigned short*> sc(3 * c->E);
+        for (int ll = 0; ll < c->L; ll++) {
+            for (int p = 0; p < 3; p++)
+                for (int ex = 0; ex < c->E; ex++) {
+                    pk[p * c->E + ex] = W->expert_pk[p][(size_t)ll * c->E + ex];
+                    sc[p * c->E + ex] = W->expert_sc[p][(size_t)ll * c->E + ex];
+                }
+            rc = jl_moe_upload_layer(e.h, ll, W->gate_w + (size_t)ll * c->E * c->d, pk.data(),
+                                     sc.data(), 0, nullptr);
+            if (rc) {
+                jl_moe_destroy(e.h);
+                return rc;
+            }
+        }
+        if (cudaMalloc(&e.xd, (size_t)e.cap * c->d * 4) != cudaSuccess ||
+            cudaMalloc(&e.od, (size_t)e.cap * c->d * 4) != cudaSuccess) {
+            jl_moe_destroy(e.h);
+            return JL_ERR_OOM;
+        }
+        g_dropins.push_back(e);
+        ent = &g_dropins.back();
+    }
+    if (B > ent->cap) return JL_ERR_CAPACITY;
+    const size_t bytes = (size_t)B * c->d * 4;
+    JL_CUDA(cudaMemcpy(ent->xd, x, bytes, cudaMemcpyHostToDevice));
+    int rc = jl_moe_forward(ent->h, l, ent->xd, B, ent->od, nullptr, nullptr, nullptr);
+    if (rc) return rc;
+    JL_CUDA(cudaMemcpy(out, ent->od, bytes, cudaMemcpyDeviceToHost));
+    return jl_moe_check(ent->h, nullptr);
+}

@@ -1,0 +1,77 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, its structs match the reference's layout, and argument
+errors are reported as status codes before any device work."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from joule_b200 import native
+
+
+@pytest.fixture(scope="module")
+def dll():
+    if not native.lib_path().exists():
+        from joule_b200 import build
+        build.build()
+    return native.get_dll()
+
+
+def header_symbols() -> list[str]:
+    txt = (ROOT / "include" / "joule_moe.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|long long|const char\*)\s+(jl_\w+)\s*\(", txt, re.M)))
+
+
+def test_header_declares_expected_entry_points():
+    syms = header_symbols()
+    for s in ("jl_q4_gemv_f32", "jl_q4_gemm_f32", "jl_moe_create", "jl_moe_forward",
+              "jl_layer_ffn_batch", "jl_q4_quantize"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(dll):
+    for s in header_symbols():
+        assert hasattr(dll, s), s
+        assert s in native.SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_struct_layouts_match_reference():
+    # KernelCfg: 8 int, float, 7 int (decode_kernel.c:269-286)
+    assert ctypes.sizeof(native.KernelCfg) == 64
+    # KernelW: 28 pointers, 2 x 3 table pointers, cos, sin, int use_i8 (+pad)
+    assert ctypes.sizeof(native.KernelW) == (28 + 6 + 2) * 8 + 8
+    assert native.KernelW.expert_pk.offset == 28 * 8
+    assert native.KernelW.use_i8.offset == 36 * 8
+
+
+def test_version(dll):
+    assert b"sm_100a" in dll.jl_version()
+
+
+def test_bad_arguments_are_status_codes(dll):
+    c = native.KernelCfg(L=1, d=2048, E=128, topk=8, intermediate=768, norm_topk_prob=1)
+    h = ctypes.c_void_p()
+    bad = native.KernelCfg(L=1, d=2000, E=128, topk=8, intermediate=768)   # d % 64 != 0
+    assert dll.jl_moe_create(ctypes.byref(bad), 16, ctypes.byref(h)) == -1
+    bad = native.KernelCfg(L=1, d=2048, E=128, topk=20, intermediate=768)  # topk > 16
+    assert dll.jl_moe_create(ctypes.byref(bad), 16, ctypes.byref(h)) == -1
+    bad = native.KernelCfg(L=1, d=2048, E=128, topk=8, intermediate=768, expert_i8=1)
+    assert dll.jl_moe_create(ctypes.byref(bad), 16, ctypes.byref(h)) == -1
+    assert dll.jl_moe_create(ctypes.byref(c), 0, ctypes.byref(h)) == -1
+    assert dll.jl_q4_gemv_f32(None, None, None, None, 64, 256, 64, None) == -1
+    assert dll.jl_q4_gemv_f32(1, 16, 16, 16, 64, 256, 32, None) == -1      # group != 64
+    assert dll.jl_q4_gemm_f32(16, 16, 1, 16, 16, 64, 100, 64, None) == -1  # d % 64 != 0
+    assert dll.jl_q4_quantize(None, 64, None, None, None) == -1
+    assert dll.jl_moe_forward(None, 0, None, 1, None, None, None, None) == -1
+    assert dll.jl_moe_set_path(None, 0) == -1
+    assert dll.jl_moe_destroy(None) == 0
+
+
+def test_loader_fails_loudly_without_library(tmp_path, monkeypatch):
+    monkeypatch.setattr(native, "_HERE", tmp_path)
+    monkeypatch.setattr(native, "_DLL_CACHE", {})
+    with pytest.raises(RuntimeError, match="not built"):
+        native.get_dll()
