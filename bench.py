@@ -187,54 +187,67 @@ def routing_unions(moe, xs, B):
     return U
 
 
-def time_batch(moe, xs, outs, B, steps, warmup, ws):
-    """Device-resident timing: one CUDA graph per timed step (48 layers), with
-    phase events around every layer's kernels."""
+def capture_step(moe, xs, outs, B, mask, stream, layers):
+    """One CUDA graph: `layers` consecutive layer forwards (phases in `mask`)."""
     import torch
-    L = moe.cfg.L
-    stream = torch.cuda.Stream()
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(L)]
-          for _ in range(steps)]
-    lib = moe._L
-    graphs = []
+    g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
-        for l in range(L):        # eager warm-up (sets kernel attributes outside capture)
-            moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
-        stream.synchronize()
-        for s in range(steps):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                for l in range(L):
-                    import ctypes
-                    arr = (ctypes.c_void_p * 5)(*[e.cuda_event for e in ev[s][l]])
-                    lib.jl_moe_set_phase_events(moe.h, arr, 5)
-                    moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
-            graphs.append(g)
-        lib.jl_moe_set_phase_events(moe.h, None, 0)
+        with torch.cuda.graph(g, stream=stream):
+            for l in layers:
+                moe.forward_phases(l, xs[l, :B], outs[l, :B], mask, stream=stream)
+    return g
+
+
+def replay_ms(g, reps, warmup, stream, ws=1):
+    """Mean ms per replay of graph g: warm-up replays, then `reps` replays
+    back to back between two events (barrier + synchronize on both sides)."""
+    import torch
+    with torch.cuda.stream(stream):
         for _ in range(warmup):
-            graphs[0].replay()
-        stream.synchronize()
+            g.replay()
+    stream.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for g in graphs:
-        g.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            g.replay()
     t1.record(stream)
     t1.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
-    total_ms = t0.elapsed_time(t1)
-    phase = np.zeros(4)
-    for s in range(steps):
-        for l in range(L):
-            e = ev[s][l]
-            for i in range(4):
-                phase[i] += e[i].elapsed_time(e[i + 1])
+    return t0.elapsed_time(t1) / reps
+
+
+def time_batch(moe, xs, outs, B, steps, warmup, ws):
+    """The timed region: `steps` replays of the 48-layer step graph. Then each
+    phase alone (48 back-to-back launches of one kernel, reading the routing
+    the last full layer left) to attribute the time."""
+    import torch
+    L = moe.cfg.L
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for l in range(L):        # eager warm-up (kernel attributes are set outside capture)
+            moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
+    stream.synchronize()
+    g = capture_step(moe, xs, outs, B, 7, stream, range(L))
+    step_ms = replay_ms(g, steps, warmup, stream, ws)
     moe.check()
-    del graphs
-    return total_ms, phase / (steps * L)   # ms per layer-launch of each phase
+    phase = {}
+    for name, mask in (("router", 1), ("gateup", 2), ("down_combine", 4)):
+        gp = capture_step(moe, xs, outs, B, mask, stream, range(L))
+        phase[name] = replay_ms(gp, max(3, steps // 2), 2, stream) / L
+        del gp
+    # leave the workspace consistent (full layers) for later users
+    with torch.cuda.stream(stream):
+        for l in range(L):
+            moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
+    stream.synchronize()
+    moe.check()
+    del g
+    return step_ms * steps, phase
 
 
 def e2e_dropin(host, B, steps, warmup, seed=11):
@@ -319,6 +332,7 @@ def cpu_model():
 def run_ours(a):
     import torch
     from joule_b200.moe import MoELayers, make_cfg
+    SHAPE["L"] = a.layers
     ws, rank, local = dist_init()
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
     sweep = sorted(set(int(b) for b in a.sweep.split(",")) | {a.batch})
@@ -352,9 +366,8 @@ def run_ours(a):
             tok_s=ws * B * a.steps / (total_ms / 1e3), ms_per_step=ms_step,
             us_per_layer=ms_step * 1e3 / L, mean_U=float(np.mean(U)),
             layer_gbs=sum(layer_bytes) / (ms_step / 1e3) / 1e9,
-            phase_us=dict(router=phase[0] * 1e3, gateup=phase[1] * 1e3, down=phase[2] * 1e3,
-                          combine=phase[3] * 1e3),
-            gateup_gbs=float(np.mean(gu_bytes)) / (phase[1] / 1e3) / 1e9,
+            phase_us={k: v * 1e3 for k, v in phase.items()},
+            gateup_gbs=float(np.mean(gu_bytes)) / (phase["gateup"] / 1e3) / 1e9,
             gateup_bytes_per_launch=float(np.mean(gu_bytes)))
         rec["layer_frac_of_hbm"] = rec["layer_gbs"] / hbm
         per_b[str(B)] = rec
@@ -393,7 +406,7 @@ def run_ours(a):
 
 
 def launches_per_step(B):
-    # per layer: router (+topk, dispatch when B > 8), gate/up, down, combine
+    # per layer: router (+ top-k and dispatch kernels when B > 8), gate/up, down, combine
     return SHAPE["L"] * (4 if B <= 8 else 6)
 
 
@@ -473,6 +486,7 @@ def main():
     ap.add_argument("--sweep", default="1,8,32,64")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-layers", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=48, help="MoE layers per step (48 = the model)")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
     a = ap.parse_args()

@@ -159,7 +159,7 @@ int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
                           const float* w_down, void* stream);
 
 /* Path selection for jl_moe_forward. */
-#define JL_PATH_AUTO 0  /* exact for B <= 8, tensor-core beyond */
+#define JL_PATH_AUTO 0  /* exact for B <= 8, tensor-core beyond (d % 512 == 0) */
 #define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order */
 #define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
 int jl_moe_set_path(jl_moe* h, int path);
@@ -171,6 +171,14 @@ int jl_moe_set_path(jl_moe* h, int path);
  * weights [B, topk] fp32. Enqueued on `stream`; returns after launch. */
 int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out,
                    int* top, float* tw, void* stream);
+
+/* jl_moe_forward restricted to the phases in `mask` (1 = router + dispatch,
+ * 2 = gate/up + SwiGLU, 4 = down + combine; 7 = the full layer). A phase
+ * reads what the previous phase of the LAST call left in the workspace, so a
+ * partial mask is for profiling one kernel in isolation. No counterpart in
+ * the reference. */
+int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, float* out,
+                          int* top, float* tw, int mask, void* stream);
 
 /* Debug / parity: copies (device) the router logits [B, E], the union
  * experts sel [U], offsets uh [U+1] and the slot map uidx/uw [B*topk] built
@@ -191,12 +199,22 @@ int jl_moe_check(jl_moe* h, void* stream);
 int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l,
                        const float* x, int B, float* out);
 
-/* Phase timing: when n > 0, each jl_moe_forward records events[0] before the
- * router, events[1] after it, events[2] after gate/up+SwiGLU, events[3]
- * after down and events[4] after the combine (n <= 5 records the first n),
- * on the forward's stream. events are cudaEvent_t handles; n = 0 turns it
- * off. No counterpart in the reference (its profiling is wall-clock,
- * batch_bench.py:58-68). */
+/* Device-side trace (the counterpart of the reference's g_trace breadcrumbs,
+ * decode_kernel.c:22-28): with enable = 1 the kernels of later forwards stamp
+ * %globaltimer (ns) at phase boundaries into a 64-slot device buffer, 16
+ * slots per kernel (router, gate/up, down, combine), written by thread 0 of
+ * one block. out (host, n slots; nullable when n = 0) receives the buffer
+ * (synchronises `stream`); enable = 0 stops later launches from tracing.
+ * The buffer stays allocated until jl_moe_destroy, because CUDA graphs
+ * captured while tracing keep writing to it. */
+int jl_moe_trace(jl_moe* h, int enable, long long* out, int n, void* stream);
+
+/* Phase timing: when n > 0, each jl_moe_forward[_phases] records events[0]
+ * before the router, events[1] after it, events[2] after gate/up+SwiGLU and
+ * events[3] after down+combine (n < 4 records the first n), on the forward's
+ * stream; under stream capture they become external event-record nodes.
+ * events are cudaEvent_t handles; n = 0 turns it off. No counterpart in the
+ * reference (its profiling is wall-clock, batch_bench.py:58-68). */
 int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n);
 
 /* Bytes of device memory the handle holds (store + workspace). */

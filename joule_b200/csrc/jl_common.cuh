@@ -87,22 +87,52 @@ __device__ __forceinline__ float hsum8(const float (&l)[8]) {
     return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
 }
 
-// Eight Q4 values of one 32-bit word as exact floats (nib - 8). Element j of
-// the word is nibble j (bits 4j..4j+3): byte j/2, low nibble first
-// (q4_store.py:53). Each nibble is OR-ed into the mantissa of 2^23 at its own
-// bit position and rescaled by an exact FMA, so no shift is needed for the
-// low five nibbles.
-__device__ __forceinline__ void dequant8(uint32_t w, float (&a)[8]) {
+// Eight Q4 values of one 32-bit word as exact floats (nib - 8), as four
+// float2 pairs (elements 2i, 2i+1). Element j of the word is nibble j (bits
+// 4j..4j+3): byte j/2, low nibble first (q4_store.py:53). Each nibble is
+// OR-ed into the mantissa of 2^23 at its own bit position and rescaled by an
+// exact packed FMA (v * 2^-4j - (2^(23-4j) + 8) is exact), so only one shift
+// per word is needed.
+__device__ __forceinline__ void dequant8x2(uint32_t w, float2 (&a)[4]) {
     const uint32_t M = 0x4B000000u;  // 2^23
-    a[0] = __fadd_rn(__uint_as_float((w & 0x0000000Fu) | M), -8388616.0f);
-    a[1] = __fmaf_rn(__uint_as_float((w & 0x000000F0u) | M), 0.0625f, -524296.0f);
-    a[2] = __fmaf_rn(__uint_as_float((w & 0x00000F00u) | M), 0.00390625f, -32776.0f);
-    a[3] = __fmaf_rn(__uint_as_float((w & 0x0000F000u) | M), 0.000244140625f, -2056.0f);
-    a[4] = __fmaf_rn(__uint_as_float((w & 0x000F0000u) | M), 1.52587890625e-05f, -136.0f);
-    const uint32_t h = w >> 12;  // nibbles 5..7 -> bits 8..19
-    a[5] = __fmaf_rn(__uint_as_float((h & 0x00000F00u) | M), 0.00390625f, -32776.0f);
-    a[6] = __fmaf_rn(__uint_as_float((h & 0x0000F000u) | M), 0.000244140625f, -2056.0f);
-    a[7] = __fmaf_rn(__uint_as_float((h & 0x000F0000u) | M), 1.52587890625e-05f, -136.0f);
+    const uint32_t h = w >> 12;      // nibbles 5..7 -> bits 8..19
+    const float2 v0 = make_float2(__uint_as_float((w & 0x0000000Fu) | M),
+                                  __uint_as_float((w & 0x000000F0u) | M));
+    const float2 v1 = make_float2(__uint_as_float((w & 0x00000F00u) | M),
+                                  __uint_as_float((w & 0x0000F000u) | M));
+    const float2 v2 = make_float2(__uint_as_float((w & 0x000F0000u) | M),
+                                  __uint_as_float((h & 0x00000F00u) | M));
+    const float2 v3 = make_float2(__uint_as_float((h & 0x0000F000u) | M),
+                                  __uint_as_float((h & 0x000F0000u) | M));
+    a[0] = __ffma2_rn(v0, make_float2(1.0f, 0.0625f), make_float2(-8388616.0f, -524296.0f));
+    a[1] = __ffma2_rn(v1, make_float2(0.00390625f, 0.000244140625f), make_float2(-32776.0f, -2056.0f));
+    a[2] = __ffma2_rn(v2, make_float2(1.52587890625e-05f, 0.00390625f), make_float2(-136.0f, -32776.0f));
+    a[3] = __ffma2_rn(v3, make_float2(0.000244140625f, 1.52587890625e-05f), make_float2(-2056.0f, -136.0f));
+}
+
+// Scalar form of dequant8x2 (same values).
+__device__ __forceinline__ void dequant8(uint32_t w, float (&a)[8]) {
+    float2 p[4];
+    dequant8x2(w, p);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        a[2 * i] = p[i].x;
+        a[2 * i + 1] = p[i].y;
+    }
+}
+
+// hsum8 over four float2 lane pairs {l0,l1},{l2,l3},{l4,l5},{l6,l7}.
+__device__ __forceinline__ float hsum8x2(const float2 (&l)[4]) {
+    const float2 s01 = __fadd2_rn(l[0], l[2]);  // (l0+l4, l1+l5)
+    const float2 s23 = __fadd2_rn(l[1], l[3]);  // (l2+l6, l3+l7)
+    const float2 t = __fadd2_rn(s01, s23);      // (s0+s2, s1+s3)
+    return __fadd_rn(t.x, t.y);
+}
+
+// fp16 bits -> fp32 by the hardware conversion: exact for every finite half
+// (subnormals included), equal to fp16_to_f32 except for NaN payloads.
+__device__ __forceinline__ float half_bits_to_f32(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
 }
 
 // ---------------------------------------------------------------------------
@@ -175,11 +205,36 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Phase stamp for the optional trace buffer (thread 0 of the calling block).
+__device__ __forceinline__ void trace_point(long long* trace, int kind, int slot) {
+    if (trace != nullptr && threadIdx.x == 0) trace[kind * 16 + slot] = (long long)globaltimer_ns();
+}
+
 __device__ __forceinline__ void griddep_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic dependent launch (PDL) enabled: the kernel may
+// start while the previous kernel on the stream finishes; it must call
+// griddep_wait() before touching that kernel's outputs.
+template <typename... KArgs, typename... Args>
+inline int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                  Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...) == cudaSuccess ? JL_OK
+                                                                                       : JL_ERR_CUDA;
 }
 
 }  // namespace jl

@@ -3,22 +3,28 @@
 // q4_row_dot_B, decode_kernel.c:770-858), so the layer output is
 // bit-identical to the reference's for the same inputs.
 //
-// Work decomposition: a (row, 64-value group) product p = hsum8(...) * scale
-// is independent of every other; only the per-row sum over groups is a
-// sequential chain. Each block stages one 32-row block of an expert's
-// matrices with 1-D bulk copies (one mbarrier per warp), every thread
-// computes p for its row of a tile (lane = row), and one warp then runs the
-// per-row chains from shared memory. Tokens routed to the expert are staged
-// in shared memory and read as warp-uniform broadcasts.
+// Work decomposition: the product p = hsum8(...) * scale of one (row, 64-value
+// group) is independent of every other; only the per-row sum over groups is a
+// sequential chain. A block takes one 32-row block of an expert's matrices;
+// each warp stages its share of the tiles with 1-D bulk copies on its own
+// mbarrier, every lane computes p for its row (lane = row) of each tile, and
+// one warp per part then runs the per-row chains from shared memory. The
+// products use Blackwell's packed FP32x2 FMA (__ffma2_rn), which rounds each
+// lane exactly like the scalar FMA, so lane pairs of the reference's 8-wide
+// accumulator advance in one instruction. Tokens routed to the expert are
+// staged in shared memory and read as warp-uniform broadcasts.
+#include <algorithm>
+
 #include "jl_common.cuh"
 #include "jl_internal.h"
 
 namespace jl {
 
-constexpr int kGuWarps = 8;    // gate/up block: warps 0-3 gate, 4-7 up
-constexpr int kGuTok = 2;      // tokens per pass (gate/up)
+constexpr int kGuWarpsPerPart = 8;  // gate/up block: warps 0-7 gate, 8-15 up
+constexpr int kGuWarps = 2 * kGuWarpsPerPart;
+constexpr int kGuTok = 2;           // tokens per pass (gate/up)
 constexpr int kDnWarps = 4;
-constexpr int kDnTok = 4;      // tokens per pass (down)
+constexpr int kDnTok = 4;           // tokens per pass (down)
 
 // p for NT tokens of one tile row: q0/q1 = the row's 32 bytes, xs = token
 // rows (stride `xstride`) starting at this group's first column.
@@ -26,93 +32,113 @@ template <int NT>
 __device__ __forceinline__ void tile_row_products(uint4 q0, uint4 q1, float s, const float* xs,
                                                   int xstride, float (&p)[NT]) {
     const uint32_t wq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    float lane[NT][8];
+    float2 lane[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; t++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) lane[t][j] = 0.0f;
+        for (int j = 0; j < 4; j++) lane[t][j] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int w = 0; w < 8; w++) {
-        float a[8];
-        dequant8(wq[w], a);
+        float2 a[4];
+        dequant8x2(wq[w], a);
 #pragma unroll
         for (int t = 0; t < NT; t++) {
             const float4 x0 = *reinterpret_cast<const float4*>(xs + t * xstride + w * 8);
             const float4 x1 = *reinterpret_cast<const float4*>(xs + t * xstride + w * 8 + 4);
-            lane[t][0] = __fmaf_rn(a[0], x0.x, lane[t][0]);
-            lane[t][1] = __fmaf_rn(a[1], x0.y, lane[t][1]);
-            lane[t][2] = __fmaf_rn(a[2], x0.z, lane[t][2]);
-            lane[t][3] = __fmaf_rn(a[3], x0.w, lane[t][3]);
-            lane[t][4] = __fmaf_rn(a[4], x1.x, lane[t][4]);
-            lane[t][5] = __fmaf_rn(a[5], x1.y, lane[t][5]);
-            lane[t][6] = __fmaf_rn(a[6], x1.z, lane[t][6]);
-            lane[t][7] = __fmaf_rn(a[7], x1.w, lane[t][7]);
+            lane[t][0] = __ffma2_rn(a[0], make_float2(x0.x, x0.y), lane[t][0]);
+            lane[t][1] = __ffma2_rn(a[1], make_float2(x0.z, x0.w), lane[t][1]);
+            lane[t][2] = __ffma2_rn(a[2], make_float2(x1.x, x1.y), lane[t][2]);
+            lane[t][3] = __ffma2_rn(a[3], make_float2(x1.z, x1.w), lane[t][3]);
         }
     }
 #pragma unroll
-    for (int t = 0; t < NT; t++) p[t] = __fmul_rn(hsum8(lane[t]), s);
+    for (int t = 0; t < NT; t++) p[t] = __fmul_rn(hsum8x2(lane[t]), s);
 }
 
-// Products for every tile a warp owns, for `nt` (<= NTMAX) tokens.
-// Tiles are [g_lo, g_hi) of part `pi` (smem tile index pi*ng + g).
+// Products for tiles [g_lo, g_hi) of part `pi` (smem tile index pi*ng + g) for
+// `nt` (<= NTMAX) tokens; p_s layout [(pi*NTMAX + t)*ng + g][32].
 template <int NTMAX>
-__device__ __forceinline__ void warp_tiles(const uint8_t* w_s, const uint16_t* sc_s,
+__device__ __forceinline__ bool warp_tiles(const uint8_t* w_s, const uint16_t* sc_s,
                                            const float* x_s, int xstride, float* p_s, int pi,
-                                           int ng, int g_lo, int g_hi, int nt) {
+                                           int ng, int g_lo, int g_hi, int nt, uint64_t* bars,
+                                           bool wait, int* err) {
     const int lane = threadIdx.x & 31;
     for (int g = g_lo; g < g_hi; g++) {
+        // first pass: tile g may still be in flight; compute overlaps the rest
+        if (wait && !mbar_wait_bounded(&bars[g - g_lo], 0, err)) return false;
         const int ti = pi * ng + g;
         const uint4 q0 = *reinterpret_cast<const uint4*>(w_s + (size_t)ti * kTileBytes + lane * 16);
         const uint4 q1 =
             *reinterpret_cast<const uint4*>(w_s + (size_t)ti * kTileBytes + 512 + lane * 16);
-        const float s = fp16_to_f32(sc_s[ti * kTileRows + lane]);
+        const float s = half_bits_to_f32(sc_s[ti * kTileRows + lane]);
         const float* xg = x_s + g * kGroup;
-        // p_s layout: [(pi*NTMAX + t)*ng + g][32]
+        float* pp = p_s + ((size_t)(pi * NTMAX) * ng + g) * 32 + lane;
+        const size_t tstride = (size_t)ng * 32;
         if (nt == 1) {
             float p[1];
             tile_row_products<1>(q0, q1, s, xg, xstride, p);
-            p_s[((pi * NTMAX + 0) * ng + g) * 32 + lane] = p[0];
+            pp[0] = p[0];
         } else if (NTMAX >= 2 && nt == 2) {
             float p[2];
             tile_row_products<2>(q0, q1, s, xg, xstride, p);
-#pragma unroll
-            for (int t = 0; t < 2; t++) p_s[((pi * NTMAX + t) * ng + g) * 32 + lane] = p[t];
+            pp[0] = p[0];
+            pp[tstride] = p[1];
         } else if (NTMAX >= 3 && nt == 3) {
             float p[3];
             tile_row_products<3>(q0, q1, s, xg, xstride, p);
 #pragma unroll
-            for (int t = 0; t < 3; t++) p_s[((pi * NTMAX + t) * ng + g) * 32 + lane] = p[t];
+            for (int t = 0; t < 3; t++) pp[t * tstride] = p[t];
         } else if (NTMAX >= 4) {
             float p[4];
             tile_row_products<4>(q0, q1, s, xg, xstride, p);
 #pragma unroll
-            for (int t = 0; t < 4; t++) p_s[((pi * NTMAX + t) * ng + g) * 32 + lane] = p[t];
+            for (int t = 0; t < 4; t++) pp[t * tstride] = p[t];
         }
     }
+    return true;
 }
 
-// Issue this warp's bulk copies (tiles + scales) on its own mbarrier.
+constexpr int kMaxTilesPerWarp = 8;
+
+// Issue this warp's bulk copies: tile i (1 KB) and its 32 scales on mbarrier
+// bars[i], so the warp can start on tile 0 while later tiles are in flight.
 __device__ __forceinline__ void warp_stage(uint8_t* w_dst, uint16_t* sc_dst, const uint8_t* w_src,
-                                           const uint16_t* sc_src, int ntiles, uint64_t* bar) {
+                                           const uint16_t* sc_src, int ntiles, uint64_t* bars) {
     if ((threadIdx.x & 31) == 0) {
-        mbar_init(bar, 1);
+        for (int i = 0; i < ntiles; i++) mbar_init(&bars[i], 1);
         mbar_fence_init();
-        if (ntiles > 0) {
-            const uint32_t tb = (uint32_t)ntiles * kTileBytes, sb = (uint32_t)ntiles * kTileRows * 2;
-            mbar_expect_tx(bar, tb + sb);
-            bulk_g2s(w_dst, w_src, tb, bar);
-            bulk_g2s(sc_dst, sc_src, sb, bar);
-        } else {
-            mbar_arrive(bar);
+        for (int i = 0; i < ntiles; i++) {
+            mbar_expect_tx(&bars[i], kTileBytes + kTileRows * 2);
+            bulk_g2s(w_dst + (size_t)i * kTileBytes, w_src + (size_t)i * kTileBytes, kTileBytes, &bars[i]);
+            bulk_g2s(sc_dst + i * kTileRows, sc_src + i * kTileRows, kTileRows * 2, &bars[i]);
         }
     }
     __syncwarp();
 }
 
+// Wait (bounded) for every tile copy of this warp: a block must not exit
+// while its bulk copies are still landing in shared memory.
+__device__ __forceinline__ void warp_drain(uint64_t* bars, int ntiles, int* err) {
+    for (int i = 0; i < ntiles; i++) mbar_wait_bounded(&bars[i], 0, err);
+}
+
+// Sequential per-row sum over ng group products (lane = row).
+__device__ __forceinline__ float row_chain(const float* pp, int ng) {
+    float acc = 0.0f;
+    int g = 0;
+    for (; g + 4 <= ng; g += 4) {
+        const float a = pp[(g + 0) * 32], b = pp[(g + 1) * 32];
+        const float c = pp[(g + 2) * 32], d = pp[(g + 3) * 32];
+        acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, a), b), c), d);
+    }
+    for (; g < ng; g++) acc = __fadd_rn(acc, pp[g * 32]);
+    return acc;
+}
+
 // ---------------------------------------------------------------------------
 // gate/up + SwiGLU. grid = (m/32 row blocks, max union size); block (rb, u)
-// handles rows 32rb..32rb+31 of expert sel[u]'s gate and up for all of its
-// tokens and writes act[slot][row] = silu(g) * u.
+// handles rows 32rb..32rb+31 of expert sel[u]'s gate (warps 0-7) and up
+// (warps 8-15) for all of its tokens and writes act[slot][row] = silu(g) * u.
 __global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
     const uint8_t* __restrict__ store_l, jl_layout L, int k, const float* __restrict__ x,
     jl_ws ws) {
@@ -124,20 +150,25 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
     uint16_t* sc_s = reinterpret_cast<uint16_t*>(w_s + (size_t)2 * ng * kTileBytes);  // [2*ng*32]
     float* x_s = reinterpret_cast<float*>(sc_s + 2 * ng * kTileRows);     // [kGuTok, d]
     float* p_s = x_s + kGuTok * d;                                         // [2, kGuTok, ng, 32]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + 2 * kGuTok * ng * 32);
+    float* gu_s = p_s + 2 * kGuTok * ng * 32;                              // [kGuTok, 32] up sums
+    uint64_t* bars = reinterpret_cast<uint64_t*>(gu_s + kGuTok * 32) + warp * kMaxTilesPerWarp;
+    long long* tr = (rb == 0 && u == 0) ? ws.trace : nullptr;
+    trace_point(tr, kTraceGateup, 0);
     griddep_wait();
+    griddep_launch_dependents();
+    trace_point(tr, kTraceGateup, 1);
     if (u >= *ws.U) return;
     const int e = ws.sel[u];
     const int s0 = ws.uh[u], n = ws.uh[u + 1] - s0;
     const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
-    const int pi = warp >> 2, q = warp & 3;
-    const int g_lo = q * ng / 4, g_hi = (q + 1) * ng / 4;
+    const int pi = warp / kGuWarpsPerPart, q = warp % kGuWarpsPerPart;
+    const int g_lo = q * ng / kGuWarpsPerPart, g_hi = (q + 1) * ng / kGuWarpsPerPart;
     {
         const size_t t0 = (size_t)rb * ng + g_lo;
         warp_stage(w_s + (size_t)(pi * ng + g_lo) * kTileBytes, sc_s + (pi * ng + g_lo) * kTileRows,
                    rec + L.tiles_off(pi) + t0 * kTileBytes,
                    reinterpret_cast<const uint16_t*>(rec + L.scales_off(pi)) + t0 * kTileRows,
-                   g_hi - g_lo, &bars[warp]);
+                   g_hi - g_lo, bars);
     }
     bool ok = true;
     for (int c0 = 0; c0 < n; c0 += kGuTok) {
@@ -149,25 +180,25 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
                 reinterpret_cast<const float4*>(x + (size_t)b * d)[c];
         }
         __syncthreads();
-        if (c0 == 0) ok = mbar_wait_bounded(&bars[warp], 0, ws.err);
-        if (ok) warp_tiles<kGuTok>(w_s, sc_s, x_s, d, p_s, pi, ng, g_lo, g_hi, nt);
+        if (c0 == 0) trace_point(tr, kTraceGateup, 2);
+        if (ok) ok = warp_tiles<kGuTok>(w_s, sc_s, x_s, d, p_s, pi, ng, g_lo, g_hi, nt, bars, c0 == 0,
+                                        ws.err);
         __syncthreads();
-        if (warp == 0) {
+        if (c0 == 0) trace_point(tr, kTraceGateup, 3);
+        if (warp == 1)  // up chains
+            for (int t = 0; t < nt; t++)
+                gu_s[t * 32 + lane] = row_chain(p_s + (size_t)((1 * kGuTok + t) * ng) * 32 + lane, ng);
+        __syncthreads();
+        if (warp == 0)  // gate chains + SwiGLU
             for (int t = 0; t < nt; t++) {
-                float ga = 0.0f, ua = 0.0f;
-                const float* pg = p_s + (size_t)((0 * kGuTok + t) * ng) * 32 + lane;
-                const float* pu = p_s + (size_t)((1 * kGuTok + t) * ng) * 32 + lane;
-                for (int g = 0; g < ng; g++) {
-                    ga = __fadd_rn(ga, pg[g * 32]);
-                    ua = __fadd_rn(ua, pu[g * 32]);
-                }
+                const float ga = row_chain(p_s + (size_t)((0 * kGuTok + t) * ng) * 32 + lane, ng);
                 const int slot = ws.uidx[s0 + c0 + t];
-                ws.act[(size_t)slot * m + rb * kTileRows + lane] = silu_mul(ga, ua);
+                ws.act[(size_t)slot * m + rb * kTileRows + lane] = silu_mul(ga, gu_s[t * 32 + lane]);
             }
-        }
         __syncthreads();
     }
-    if (n == 0) mbar_wait_bounded(&bars[warp], 0, ws.err);  // never leave copies in flight
+    trace_point(tr, kTraceGateup, 4);
+    if (n == 0 || !ok) warp_drain(bars, g_hi - g_lo, ws.err);  // never leave copies in flight
 }
 
 // ---------------------------------------------------------------------------
@@ -185,9 +216,15 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
     uint16_t* sc_s = reinterpret_cast<uint16_t*>(w_s + (size_t)ng * kTileBytes);
     float* a_s = reinterpret_cast<float*>(sc_s + ng * kTileRows);  // [kDnTok, m]
     float* p_s = a_s + kDnTok * m;                                 // [kDnTok, ng, 32]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kDnTok * ng * 32);
-    griddep_wait();
-    if (u >= *ws.U) return;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kDnTok * ng * 32) + warp * kMaxTilesPerWarp;
+    // The routing (U, sel, uh) was written by the router, which completed
+    // before the gate/up kernel's blocks passed their wait and released this
+    // grid; only act (gate/up's output) needs griddep_wait. So this block's
+    // down weights are fetched while gate/up is still running.
+    long long* tr = (rb == 0 && u == 0) ? ws.trace : nullptr;
+    trace_point(tr, kTraceDown, 0);
+    const int U = *ws.U;
+    if (u >= U) return;
     const int e = ws.sel[u];
     const int s0 = ws.uh[u], n = ws.uh[u + 1] - s0;
     const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
@@ -197,8 +234,11 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
         warp_stage(w_s + (size_t)g_lo * kTileBytes, sc_s + g_lo * kTileRows,
                    rec + L.tiles_off(2) + t0 * kTileBytes,
                    reinterpret_cast<const uint16_t*>(rec + L.scales_off(2)) + t0 * kTileRows,
-                   g_hi - g_lo, &bars[warp]);
+                   g_hi - g_lo, bars);
     }
+    griddep_wait();
+    griddep_launch_dependents();
+    trace_point(tr, kTraceDown, 1);
     bool ok = true;
     for (int c0 = 0; c0 < n; c0 += kDnTok) {
         const int nt = min(kDnTok, n - c0);
@@ -209,23 +249,22 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
                 reinterpret_cast<const float4*>(ws.act + (size_t)slot * m)[c];
         }
         __syncthreads();
-        if (c0 == 0) ok = mbar_wait_bounded(&bars[warp], 0, ws.err);
-        if (ok) warp_tiles<kDnTok>(w_s, sc_s, a_s, m, p_s, 0, ng, g_lo, g_hi, nt);
+        if (c0 == 0) trace_point(tr, kTraceDown, 2);
+        if (ok) ok = warp_tiles<kDnTok>(w_s, sc_s, a_s, m, p_s, 0, ng, g_lo, g_hi, nt, bars, c0 == 0,
+                                        ws.err);
         __syncthreads();
-        if (warp == 0) {
-            for (int t = 0; t < nt; t++) {
-                float acc = 0.0f;
-                const float* pp = p_s + (size_t)(t * ng) * 32 + lane;
-                for (int g = 0; g < ng; g++) acc = __fadd_rn(acc, pp[g * 32]);
-                const int pos = s0 + c0 + t;
-                const int slot = ws.uidx[pos];
-                ws.y[(size_t)slot * d + rb * kTileRows + lane] =
-                    __fadd_rn(0.0f, __fmul_rn(ws.uw[pos], acc));
-            }
+        if (warp < nt) {  // one warp per token
+            const int t = warp;
+            const float acc = row_chain(p_s + (size_t)(t * ng) * 32 + lane, ng);
+            const int pos = s0 + c0 + t;
+            const int slot = ws.uidx[pos];
+            ws.y[(size_t)slot * d + rb * kTileRows + lane] =
+                __fadd_rn(0.0f, __fmul_rn(ws.uw[pos], acc));
         }
         __syncthreads();
     }
-    if (n == 0) mbar_wait_bounded(&bars[warp], 0, ws.err);
+    trace_point(tr, kTraceDown, 3);
+    if (n == 0 || !ok) warp_drain(bars, g_hi - g_lo, ws.err);
 }
 
 // ---------------------------------------------------------------------------
@@ -234,7 +273,11 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
 // leaves every nonzero partial sum unchanged). Also copies top/tw out.
 __global__ void k_combine(int B, int k, int d, jl_ws ws, float* __restrict__ out,
                           int* __restrict__ top, float* __restrict__ tw) {
+    long long* tr = (blockIdx.x == 0 && blockIdx.y == 0) ? ws.trace : nullptr;
+    trace_point(tr, kTraceCombine, 0);
     griddep_wait();
+    griddep_launch_dependents();
+    trace_point(tr, kTraceCombine, 1);
     const int b = blockIdx.y;
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (c < d) {
@@ -253,17 +296,20 @@ __global__ void k_combine(int B, int k, int d, jl_ws ws, float* __restrict__ out
         if (top) top[b * k + threadIdx.x] = ws.top[b * k + threadIdx.x];
         if (tw) tw[b * k + threadIdx.x] = ws.tw[b * k + threadIdx.x];
     }
+    __syncthreads();
+    trace_point(tr, kTraceCombine, 2);
 }
 
 size_t gateup_smem(int d) {
     const int ng = d / kGroup;
     return (size_t)2 * ng * kTileBytes + (size_t)2 * ng * kTileRows * 2 + (size_t)kGuTok * d * 4 +
-           (size_t)2 * kGuTok * ng * 32 * 4 + kGuWarps * 8;
+           (size_t)2 * kGuTok * ng * 32 * 4 + (size_t)kGuTok * 32 * 4 +
+           (size_t)kGuWarps * kMaxTilesPerWarp * 8;
 }
 size_t down_smem(int m) {
     const int ng = m / kGroup;
     return (size_t)ng * kTileBytes + (size_t)ng * kTileRows * 2 + (size_t)kDnTok * m * 4 +
-           (size_t)kDnTok * ng * 32 * 4 + kDnWarps * 8;
+           (size_t)kDnTok * ng * 32 * 4 + (size_t)kDnWarps * kMaxTilesPerWarp * 8;
 }
 
 }  // namespace jl
@@ -285,12 +331,11 @@ int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float*
     const int umax = std::min(h->E, B * h->k);
     const size_t gsm = gateup_smem(h->d);
     if (gsm > 220 * 1024) return JL_ERR_INVALID;
+    if ((h->d / kGroup + kGuWarpsPerPart - 1) / kGuWarpsPerPart > kMaxTilesPerWarp) return JL_ERR_INVALID;
     int rc = exact_attrs();
     if (rc) return rc;
-    k_gateup_exact<<<dim3(h->m / kTileRows, umax), kGuWarps * 32, gsm, s>>>(store_l, h->lay, h->k,
-                                                                            x, h->ws);
-    JL_LAUNCH_CHECK();
-    return JL_OK;
+    return launch(k_gateup_exact, dim3(h->m / kTileRows, umax), dim3(kGuWarps * 32), gsm, s,
+                  store_l, h->lay, h->k, x, h->ws);
 }
 
 int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s) {
@@ -298,18 +343,16 @@ int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStr
     const int umax = std::min(h->E, B * h->k);
     const size_t dsm = down_smem(h->m);
     if (dsm > 220 * 1024) return JL_ERR_INVALID;
+    if ((h->m / kGroup + kDnWarps - 1) / kDnWarps > kMaxTilesPerWarp) return JL_ERR_INVALID;
     int rc = exact_attrs();
     if (rc) return rc;
-    k_down_exact<<<dim3(h->d / kTileRows, umax), kDnWarps * 32, dsm, s>>>(store_l, h->lay, h->ws);
-    JL_LAUNCH_CHECK();
-    return JL_OK;
+    return launch(k_down_exact, dim3(h->d / kTileRows, umax), dim3(kDnWarps * 32), dsm, s, store_l,
+                  h->lay, h->ws);
 }
 
 int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s) {
     using namespace jl;
     const int tpb = 128;
     dim3 grid((h->d / 4 + tpb - 1) / tpb, B);
-    k_combine<<<grid, tpb, 0, s>>>(B, h->k, h->d, h->ws, out, top, tw);
-    JL_LAUNCH_CHECK();
-    return JL_OK;
+    return launch(k_combine, grid, dim3(tpb), 0, s, B, h->k, h->d, h->ws, out, top, tw);
 }

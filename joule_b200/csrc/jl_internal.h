@@ -7,6 +7,8 @@
 
 #include "joule_moe.h"
 
+#include <cuda_fp16.h>
+
 // Device tile layout of one part matrix W[R, C] (R % 32 == 0, C % 64 == 0):
 // tiles (rb, g) for row block rb < R/32 and group g < C/64, tile index
 // rb*(C/64) + g, 1024 bytes each: [half h][row t][16 B] = bytes 16h..16h+15
@@ -44,8 +46,21 @@ struct jl_ws {
     float* act;      // [Bmax*k, m] SwiGLU output per slot
     float* y;        // [Bmax*k, d] weighted expert output per slot
     int* counter;    // [1] last-block counter of the router kernel
+    int* rb_count;   // [d/32] finished expert blocks per down row block (combine)
     int* err;        // [1] device error word (jl::kErr* bits)
+    long long* trace;  // [kTraceSlots] phase timestamps, nullptr when tracing is off
+    // tensor-core path
+    int* tc_ntiles;    // [1] token tiles of the current layer
+    int* tc_tile;      // [max tiles][4]: expert, tokens, first uidx position, padded row offset
+    __half* xc;        // [2 planes][rows x d] token tiles, fp16 hi / lo, UMMA core layout
+    __half* ac;        // [2 planes][rows x m] SwiGLU activations, same layout
+    size_t xc_plane, ac_plane;  // halves per plane
 };
+
+// Trace buffer layout: per kernel kind a row of 16 slots of %globaltimer
+// stamps (ns) taken by thread 0 of one chosen block.
+constexpr int kTraceRouter = 0, kTraceGateup = 1, kTraceDown = 2, kTraceCombine = 3;
+constexpr int kTraceSlots = 4 * 16;
 
 struct jl_moe {
     int device;
@@ -61,6 +76,7 @@ struct jl_moe {
     size_t ws_bytes;
     size_t store_bytes;
     int last_B;
+    long long* trace_buf;     // trace buffer: kept until destroy (captured graphs hold it)
     cudaEvent_t phase_ev[5];  // optional phase timing events
     int n_phase_ev;
     // host staging for uploads from host memory
@@ -85,3 +101,8 @@ int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float*
                            cudaStream_t s);
 int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
 int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s);
+
+// jl_tc.cu: tensor-core expert FFN (permute -> gate/up+SwiGLU -> down).
+size_t jl_tc_ws_bytes(int Bmax, int E, int k, int d, int m, size_t* xc_plane, size_t* ac_plane);
+int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
+                         cudaStream_t s);

@@ -12,6 +12,8 @@ namespace {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+constexpr int kExactMaxB = 8;  // JL_PATH_AUTO: CUDA-core exact path up to this batch
+
 int check_shape(const KernelCfg* c) {
     if (!c) return JL_ERR_INVALID;
     if (c->L < 1 || c->d < 64 || c->E < 1 || c->topk < 1 || c->intermediate < 64)
@@ -23,13 +25,16 @@ int check_shape(const KernelCfg* c) {
 }
 
 struct ws_plan {
-    size_t off[14];
+    size_t off[16];
     size_t total;
+    size_t xc_plane, ac_plane;
 };
 
 ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
     const size_t S = (size_t)Bmax * k;
-    const size_t sizes[14] = {
+    size_t xc_plane = 0, ac_plane = 0;
+    const size_t tc_bytes = jl_tc_ws_bytes(Bmax, E, k, d, m, &xc_plane, &ac_plane);
+    const size_t sizes[16] = {
         (size_t)Bmax * E * 4,  // logits
         S * 4,                 // top
         S * 4,                 // tw
@@ -44,10 +49,14 @@ ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
         S * d * 4,             // y
         16,                    // counter
         16,                    // err
+        (size_t)d / 32 * 4,    // rb_count
+        tc_bytes,              // tensor-core path: xc, ac, tile table, tile count
     };
     ws_plan p;
+    p.xc_plane = xc_plane;
+    p.ac_plane = ac_plane;
     size_t o = 0;
-    for (int i = 0; i < 14; i++) {
+    for (int i = 0; i < 16; i++) {
         p.off[i] = o;
         o = align_up(o + sizes[i], 256);
     }
@@ -115,6 +124,18 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
     h->ws.y = (float*)(b + wp.off[11]);
     h->ws.counter = (int*)(b + wp.off[12]);
     h->ws.err = (int*)(b + wp.off[13]);
+    h->ws.rb_count = (int*)(b + wp.off[14]);
+    {
+        uint8_t* t = b + wp.off[15];
+        h->ws.xc_plane = wp.xc_plane;
+        h->ws.ac_plane = wp.ac_plane;
+        h->ws.xc = (__half*)t;
+        t += wp.xc_plane * 2 * sizeof(__half);
+        h->ws.ac = (__half*)t;
+        t += wp.ac_plane * 2 * sizeof(__half);
+        h->ws.tc_ntiles = (int*)t;
+        h->ws.tc_tile = (int*)(t + 16);
+    }
     if (cudaMemset(h->ws_base, 0, h->ws_bytes) != cudaSuccess ||
         cudaMemset(h->gate_w, 0, gw) != cudaSuccess) {
         jl_moe_destroy(h);
@@ -126,6 +147,7 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
 
 extern "C" int jl_moe_destroy(jl_moe* h) {
     if (!h) return JL_OK;
+    if (h->trace_buf) cudaFree(h->trace_buf);
     if (h->gate_w) cudaFree(h->gate_w);
     if (h->store) cudaFree(h->store);
     if (h->ws_base) cudaFree(h->ws_base);
@@ -138,13 +160,33 @@ extern "C" int jl_moe_destroy(jl_moe* h) {
 
 extern "C" int jl_moe_set_path(jl_moe* h, int path) {
     if (!h || path < JL_PATH_AUTO || path > JL_PATH_TC) return JL_ERR_INVALID;
-    if (path == JL_PATH_TC) return JL_ERR_INVALID;  // tensor-core path not built in this library
     h->path = path;
     return JL_OK;
 }
 
+extern "C" int jl_moe_trace(jl_moe* h, int enable, long long* out, int n, void* stream) {
+    if (!h || n < 0 || (n > 0 && !out)) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (enable && !h->trace_buf) {
+        if (cudaMalloc(&h->trace_buf, kTraceSlots * sizeof(long long)) != cudaSuccess) return JL_ERR_OOM;
+        JL_CUDA(cudaMemset(h->trace_buf, 0, kTraceSlots * sizeof(long long)));
+    }
+    // Launches after this call pass the buffer (or nullptr); graphs captured
+    // earlier keep the pointer they captured, so the buffer is only freed by
+    // jl_moe_destroy.
+    h->ws.trace = enable ? h->trace_buf : nullptr;
+    if (n > 0 && h->trace_buf) {
+        JL_CUDA(cudaMemcpyAsync(out, h->trace_buf, (size_t)std::min(n, kTraceSlots) * sizeof(long long),
+                                cudaMemcpyDeviceToHost, s));
+        JL_CUDA(cudaStreamSynchronize(s));
+    }
+    return JL_OK;
+}
+
 extern "C" int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n) {
-    if (!h || n < 0 || n > 5 || (n > 0 && !events)) return JL_ERR_INVALID;
+    if (!h || n < 0 || n > 4 || (n > 0 && !events)) return JL_ERR_INVALID;
+    for (int i = 0; i < n; i++)
+        if (!events[i]) return JL_ERR_INVALID;
     for (int i = 0; i < n; i++) h->phase_ev[i] = (cudaEvent_t)events[i];
     h->n_phase_ev = n;
     return JL_OK;
@@ -219,9 +261,10 @@ extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gat
     return JL_OK;
 }
 
-extern "C" int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out, int* top,
-                              float* tw, void* stream) {
-    if (!h || !x || !out || l < 0 || l >= h->L || B < 1) return JL_ERR_INVALID;
+extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, float* out,
+                                     int* top, float* tw, int mask, void* stream) {
+    if (!h || !x || !out || l < 0 || l >= h->L || B < 1 || mask < 1 || mask > 7)
+        return JL_ERR_INVALID;
     if (B > h->max_tokens) return JL_ERR_CAPACITY;
     if (!h->uploaded[l]) return JL_ERR_NOT_READY;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
@@ -229,23 +272,41 @@ extern "C" int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* ou
     cudaStream_t s = (cudaStream_t)stream;
     const unsigned short* gw = h->gate_w + (size_t)l * h->E * h->d;
     const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    // Inside stream capture an event record must be an external node to be
+    // timed when the graph replays; outside capture it is a plain record.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (h->n_phase_ev > 0 && cudaStreamIsCapturing(s, &cap) != cudaSuccess) return JL_ERR_CUDA;
     auto mark = [&](int i) -> int {
-        if (i < h->n_phase_ev && cudaEventRecord(h->phase_ev[i], s) != cudaSuccess)
-            return JL_ERR_CUDA;
-        return JL_OK;
+        if (i >= h->n_phase_ev) return JL_OK;
+        const cudaError_t e = (cap == cudaStreamCaptureStatusActive)
+                                  ? cudaEventRecordWithFlags(h->phase_ev[i], s, cudaEventRecordExternal)
+                                  : cudaEventRecord(h->phase_ev[i], s);
+        return e == cudaSuccess ? JL_OK : JL_ERR_CUDA;
     };
     int rc = mark(0);
-    if (!rc) rc = jl_launch_route(h, gw, x, B, s);
+    if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, s);
     if (!rc) rc = mark(1);
-    if (!rc) rc = jl_launch_gateup_exact(h, store_l, x, B, s);
-    if (!rc) rc = mark(2);
-    if (!rc) rc = jl_launch_down_exact(h, store_l, B, s);
+    const bool tc_ok = h->d % 512 == 0 && h->m % 64 == 0;
+    const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
+    if (tc) {
+        // the tensor-core kernels run as one unit (permute, gate/up, down)
+        if (!rc && (mask & 2)) rc = jl_launch_experts_tc(h, store_l, x, B, s);
+        if (!rc) rc = mark(2);
+    } else {
+        if (!rc && (mask & 2)) rc = jl_launch_gateup_exact(h, store_l, x, B, s);
+        if (!rc) rc = mark(2);
+        if (!rc && (mask & 4)) rc = jl_launch_down_exact(h, store_l, B, s);
+    }
+    if (!rc && (mask & 4)) rc = jl_launch_combine(h, B, out, top, tw, s);
     if (!rc) rc = mark(3);
-    if (!rc) rc = jl_launch_combine(h, B, out, top, tw, s);
-    if (!rc) rc = mark(4);
     if (rc) return rc;
     h->last_B = B;
     return JL_OK;
+}
+
+extern "C" int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out, int* top,
+                              float* tw, void* stream) {
+    return jl_moe_forward_phases(h, l, x, B, out, top, tw, 7, stream);
 }
 
 extern "C" int jl_moe_debug_routing(jl_moe* h, int B, float* logits, int* sel, int* uh, int* uidx,

@@ -116,6 +116,20 @@ class MoELayers:
                                      _stream(stream)), "jl_moe_forward")
         return out
 
+    def forward_phases(self, l: int, x: torch.Tensor, out: torch.Tensor, mask: int,
+                       stream=None) -> torch.Tensor:
+        """Only the phases in mask (1 router, 2 gate/up, 4 down+combine); for profiling."""
+        check(self._L.jl_moe_forward_phases(self.h, l, _ptr(x), x.shape[0], _ptr(out), None, None,
+                                            mask, _stream(stream)), "jl_moe_forward_phases")
+        return out
+
+    def trace(self, enable: bool = True) -> "np.ndarray | None":
+        """Turn the device trace on/off; returns the [4, 16] ns stamps when on."""
+        buf = np.zeros(64, np.int64)
+        check(self._L.jl_moe_trace(self.h, 1 if enable else 0, buf.ctypes.data if enable else None,
+                                   64 if enable else 0, _stream(None)), "jl_moe_trace")
+        return buf.reshape(4, 16) if enable else None
+
     def check(self, stream=None) -> None:
         check(self._L.jl_moe_check(self.h, _stream(stream)), "jl_moe_check")
 

@@ -71,10 +71,12 @@ SIGNATURES = {
     "jl_moe_quantize_layer": ([_P, _I, _P, _P, _P, _P, _P], _I),
     "jl_moe_set_path": ([_P, _I], _I),
     "jl_moe_forward": ([_P, _I, _P, _I, _P, _P, _P, _P], _I),
+    "jl_moe_forward_phases": ([_P, _I, _P, _I, _P, _P, _P, _I, _P], _I),
     "jl_moe_debug_routing": ([_P, _I, _P, _P, _P, _P, _P, ctypes.POINTER(_I), _P], _I),
     "jl_moe_check": ([_P, _P], _I),
     "jl_layer_ffn_batch": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _I, _P, _I, _P], _I),
     "jl_moe_set_phase_events": ([_P, _P, _I], _I),
+    "jl_moe_trace": ([_P, _I, _P, _I, _P], _I),
     "jl_moe_device_bytes": ([_P], _LL),
     "jl_version": ([], ctypes.c_char_p),
 }

@@ -18,9 +18,11 @@ pytestmark = pytest.mark.gpu
 
 
 def to_moe(lay, max_tokens=64):
-    from joule_b200.moe import MoELayers, make_cfg
+    """A one-layer handle on the exact (reference-order) path."""
+    from joule_b200.moe import PATH_EXACT, MoELayers, make_cfg
     moe = MoELayers(make_cfg(1, lay.d, lay.E, lay.k, lay.m, lay.norm_topk_prob), max_tokens)
     moe.upload_layer(0, lay.gate_w, lay.packed, lay.scales)
+    moe.set_path(PATH_EXACT)
     return moe
 
 
@@ -215,6 +217,7 @@ def test_quantize_layer_matches_host_upload():
             lay.scales[p][e], lay.packed[p][e] = q4.quantize(w[e].numpy())
     a = to_moe(lay)
     b = MoELayers(make_cfg(1, d, E, k, m, 1), 64)
+    b.set_path(1)
     b.quantize_layer(0, torch.from_numpy(gw.view(np.int16)).cuda(), wg.cuda(), wu.cuda(), wd.cuda())
     x = olayer.hidden(6, d, 1)
     assert np.array_equal(run(a, x)[0], run(b, x)[0])
@@ -233,3 +236,36 @@ def test_errors_are_reported():
         moe.forward(0, torch.zeros(5, 256, device="cuda"))
     moe.forward(0, x)
     moe.check()
+
+
+def test_forward_captured_in_cuda_graph_with_phase_events():
+    """The forward is capturable (no host sync, no allocation) and its phase
+    events become timed nodes of the graph."""
+    import ctypes
+    from oracle import layer as olayer
+    g = golden("moe_qwen3_b4")
+    lay = seeded_layer("qwen3")
+    moe = to_moe(lay)
+    x = torch.from_numpy(olayer.hidden(4, lay.d, int(g["seeds"][2]))).cuda()
+    out = torch.empty_like(x)
+    stream = torch.cuda.Stream()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    for e in evs:
+        e.record(stream)
+    stream.synchronize()
+    with torch.cuda.stream(stream):
+        moe.forward(0, x, out, stream=stream)          # eager first call
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in evs])
+            assert moe._L.jl_moe_set_phase_events(moe.h, arr, 4) == 0
+            moe.forward(0, x, out, stream=stream)
+        assert moe._L.jl_moe_set_phase_events(moe.h, None, 0) == 0
+        out.zero_()
+        graph.replay()
+        stream.synchronize()
+    moe.check()
+    assert np.array_equal(out.cpu().numpy(), g["out"])
+    times = [evs[i].elapsed_time(evs[i + 1]) for i in range(3)]
+    assert all(t > 0 for t in times), times
