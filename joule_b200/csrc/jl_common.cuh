@@ -23,7 +23,8 @@ namespace jl {
 constexpr int kGroup = 64;        // Q4 group (q4_store.py:23)
 constexpr int kGroupBytes = 32;   // packed bytes per group
 constexpr int kTileRows = 32;     // rows per device tile
-constexpr int kTileBytes = kTileRows * kGroupBytes;  // 1024
+constexpr int kTileBytes = kTileRows * kGroupBytes;  // 1024 packed bytes per tile
+constexpr int kTileRec = kTileBytes + kTileRows * 2;  // 1088: a tile's packed bytes + its 32 scales
 
 // Device error codes written into a handle's error word.
 constexpr int kErrTimeout = 1;
@@ -180,18 +181,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for phase `parity` of an mbarrier with a time bound. On timeout the
-// error word gets kErrTimeout and false is returned.
+// Wait for phase `parity` of an mbarrier with a time bound. The bound is
+// counted in SM clock cycles (clock64 is cheap to read; %globaltimer is not),
+// checked every 64 polls: 4e9 cycles is at least 2 s at any B200 SM clock.
+// On timeout the error word gets kErrTimeout and false is returned.
+constexpr long long kWaitLimitCycles = 4000000000ll;
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    const long long t0 = clock64();
+    for (int i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0 && clock64() - t0 > kWaitLimitCycles) {
             if (err) atomicOr(err, kErrTimeout);
             return false;
         }
     }
-    return true;
+}
+
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy ones (bulk copies, tensor-core operand reads) on the same bytes:
+// a consumer that read a ring stage with plain loads runs it before releasing
+// the stage to the producer's next bulk copy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Global -> shared bulk copy completing on `bar` (bytes % 16 == 0, both

@@ -58,19 +58,18 @@ __device__ __forceinline__ void tile_row_products(uint4 q0, uint4 q1, float s, c
 // Products for tiles [g_lo, g_hi) of part `pi` (smem tile index pi*ng + g) for
 // `nt` (<= NTMAX) tokens; p_s layout [(pi*NTMAX + t)*ng + g][32].
 template <int NTMAX>
-__device__ __forceinline__ bool warp_tiles(const uint8_t* w_s, const uint16_t* sc_s,
-                                           const float* x_s, int xstride, float* p_s, int pi,
+__device__ __forceinline__ bool warp_tiles(const uint8_t* w_s, const float* x_s, int xstride,
+                                           float* p_s, int pi,
                                            int ng, int g_lo, int g_hi, int nt, uint64_t* bars,
                                            bool wait, int* err) {
     const int lane = threadIdx.x & 31;
     for (int g = g_lo; g < g_hi; g++) {
         // first pass: tile g may still be in flight; compute overlaps the rest
         if (wait && !mbar_wait_bounded(&bars[g - g_lo], 0, err)) return false;
-        const int ti = pi * ng + g;
-        const uint4 q0 = *reinterpret_cast<const uint4*>(w_s + (size_t)ti * kTileBytes + lane * 16);
-        const uint4 q1 =
-            *reinterpret_cast<const uint4*>(w_s + (size_t)ti * kTileBytes + 512 + lane * 16);
-        const float s = half_bits_to_f32(sc_s[ti * kTileRows + lane]);
+        const uint8_t* tile = w_s + (size_t)(pi * ng + g) * kTileRec;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(tile + lane * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(tile + 512 + lane * 16);
+        const float s = half_bits_to_f32(reinterpret_cast<const uint16_t*>(tile + kTileBytes)[lane]);
         const float* xg = x_s + g * kGroup;
         float* pp = p_s + ((size_t)(pi * NTMAX) * ng + g) * 32 + lane;
         const size_t tstride = (size_t)ng * 32;
@@ -100,17 +99,18 @@ __device__ __forceinline__ bool warp_tiles(const uint8_t* w_s, const uint16_t* s
 
 constexpr int kMaxTilesPerWarp = 8;
 
-// Issue this warp's bulk copies: tile i (1 KB) and its 32 scales on mbarrier
-// bars[i], so the warp can start on tile 0 while later tiles are in flight.
-__device__ __forceinline__ void warp_stage(uint8_t* w_dst, uint16_t* sc_dst, const uint8_t* w_src,
-                                           const uint16_t* sc_src, int ntiles, uint64_t* bars) {
+// Issue this warp's bulk copies: tile record i (1088 B: packed + scales) on
+// mbarrier bars[i], so the warp can start on tile 0 while later tiles are in
+// flight. Tiles g in [g_lo, g_hi) of part p, row block rb.
+__device__ __forceinline__ void warp_stage(uint8_t* w_dst, const uint8_t* rec, const jl_layout& L,
+                                           int p, int rb, int g_lo, int g_hi, uint64_t* bars) {
     if ((threadIdx.x & 31) == 0) {
+        const int ntiles = g_hi - g_lo;
         for (int i = 0; i < ntiles; i++) mbar_init(&bars[i], 1);
         mbar_fence_init();
         for (int i = 0; i < ntiles; i++) {
-            mbar_expect_tx(&bars[i], kTileBytes + kTileRows * 2);
-            bulk_g2s(w_dst + (size_t)i * kTileBytes, w_src + (size_t)i * kTileBytes, kTileBytes, &bars[i]);
-            bulk_g2s(sc_dst + i * kTileRows, sc_src + i * kTileRows, kTileRows * 2, &bars[i]);
+            mbar_expect_tx(&bars[i], kTileRec);
+            bulk_g2s(w_dst + (size_t)i * kTileRec, rec + L.tile_off(p, rb, g_lo + i), kTileRec, &bars[i]);
         }
     }
     __syncwarp();
@@ -146,9 +146,8 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
     const int d = L.d, m = L.m, ng = d / kGroup;
     const int rb = blockIdx.x, u = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* w_s = smem;                                                   // [2*ng] tiles
-    uint16_t* sc_s = reinterpret_cast<uint16_t*>(w_s + (size_t)2 * ng * kTileBytes);  // [2*ng*32]
-    float* x_s = reinterpret_cast<float*>(sc_s + 2 * ng * kTileRows);     // [kGuTok, d]
+    uint8_t* w_s = smem;                                                   // [2*ng] tile records
+    float* x_s = reinterpret_cast<float*>(w_s + (size_t)2 * ng * kTileRec);  // [kGuTok, d]
     float* p_s = x_s + kGuTok * d;                                         // [2, kGuTok, ng, 32]
     float* gu_s = p_s + 2 * kGuTok * ng * 32;                              // [kGuTok, 32] up sums
     uint64_t* bars = reinterpret_cast<uint64_t*>(gu_s + kGuTok * 32) + warp * kMaxTilesPerWarp;
@@ -163,13 +162,7 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
     const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
     const int pi = warp / kGuWarpsPerPart, q = warp % kGuWarpsPerPart;
     const int g_lo = q * ng / kGuWarpsPerPart, g_hi = (q + 1) * ng / kGuWarpsPerPart;
-    {
-        const size_t t0 = (size_t)rb * ng + g_lo;
-        warp_stage(w_s + (size_t)(pi * ng + g_lo) * kTileBytes, sc_s + (pi * ng + g_lo) * kTileRows,
-                   rec + L.tiles_off(pi) + t0 * kTileBytes,
-                   reinterpret_cast<const uint16_t*>(rec + L.scales_off(pi)) + t0 * kTileRows,
-                   g_hi - g_lo, bars);
-    }
+    warp_stage(w_s + (size_t)(pi * ng + g_lo) * kTileRec, rec, L, pi, rb, g_lo, g_hi, bars);
     bool ok = true;
     for (int c0 = 0; c0 < n; c0 += kGuTok) {
         const int nt = min(kGuTok, n - c0);
@@ -181,7 +174,7 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_gateup_exact(
         }
         __syncthreads();
         if (c0 == 0) trace_point(tr, kTraceGateup, 2);
-        if (ok) ok = warp_tiles<kGuTok>(w_s, sc_s, x_s, d, p_s, pi, ng, g_lo, g_hi, nt, bars, c0 == 0,
+        if (ok) ok = warp_tiles<kGuTok>(w_s, x_s, d, p_s, pi, ng, g_lo, g_hi, nt, bars, c0 == 0,
                                         ws.err);
         __syncthreads();
         if (c0 == 0) trace_point(tr, kTraceGateup, 3);
@@ -212,9 +205,8 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
     const int d = L.d, m = L.m, ng = m / kGroup;
     const int rb = blockIdx.x, u = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* w_s = smem;
-    uint16_t* sc_s = reinterpret_cast<uint16_t*>(w_s + (size_t)ng * kTileBytes);
-    float* a_s = reinterpret_cast<float*>(sc_s + ng * kTileRows);  // [kDnTok, m]
+    uint8_t* w_s = smem;                                                // [ng] tile records
+    float* a_s = reinterpret_cast<float*>(w_s + (size_t)ng * kTileRec);  // [kDnTok, m]
     float* p_s = a_s + kDnTok * m;                                 // [kDnTok, ng, 32]
     uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kDnTok * ng * 32) + warp * kMaxTilesPerWarp;
     // The routing (U, sel, uh) was written by the router, which completed
@@ -229,13 +221,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
     const int s0 = ws.uh[u], n = ws.uh[u + 1] - s0;
     const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
     const int g_lo = warp * ng / kDnWarps, g_hi = (warp + 1) * ng / kDnWarps;
-    {
-        const size_t t0 = (size_t)rb * ng + g_lo;
-        warp_stage(w_s + (size_t)g_lo * kTileBytes, sc_s + g_lo * kTileRows,
-                   rec + L.tiles_off(2) + t0 * kTileBytes,
-                   reinterpret_cast<const uint16_t*>(rec + L.scales_off(2)) + t0 * kTileRows,
-                   g_hi - g_lo, bars);
-    }
+    warp_stage(w_s + (size_t)g_lo * kTileRec, rec, L, 2, rb, g_lo, g_hi, bars);
     griddep_wait();
     griddep_launch_dependents();
     trace_point(tr, kTraceDown, 1);
@@ -250,7 +236,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_down_exact(const uint8_t* __r
         }
         __syncthreads();
         if (c0 == 0) trace_point(tr, kTraceDown, 2);
-        if (ok) ok = warp_tiles<kDnTok>(w_s, sc_s, a_s, m, p_s, 0, ng, g_lo, g_hi, nt, bars, c0 == 0,
+        if (ok) ok = warp_tiles<kDnTok>(w_s, a_s, m, p_s, 0, ng, g_lo, g_hi, nt, bars, c0 == 0,
                                         ws.err);
         __syncthreads();
         if (warp < nt) {  // one warp per token
@@ -302,13 +288,13 @@ __global__ void k_combine(int B, int k, int d, jl_ws ws, float* __restrict__ out
 
 size_t gateup_smem(int d) {
     const int ng = d / kGroup;
-    return (size_t)2 * ng * kTileBytes + (size_t)2 * ng * kTileRows * 2 + (size_t)kGuTok * d * 4 +
+    return (size_t)2 * ng * kTileRec + (size_t)kGuTok * d * 4 +
            (size_t)2 * kGuTok * ng * 32 * 4 + (size_t)kGuTok * 32 * 4 +
            (size_t)kGuWarps * kMaxTilesPerWarp * 8;
 }
 size_t down_smem(int m) {
     const int ng = m / kGroup;
-    return (size_t)ng * kTileBytes + (size_t)ng * kTileRows * 2 + (size_t)kDnTok * m * 4 +
+    return (size_t)ng * kTileRec + (size_t)kDnTok * m * 4 +
            (size_t)kDnTok * ng * 32 * 4 + (size_t)kDnWarps * kMaxTilesPerWarp * 8;
 }
 

@@ -9,25 +9,30 @@
 
 #include <cuda_fp16.h>
 
-// Device tile layout of one part matrix W[R, C] (R % 32 == 0, C % 64 == 0):
-// tiles (rb, g) for row block rb < R/32 and group g < C/64, tile index
-// rb*(C/64) + g, 1024 bytes each: [half h][row t][16 B] = bytes 16h..16h+15
-// of row (32 rb + t)'s group g. Scales: fp16 at (rb*(C/64) + g)*32 + t.
-// A warp reading one tile (lane t = row t) issues two fully coalesced
-// 512-byte loads and one 64-byte scale load.
+// Device layout of the Q4 store. A tile is 32 rows x one 64-value group of a
+// part matrix, stored as a 1088-byte record: [half h][row t][16 B] (bytes
+// 16h..16h+15 of row t's group; 1024 B) followed by the 32 fp16 scales. A
+// warp reading one tile (lane t = row t) issues two fully coalesced 512-byte
+// loads and one 64-byte load.
 //
-// One expert record (per layer, per expert; record bytes identical to the
-// reference's three Q4 records, q4_store.py:150-158):
-//   [gate tiles m*d/2][up tiles m*d/2][down tiles d*m/2]
-//   [gate scales m*d/32][up scales m*d/32][down scales d*m/32]
+// Tiles are grouped so that every K step of the tensor-core path is ONE
+// contiguous 4352-byte copy:
+//   gate/up: for M-tile mt (gate rows and up rows 64mt..64mt+63), for group g:
+//            [gate rb=2mt][gate rb=2mt+1][up rb=2mt][up rb=2mt+1]
+//   down:    for M-tile mt (rows 128mt..128mt+127 of d), for group g:
+//            [rb=4mt][rb=4mt+1][rb=4mt+2][rb=4mt+3]
+// One expert record (per layer, per expert) = all gate/up tiles, then all
+// down tiles; its size equals the reference's three Q4 records together
+// (q4_store.py:150-158).
 struct jl_layout {
     int d, m, E;
-    size_t part_tiles;    // m*d/2 (every part has m*d values)
-    size_t part_scales;   // m*d/32 bytes
-    size_t rec_bytes;     // 3*(part_tiles + part_scales)
-    __host__ __device__ size_t tiles_off(int p) const { return (size_t)p * part_tiles; }
-    __host__ __device__ size_t scales_off(int p) const {
-        return 3 * part_tiles + (size_t)p * part_scales;
+    int ngd, ngm;      // groups per row: d/64 (gate, up), m/64 (down)
+    size_t dn_off;     // byte offset of the down tiles inside a record
+    size_t rec_bytes;  // bytes per expert record
+    // byte offset of tile (part p in gate/up/down, row block rb, group g)
+    __host__ __device__ size_t tile_off(int p, int rb, int g) const {
+        if (p < 2) return ((size_t)((rb >> 1) * ngd + g) * 4 + p * 2 + (rb & 1)) * 1088u;
+        return dn_off + ((size_t)((rb >> 2) * ngm + g) * 4 + (rb & 3)) * 1088u;
     }
 };
 
@@ -52,8 +57,8 @@ struct jl_ws {
     // tensor-core path
     int* tc_ntiles;    // [1] token tiles of the current layer
     int* tc_tile;      // [max tiles][4]: expert, tokens, first uidx position, padded row offset
-    __half* xc;        // [2 planes][rows x d] token tiles, fp16 hi / lo, UMMA core layout
-    __half* ac;        // [2 planes][rows x m] SwiGLU activations, same layout
+    __half* xc;        // token tiles: per tile [d/8][2N rows: hi, lo][8] fp16 (UMMA core layout)
+    __half* ac;        // SwiGLU activations of the tiles, same layout over m
     size_t xc_plane, ac_plane;  // halves per plane
 };
 
@@ -89,8 +94,8 @@ struct jl_moe {
 // ---- launchers (return JL_OK or JL_ERR_*) --------------------------------
 
 // jl_store.cu
-int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int R, int C,
-                          uint8_t* tiles, uint16_t* scales, cudaStream_t s);
+int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, const jl_layout& L,
+                          uint8_t* rec, cudaStream_t s);
 
 // jl_router.cu: logits + (small B) top-k + dispatch; (large B) separate kernels.
 int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float* x, int B,
@@ -103,6 +108,7 @@ int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStr
 int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s);
 
 // jl_tc.cu: tensor-core expert FFN (permute -> gate/up+SwiGLU -> down).
+// The tile table is built at the end of the dispatch step (jl_tiles.cuh).
 size_t jl_tc_ws_bytes(int Bmax, int E, int k, int d, int m, size_t* xc_plane, size_t* ac_plane);
 int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
                          cudaStream_t s);

@@ -18,7 +18,8 @@ int check_shape(const KernelCfg* c) {
     if (!c) return JL_ERR_INVALID;
     if (c->L < 1 || c->d < 64 || c->E < 1 || c->topk < 1 || c->intermediate < 64)
         return JL_ERR_INVALID;
-    if (c->d % 64 || c->intermediate % 64) return JL_ERR_INVALID;  // whole Q4 groups
+    // whole Q4 groups; gate/up M-tiles of 64 rows, down M-tiles of 128 rows
+    if (c->d % 128 || c->intermediate % 64) return JL_ERR_INVALID;
     if (c->E > 256 || c->topk > 16 || c->topk > c->E) return JL_ERR_INVALID;
     if (c->expert_i8 || c->expert_bf16) return JL_ERR_INVALID;       // Q4 store only
     return JL_OK;
@@ -92,9 +93,10 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
     h->lay.d = h->d;
     h->lay.m = h->m;
     h->lay.E = h->E;
-    h->lay.part_tiles = (size_t)h->m * h->d / 2;
-    h->lay.part_scales = (size_t)h->m * h->d / 32;
-    h->lay.rec_bytes = 3 * (h->lay.part_tiles + h->lay.part_scales);
+    h->lay.ngd = h->d / 64;
+    h->lay.ngm = h->m / 64;
+    h->lay.dn_off = (size_t)(h->m / 64) * h->lay.ngd * 4 * 1088;
+    h->lay.rec_bytes = h->lay.dn_off + (size_t)(h->d / 128) * h->lay.ngm * 4 * 1088;
     h->store_bytes = (size_t)h->L * h->E * h->lay.rec_bytes;
     const ws_plan wp = plan_ws(max_tokens, h->E, h->k, h->d, h->m);
     h->ws_bytes = wp.total;
@@ -223,8 +225,7 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
             uint16_t* st_sc = (uint16_t*)(h->dev_stage + pkb);
             JL_CUDA(cudaMemcpyAsync(st_pk, src_pk, pkb, kind, s));
             JL_CUDA(cudaMemcpyAsync(st_sc, src_sc, scb, kind, s));
-            int rc = jl_launch_repack_part(st_pk, st_sc, R, C, rec + h->lay.tiles_off(p),
-                                           (uint16_t*)(rec + h->lay.scales_off(p)), s);
+            int rc = jl_launch_repack_part(st_pk, st_sc, p, h->lay, rec, s);
             if (rc) return rc;
         }
     }
@@ -250,9 +251,7 @@ extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gat
             uint16_t* st_sc = (uint16_t*)(h->dev_stage + numel / 2);
             int rc = jl_q4_quantize(src[p] + (size_t)e * numel, (long long)numel, st_sc, st_pk, s);
             if (rc) return rc;
-            rc = jl_launch_repack_part(st_pk, st_sc, part_rows(h, p), part_cols(h, p),
-                                       rec + h->lay.tiles_off(p),
-                                       (uint16_t*)(rec + h->lay.scales_off(p)), s);
+            rc = jl_launch_repack_part(st_pk, st_sc, p, h->lay, rec, s);
             if (rc) return rc;
         }
     }

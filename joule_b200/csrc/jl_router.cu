@@ -6,6 +6,7 @@
 
 #include "jl_common.cuh"
 #include "jl_internal.h"
+#include "jl_tiles.cuh"
 
 #include <algorithm>
 
@@ -647,6 +648,7 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kClusterT
                             reinterpret_cast<int*>(scratch + kRouteTB * (kMaxE + 64)));
     }
     __syncthreads();
+    if (tid < 32) tc_build_tiles(ws);
     trace_point(tr, kTraceRouter, 6);
 }
 
@@ -667,6 +669,8 @@ __global__ void k_dispatch(int B, int k, int E, jl_ws ws) {
     griddep_wait();
     griddep_launch_dependents();
     dispatch_block(ws.top, ws.tw, B, k, E, ws, dsm);
+    __syncthreads();
+    if (threadIdx.x < 32) tc_build_tiles(ws);
 }
 
 }  // namespace jl

@@ -55,10 +55,12 @@ __global__ void k_quantize(const float* __restrict__ x, long long n, uint16_t* _
 
 // ---------------------------------------------------------------------------
 // Repack one part matrix from the reference layout (packed [R, C/2] u8,
-// scales [R, C/64] fp16, row-major) into the device tile layout.
-// Thread = (tile, row t, half h): one 16-byte move; half 0 also moves the scale.
-__global__ void k_repack(const uint8_t* __restrict__ pk, const uint16_t* __restrict__ sc, int R,
-                         int C, uint8_t* __restrict__ tiles, uint16_t* __restrict__ tsc) {
+// scales [R, C/64] fp16, row-major) into the device tile records of one
+// expert record. Thread = (tile, row t, half h): one 16-byte move; half 0
+// also moves the row's scale.
+__global__ void k_repack(const uint8_t* __restrict__ pk, const uint16_t* __restrict__ sc, int p,
+                         jl_layout L, uint8_t* __restrict__ rec) {
+    const int R = p < 2 ? L.m : L.d, C = p < 2 ? L.d : L.m;
     const int ng = C / kGroup;
     const long long ntiles = (long long)(R / kTileRows) * ng;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // tile*64 + h*32 + t
@@ -68,9 +70,10 @@ __global__ void k_repack(const uint8_t* __restrict__ pk, const uint16_t* __restr
     const int t = (int)idx & 31;
     const int rb = (int)(tile / ng), g = (int)(tile % ng);
     const int row = rb * kTileRows + t;
+    uint8_t* dst = rec + L.tile_off(p, rb, g);
     const uint4 v = *reinterpret_cast<const uint4*>(pk + (size_t)row * (C / 2) + (size_t)g * kGroupBytes + h * 16);
-    *reinterpret_cast<uint4*>(tiles + tile * kTileBytes + h * 512 + t * 16) = v;
-    if (h == 0) tsc[tile * kTileRows + t] = sc[(size_t)row * ng + g];
+    *reinterpret_cast<uint4*>(dst + h * 512 + t * 16) = v;
+    if (h == 0) reinterpret_cast<uint16_t*>(dst + kTileBytes)[t] = sc[(size_t)row * ng + g];
 }
 
 // ---------------------------------------------------------------------------
@@ -166,13 +169,13 @@ extern "C" int jl_q4_quantize(const float* x, long long n, unsigned short* scale
     return JL_OK;
 }
 
-int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int R, int C,
-                          uint8_t* tiles, uint16_t* scales, cudaStream_t s) {
+int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, const jl_layout& L,
+                          uint8_t* rec, cudaStream_t s) {
+    const int R = p < 2 ? L.m : L.d, C = p < 2 ? L.d : L.m;
     if (R % jl::kTileRows || C % jl::kGroup) return JL_ERR_INVALID;
     const long long threads = (long long)(R / jl::kTileRows) * (C / jl::kGroup) * 64;
     const int tpb = 256;
-    jl::k_repack<<<(unsigned)((threads + tpb - 1) / tpb), tpb, 0, s>>>(pk_ref, sc_ref, R, C, tiles,
-                                                                       scales);
+    jl::k_repack<<<(unsigned)((threads + tpb - 1) / tpb), tpb, 0, s>>>(pk_ref, sc_ref, p, L, rec);
     JL_LAUNCH_CHECK();
     return JL_OK;
 }

@@ -1,19 +1,21 @@
 // Tensor-core (tcgen05) path of the expert FFN for larger batches.
 //
 // Per layer, after routing:
-//   k_tc_permute  gathers the tokens of every union expert into token tiles
-//                 (<= 64 tokens, padded to a multiple of 16) and writes them
-//                 as fp16 hi/lo pairs (x = hi + lo, ~22 significant bits) in
-//                 the UMMA K-major "interleaved" core layout; it also writes
-//                 the tile table (expert, tile, tokens, row offsets).
+//   tc_build_tiles (end of the dispatch step) cuts every union expert's
+//                 tokens into tiles of <= 64 (padded to a multiple of 16).
+//   k_tc_permute  gathers each tile's tokens and writes them as fp16 hi/lo
+//                 pairs (x = hi + lo, ~22 significant bits) in the UMMA
+//                 K-major "interleaved" core layout, hi rows then lo rows, so
+//                 one MMA of N = 2 x tokens covers both (the epilogue adds the
+//                 two accumulator halves).
 //   k_gateup_tc   one CTA per (tile, 64 gate rows + the matching 64 up rows):
-//                 a producer warp streams the Q4 tiles and the token tiles
-//                 through a 4-stage shared-memory ring with 1-D bulk copies;
+//                 two producer warps stream the Q4 tiles (8-stage ring) and
+//                 the token tiles (4-stage ring) with 1-D bulk copies;
 //                 4 dequant warps turn each 64-value group into fp16
 //                 (n - 8) * scale (correctly rounded) and store it straight
 //                 into tensor memory as the MMA's A operand (lane = weight
-//                 row); one thread issues tcgen05.mma (M=128, N=tokens,
-//                 K=16, fp32 accumulate in TMEM) for hi and lo. The epilogue
+//                 row); one thread issues tcgen05.mma (M=128, N=2 x tokens,
+//                 K=16, fp32 accumulate in TMEM). The epilogue
 //                 reads the accumulator with tcgen05.ld, applies SwiGLU and
 //                 writes the activations (hi/lo, same core layout) for down.
 //   k_down_tc     the same pipeline over the down matrix (M=128 rows of d,
@@ -32,19 +34,14 @@
 
 #include "jl_common.cuh"
 #include "jl_internal.h"
+#include "jl_tiles.cuh"
 
 namespace jl {
 
-constexpr int kTcNT = 64;            // max tokens per tile (MMA N <= 64)
-constexpr int kTcStages = 4;         // shared-memory ring depth
 constexpr int kTcDqWarps = 4;        // dequant/epilogue warps = TMEM lanes 0..127
-constexpr int kTcThreads = (kTcDqWarps + 2) * 32;  // + producer warp + MMA warp
-constexpr int kTcTmemCols = 128;     // A double buffer (2 x 32) + accumulator (<= 64)
-constexpr int kTcAccCol = 64;
-constexpr int kTcQ4Stage = 4 * kTileBytes + 4 * kTileRows * 2;  // 4 tiles + their scales
-constexpr int kTcBStage = 2 * kTcNT * 128;                         // hi + lo, 64 K values
-// position p of an 8-value K chunk holds element kPerm[p]; kPermInv is its inverse
-__constant__ int kPermInvC[8] = {0, 2, 4, 6, 1, 3, 5, 7};
+constexpr int kTcQ4Stage = 4 * kTileRec;  // the 4 contiguous tile records of one K step
+constexpr int kTcBStage = 2 * kTcNT * 128;  // 8 K chunks x (hi + lo rows) x 16 B, 64 K values
+// position p of an 8-value K chunk holds element kPerm[p] = {0,4,1,5,2,6,3,7}[p]
 
 __host__ __device__ inline int tc_max_tiles(int S, int E) { return S / kTcNT + E + 1; }
 
@@ -102,6 +99,15 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// hi + lo accumulator columns of 16 tokens
+__device__ __forceinline__ void tc_ld_sum16(uint32_t taddr_hi, uint32_t taddr_lo, float (&v)[16]) {
+    float a[16], b[16];
+    tc_ld16(taddr_hi, a);
+    tc_ld16(taddr_lo, b);
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = a[i] + b[i];
+}
+
 // UMMA shared-memory descriptor, K-major, no swizzle: core matrices of 8 rows
 // x 16 bytes; `lbo` = bytes between the two 8-value K halves of one MMA,
 // `sbo` = bytes between 8-row groups.
@@ -120,16 +126,26 @@ __device__ __forceinline__ uint32_t umma_idesc_f16(int N) {
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err,
                                         volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(err, kErrTimeout);
-            *abort = 1;
-            return false;
+    const long long t0 = clock64();
+    for (int i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                atomicOr(err, kErrTimeout);
+                *abort = 1;
+                return false;
+            }
         }
     }
-    return true;
+}
+
+// Warp-wide form for the warps that go on to tcgen05.ld / tcgen05.st: those
+// are .sync.aligned, so every lane must leave the spin together and agree on
+// the outcome (each lane polls on its own and may exit at another iteration).
+__device__ __forceinline__ bool tc_wait_warp(uint64_t* bar, uint32_t parity, int* err,
+                                             volatile int* abort) {
+    return __all_sync(0xffffffffu, tc_wait(bar, parity, err, abort));
 }
 
 // 64 Q4 values of one row (32 bytes) -> 32 words of fp16 pairs (n - 8) * s,
@@ -174,75 +190,19 @@ __device__ __forceinline__ void split_chunk(const float (&x)[8], uint4& hi, uint
 }
 
 // ---------------------------------------------------------------------------
-// Tile table + activation gather. grid = (max tiles, d / 512); block 256.
-
-// rows of expert with n tokens in the padded tile space: full 64-token tiles
-// plus the last tile rounded up to 16.
-__device__ __forceinline__ int tc_rows(int n) { return (n / kTcNT) * kTcNT + ((n % kTcNT + 15) & ~15); }
-
-// Locate tile `ti`: its expert u, tile j, first uidx position and row offset.
-// Warp 0 scans the union (U <= 256) in chunks of 32. Returns false past the end.
-__device__ bool tc_find_tile(const jl_ws& ws, int ti, int* info /* smem [6] */) {
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        const int U = *ws.U;
-        int tiles_before = 0, rows_before = 0, found = 0;
-        for (int u0 = 0; u0 < U; u0 += 32) {  // full scan: tiles_before ends as the total
-            const int u = u0 + lane;
-            const int n = (u < U) ? ws.uh[u + 1] - ws.uh[u] : 0;
-            const int t = (n + kTcNT - 1) / kTcNT, r = tc_rows(n);
-            int ti_inc = t, r_inc = r;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int a = __shfl_up_sync(0xffffffffu, ti_inc, o);
-                const int b = __shfl_up_sync(0xffffffffu, r_inc, o);
-                if (lane >= o) {
-                    ti_inc += a;
-                    r_inc += b;
-                }
-            }
-            const int t_ex = tiles_before + ti_inc - t, r_ex = rows_before + r_inc - r;
-            const bool mine = u < U && ti >= t_ex && ti < t_ex + t;
-            const unsigned bal = __ballot_sync(0xffffffffu, mine);
-            if (mine) {
-                const int j = ti - t_ex;
-                info[0] = 1;
-                info[1] = u;
-                info[2] = j;
-                info[3] = min(kTcNT, n - j * kTcNT);     // tokens in the tile
-                info[4] = ws.uh[u] + j * kTcNT;          // first uidx position
-                info[5] = r_ex + j * kTcNT;              // padded row offset
-            }
-            found |= bal != 0;
-            tiles_before += __shfl_sync(0xffffffffu, ti_inc, 31);
-            rows_before += __shfl_sync(0xffffffffu, r_inc, 31);
-        }
-        if (!found && lane == 0) info[0] = 0;
-        if (lane == 0 && ti == 0 && blockIdx.y == 0) ws.tc_ntiles[0] = tiles_before;
-    }
-    __syncthreads();
-    return info[0] != 0;
-}
-
+// Activation gather: grid = (max tiles, d / 512), block 256. Block (t, y)
+// writes K chunks [64y, 64y + 64) of tile t as fp16 hi/lo in core layout.
 __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x, int d, int k,
                                                     jl_ws ws) {
-    __shared__ int info[6];
     griddep_wait();
     griddep_launch_dependents();
     const int ti = blockIdx.x;
-    // the total tile count is written by tile 0's block even when it has work
-    if (!tc_find_tile(ws, ti, info)) return;
-    const int n = info[3], N = (n + 15) & ~15, pos0 = info[4], row0 = info[5];
-    if (blockIdx.y == 0 && threadIdx.x == 0) {
-        ws.tc_tile[ti * 4 + 0] = ws.sel[info[1]];  // expert id of union position u
-        ws.tc_tile[ti * 4 + 1] = n;
-        ws.tc_tile[ti * 4 + 2] = pos0;
-        ws.tc_tile[ti * 4 + 3] = row0;
-    }
-    // K slice of this block: chunks kc in [kc0, kc0 + 64)
+    if (ti >= *ws.tc_ntiles) return;
+    const int n = ws.tc_tile[ti * 4 + 1], N = (n + 15) & ~15;
+    const int pos0 = ws.tc_tile[ti * 4 + 2], row0 = ws.tc_tile[ti * 4 + 3];
     const int kc0 = blockIdx.y * 64, kcn = min(64, d / 8 - kc0);
-    __half* hi = ws.xc + (size_t)row0 * d;
-    __half* lo = ws.xc + ws.xc_plane + (size_t)row0 * d;
+    // tile layout: [kc][2N rows: hi rows 0..N-1, lo rows N..2N-1][8 halves]
+    __half* base = ws.xc + (size_t)2 * row0 * d;
     for (int i = threadIdx.x; i < N * kcn; i += blockDim.x) {
         const int r = i % N, kc = kc0 + i / N;
         uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
@@ -253,32 +213,49 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
             const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
             split_chunk(v, vh, vl);
         }
-        *reinterpret_cast<uint4*>(hi + (size_t)kc * N * 8 + r * 8) = vh;
-        *reinterpret_cast<uint4*>(lo + (size_t)kc * N * 8 + r * 8) = vl;
+        __half* blk = base + (size_t)kc * 2 * N * 8;
+        *reinterpret_cast<uint4*>(blk + r * 8) = vh;
+        *reinterpret_cast<uint4*>(blk + (N + r) * 8) = vl;
     }
 }
 
 // ---------------------------------------------------------------------------
-// The grouped GEMM CTA (shared by gate/up and down).
+// The grouped GEMM CTA (shared by gate/up and down). Roles:
+//   warps 0-3  dequant (thread = A row = TMEM lane) and epilogue
+//   warp 4     Q4 producer: weight tiles + scales, 8-stage ring
+//   warp 5     activation producer: hi/lo K chunks, 4-stage ring
+//   warp 6     MMA issuer; TMEM allocation
+// The weight ring is released as soon as the dequant warps have the bytes in
+// registers, so the weight stream runs up to 8 chunks ahead of the MMAs; the
+// 4 TMEM A buffers let dequant run 4 chunks ahead.
+
+constexpr int kTcQS = 8;   // weight stages
+constexpr int kTcBS = 4;   // activation stages
+constexpr int kTcAB = 4;   // TMEM A buffers (32 columns each)
+constexpr int kTcAcc = kTcAB * 32;  // accumulator column
+constexpr int kTcCols = 256;
+constexpr int kTcWarps = 7;
 
 struct TcSmem {
-    uint64_t full[kTcStages], empty[kTcStages], a_full[2], a_empty[2], acc_full;
+    uint64_t q4_full[kTcQS], q4_empty[kTcQS];
+    uint64_t b_full[kTcBS], b_empty[kTcBS];
+    uint64_t a_full[kTcAB], a_empty[kTcAB];
+    uint64_t acc_full;
     uint32_t tmem_base;
     int abort;
     int info[4];  // expert, tokens, first uidx position, row offset
 };
 
-// smem: [TcSmem][q4 ring][b ring]; the b ring is reused by the epilogue
-constexpr size_t kTcSmemQ4Off = 256;
-constexpr size_t kTcSmemBOff = kTcSmemQ4Off + (size_t)kTcStages * kTcQ4Stage;
-constexpr size_t kTcSmemBytes = kTcSmemBOff + (size_t)kTcStages * kTcBStage;
+constexpr size_t kTcSmemQ4Off = 512;
+constexpr size_t kTcSmemBOff = kTcSmemQ4Off + (size_t)kTcQS * kTcQ4Stage;
+constexpr size_t kTcSmemBytes = kTcSmemBOff + (size_t)kTcBS * kTcBStage;
 
 // is_down: A = down rows [mt*128, +128) of d (4 tiles of 32 rows), K = m,
 //          B = activations; epilogue y = w * acc.
 // else:    A = gate rows [mt*64, +64) then up rows [mt*64, +64), K = d,
 //          B = tokens; epilogue act = silu(g) * u.
 template <bool is_down>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcWarps * 32, 1)
     k_expert_tc(const uint8_t* __restrict__ store_l, jl_layout L, jl_ws ws) {
     extern __shared__ __align__(1024) uint8_t smem[];
     TcSmem& sh = *reinterpret_cast<TcSmem*>(smem);
@@ -290,30 +267,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int ti = blockIdx.x / MT, mt = blockIdx.x % MT;
     const int K = is_down ? m : d;
     const int nchunks = K / kGroup;
+    long long* tr = (blockIdx.x == 0) ? ws.trace : nullptr;
+    const int tk = is_down ? kTraceDown : kTraceGateup;
+    trace_point(tr, tk, 0);
     griddep_wait();
     griddep_launch_dependents();
     if (ti >= *ws.tc_ntiles) return;
+    trace_point(tr, tk, 1);
     if (threadIdx.x == 0) {
         sh.info[0] = ws.tc_tile[ti * 4 + 0];
         sh.info[1] = ws.tc_tile[ti * 4 + 1];
         sh.info[2] = ws.tc_tile[ti * 4 + 2];
         sh.info[3] = ws.tc_tile[ti * 4 + 3];
         sh.abort = 0;
-        for (int s = 0; s < kTcStages; s++) {
-            mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], kTcDqWarps * 32 + 1);
+        for (int s = 0; s < kTcQS; s++) {
+            mbar_init(&sh.q4_full[s], 1);
+            mbar_init(&sh.q4_empty[s], kTcDqWarps * 32);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int s = 0; s < kTcBS; s++) {
+            mbar_init(&sh.b_full[s], 1);
+            mbar_init(&sh.b_empty[s], 1);
+        }
+        for (int b = 0; b < kTcAB; b++) {
             mbar_init(&sh.a_full[b], kTcDqWarps * 32);
             mbar_init(&sh.a_empty[b], 1);
         }
         mbar_init(&sh.acc_full, 1);
         mbar_fence_init();
     }
-    if (warp == kTcDqWarps + 1) {  // TMEM allocation by one full warp
+    if (warp == 6) {  // TMEM allocation by one full warp
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&sh.tmem_base)),
-                     "r"(kTcTmemCols));
+                     "r"(kTcCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -322,68 +307,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = sh.tmem_base;
     const int e = sh.info[0], n = sh.info[1], N = (n + 15) & ~15, pos0 = sh.info[2], row0 = sh.info[3];
     const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
-    const int ngK = K / kGroup;  // groups per weight row
-    const uint32_t b_part = (uint32_t)N * 128;  // bytes of one hi or lo chunk (8 K-chunks x N rows x 16 B)
+    const uint32_t b_stage = (uint32_t)N * 256;  // 8 K-chunks x 2N rows (hi, lo) x 16 B
 
-    if (warp == kTcDqWarps) {
-        // ---------------- producer: Q4 tiles + token chunks
+    if (warp == 4) {
+        // ---------------- weight producer
         if (lane == 0) {
-            const __half* bsrc = is_down ? ws.ac + (size_t)row0 * m : ws.xc + (size_t)row0 * d;
-            const size_t plane = is_down ? ws.ac_plane : ws.xc_plane;
             int issued = 0;
             for (int c = 0; c < nchunks; c++) {
-                const int s = c % kTcStages;
-                if (c >= kTcStages &&
-                    !tc_wait(&sh.empty[s], ((c / kTcStages) - 1) & 1, ws.err, &sh.abort))
+                const int s = c % kTcQS;
+                if (c >= kTcQS && !tc_wait(&sh.q4_empty[s], ((c / kTcQS) - 1) & 1, ws.err, &sh.abort))
                     break;
                 uint8_t* q = q4_ring + (size_t)s * kTcQ4Stage;
-                uint8_t* bb = b_ring + (size_t)s * kTcBStage;
-                mbar_expect_tx(&sh.full[s], kTcQ4Stage + 2 * b_part);
-                for (int t = 0; t < 4; t++) {
-                    int p, rb;
-                    if (is_down) {
-                        p = 2;
-                        rb = mt * 4 + t;
-                    } else {
-                        p = t >> 1;
-                        rb = mt * 2 + (t & 1);
-                    }
-                    const size_t tile = (size_t)rb * ngK + c;
-                    bulk_g2s(q + t * kTileBytes, rec + L.tiles_off(p) + tile * kTileBytes, kTileBytes,
-                             &sh.full[s]);
-                    bulk_g2s(q + 4 * kTileBytes + t * kTileRows * 2,
-                             rec + L.scales_off(p) + tile * kTileRows * 2, kTileRows * 2, &sh.full[s]);
-                }
-                const size_t koff = (size_t)c * 8 * N * 8;  // halves: 8 K-chunks of N rows x 8
-                bulk_g2s(bb, bsrc + koff, b_part, &sh.full[s]);
-                bulk_g2s(bb + b_part, bsrc + plane + koff, b_part, &sh.full[s]);
+                mbar_expect_tx(&sh.q4_full[s], kTcQ4Stage);
+                // gate/up: [gate 2mt][gate 2mt+1][up 2mt][up 2mt+1]; down: rb 4mt..4mt+3
+                const size_t off = is_down ? L.tile_off(2, mt * 4, c) : L.tile_off(0, mt * 2, c);
+                bulk_g2s(q, rec + off, kTcQ4Stage, &sh.q4_full[s]);
                 issued = c + 1;
             }
-            // never leave bulk copies landing in a CTA that is about to exit
-            for (int c = std::max(0, issued - kTcStages); c < issued; c++)
-                mbar_wait_bounded(&sh.full[c % kTcStages], (c / kTcStages) & 1, ws.err);
+            for (int c = std::max(0, issued - kTcQS); c < issued; c++)  // no copies left in flight
+                mbar_wait_bounded(&sh.q4_full[c % kTcQS], (c / kTcQS) & 1, ws.err);
         }
-    } else if (warp == kTcDqWarps + 1) {
-        // ---------------- MMA issuer
+    } else if (warp == 5) {
+        // ---------------- activation producer
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16(N);
+            const __half* bsrc = is_down ? ws.ac + (size_t)2 * row0 * m : ws.xc + (size_t)2 * row0 * d;
+            int issued = 0;
             for (int c = 0; c < nchunks; c++) {
-                const int s = c % kTcStages, ab = c & 1;
-                if (!tc_wait(&sh.a_full[ab], (c >> 1) & 1, ws.err, &sh.abort)) break;
-                if (!tc_wait(&sh.full[s], (c / kTcStages) & 1, ws.err, &sh.abort)) break;
+                const int s = c % kTcBS;
+                if (c >= kTcBS && !tc_wait(&sh.b_empty[s], ((c / kTcBS) - 1) & 1, ws.err, &sh.abort))
+                    break;
+                uint8_t* bb = b_ring + (size_t)s * kTcBStage;
+                mbar_expect_tx(&sh.b_full[s], b_stage);
+                bulk_g2s(bb, bsrc + (size_t)c * 8 * 2 * N * 8, b_stage, &sh.b_full[s]);
+                issued = c + 1;
+            }
+            for (int c = std::max(0, issued - kTcBS); c < issued; c++)
+                mbar_wait_bounded(&sh.b_full[c % kTcBS], (c / kTcBS) & 1, ws.err);
+        }
+    } else if (warp == 6) {
+        // ---------------- MMA issuer: per K step one MMA over 2N columns
+        // (hi rows -> accumulator columns [0, N), lo rows -> [N, 2N))
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(2 * N);
+            const uint64_t desc0 = umma_desc(b_ring, (uint32_t)N * 32, 128);
+            const uint64_t kstep = (uint64_t)((2 * N * 32) >> 4);      // 2 K chunks of 2N rows
+            const uint64_t sstep = (uint64_t)(kTcBStage >> 4);
+            for (int c = 0; c < nchunks; c++) {
+                const int ab = c % kTcAB, sb = c % kTcBS;
+                if (!tc_wait(&sh.a_full[ab], (c / kTcAB) & 1, ws.err, &sh.abort)) break;
+                if (!tc_wait(&sh.b_full[sb], (c / kTcBS) & 1, ws.err, &sh.abort)) break;
                 tc_fence_after();
-                const uint8_t* bb = b_ring + (size_t)s * kTcBStage;
+                const uint64_t dsb = desc0 + sb * sstep;
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++)
-#pragma unroll
-                    for (int part = 0; part < 2; part++) {
-                        const uint64_t desc =
-                            umma_desc(bb + part * b_part + (size_t)ks * 2 * N * 16, (uint32_t)N * 16, 128);
-                        tc_mma_ts(tmem + kTcAccCol, tmem + ab * 32 + ks * 8, desc, idesc,
-                                  (c | ks | part) ? 1u : 0u);
-                    }
+                    tc_mma_ts(tmem + kTcAcc, tmem + ab * 32 + ks * 8, dsb + ks * kstep, idesc,
+                              (c | ks) ? 1u : 0u);
                 tc_commit(&sh.a_empty[ab]);
-                tc_commit(&sh.empty[s]);
+                tc_commit(&sh.b_empty[sb]);
             }
             tc_commit(&sh.acc_full);
         }
@@ -391,32 +371,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---------------- dequant warps: thread = A row (TMEM lane)
         const int row = warp * 32 + lane;
         for (int c = 0; c < nchunks; c++) {
-            const int s = c % kTcStages, ab = c & 1;
-            if (!tc_wait(&sh.full[s], (c / kTcStages) & 1, ws.err, &sh.abort)) break;
-            const uint8_t* q = q4_ring + (size_t)s * kTcQ4Stage + warp * kTileBytes;
+            const int s = c % kTcQS, ab = c % kTcAB;
+            if (!tc_wait_warp(&sh.q4_full[s], (c / kTcQS) & 1, ws.err, &sh.abort)) break;
+            if (c < 8) trace_point(tr, tk, 2 + c);
+            const uint8_t* q = q4_ring + (size_t)s * kTcQ4Stage + warp * kTileRec;
             const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
             const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
-            const uint16_t sb = reinterpret_cast<const uint16_t*>(
-                q4_ring + (size_t)s * kTcQ4Stage + 4 * kTileBytes)[warp * kTileRows + lane];
-            mbar_arrive(&sh.empty[s]);  // this stage's Q4 bytes are in registers
+            const uint16_t sb = reinterpret_cast<const uint16_t*>(q + kTileBytes)[lane];
+            // the stage's bytes are in registers; the next bulk copy into it is an
+            // async-proxy write, ordered after these plain loads by the proxy fence
+            fence_proxy_async_smem();
+            mbar_arrive(&sh.q4_empty[s]);
             uint32_t a[32];
             dequant_row_f16(q0, q1, __ushort_as_half(sb), a);
-            if (c >= 2 && !tc_wait(&sh.a_empty[ab], ((c >> 1) - 1) & 1, ws.err, &sh.abort)) break;
+            if (c >= kTcAB && !tc_wait_warp(&sh.a_empty[ab], ((c / kTcAB) - 1) & 1, ws.err, &sh.abort))
+                break;
+            // order this TMEM write after the MMAs that read the buffer (released by a_empty)
+            tc_fence_after();
             tc_st32(tmem + ((uint32_t)(warp * 32) << 16) + ab * 32, a);
             tc_wait_st();
             tc_fence_before();
             mbar_arrive(&sh.a_full[ab]);
         }
         // ---------------- epilogue
-        const bool ok = tc_wait(&sh.acc_full, 0, ws.err, &sh.abort);
+        trace_point(tr, tk, 10);
+        const bool ok = tc_wait_warp(&sh.acc_full, 0, ws.err, &sh.abort);
         tc_fence_after();
-        float* scr = reinterpret_cast<float*>(b_ring);  // ring is idle once acc_full completed
+        trace_point(tr, tk, 11);
+        // the activation ring is idle once acc_full completed (every bulk copy into it
+        // landed and every MMA read of it finished); reuse it as epilogue scratch
+        fence_proxy_async_smem();
+        float* scr = reinterpret_cast<float*>(b_ring);
         if (ok) {
-            const uint32_t tacc = tmem + ((uint32_t)(warp * 32) << 16) + kTcAccCol;
+            const uint32_t tacc = tmem + ((uint32_t)(warp * 32) << 16) + kTcAcc;
             if (is_down) {
                 for (int t0 = 0; t0 < N; t0 += 16) {
                     float v[16];
-                    tc_ld16(tacc + t0, v);
+                    tc_ld_sum16(tacc + t0, tacc + N + t0, v);
                     for (int i = 0; i < 16 && t0 + i < n; i++) {
                         const int pos = pos0 + t0 + i;
                         const int slot = ws.uidx[pos];
@@ -424,22 +415,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
             } else {
-                // up rows (warps 2,3) -> smem; gate rows (warps 0,1) combine
+                // up rows (warps 2,3) -> smem; gate rows (warps 0,1) apply SwiGLU
                 float* up_s = scr;                                            // [64 rows][kTcNT]
                 __half* act_s = reinterpret_cast<__half*>(scr + 64 * kTcNT);  // [2][kTcNT][64]
                 if (warp >= 2)
                     for (int t0 = 0; t0 < N; t0 += 16) {
                         float v[16];
-                        tc_ld16(tacc + t0, v);
+                        tc_ld_sum16(tacc + t0, tacc + N + t0, v);
 #pragma unroll
                         for (int i = 0; i < 16; i++) up_s[(row - 64) * kTcNT + t0 + i] = v[i];
                     }
                 asm volatile("bar.sync 1, %0;" ::"r"(kTcDqWarps * 32) : "memory");
                 if (warp < 2) {
-                    const int kc = row >> 3, pp = kPermInvC[row & 7];
+                    const int j = row & 7, kc = row >> 3;
+                    const int pp = j < 4 ? 2 * j : 2 * (j - 4) + 1;  // position of element j (kPerm inverse)
                     for (int t0 = 0; t0 < N; t0 += 16) {
                         float v[16];
-                        tc_ld16(tacc + t0, v);
+                        tc_ld_sum16(tacc + t0, tacc + N + t0, v);
 #pragma unroll
                         for (int i = 0; i < 16; i++) {
                             const float a = silu_mul(v[i], up_s[row * kTcNT + t0 + i]);
@@ -451,29 +443,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
                 asm volatile("bar.sync 1, %0;" ::"r"(kTcDqWarps * 32) : "memory");
-                // copy out: chunk (t, kc) of 8 halves -> ac core layout
-                __half* ahi = ws.ac + (size_t)row0 * m;
-                __half* alo = ws.ac + ws.ac_plane + (size_t)row0 * m;
+                // copy out: chunk (t, kc) of 8 halves -> ac tile layout [kc][2N][8]
+                __half* abase = ws.ac + (size_t)2 * row0 * m;
                 for (int i = row; i < N * 8; i += kTcDqWarps * 32) {
                     const int t = i % N, kcl = i / N;
-                    const size_t dst = (size_t)(mt * 8 + kcl) * N * 8 + (size_t)t * 8;
+                    __half* blk = abase + (size_t)(mt * 8 + kcl) * 2 * N * 8;
                     uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
                     if (t < n) {
                         vh = *reinterpret_cast<const uint4*>(act_s + t * 64 + kcl * 8);
                         vl = *reinterpret_cast<const uint4*>(act_s + kTcNT * 64 + t * 64 + kcl * 8);
                     }
-                    *reinterpret_cast<uint4*>(ahi + dst) = vh;
-                    *reinterpret_cast<uint4*>(alo + dst) = vl;
+                    *reinterpret_cast<uint4*>(blk + t * 8) = vh;
+                    *reinterpret_cast<uint4*>(blk + (N + t) * 8) = vl;
                 }
             }
         }
     }
+    trace_point(tr, tk, 12);
     tc_fence_before();
     __syncthreads();
-    if (warp == kTcDqWarps + 1) {
+    if (warp == 6) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(kTcTmemCols));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols));
     }
 }
 
@@ -485,7 +476,7 @@ size_t jl_tc_ws_bytes(int Bmax, int E, int k, int d, int m, size_t* xc_plane, si
     const int S = Bmax * k;
     const int tiles = jl::tc_max_tiles(S, E);
     const size_t rows = (size_t)S + 15 * (size_t)tiles;
-    *xc_plane = rows * d;  // halves per hi/lo plane
+    *xc_plane = rows * d;  // halves per hi (or lo) plane; tiles interleave both
     *ac_plane = rows * m;
     return (*xc_plane + *ac_plane) * 2 * sizeof(__half) + (size_t)tiles * 4 * sizeof(int) + 16;
 }
@@ -505,9 +496,9 @@ int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x
     const int tiles = tc_max_tiles(B * h->k, h->E);
     int rc = launch(k_tc_permute, dim3(tiles, h->d / 512), dim3(256), 0, s, x, h->d, h->k, h->ws);
     if (rc) return rc;
-    rc = launch(k_expert_tc<false>, dim3(tiles * (h->m / 64)), dim3(kTcThreads), kTcSmemBytes, s,
+    rc = launch(k_expert_tc<false>, dim3(tiles * (h->m / 64)), dim3(kTcWarps * 32), kTcSmemBytes, s,
                 store_l, h->lay, h->ws);
     if (rc) return rc;
-    return launch(k_expert_tc<true>, dim3(tiles * (h->d / 128)), dim3(kTcThreads), kTcSmemBytes, s,
+    return launch(k_expert_tc<true>, dim3(tiles * (h->d / 128)), dim3(kTcWarps * 32), kTcSmemBytes, s,
                   store_l, h->lay, h->ws);
 }
