@@ -217,6 +217,22 @@ int jl_moe_trace(jl_moe* h, int enable, long long* out, int n, void* stream);
  * reference (its profiling is wall-clock, batch_bench.py:58-68). */
 int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n);
 
+/* Router + softmax/top-k (+ optional renorm) for B <= 64 tokens with no
+ * device allocation and no handle. No counterpart in the reference.
+ * gate_w [E, d] bf16 and x [B, d] fp32 are device memory, 16-byte aligned;
+ * top [B, topk] int32 and tw [B, topk] fp32 (device) receive the same ids
+ * and weights as jl_moe_forward's top/tw. The [B, E] logits go to a static
+ * 64 KiB device array (64 tokens x 256 experts), one per device, so:
+ * B > 64 returns JL_ERR_CAPACITY and E > 256 JL_ERR_INVALID; calls on one
+ * device must not overlap (one stream, or ordered by events); the first call
+ * on a device performs a one-time setup that must precede any stream
+ * capture. dev_status (nullable, device int) must hold 0 before the call;
+ * the kernels OR bit 1 into it when a bounded wait runs out. For hosts that
+ * must not allocate per request. */
+int jl_route_noalloc(const unsigned short* gate_w, const float* x, int B, int E,
+                     int d, int topk, int norm_topk_prob, int* top, float* tw,
+                     int* dev_status, void* stream);
+
 /* Bytes of device memory the handle holds (store + workspace). */
 long long jl_moe_device_bytes(const jl_moe* h);
 

@@ -101,6 +101,12 @@ int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, 
 int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float* x, int B,
                     cudaStream_t s);
 
+// jl_router.cu: routing only (logits -> top-k) with a caller-built ws; used by
+// the entry point that allocates nothing (jl_noalloc.cu).
+int jl_router_topk_prepare();
+int jl_launch_router_topk(const jl_ws& ws, const unsigned short* gate_w, const float* x, int B, int E,
+                          int d, int k, int norm, cudaStream_t s);
+
 // jl_exact.cu: CUDA-core expert FFN in the reference's arithmetic order.
 int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
                            cudaStream_t s);

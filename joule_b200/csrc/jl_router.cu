@@ -714,3 +714,26 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
     const size_t dsm = (size_t)dispatch_smem_ints(E, T / 32) * 4;
     return launch(k_dispatch, dim3(1), dim3(T), dsm, s, B, k, E, h->ws);
 }
+
+// Routing only, into buffers the caller chooses: k_router (no fused tail)
+// then k_topk. ws.logits ([B, E] fp32 scratch), ws.top / ws.tw (the outputs)
+// and ws.err are the only workspace fields these two kernels touch.
+int jl_router_topk_prepare() {
+    JL_CUDA(cudaFuncSetAttribute(jl::k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+    return JL_OK;
+}
+
+int jl_launch_router_topk(const jl_ws& ws, const unsigned short* gate_w, const float* x, int B, int E,
+                          int d, int k, int norm, cudaStream_t s) {
+    using namespace jl;
+    if (E > kMaxE || k > kMaxK || k < 1 || E < k || B < 1 || d < 8 || d % 8) return JL_ERR_INVALID;
+    const int TB = kRouteTB;
+    const size_t smem = (size_t)kRouteEPB * (d * 2 + 16) + (size_t)TB * d * 4;
+    if (smem > 220 * 1024) return JL_ERR_INVALID;
+    dim3 grid((E + kRouteEPB - 1) / kRouteEPB, (B + TB - 1) / TB);
+    int rc = launch(k_router, grid, dim3(32 * TB), smem, s, gate_w, x, B, E, d, k, norm, ws, 0);
+    if (rc) return rc;
+    const int wpb = 8;
+    return launch(k_topk, dim3((B + wpb - 1) / wpb), dim3(32 * wpb), (size_t)wpb * kMaxE * 4, s,
+                  (const float*)ws.logits, B, E, k, norm, ws);
+}

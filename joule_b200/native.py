@@ -77,6 +77,7 @@ SIGNATURES = {
     "jl_layer_ffn_batch": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _I, _P, _I, _P], _I),
     "jl_moe_set_phase_events": ([_P, _P, _I], _I),
     "jl_moe_trace": ([_P, _I, _P, _I, _P], _I),
+    "jl_route_noalloc": ([_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P], _I),
     "jl_moe_device_bytes": ([_P], _LL),
     "jl_version": ([], ctypes.c_char_p),
 }
