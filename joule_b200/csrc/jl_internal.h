@@ -73,7 +73,7 @@ struct jl_moe {
     int max_tokens;
     int path;
     jl_layout lay;
-    unsigned short* gate_w;   // [L, E, d] bf16
+    unsigned short* gate_w;   // [L, E, 8, d/8 + 8] bf16, lane-major rows (jl_launch_repack_router)
     uint8_t* store;           // [L, E] records
     unsigned char* uploaded;  // host flags [L]
     jl_ws ws;
@@ -87,7 +87,7 @@ struct jl_moe {
     // host staging for uploads from host memory
     void* pinned;
     size_t pinned_bytes;
-    uint8_t* dev_stage;       // device staging for one expert's reference records
+    uint8_t* dev_stage;       // device staging: one expert's reference records, or one layer's router rows
     size_t dev_stage_bytes;
 };
 
@@ -97,9 +97,19 @@ struct jl_moe {
 int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, const jl_layout& L,
                           uint8_t* rec, cudaStream_t s);
 
-// jl_router.cu: logits + (small B) top-k + dispatch; (large B) separate kernels.
+// Router weights [E, d] bf16 (reference layout, device) -> lane-major rows
+// [E][8][d/8 + 8] (what jl_moe keeps in gate_w): lane j of expert e holds
+// src[e][j + 8t], t < d/8, then 8 halves of padding, so the rows of one
+// expert (and of consecutive experts) are one contiguous block whose rows
+// start 16 bytes apart modulo 128: shared-memory rows without bank conflicts.
+__host__ __device__ inline int router_row_halves(int d) { return d / 8 + 8; }
+__host__ __device__ inline size_t router_expert_halves(int d) { return (size_t)8 * router_row_halves(d); }
+int jl_launch_repack_router(const uint16_t* src, uint16_t* dst, int E, int d, cudaStream_t s);
+
+// jl_router.cu: logits, softmax/top-k and dispatch on thread-block clusters;
+// `tiles` also builds the tensor-core tile table.
 int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float* x, int B,
-                    cudaStream_t s);
+                    bool tiles, cudaStream_t s);
 
 // jl_router.cu: routing only (logits -> top-k) with a caller-built ws; used by
 // the entry point that allocates nothing (jl_noalloc.cu).

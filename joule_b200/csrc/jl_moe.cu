@@ -100,9 +100,9 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
     h->store_bytes = (size_t)h->L * h->E * h->lay.rec_bytes;
     const ws_plan wp = plan_ws(max_tokens, h->E, h->k, h->d, h->m);
     h->ws_bytes = wp.total;
-    h->dev_stage_bytes = h->lay.rec_bytes;
+    h->dev_stage_bytes = std::max(h->lay.rec_bytes, (size_t)h->E * h->d * 2);
     h->uploaded = (unsigned char*)calloc(h->L, 1);
-    const size_t gw = (size_t)h->L * h->E * h->d * 2;
+    const size_t gw = (size_t)h->L * h->E * router_expert_halves(h->d) * 2;
     if (!h->uploaded || cudaMalloc(&h->gate_w, gw) != cudaSuccess ||
         cudaMalloc(&h->store, h->store_bytes) != cudaSuccess ||
         cudaMalloc(&h->ws_base, h->ws_bytes) != cudaSuccess ||
@@ -196,7 +196,7 @@ extern "C" int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n) {
 
 extern "C" long long jl_moe_device_bytes(const jl_moe* h) {
     if (!h) return 0;
-    return (long long)(h->store_bytes + h->ws_bytes + (size_t)h->L * h->E * h->d * 2 +
+    return (long long)(h->store_bytes + h->ws_bytes + (size_t)h->L * h->E * router_expert_halves(h->d) * 2 +
                        h->dev_stage_bytes);
 }
 
@@ -209,9 +209,11 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
     if (!h || l < 0 || l >= h->L || !gate_w || !pk || !sc) return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
     const size_t gw = (size_t)h->E * h->d * 2;
-    JL_CUDA(cudaMemcpyAsync(h->gate_w + (size_t)l * h->E * h->d, gate_w, gw,
-                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
     const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    JL_CUDA(cudaMemcpyAsync(h->dev_stage, gate_w, gw, kind, s));
+    int rc0 = jl_launch_repack_router((const uint16_t*)h->dev_stage, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d),
+                                      h->E, h->d, s);
+    if (rc0) return rc0;
     uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
     for (int e = 0; e < h->E; e++) {
         uint8_t* rec = store_l + (size_t)e * h->lay.rec_bytes;
@@ -239,8 +241,9 @@ extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gat
                                      void* stream) {
     if (!h || l < 0 || l >= h->L || !gate_w || !w_gate || !w_up || !w_down) return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
-    JL_CUDA(cudaMemcpyAsync(h->gate_w + (size_t)l * h->E * h->d, gate_w, (size_t)h->E * h->d * 2,
-                            cudaMemcpyDeviceToDevice, s));
+    int rc0 = jl_launch_repack_router(gate_w, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d), h->E,
+                                      h->d, s);
+    if (rc0) return rc0;
     uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
     const float* src[3] = {w_gate, w_up, w_down};
     const size_t numel = (size_t)h->m * h->d;
@@ -269,7 +272,7 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
         return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
-    const unsigned short* gw = h->gate_w + (size_t)l * h->E * h->d;
+    const unsigned short* gw = h->gate_w + (size_t)l * h->E * router_expert_halves(h->d);
     const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
     // Inside stream capture an event record must be an external node to be
     // timed when the graph replays; outside capture it is a plain record.
@@ -283,10 +286,10 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
         return e == cudaSuccess ? JL_OK : JL_ERR_CUDA;
     };
     int rc = mark(0);
-    if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, s);
-    if (!rc) rc = mark(1);
     const bool tc_ok = h->d % 512 == 0 && h->m % 64 == 0;
     const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
+    if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, tc, s);
+    if (!rc) rc = mark(1);
     if (tc) {
         // the tensor-core kernels run as one unit (permute, gate/up, down)
         if (!rc && (mask & 2)) rc = jl_launch_experts_tc(h, store_l, x, B, s);

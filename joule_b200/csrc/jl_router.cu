@@ -14,7 +14,6 @@ namespace jl {
 
 constexpr int kRouteEPB = 4;      // experts per router block
 constexpr int kRouteTB = 8;       // tokens per router block (one warp each)
-constexpr int kFuseTailMaxB = 8;  // B up to which the last router block routes + dispatches
 constexpr int kMaxK = 16;         // top-k capacity (the reference caps topk at 16, ws_init)
 constexpr int kMaxE = 256;
 
@@ -138,7 +137,22 @@ __host__ __device__ inline int dispatch_smem_ints(int E, int W) { return 6 * E +
 
 __device__ __forceinline__ int clamp_e(int e, int E) { return (e < 0 || e >= E) ? 0 : e; }
 
-__device__ void dispatch_block(const int* top, const float* tw, int B, int k, int E,
+// comb: token b's slots in the union order of their experts (stable for
+// equal positions). Slot s goes to position #{i2 : (u[i2], i2) < (u[i], i)}
+// of its token's k-slot list.
+__device__ __forceinline__ void comb_slot(const int* top, const int* upos, int s, int k, int E,
+                                          int* comb) {
+    const int b = s / k, i = s - b * k;
+    const int u = upos[clamp_e(top[s], E)];
+    int r = 0;
+    for (int i2 = 0; i2 < k; i2++) {
+        const int u2 = upos[clamp_e(top[b * k + i2], E)];
+        r += (u2 < u) || (u2 == u && i2 < i);
+    }
+    comb[b * k + r] = s;
+}
+
+__device__ __forceinline__ void dispatch_block(const int* top, const float* tw, int B, int k, int E,
                                const jl_ws& ws, int* sm) {
     const int S = B * k;
     const int T = blockDim.x, tid = threadIdx.x, W = T >> 5, warp = tid >> 5, lane = tid & 31;
@@ -250,21 +264,7 @@ __device__ void dispatch_block(const int* top, const float* tw, int B, int k, in
         if (valid && lane == __ffs(peers) - 1) wrun[warp * E + e] += __popc(peers);
         __syncwarp();
     }
-    for (int b = tid; b < B; b += T) {
-        int us[kMaxK], ss[kMaxK];
-        for (int i = 0; i < k; i++) {
-            const int u = upos[clamp_e(top[b * k + i], E)];
-            int j = i;
-            while (j > 0 && us[j - 1] > u) {
-                us[j] = us[j - 1];
-                ss[j] = ss[j - 1];
-                j--;
-            }
-            us[j] = u;
-            ss[j] = b * k + i;
-        }
-        for (int i = 0; i < k; i++) ws.comb[b * k + i] = ss[i];
-    }
+    for (int s = tid; s < S; s += T) comb_slot(top, upos, s, k, E, ws.comb);
 }
 
 // ---------------------------------------------------------------------------
@@ -335,32 +335,40 @@ __global__ void k_router(const uint16_t* __restrict__ gate_w, const float* __res
 }
 
 // ---------------------------------------------------------------------------
-// Small-batch routing tail, run by one whole CTA (B <= 8). G = blockDim /
-// next_pow2(B) threads share a token (G >= 32) and synchronise on named
-// barrier 1 + token. Same arithmetic as route_token_warp: max, expf_fast,
-// sequential sum (one thread, vector loads), division, rank-based top-k in
-// (p desc, index asc) order, sequential renorm.
+// Routing of up to 8 tokens by one whole CTA (decode_kernel.c:1425-1448).
+// G = blockDim / next_pow2(nb) threads share a token and synchronise on
+// named barrier 1 + token. Same arithmetic as route_token_warp: max,
+// expf_fast, a SEQUENTIAL sum in expert order (one thread; loads run ahead of
+// the dependent adds), division, top-k, sequential renorm. The top-k ranks
+// every expert by a 64-bit key (p bits << 32 | ~e): p >= 0, so a larger key
+// means a larger p or, for equal p, a smaller index — the order in which the
+// reference's k strict-'>' argmax passes pick. With G >= 2E two threads
+// share an expert's comparisons.
 __device__ __forceinline__ void named_barrier(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-__device__ void route_tokens_cta(const float* lg_s, int B, int E, int k, int norm, const jl_ws& ws,
-                                 float* scratch) {
-    const int T = blockDim.x, tid = threadIdx.x;
-    const int Bp = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
-    const int G = T / Bp, b = tid / G, gl = tid % G;
+__host__ __device__ inline int route_scratch_bytes(int E) {
     const int Ep = (E + 3) & ~3;
-    float* p_s = scratch + b * (Ep + 64);  // [Ep] probabilities, then 64 floats of misc
-    float* misc = p_s + Ep;                // [0..31] warp maxima, [32] max, [33] sum, [40..55] top-k weights
-    const bool active = b < B;
-    const int bar_id = 1 + b;
-    if (active) {
-        const float* lg = lg_s + b * E;
+    return Ep * 8 + Ep * 4 + 2 * Ep * 4 + 64 * 4;  // keys, p, rank halves, misc
+}
+
+__device__ __forceinline__ void route_tokens_cta(const float* lg_s, int nb, int b0, int E, int k, int norm,
+                                 const jl_ws& ws, uint8_t* scratch) {
+    const int T = blockDim.x, tid = threadIdx.x;
+    const int nbp = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8;
+    const int G = T / nbp, tb = tid / G, gl = tid % G;
+    const int Ep = (E + 3) & ~3;
+    uint8_t* base = scratch + (size_t)tb * route_scratch_bytes(E);
+    unsigned long long* key_s = reinterpret_cast<unsigned long long*>(base);
+    float* p_s = reinterpret_cast<float*>(base + Ep * 8);
+    int* rk_s = reinterpret_cast<int*>(p_s + Ep);  // [2][Ep] partial ranks
+    float* misc = reinterpret_cast<float*>(rk_s + 2 * Ep);  // [0..7] warp maxima, [8] sum, [16..31] top-k p
+    const int bar_id = 1 + tb;
+    if (tb < nb) {
+        const float* lg = lg_s + tb * E;
         float mx = -1e30f;
-        for (int e = gl; e < E; e += G) {
-            const float v = lg[e];
-            if (v > mx) mx = v;
-        }
+        for (int e = gl; e < E; e += G) mx = fmaxf(mx, lg[e]);
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         if ((gl & 31) == 0) misc[gl >> 5] = mx;
@@ -369,53 +377,71 @@ __device__ void route_tokens_cta(const float* lg_s, int B, int E, int k, int nor
         for (int w = 1; w < G / 32; w++) mx = fmaxf(mx, misc[w]);
         for (int e = gl; e < Ep; e += G) p_s[e] = (e < E) ? expf_fast(__fsub_rn(lg[e], mx)) : 0.0f;
         named_barrier(bar_id, G);
-        if (gl == 0) {  // the sum runs sequentially in expert order
+        if (gl == 0) {  // zeros past E leave the positive sum unchanged
+            const float4* q4 = reinterpret_cast<const float4*>(p_s);
+            const int n4 = Ep / 4;
             float sum = 0.0f;
-            for (int c = 0; c < Ep / 4; c += 8) {
-                float4 q[8];
+            float4 cur[8], nxt[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) cur[i] = i < n4 ? q4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c = 0; c < n4; c += 8) {
 #pragma unroll
                 for (int i = 0; i < 8; i++)
-                    q[i] = (c + i < Ep / 4) ? reinterpret_cast<const float4*>(p_s)[c + i]
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                    nxt[i] = c + 8 + i < n4 ? q4[c + 8 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    sum = __fadd_rn(sum, q[i].x);
-                    sum = __fadd_rn(sum, q[i].y);
-                    sum = __fadd_rn(sum, q[i].z);
-                    sum = __fadd_rn(sum, q[i].w);
+                    sum = __fadd_rn(sum, cur[i].x);
+                    sum = __fadd_rn(sum, cur[i].y);
+                    sum = __fadd_rn(sum, cur[i].z);
+                    sum = __fadd_rn(sum, cur[i].w);
                 }
+#pragma unroll
+                for (int i = 0; i < 8; i++) cur[i] = nxt[i];
             }
-            misc[33] = sum;
+            misc[8] = sum;
         }
         named_barrier(bar_id, G);
-        const float sum = misc[33];
-        for (int e = gl; e < E; e += G) p_s[e] = __fdiv_rn(p_s[e], sum);
+        const float sum = misc[8];
+        for (int e = gl; e < E; e += G) {
+            const float pe = __fdiv_rn(p_s[e], sum);
+            p_s[e] = pe;
+            key_s[e] = ((unsigned long long)__float_as_uint(pe) << 32) | (0xFFFFFFFFu - (unsigned)e);
+        }
+        named_barrier(bar_id, G);
+        const int halves = G >= 2 * E ? 2 : 1;
+        const int span = E / halves;  // E is even when halves == 2 (E <= G / 2, G a power of 2)
+        for (int i = gl; i < E * halves; i += G) {
+            const int e = i % E, h = i / E;
+            const unsigned long long me = key_s[e];
+            const int lo = h * span, hi = h == halves - 1 ? E : lo + span;
+            int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+            int e2 = lo;
+            for (; e2 + 4 <= hi; e2 += 4) {
+                r0 += key_s[e2] > me;
+                r1 += key_s[e2 + 1] > me;
+                r2 += key_s[e2 + 2] > me;
+                r3 += key_s[e2 + 3] > me;
+            }
+            for (; e2 < hi; e2++) r0 += key_s[e2] > me;
+            rk_s[h * Ep + e] = r0 + r1 + r2 + r3;
+        }
         named_barrier(bar_id, G);
         for (int e = gl; e < E; e += G) {
-            const float pe = p_s[e];
-            int rank = 0;
-            for (int c = 0; c < Ep / 4; c++) {
-                const float4 q = reinterpret_cast<const float4*>(p_s)[c];
-                const int e2 = 4 * c;
-                rank += (q.x > pe) || (q.x == pe && e2 + 0 < e);
-                rank += (e2 + 1 < E) && ((q.y > pe) || (q.y == pe && e2 + 1 < e));
-                rank += (e2 + 2 < E) && ((q.z > pe) || (q.z == pe && e2 + 2 < e));
-                rank += (e2 + 3 < E) && ((q.w > pe) || (q.w == pe && e2 + 3 < e));
-            }
+            const int rank = rk_s[e] + (halves == 2 ? rk_s[Ep + e] : 0);
             if (rank < k) {
-                ws.top[b * k + rank] = e;
-                misc[40 + rank] = pe;
+                ws.top[(b0 + tb) * k + rank] = e;
+                misc[16 + rank] = p_s[e];
             }
         }
         named_barrier(bar_id, G);
         if (gl < k) {
-            float w = misc[40 + gl];
+            float w = misc[16 + gl];
             if (norm) {
                 float ssum = 0.0f;
-                for (int i = 0; i < k; i++) ssum = __fadd_rn(ssum, misc[40 + i]);
+                for (int i = 0; i < k; i++) ssum = __fadd_rn(ssum, misc[16 + i]);
                 w = __fdiv_rn(w, ssum);
             }
-            ws.tw[b * k + gl] = w;
+            ws.tw[(b0 + tb) * k + gl] = w;
         }
     }
     __syncthreads();
@@ -425,7 +451,7 @@ __device__ void route_tokens_cta(const float* lg_s, int B, int E, int k, int nor
 // union positions in first-appearance order from __match_any_sync leaders,
 // offsets by a warp scan, ranks inside an expert by running counts.
 // Same outputs as dispatch_block. `sm` holds 4*E + 2 ints.
-__device__ void dispatch_warp_small(const int* top, const float* tw, int B, int k, int E,
+__device__ __forceinline__ void dispatch_warp_small(const int* top, const float* tw, int B, int k, int E,
                                     const jl_ws& ws, int* sm) {
     const int lane = threadIdx.x & 31, S = B * k;
     const unsigned lt = (1u << lane) - 1u;
@@ -499,157 +525,220 @@ __device__ void dispatch_warp_small(const int* top, const float* tw, int B, int 
         if (valid && lane == __ffs(peers) - 1) run[e] += __popc(peers);
         __syncwarp();
     }
-    if (lane < B) {
-        const int b = lane;
-        int us[kMaxK], ss[kMaxK];
-        for (int i = 0; i < k; i++) {
-            const int u = upos[clamp_e(top[b * k + i], E)];
-            int j = i;
-            while (j > 0 && us[j - 1] > u) {
-                us[j] = us[j - 1];
-                ss[j] = ss[j - 1];
-                j--;
-            }
-            us[j] = u;
-            ss[j] = b * k + i;
-        }
-        for (int i = 0; i < k; i++) ws.comb[b * k + i] = ss[i];
-    }
-}
-
-// B == 1: the union is the top-k list itself (distinct experts in slot order).
-__device__ void dispatch_one(int k, const jl_ws& ws) {
-    const int i = threadIdx.x;
-    if (i < k) {
-        ws.sel[i] = ws.top[i];
-        ws.uh[i] = i;
-        ws.uidx[i] = i;
-        ws.uw[i] = ws.tw[i];
-        ws.slot_pos[i] = i;
-        ws.comb[i] = i;
-    }
-    if (i == 0) {
-        ws.uh[k] = k;
-        *ws.U = k;
-    }
+    for (int s = lane; s < S; s += 32) comb_slot(top, upos, s, k, E, ws.comb);
 }
 
 // ---------------------------------------------------------------------------
-// Small-batch router (B <= 8) on one 8-CTA thread-block cluster. CTA r stages
-// router rows [r*EPC, (r+1)*EPC) (bulk copies issued before waiting on the
-// previous kernel) and the B token rows, computes its logits in the
-// reference's order (up to 4 independent chains per thread), and stores them
-// into the leader CTA's shared memory over DSMEM; after the cluster barrier
-// the leader routes every token (one warp each) and builds the dispatch.
+// Router on 8-CTA thread-block clusters, one cluster per group of TPC tokens
+// (TPC = route_tpc(B), so up to 32 clusters run at once). CTA r of a cluster
+// stages router rows [r*EPC, (r+1)*EPC) by bulk copies issued before waiting
+// on the previous kernel (they do not depend on it), then the cluster's token
+// rows; it computes their logits in the reference's order (8 lane chains of
+// FMAs in k order plus the AVX tree) and stores them into the leader CTA's
+// shared memory over DSMEM. After the cluster barrier the leader routes its
+// tokens. The last leader to finish (a global arrival counter) builds the
+// dispatch for all B tokens and the tensor-core tile table.
 constexpr int kClusterCTAs = 8;
 constexpr int kClusterThreads = 256;
+constexpr int kMaxTPC = 8;
 
-template <int R>
-__device__ __forceinline__ void cluster_logits(const uint8_t* g_s, int grow, const float* x_s,
-                                               int d, int B, int E, int e0, int ne, float* lg_lead,
+__host__ __device__ inline int route_tpc(int B) {  // tokens per cluster: 1, 2, 4 or 8
+    const int t = (B + 31) / 32;
+    return t <= 1 ? 1 : t <= 2 ? 2 : t <= 4 ? 4 : kMaxTPC;
+}
+
+// Shared-memory rows of the cluster router: router row (expert ee, lane j)
+// holds that lane's d/8 bf16 weights plus 8 halves of padding, exactly as the
+// lane-major HBM layout keeps them (one bulk copy per CTA); token row (tb, j)
+// holds x[tb][j + 8t] for t < d/8, padded by 4 floats. With rows 16 bytes
+// apart modulo 128, the 8 lanes x 4 experts of a warp read distinct banks.
+__host__ __device__ inline int router_gstride(int d) { return router_row_halves(d); }  // halves
+__host__ __device__ inline int router_xstride(int d) { return d / 8 + 4; }             // floats
+
+// Thread t < ne*8 owns lane j = t % 8 of expert ee = t / 8 for all NB tokens
+// of the cluster (nb <= NB live; the rest recompute token 0 and are not
+// stored). Each step reads the lane's next 8 weights (one 16-byte load,
+// shared by the NB tokens) and 8 activations per token (two), and the loads
+// of step t + 8 are issued before the FMAs of step t: the dependent FMA chain
+// of each (token, lane), in k order as the reference's lane j, sets the pace.
+template <int NB>
+__device__ __forceinline__ void cluster_logits(const uint16_t* g_s, const float* x_s, int d, int nb,
+                                               int E, int e0, int ne, int b0, float* lg_lead,
                                                float* lg_glob) {
     const int tid = threadIdx.x;
-    float acc[R];
-    int idx[R];
+    if ((tid & ~31) >= ne * 8) return;  // whole warp idle (warp-uniform)
+    const int gs = router_gstride(d), xs = router_xstride(d), c8 = d / 8;
+    const int live = tid < ne * 8;
+    const int j = tid & 7, ee = live ? tid >> 3 : 0;
+    const uint16_t* gp = g_s + (size_t)(ee * 8 + j) * gs;
+    const float* xp[NB];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
+    for (int r = 0; r < NB; r++) xp[r] = x_s + (size_t)((r < nb ? r : 0) * 8 + j) * xs;
+    float acc[NB];
+    float4 xc0[NB], xc1[NB];
+    uint4 gc = *reinterpret_cast<const uint4*>(gp);
+#pragma unroll
+    for (int r = 0; r < NB; r++) {
         acc[r] = 0.0f;
-        idx[r] = tid + r * kClusterThreads;
+        xc0[r] = *reinterpret_cast<const float4*>(xp[r]);
+        xc1[r] = *reinterpret_cast<const float4*>(xp[r] + 4);
     }
-    const int items = ne * B * 8;
-    const uint16_t* gr[R];
-    const float* xr[R];
+    for (int t0 = 0; t0 < c8; t0 += 8) {
+        const int tn = (t0 + 8 < c8) ? t0 + 8 : t0;
+        const uint4 gn = *reinterpret_cast<const uint4*>(gp + tn);
+        float4 xn0[NB], xn1[NB];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        const int it = idx[r] < items ? idx[r] : 0;
-        const int j = it & 7, L = it >> 3, ee = L / B, tb = L % B;
-        gr[r] = reinterpret_cast<const uint16_t*>(g_s + ee * grow) + j;
-        xr[r] = x_s + tb * d + j;
+        for (int r = 0; r < NB; r++) {
+            xn0[r] = *reinterpret_cast<const float4*>(xp[r] + tn);
+            xn1[r] = *reinterpret_cast<const float4*>(xp[r] + tn + 4);
+        }
+        const uint32_t w[4] = {gc.x, gc.y, gc.z, gc.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float lo = __uint_as_float(w[q] << 16), hi = __uint_as_float(w[q] & 0xFFFF0000u);
+#pragma unroll
+            for (int r = 0; r < NB; r++) {
+                const float x0 = q == 0 ? xc0[r].x : q == 1 ? xc0[r].z : q == 2 ? xc1[r].x : xc1[r].z;
+                const float x1 = q == 0 ? xc0[r].y : q == 1 ? xc0[r].w : q == 2 ? xc1[r].y : xc1[r].w;
+                acc[r] = __fmaf_rn(lo, x0, acc[r]);
+                acc[r] = __fmaf_rn(hi, x1, acc[r]);
+            }
+        }
+        gc = gn;
+#pragma unroll
+        for (int r = 0; r < NB; r++) {
+            xc0[r] = xn0[r];
+            xc1[r] = xn1[r];
+        }
     }
-    const int c8 = d / 8;
-#pragma unroll 16
-    for (int t = 0; t < c8; t++)
 #pragma unroll
-        for (int r = 0; r < R; r++)
-            acc[r] = __fmaf_rn(bf16_to_f32(gr[r][8 * t]), xr[r][8 * t], acc[r]);
-#pragma unroll
-    for (int r = 0; r < R; r++) {
+    for (int r = 0; r < NB; r++) {
         float a = acc[r];
         a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
         a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
         a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        const int it = idx[r];
-        if (it < items && (it & 7) == 0) {
-            const int L = it >> 3, ee = L / B, tb = L % B;
-            lg_lead[tb * E + e0 + ee] = a;
-            lg_glob[(size_t)tb * E + e0 + ee] = a;
+        if (live && j == 0 && r < nb) {
+            lg_lead[r * E + e0 + ee] = a;
+            lg_glob[(size_t)(b0 + r) * E + e0 + ee] = a;
         }
     }
 }
 
+__host__ __device__ inline int dispatch_smem_bytes(int B, int k, int E) {
+    return B * k * 8 + dispatch_smem_ints(E, kClusterThreads / 32) * 4;
+}
+
 __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kClusterThreads)
     k_router_cluster(const uint16_t* __restrict__ gate_w, const float* __restrict__ x, int B, int E,
-                     int d, int k, int norm, jl_ws ws, int lg_off) {
+                     int d, int k, int norm, jl_ws ws, int tpc, int lg_off, int fuse_dispatch,
+                     int tiles) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bar[2];
+    __shared__ uint64_t bar;
+    __shared__ int is_last;
     const int tid = threadIdx.x;
     const int rank = (int)cluster.block_rank();
+    const int nclusters = gridDim.x / kClusterCTAs;
+    const int cl = blockIdx.x / kClusterCTAs;
+    const int b0 = cl * tpc, nb = min(tpc, B - b0);
     const int EPC = (E + kClusterCTAs - 1) / kClusterCTAs;
     const int e0 = rank * EPC, ne = max(0, min(EPC, E - e0));
-    const int grow = d * 2 + 16;  // padded router row: the 4 experts of a warp hit distinct banks
-    uint8_t* g_s = smem;
-    float* x_s = reinterpret_cast<float*>(smem + (size_t)EPC * grow);
-    float* lg_s = reinterpret_cast<float*>(smem + lg_off);  // [B, E] logits (leader CTA's are read)
+    const int gs = router_gstride(d), xs = router_xstride(d);
+    uint16_t* g_s = reinterpret_cast<uint16_t*>(smem);                         // [EPC * 8][gs]
+    float* x_s = reinterpret_cast<float*>(smem + (size_t)EPC * 8 * gs * 2);   // [tpc * 8][xs]
+    float* lg_s = reinterpret_cast<float*>(smem + lg_off);  // [tpc, E] logits (the leader's are read)
     long long* tr = (blockIdx.x == 0) ? ws.trace : nullptr;
     trace_point(tr, kTraceRouter, 0);
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+    if (tid == 0) {  // router rows do not depend on the previous kernel: fetch them first
+        mbar_init(&bar, 1);
         mbar_fence_init();
-        mbar_expect_tx(&bar[0], (uint32_t)(ne * d * 2));
-        for (int r = 0; r < ne; r++)
-            bulk_g2s(g_s + (size_t)r * grow, gate_w + (size_t)(e0 + r) * d, (uint32_t)(d * 2), &bar[0]);
-        if (ne == 0) mbar_arrive(&bar[0]);
+        if (ne > 0) {
+            const uint32_t bytes = (uint32_t)(ne * router_expert_halves(d) * 2);
+            mbar_expect_tx(&bar, bytes);
+            bulk_g2s(g_s, gate_w + (size_t)e0 * router_expert_halves(d), bytes, &bar);
+        } else {
+            mbar_arrive(&bar);
+        }
     }
     griddep_wait();  // x is the previous kernel's output
     griddep_launch_dependents();
     trace_point(tr, kTraceRouter, 1);
-    if (tid == 0) {
-        mbar_expect_tx(&bar[1], (uint32_t)(B * d * 4));
-        bulk_g2s(x_s, x, (uint32_t)(B * d * 4), &bar[1]);
+    // token rows, transposed into lane rows
+    for (int q = tid; q < nb * d / 4; q += kClusterThreads) {
+        const int tb = q / (d / 4), i = (q % (d / 4)) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(x + (size_t)(b0 + tb) * d + i);
+        float* row = x_s + (size_t)(tb * 8 + (i & 7)) * xs + (i >> 3);
+        row[0] = v.x;
+        row[xs] = v.y;
+        row[2 * xs] = v.z;
+        row[3 * xs] = v.w;
     }
     __syncthreads();
-    const bool ok = mbar_wait_bounded(&bar[0], 0, ws.err) & mbar_wait_bounded(&bar[1], 0, ws.err);
+    const bool ok = mbar_wait_bounded(&bar, 0, ws.err);
     trace_point(tr, kTraceRouter, 2);
     float* lg_lead = cluster.map_shared_rank(lg_s, 0);
     if (ok && ne > 0) {
-        const int items = ne * B * 8;
-        if (items <= kClusterThreads)
-            cluster_logits<1>(g_s, grow, x_s, d, B, E, e0, ne, lg_lead, ws.logits);
-        else if (items <= 2 * kClusterThreads)
-            cluster_logits<2>(g_s, grow, x_s, d, B, E, e0, ne, lg_lead, ws.logits);
-        else
-            cluster_logits<4>(g_s, grow, x_s, d, B, E, e0, ne, lg_lead, ws.logits);
+        if (tpc == 1) cluster_logits<1>(g_s, x_s, d, nb, E, e0, ne, b0, lg_lead, ws.logits);
+        else if (tpc == 2) cluster_logits<2>(g_s, x_s, d, nb, E, e0, ne, b0, lg_lead, ws.logits);
+        else if (tpc == 4) cluster_logits<4>(g_s, x_s, d, nb, E, e0, ne, b0, lg_lead, ws.logits);
+        else cluster_logits<8>(g_s, x_s, d, nb, E, e0, ne, b0, lg_lead, ws.logits);
     }
     trace_point(tr, kTraceRouter, 3);
     cluster.sync();
     if (rank != 0) return;
     trace_point(tr, kTraceRouter, 4);
-    // leader: staging no longer needed; scratch [8][kMaxE + 64] floats, then dispatch ints
-    float* scratch = reinterpret_cast<float*>(smem);
-    route_tokens_cta(lg_s, B, E, k, norm, ws, scratch);
+    // leader: the staging area is free; routing scratch, then dispatch scratch
+    route_tokens_cta(lg_s, nb, b0, E, k, norm, ws, smem);
     trace_point(tr, kTraceRouter, 5);
-    if (B == 1) {
-        dispatch_one(k, ws);
-    } else if (tid < 32) {
-        dispatch_warp_small(ws.top, ws.tw, B, k, E, ws,
-                            reinterpret_cast<int*>(scratch + kRouteTB * (kMaxE + 64)));
+    if (!fuse_dispatch) return;  // k_dispatch follows
+    if (nclusters > 1) {
+        if (tid == 0) {
+            __threadfence();
+            is_last = atomicAdd(ws.counter, 1) == nclusters - 1;
+        }
+        __syncthreads();
+        if (!is_last) return;
+        __threadfence();
+        if (tid == 0) *ws.counter = 0;
+        tr = ws.trace;  // the last leader stamps the dispatch
+    }
+    trace_point(tr, kTraceRouter, 6);
+    // every token's ids and weights, read through L2 (other clusters wrote them)
+    const int S = B * k;
+    int* top_s = reinterpret_cast<int*>(smem);
+    float* tw_s = reinterpret_cast<float*>(top_s + S);
+    int* dsm = reinterpret_cast<int*>(tw_s + S);
+    for (int i = tid; i < S; i += kClusterThreads) {
+        top_s[i] = __ldcg(ws.top + i);
+        tw_s[i] = __ldcg(ws.tw + i);
     }
     __syncthreads();
-    if (tid < 32) tc_build_tiles(ws);
-    trace_point(tr, kTraceRouter, 6);
+    trace_point(tr, kTraceRouter, 7);
+    if (B == 1) {
+        if (tid < k) {
+            ws.sel[tid] = top_s[tid];
+            ws.uh[tid] = tid;
+            ws.uidx[tid] = tid;
+            ws.uw[tid] = tw_s[tid];
+            ws.slot_pos[tid] = tid;
+            ws.comb[tid] = tid;
+        }
+        if (tid == 0) {
+            ws.uh[k] = k;
+            *ws.U = k;
+        }
+    } else if (S <= 128 && B <= 32) {
+        if (tid < 32) dispatch_warp_small(top_s, tw_s, B, k, E, ws, dsm);
+    } else {
+        dispatch_block(top_s, tw_s, B, k, E, ws, dsm);
+    }
+    trace_point(tr, kTraceRouter, 8);
+    if (tiles) {
+        __syncthreads();
+        if (tid < 32) tc_build_tiles(ws);
+        trace_point(tr, kTraceRouter, 9);
+    }
 }
 
 __global__ void k_topk(const float* __restrict__ logits, int B, int E, int k, int norm,
@@ -676,43 +765,34 @@ __global__ void k_dispatch(int B, int k, int E, jl_ws ws) {
 }  // namespace jl
 
 int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float* x, int B,
-                    cudaStream_t s) {
+                    bool tiles, cudaStream_t s) {
     using namespace jl;
     const int E = h->E, d = h->d, k = h->k;
     if (E > kMaxE || k > kMaxK || k < 1 || E < k) return JL_ERR_INVALID;
     static bool attr = false;
     if (!attr) {
-        JL_CUDA(cudaFuncSetAttribute(k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
         JL_CUDA(cudaFuncSetAttribute(k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
         JL_CUDA(cudaFuncSetAttribute(k_router_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
         attr = true;
     }
-    if (B <= kFuseTailMaxB) {
-        const int EPC = (E + kClusterCTAs - 1) / kClusterCTAs;
-        // [router rows | token rows] staging, reused by the leader's tail; logits after both
-        const size_t stage = (size_t)EPC * (d * 2 + 16) + (size_t)kRouteTB * d * 4;
-        const size_t tail = ((size_t)kRouteTB * (kMaxE + 64) + 4 * E + 2) * 4;
-        const size_t lg_off = (std::max(stage, tail) + 127) / 128 * 128;
-        const size_t smem = lg_off + (size_t)kRouteTB * E * 4;
-        if (smem > 220 * 1024) return JL_ERR_INVALID;
-        return launch(k_router_cluster, dim3(kClusterCTAs), dim3(kClusterThreads), smem, s, gate_w_l,
-                      x, B, E, d, k, h->norm, h->ws, (int)lg_off);
-    }
-    const int TB = kRouteTB;
-    const int threads = 32 * TB;
-    const size_t smem = (size_t)kRouteEPB * (d * 2 + 16) + (size_t)TB * d * 4;
+    if (d % 128) return JL_ERR_INVALID;
+    const int tpc = route_tpc(B);
+    const int ncl = (B + tpc - 1) / tpc;
+    const int EPC = (E + kClusterCTAs - 1) / kClusterCTAs;
+    const size_t stage = (size_t)EPC * 8 * router_gstride(d) * 2 + (size_t)tpc * 8 * router_xstride(d) * 4;
+    // the dispatch runs in the last leader when its scratch fits, else in k_dispatch
+    const size_t dsp = (size_t)dispatch_smem_bytes(B, k, E);
+    const int fuse = dsp <= 64 * 1024;
+    const size_t tail = std::max((size_t)kMaxTPC * route_scratch_bytes(E), fuse ? dsp : (size_t)0);
+    const size_t lg_off = (std::max(stage, tail) + 127) / 128 * 128;
+    const size_t smem = lg_off + (size_t)tpc * E * 4;
     if (smem > 220 * 1024) return JL_ERR_INVALID;
-    dim3 grid((E + kRouteEPB - 1) / kRouteEPB, (B + TB - 1) / TB);
-    int rc = launch(k_router, grid, dim3(threads), smem, s, gate_w_l, x, B, E, d, k, h->norm,
-                    h->ws, 0);
-    if (rc) return rc;
-    const int wpb = 8;
-    rc = launch(k_topk, dim3((B + wpb - 1) / wpb), dim3(32 * wpb), (size_t)wpb * kMaxE * 4, s,
-                (const float*)h->ws.logits, B, E, k, h->norm, h->ws);
-    if (rc) return rc;
+    int rc = launch(k_router_cluster, dim3(kClusterCTAs * ncl), dim3(kClusterThreads), smem, s, gate_w_l,
+                    x, B, E, d, k, h->norm, h->ws, tpc, (int)lg_off, fuse, tiles ? 1 : 0);
+    if (rc || fuse) return rc;
     const int T = 1024;
-    const size_t dsm = (size_t)dispatch_smem_ints(E, T / 32) * 4;
-    return launch(k_dispatch, dim3(1), dim3(T), dsm, s, B, k, E, h->ws);
+    return launch(k_dispatch, dim3(1), dim3(T), (size_t)dispatch_smem_ints(E, T / 32) * 4, s, B, k, E,
+                  h->ws);
 }
 
 // Routing only, into buffers the caller chooses: k_router (no fused tail)

@@ -77,6 +77,24 @@ __global__ void k_repack(const uint8_t* __restrict__ pk, const uint16_t* __restr
 }
 
 // ---------------------------------------------------------------------------
+// Router weights, lane-major: the reference's row e of gate_w [E, d] becomes
+// 8 runs dst[e][j][t] = src[e][j + 8t] (t < d/8), one per lane j of its 8-wide
+// accumulator (decode_kernel.c:234-256), each followed by 8 halves of zero
+// padding, so the router reads a lane's next 8 steps with one 16-byte load
+// and a CTA's experts with one bulk copy. Thread = one destination half.
+__global__ void k_repack_router(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int E,
+                                int d) {
+    const int c8 = d / 8, rh = router_row_halves(d);
+    const long long n = (long long)E * 8 * rh;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long row = i / rh;
+    const int t = (int)(i % rh), j = (int)(row % 8);
+    const long long e = row / 8;
+    dst[i] = t < c8 ? src[e * d + j + 8 * t] : (uint16_t)0;
+}
+
+// ---------------------------------------------------------------------------
 // Standalone exact Q4 GEMM over the reference layout: thread = one row, all
 // groups in order, up to 8 activation rows per pass staged in shared memory.
 // The per-row sum follows decode_kernel.c:770-858 exactly.
@@ -176,6 +194,15 @@ int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, 
     const long long threads = (long long)(R / jl::kTileRows) * (C / jl::kGroup) * 64;
     const int tpb = 256;
     jl::k_repack<<<(unsigned)((threads + tpb - 1) / tpb), tpb, 0, s>>>(pk_ref, sc_ref, p, L, rec);
+    JL_LAUNCH_CHECK();
+    return JL_OK;
+}
+
+int jl_launch_repack_router(const uint16_t* src, uint16_t* dst, int E, int d, cudaStream_t s) {
+    if (E < 1 || d < 8 || d % 8) return JL_ERR_INVALID;
+    const long long n = (long long)E * router_expert_halves(d);
+    const int tpb = 256;
+    jl::k_repack_router<<<(unsigned)((n + tpb - 1) / tpb), tpb, 0, s>>>(src, dst, E, d);
     JL_LAUNCH_CHECK();
     return JL_OK;
 }
