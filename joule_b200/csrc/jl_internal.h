@@ -69,6 +69,7 @@ constexpr int kTraceSlots = 4 * 16;
 
 struct jl_moe {
     int device;
+    int sm_count;  // streaming multiprocessors of the device (persistent grids)
     int L, d, E, k, m, norm;
     int max_tokens;
     int path;

@@ -78,7 +78,8 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
     jl_moe* h = new (std::nothrow) jl_moe();
     if (!h) return JL_ERR_OOM;
     memset(h, 0, sizeof(*h));
-    if (cudaGetDevice(&h->device) != cudaSuccess) {
+    if (cudaGetDevice(&h->device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, h->device) != cudaSuccess) {
         delete h;
         return JL_ERR_CUDA;
     }
@@ -286,7 +287,7 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
         return e == cudaSuccess ? JL_OK : JL_ERR_CUDA;
     };
     int rc = mark(0);
-    const bool tc_ok = h->d % 512 == 0 && h->m % 64 == 0;
+    const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
     const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
     if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, tc, s);
     if (!rc) rc = mark(1);

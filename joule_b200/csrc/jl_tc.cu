@@ -40,7 +40,6 @@ namespace jl {
 
 constexpr int kTcDqWarps = 4;        // dequant/epilogue warps = TMEM lanes 0..127
 constexpr int kTcQ4Stage = 4 * kTileRec;  // the 4 contiguous tile records of one K step
-constexpr int kTcBStage = 2 * kTcNT * 128;  // 8 K chunks x (hi + lo rows) x 16 B, 64 K values
 // position p of an 8-value K chunk holds element kPerm[p] = {0,4,1,5,2,6,3,7}[p]
 
 __host__ __device__ inline int tc_max_tiles(int S, int E) { return S / kTcNT + E + 1; }
@@ -99,13 +98,31 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// hi + lo accumulator columns of 16 tokens
-__device__ __forceinline__ void tc_ld_sum16(uint32_t taddr_hi, uint32_t taddr_lo, float (&v)[16]) {
-    float a[16], b[16];
-    tc_ld16(taddr_hi, a);
-    tc_ld16(taddr_lo, b);
+// 16 tokens' results from the two issuers' accumulators (each: hi columns
+// [0, N), lo columns [N, 2N)), added in a fixed order: (hi0 + hi1) + (lo0 +
+// lo1). The four loads are issued before one wait.
+__device__ __forceinline__ void tc_ld_acc16(uint32_t acc0, uint32_t acc1, int N, int t0, float (&v)[16]) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%64];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%65];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47}, [%66];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%67];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(acc0 + t0), "r"(acc1 + t0), "r"(acc0 + N + t0), "r"(acc1 + N + t0)
+        : "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = a[i] + b[i];
+    for (int i = 0; i < 16; i++)
+        v[i] = (__uint_as_float(r[i]) + __uint_as_float(r[16 + i])) +
+               (__uint_as_float(r[32 + i]) + __uint_as_float(r[48 + i]));
 }
 
 // UMMA shared-memory descriptor, K-major, no swizzle: core matrices of 8 rows
@@ -146,6 +163,14 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
 __device__ __forceinline__ bool tc_wait_warp(uint64_t* bar, uint32_t parity, int* err,
                                              volatile int* abort) {
     return __all_sync(0xffffffffu, tc_wait(bar, parity, err, abort));
+}
+
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\telect.sync r|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
 }
 
 // 64 Q4 values of one row (32 bytes) -> 32 words of fp16 pairs (n - 8) * s,
@@ -220,234 +245,323 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
 }
 
 // ---------------------------------------------------------------------------
-// The grouped GEMM CTA (shared by gate/up and down). Roles:
-//   warps 0-3  dequant (thread = A row = TMEM lane) and epilogue
-//   warp 4     Q4 producer: weight tiles + scales, 8-stage ring
-//   warp 5     activation producer: hi/lo K chunks, 4-stage ring
-//   warp 6     MMA issuer; TMEM allocation
-// The weight ring is released as soon as the dequant warps have the bytes in
-// registers, so the weight stream runs up to 8 chunks ahead of the MMAs; the
-// 4 TMEM A buffers let dequant run 4 chunks ahead.
+// Persistent grouped GEMM (gate/up and down). One CTA per SM walks the work
+// items blockIdx.x, blockIdx.x + gridDim.x, ... where an item is one token
+// tile x one block of 128 weight rows (gate/up: 64 gate + 64 up rows). Each
+// role walks the same item sequence, so the rings run on across items. Roles:
+//   warps 0-3   epilogue: thread = accumulator row = TMEM lane
+//   warps 4-7   dequant warpgroup 0 (even K steps of the CTA's stream)
+//   warps 8-11  dequant warpgroup 1 (odd K steps)
+//   warp 12     weight producer: 6 stages of 4 K steps (17,408 B, one bulk copy)
+//   warp 13     activation producer: 2 stages of 32 KB (one bulk copy each)
+//   warps 14-15 MMA issuers: issuer w takes the K steps of parity w into its
+//               own accumulator; the epilogue adds the two in a fixed order
+// TMEM (512 columns): 8 A buffers of 32 columns (one 64-value K step each),
+// then accumulators [issuer][buffer] of 2 x kTcNT columns; items alternate
+// buffers, so the epilogue of item i overlaps the main loop of item i + 1.
+// Two costs shape this: a bulk copy costs its issuing thread a few hundred
+// nanoseconds whatever its size (4 KB copies cap an SM near 20 GB/s; 16 KB
+// and larger reach its HBM share), and a tcgen05.mma costs its issuing
+// thread tens of cycles whatever N is (issued from a converged warp through
+// elect.sync: a lone diverged lane issues about half as fast), while the
+// tensor core takes several issuers' MMAs at once. Every dequant thread
+// consumes every weight stage (warpgroup w takes its K steps of parity w); A
+// buffer b always serves K steps of parity b % 2, i.e. one warpgroup and one
+// issuer.
+constexpr int kPQK = 4;    // K steps per weight stage: one 17,408-byte bulk copy
+constexpr int kPQ = 6;     // weight stages
+constexpr int kPBBytes = 32 * 1024;  // activation stage: 8 / (N/16) K steps of 2N rows
+constexpr int kPB = 2;     // activation stages
+constexpr int kPA = 8;     // TMEM A buffers (one K step each)
+constexpr int kPI = 2;     // MMA issuers
+constexpr int kPAccCols = 2 * kTcNT;  // accumulator columns (hi + lo rows of a tile)
+constexpr int kPWarps = 14 + kPI;
+constexpr int kPThreads = kPWarps * 32;
+constexpr int kPStage = kPQK * kTcQ4Stage;
+// TMEM column of accumulator (issuer w, buffer b): after the A buffers
+__host__ __device__ constexpr int p_acc_col(int w, int b) { return kPA * 32 + (2 * w + b) * kPAccCols; }
+static_assert(p_acc_col(kPI - 1, 1) + kPAccCols <= 512, "TMEM columns");
 
-constexpr int kTcQS = 8;   // weight stages
-constexpr int kTcBS = 4;   // activation stages
-constexpr int kTcAB = 4;   // TMEM A buffers (32 columns each)
-constexpr int kTcAcc = kTcAB * 32;  // accumulator column
-constexpr int kTcCols = 256;
-constexpr int kTcWarps = 7;
-
-struct TcSmem {
-    uint64_t q4_full[kTcQS], q4_empty[kTcQS];
-    uint64_t b_full[kTcBS], b_empty[kTcBS];
-    uint64_t a_full[kTcAB], a_empty[kTcAB];
-    uint64_t acc_full;
+struct PSmem {
+    uint64_t q4_full[kPQ], q4_empty[kPQ];
+    uint64_t b_full[kPB], b_empty[kPB];
+    uint64_t a_full[kPA], a_empty[kPA];
+    uint64_t acc_full[kPI][2], acc_empty[2];
     uint32_t tmem_base;
     int abort;
-    int info[4];  // expert, tokens, first uidx position, row offset
 };
+static_assert(sizeof(PSmem) <= 512, "barrier block");
+constexpr size_t kPQ4Off = 512;
+constexpr size_t kPBOff = kPQ4Off + (size_t)kPQ * kPStage;
+constexpr size_t kPScrOff = kPBOff + (size_t)kPB * kPBBytes;
+constexpr size_t kPScratch = 32 * 1024;  // gate/up epilogue: up rows fp32 [64][64] + act hi/lo [2][64][64]
+constexpr size_t kPSmemBytes = kPScrOff + kPScratch;
 
-constexpr size_t kTcSmemQ4Off = 512;
-constexpr size_t kTcSmemBOff = kTcSmemQ4Off + (size_t)kTcQS * kTcQ4Stage;
-constexpr size_t kTcSmemBytes = kTcSmemBOff + (size_t)kTcBS * kTcBStage;
+// K steps per activation stage for a tile of N (16 or 32) token rows: a
+// multiple of kPI, so every issuer has steps in every stage
+__device__ __forceinline__ int p_bsteps(int N) { return 8 / (N >> 4); }
 
-// is_down: A = down rows [mt*128, +128) of d (4 tiles of 32 rows), K = m,
-//          B = activations; epilogue y = w * acc.
-// else:    A = gate rows [mt*64, +64) then up rows [mt*64, +64), K = d,
-//          B = tokens; epilogue act = silu(g) * u.
+struct PItem {
+    int e, n, N, pos0, row0, mt;
+};
+__device__ __forceinline__ PItem p_item(const int* tc_tile, int item, int MT) {
+    const int ti = item / MT;
+    const int4 t = *reinterpret_cast<const int4*>(tc_tile + ti * 4);
+    PItem it;
+    it.mt = item - ti * MT;
+    it.e = t.x;
+    it.n = t.y;
+    it.N = (t.y + 15) & ~15;
+    it.pos0 = t.z;
+    it.row0 = t.w;
+    return it;
+}
+
 template <bool is_down>
-__global__ void __launch_bounds__(kTcWarps * 32, 1)
+__global__ void __launch_bounds__(kPThreads, 1)
     k_expert_tc(const uint8_t* __restrict__ store_l, jl_layout L, jl_ws ws) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    TcSmem& sh = *reinterpret_cast<TcSmem*>(smem);
-    uint8_t* q4_ring = smem + kTcSmemQ4Off;
-    uint8_t* b_ring = smem + kTcSmemBOff;
+    PSmem& sh = *reinterpret_cast<PSmem*>(smem);
+    uint8_t* q4_ring = smem + kPQ4Off;
+    uint8_t* b_ring = smem + kPBOff;
+    uint8_t* scr = smem + kPScrOff;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = L.d, m = L.m;
     const int MT = is_down ? d / 128 : m / 64;
-    const int ti = blockIdx.x / MT, mt = blockIdx.x % MT;
-    const int K = is_down ? m : d;
-    const int nchunks = K / kGroup;
+    const int nk = (is_down ? m : d) / kGroup;  // K steps per item
     long long* tr = (blockIdx.x == 0) ? ws.trace : nullptr;
     const int tk = is_down ? kTraceDown : kTraceGateup;
     trace_point(tr, tk, 0);
     griddep_wait();
     griddep_launch_dependents();
-    if (ti >= *ws.tc_ntiles) return;
+    const int n_items = *ws.tc_ntiles * MT;
+    if ((int)blockIdx.x >= n_items) return;
+    const int my_items = (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int my_steps = my_items * nk;
     trace_point(tr, tk, 1);
     if (threadIdx.x == 0) {
-        sh.info[0] = ws.tc_tile[ti * 4 + 0];
-        sh.info[1] = ws.tc_tile[ti * 4 + 1];
-        sh.info[2] = ws.tc_tile[ti * 4 + 2];
-        sh.info[3] = ws.tc_tile[ti * 4 + 3];
         sh.abort = 0;
-        for (int s = 0; s < kTcQS; s++) {
+        for (int s = 0; s < kPQ; s++) {
             mbar_init(&sh.q4_full[s], 1);
-            mbar_init(&sh.q4_empty[s], kTcDqWarps * 32);
+            mbar_init(&sh.q4_empty[s], 256);  // both dequant warpgroups
         }
-        for (int s = 0; s < kTcBS; s++) {
+        for (int s = 0; s < kPB; s++) {
             mbar_init(&sh.b_full[s], 1);
-            mbar_init(&sh.b_empty[s], 1);
+            mbar_init(&sh.b_empty[s], kPI);  // every issuer releases a stage
         }
-        for (int b = 0; b < kTcAB; b++) {
-            mbar_init(&sh.a_full[b], kTcDqWarps * 32);
+        for (int b = 0; b < kPA; b++) {
+            mbar_init(&sh.a_full[b], 128);
             mbar_init(&sh.a_empty[b], 1);
         }
-        mbar_init(&sh.acc_full, 1);
+        for (int b = 0; b < 2; b++) {
+            for (int w = 0; w < kPI; w++) mbar_init(&sh.acc_full[w][b], 1);
+            mbar_init(&sh.acc_empty[b], 128);
+        }
         mbar_fence_init();
     }
-    if (warp == 6) {  // TMEM allocation by one full warp
+    if (warp == 14) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&sh.tmem_base)),
-                     "r"(kTcCols));
+                     "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sh.tmem_base;
-    const int e = sh.info[0], n = sh.info[1], N = (n + 15) & ~15, pos0 = sh.info[2], row0 = sh.info[3];
-    const uint8_t* rec = store_l + (size_t)e * L.rec_bytes;
-    const uint32_t b_stage = (uint32_t)N * 256;  // 8 K-chunks x 2N rows (hi, lo) x 16 B
 
-    if (warp == 4) {
-        // ---------------- weight producer
+    if (warp == 12) {
+        // ---------------- weight producer: stage G = K steps [4G, 4G + 4) of the stream
         if (lane == 0) {
-            int issued = 0;
-            for (int c = 0; c < nchunks; c++) {
-                const int s = c % kTcQS;
-                if (c >= kTcQS && !tc_wait(&sh.q4_empty[s], ((c / kTcQS) - 1) & 1, ws.err, &sh.abort))
-                    break;
-                uint8_t* q = q4_ring + (size_t)s * kTcQ4Stage;
-                mbar_expect_tx(&sh.q4_full[s], kTcQ4Stage);
-                // gate/up: [gate 2mt][gate 2mt+1][up 2mt][up 2mt+1]; down: rb 4mt..4mt+3
-                const size_t off = is_down ? L.tile_off(2, mt * 4, c) : L.tile_off(0, mt * 2, c);
-                bulk_g2s(q, rec + off, kTcQ4Stage, &sh.q4_full[s]);
-                issued = c + 1;
+            const int nq = nk / kPQK;
+            int G = 0;
+            bool ok = true;
+            for (int i = 0; ok && i < my_items; i++) {
+                const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+                const uint8_t* rec = store_l + (size_t)it.e * L.rec_bytes;
+                for (int j = 0; j < nq; j++, G++) {
+                    const int s = G % kPQ;
+                    if (G >= kPQ && !tc_wait(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort)) {
+                        ok = false;
+                        break;
+                    }
+                    // the records of consecutive K steps of one row block are contiguous
+                    const size_t off = is_down ? L.tile_off(2, it.mt * 4, j * kPQK) : L.tile_off(0, it.mt * 2, j * kPQK);
+                    mbar_expect_tx(&sh.q4_full[s], kPStage);
+                    bulk_g2s(q4_ring + (size_t)s * kPStage, rec + off, kPStage, &sh.q4_full[s]);
+                }
             }
-            for (int c = std::max(0, issued - kTcQS); c < issued; c++)  // no copies left in flight
-                mbar_wait_bounded(&sh.q4_full[c % kTcQS], (c / kTcQS) & 1, ws.err);
+            for (int c = max(0, G - kPQ); c < G; c++)  // no copies left in flight
+                mbar_wait_bounded(&sh.q4_full[c % kPQ], (c / kPQ) & 1, ws.err);
         }
-    } else if (warp == 5) {
-        // ---------------- activation producer
+    } else if (warp == 13) {
+        // ---------------- activation producer: stage = kb K steps of one item's tile
         if (lane == 0) {
-            const __half* bsrc = is_down ? ws.ac + (size_t)2 * row0 * m : ws.xc + (size_t)2 * row0 * d;
-            int issued = 0;
-            for (int c = 0; c < nchunks; c++) {
-                const int s = c % kTcBS;
-                if (c >= kTcBS && !tc_wait(&sh.b_empty[s], ((c / kTcBS) - 1) & 1, ws.err, &sh.abort))
-                    break;
-                uint8_t* bb = b_ring + (size_t)s * kTcBStage;
-                mbar_expect_tx(&sh.b_full[s], b_stage);
-                bulk_g2s(bb, bsrc + (size_t)c * 8 * 2 * N * 8, b_stage, &sh.b_full[s]);
-                issued = c + 1;
+            int G = 0;
+            bool ok = true;
+            for (int i = 0; ok && i < my_items; i++) {
+                const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+                const __half* bsrc = is_down ? ws.ac + (size_t)2 * it.row0 * m : ws.xc + (size_t)2 * it.row0 * d;
+                const int kb = p_bsteps(it.N);
+                for (int c0 = 0; c0 < nk; c0 += kb, G++) {
+                    const int s = G % kPB;
+                    if (G >= kPB && !tc_wait(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort)) {
+                        ok = false;
+                        break;
+                    }
+                    // K step c: 8 chunks x 2N rows (hi, lo) x 16 B = N * 256 bytes
+                    const uint32_t bytes = (uint32_t)(min(kb, nk - c0) * it.N * 256);
+                    mbar_expect_tx(&sh.b_full[s], bytes);
+                    bulk_g2s(b_ring + (size_t)s * kPBBytes, bsrc + (size_t)c0 * 16 * it.N * 8, bytes, &sh.b_full[s]);
+                }
             }
-            for (int c = std::max(0, issued - kTcBS); c < issued; c++)
-                mbar_wait_bounded(&sh.b_full[c % kTcBS], (c / kTcBS) & 1, ws.err);
+            for (int c = max(0, G - kPB); c < G; c++)
+                mbar_wait_bounded(&sh.b_full[c % kPB], (c / kPB) & 1, ws.err);
         }
-    } else if (warp == 6) {
-        // ---------------- MMA issuer: per K step one MMA over 2N columns
-        // (hi rows -> accumulator columns [0, N), lo rows -> [N, 2N))
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16(2 * N);
-            const uint64_t desc0 = umma_desc(b_ring, (uint32_t)N * 32, 128);
-            const uint64_t kstep = (uint64_t)((2 * N * 32) >> 4);      // 2 K chunks of 2N rows
-            const uint64_t sstep = (uint64_t)(kTcBStage >> 4);
-            for (int c = 0; c < nchunks; c++) {
-                const int ab = c % kTcAB, sb = c % kTcBS;
-                if (!tc_wait(&sh.a_full[ab], (c / kTcAB) & 1, ws.err, &sh.abort)) break;
-                if (!tc_wait(&sh.b_full[sb], (c / kTcBS) & 1, ws.err, &sh.abort)) break;
+    } else if (warp >= 14) {
+        // ---------------- MMA issuers (whole warps; one elected lane issues):
+        // issuer w runs the K steps of parity w of every item, 4 MMAs (K = 16
+        // each) of N = 2 x tokens (hi rows -> accumulator columns [0, N), lo
+        // rows -> [N, 2N)) into accumulator (w, i % 2)
+        const int w = warp - 14;
+        int G = 0;  // activation stages before the current item
+        bool ok = true;
+        for (int i = 0; ok && i < my_items; i++) {
+            const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+            const int ib = i & 1;
+            if (i >= 2 && !tc_wait_warp(&sh.acc_empty[ib], ((i >> 1) - 1) & 1, ws.err, &sh.abort)) break;
+            tc_fence_after();
+            const int kb = p_bsteps(it.N);
+            const uint32_t idesc = umma_idesc_f16(2 * it.N);
+            const uint64_t desc0 = umma_desc(b_ring, (uint32_t)it.N * 32, 128);
+            const uint64_t kstep = (uint64_t)((2 * it.N * 32) >> 4);   // 16 K values of 2N rows
+            const uint64_t cstep = (uint64_t)((it.N * 256) >> 4);      // one K step
+            const uint32_t dacc = tmem + p_acc_col(w, ib);
+            for (int c = w; c < nk; c += kPI) {
+                const int g = i * nk + c, ab = g % kPA, cb = c % kb, Gs = G + c / kb, sb = Gs % kPB;
+                const int ns = min(kb, nk - (c - cb));  // K steps in this stage (a multiple of kPI)
+                if (cb == w && !tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort)) {
+                    ok = false;
+                    break;
+                }
+                if (!tc_wait_warp(&sh.a_full[ab], (g / kPA) & 1, ws.err, &sh.abort)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const uint64_t dsb = desc0 + sb * sstep;
+                const uint64_t dsb = desc0 + (uint64_t)sb * (kPBBytes >> 4) + (uint64_t)cb * cstep;
+                if (elect_one()) {
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++)
-                    tc_mma_ts(tmem + kTcAcc, tmem + ab * 32 + ks * 8, dsb + ks * kstep, idesc,
-                              (c | ks) ? 1u : 0u);
-                tc_commit(&sh.a_empty[ab]);
-                tc_commit(&sh.b_empty[sb]);
+                    for (int ks = 0; ks < 4; ks++)
+                        tc_mma_ts(dacc, tmem + ab * 32 + ks * 8, dsb + ks * kstep, idesc,
+                                  (c >= kPI || ks) ? 1u : 0u);
+                    tc_commit(&sh.a_empty[ab]);
+                    if (cb >= ns - kPI) tc_commit(&sh.b_empty[sb]);  // this issuer's last step of the stage
+                }
+                __syncwarp();
             }
-            tc_commit(&sh.acc_full);
+            G += (nk + kb - 1) / kb;
+            if (ok) {
+                if (elect_one()) tc_commit(&sh.acc_full[w][ib]);
+                __syncwarp();
+            }
         }
-    } else {
-        // ---------------- dequant warps: thread = A row (TMEM lane)
-        const int row = warp * 32 + lane;
-        for (int c = 0; c < nchunks; c++) {
-            const int s = c % kTcQS, ab = c % kTcAB;
-            if (!tc_wait_warp(&sh.q4_full[s], (c / kTcQS) & 1, ws.err, &sh.abort)) break;
-            if (c < 8) trace_point(tr, tk, 2 + c);
-            const uint8_t* q = q4_ring + (size_t)s * kTcQ4Stage + warp * kTileRec;
-            const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
-            const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
-            const uint16_t sb = reinterpret_cast<const uint16_t*>(q + kTileBytes)[lane];
-            // the stage's bytes are in registers; the next bulk copy into it is an
-            // async-proxy write, ordered after these plain loads by the proxy fence
+    } else if (warp >= 4) {
+        // ---------------- dequant warpgroups: thread = A row (TMEM lane)
+        const int wg = (warp - 4) >> 2, wl = warp & 3;
+        const int n_stages = my_steps / kPQK;
+        bool ok = true;
+        for (int G = 0; ok && G < n_stages; G++) {
+            const int s = G % kPQ;
+            if (!tc_wait_warp(&sh.q4_full[s], (G / kPQ) & 1, ws.err, &sh.abort)) break;
+            if (G < 8 && wg == 0) trace_point(tr, tk, 2 + G);
+            for (int ls = wg; ls < kPQK; ls += 2) {
+                const int g = G * kPQK + ls, ab = g % kPA;
+                const uint8_t* q = q4_ring + (size_t)s * kPStage + ls * kTcQ4Stage + wl * kTileRec;
+                const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
+                const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
+                const uint16_t sc = reinterpret_cast<const uint16_t*>(q + kTileBytes)[lane];
+                uint32_t a[32];
+                dequant_row_f16(q0, q1, __ushort_as_half(sc), a);
+                if (g >= kPA && !tc_wait_warp(&sh.a_empty[ab], ((g / kPA) - 1) & 1, ws.err, &sh.abort)) {
+                    ok = false;
+                    break;
+                }
+                // order this TMEM write after the MMAs that read the buffer (released by a_empty)
+                tc_fence_after();
+                tc_st32(tmem + ((uint32_t)(wl * 32) << 16) + ab * 32, a);
+                tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(&sh.a_full[ab]);
+            }
+            // this thread's reads of the stage are done; the next bulk copy into it is
+            // an async-proxy write, ordered after these plain loads by the proxy fence
             fence_proxy_async_smem();
             mbar_arrive(&sh.q4_empty[s]);
-            uint32_t a[32];
-            dequant_row_f16(q0, q1, __ushort_as_half(sb), a);
-            if (c >= kTcAB && !tc_wait_warp(&sh.a_empty[ab], ((c / kTcAB) - 1) & 1, ws.err, &sh.abort))
-                break;
-            // order this TMEM write after the MMAs that read the buffer (released by a_empty)
-            tc_fence_after();
-            tc_st32(tmem + ((uint32_t)(warp * 32) << 16) + ab * 32, a);
-            tc_wait_st();
-            tc_fence_before();
-            mbar_arrive(&sh.a_full[ab]);
         }
-        // ---------------- epilogue
-        trace_point(tr, tk, 10);
-        const bool ok = tc_wait_warp(&sh.acc_full, 0, ws.err, &sh.abort);
-        tc_fence_after();
-        trace_point(tr, tk, 11);
-        // the activation ring is idle once acc_full completed (every bulk copy into it
-        // landed and every MMA read of it finished); reuse it as epilogue scratch
-        fence_proxy_async_smem();
-        float* scr = reinterpret_cast<float*>(b_ring);
-        if (ok) {
-            const uint32_t tacc = tmem + ((uint32_t)(warp * 32) << 16) + kTcAcc;
+    } else {
+        // ---------------- epilogue warps 0-3: thread = accumulator row
+        const int row = warp * 32 + lane;
+        float* up_s = reinterpret_cast<float*>(scr);                                 // [64 rows][kTcNT]
+        __half* act_s = reinterpret_cast<__half*>(scr + 64 * kTcNT * sizeof(float));  // [2][kTcNT][64]
+        for (int i = 0; i < my_items; i++) {
+            const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+            const int ib = i & 1;
+            bool got = true;
+            for (int w = 0; got && w < kPI; w++)
+                got = tc_wait_warp(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort);
+            if (!got) break;
+            tc_fence_after();
+            if (i == 0) trace_point(tr, tk, 10);
+            const uint32_t lanes = (uint32_t)(warp * 32) << 16;
+            const uint32_t acc0 = tmem + lanes + p_acc_col(0, ib), acc1 = tmem + lanes + p_acc_col(1, ib);
+            const int N = it.N, n = it.n;
             if (is_down) {
                 for (int t0 = 0; t0 < N; t0 += 16) {
                     float v[16];
-                    tc_ld_sum16(tacc + t0, tacc + N + t0, v);
-                    for (int i = 0; i < 16 && t0 + i < n; i++) {
-                        const int pos = pos0 + t0 + i;
-                        const int slot = ws.uidx[pos];
-                        ws.y[(size_t)slot * d + mt * 128 + row] = ws.uw[pos] * v[i];
+                    tc_ld_acc16(acc0, acc1, N, t0, v);
+                    for (int j = 0; j < 16 && t0 + j < n; j++) {
+                        const int pos = it.pos0 + t0 + j;
+                        ws.y[(size_t)ws.uidx[pos] * d + it.mt * 128 + row] = ws.uw[pos] * v[j];
                     }
                 }
+                tc_fence_before();
+                mbar_arrive(&sh.acc_empty[ib]);
             } else {
                 // up rows (warps 2,3) -> smem; gate rows (warps 0,1) apply SwiGLU
-                float* up_s = scr;                                            // [64 rows][kTcNT]
-                __half* act_s = reinterpret_cast<__half*>(scr + 64 * kTcNT);  // [2][kTcNT][64]
                 if (warp >= 2)
                     for (int t0 = 0; t0 < N; t0 += 16) {
                         float v[16];
-                        tc_ld_sum16(tacc + t0, tacc + N + t0, v);
+                        tc_ld_acc16(acc0, acc1, N, t0, v);
 #pragma unroll
-                        for (int i = 0; i < 16; i++) up_s[(row - 64) * kTcNT + t0 + i] = v[i];
+                        for (int j = 0; j < 16; j++) up_s[(row - 64) * kTcNT + t0 + j] = v[j];
                     }
-                asm volatile("bar.sync 1, %0;" ::"r"(kTcDqWarps * 32) : "memory");
+                asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (warp < 2) {
-                    const int j = row & 7, kc = row >> 3;
-                    const int pp = j < 4 ? 2 * j : 2 * (j - 4) + 1;  // position of element j (kPerm inverse)
+                    const int j8 = row & 7, kc = row >> 3;
+                    const int pp = j8 < 4 ? 2 * j8 : 2 * (j8 - 4) + 1;  // position of element j8 (kPerm inverse)
                     for (int t0 = 0; t0 < N; t0 += 16) {
                         float v[16];
-                        tc_ld_sum16(tacc + t0, tacc + N + t0, v);
+                        tc_ld_acc16(acc0, acc1, N, t0, v);
 #pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            const float a = silu_mul(v[i], up_s[row * kTcNT + t0 + i]);
+                        for (int j = 0; j < 16; j++) {
+                            const float a = silu_mul(v[j], up_s[row * kTcNT + t0 + j]);
                             const __half h = __float2half_rn(a);
                             const __half l = __float2half_rn(a - __half2float(h));
-                            act_s[(t0 + i) * 64 + kc * 8 + pp] = h;
-                            act_s[kTcNT * 64 + (t0 + i) * 64 + kc * 8 + pp] = l;
+                            act_s[(t0 + j) * 64 + kc * 8 + pp] = h;
+                            act_s[kTcNT * 64 + (t0 + j) * 64 + kc * 8 + pp] = l;
                         }
                     }
                 }
-                asm volatile("bar.sync 1, %0;" ::"r"(kTcDqWarps * 32) : "memory");
+                // every TMEM read of the accumulators is done: hand them back to the MMA
+                tc_fence_before();
+                mbar_arrive(&sh.acc_empty[ib]);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
                 // copy out: chunk (t, kc) of 8 halves -> ac tile layout [kc][2N][8]
-                __half* abase = ws.ac + (size_t)2 * row0 * m;
-                for (int i = row; i < N * 8; i += kTcDqWarps * 32) {
-                    const int t = i % N, kcl = i / N;
-                    __half* blk = abase + (size_t)(mt * 8 + kcl) * 2 * N * 8;
+                __half* abase = ws.ac + (size_t)2 * it.row0 * m;
+                for (int q = row; q < N * 8; q += 128) {
+                    const int t = q % N, kcl = q / N;
+                    __half* blk = abase + (size_t)(it.mt * 8 + kcl) * 2 * N * 8;
                     uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
                     if (t < n) {
                         vh = *reinterpret_cast<const uint4*>(act_s + t * 64 + kcl * 8);
@@ -458,13 +572,14 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
                 }
             }
         }
+        trace_point(tr, tk, 11);
     }
     trace_point(tr, tk, 12);
     tc_fence_before();
     __syncthreads();
-    if (warp == 6) {
+    if (warp == 14) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
 }
 
@@ -487,18 +602,19 @@ int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x
     static bool attr = false;
     if (!attr) {
         JL_CUDA(cudaFuncSetAttribute(k_expert_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kTcSmemBytes));
+                                     (int)kPSmemBytes));
         JL_CUDA(cudaFuncSetAttribute(k_expert_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kTcSmemBytes));
+                                     (int)kPSmemBytes));
         attr = true;
     }
-    if (h->d % 512 || h->m % 64 || h->d % 128 || !h->ws.xc) return JL_ERR_INVALID;
+    if (h->d % 512 || h->m % 256 || !h->ws.xc) return JL_ERR_INVALID;
     const int tiles = tc_max_tiles(B * h->k, h->E);
     int rc = launch(k_tc_permute, dim3(tiles, h->d / 512), dim3(256), 0, s, x, h->d, h->k, h->ws);
     if (rc) return rc;
-    rc = launch(k_expert_tc<false>, dim3(tiles * (h->m / 64)), dim3(kTcWarps * 32), kTcSmemBytes, s,
+    const int gu_items = tiles * (h->m / 64), dn_items = tiles * (h->d / 128);
+    rc = launch(k_expert_tc<false>, dim3(std::min(h->sm_count, gu_items)), dim3(kPThreads), kPSmemBytes, s,
                 store_l, h->lay, h->ws);
     if (rc) return rc;
-    return launch(k_expert_tc<true>, dim3(tiles * (h->d / 128)), dim3(kTcWarps * 32), kTcSmemBytes, s,
-                  store_l, h->lay, h->ws);
+    return launch(k_expert_tc<true>, dim3(std::min(h->sm_count, dn_items)), dim3(kPThreads), kPSmemBytes,
+                  s, store_l, h->lay, h->ws);
 }

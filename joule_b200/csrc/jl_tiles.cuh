@@ -7,7 +7,7 @@
 
 namespace jl {
 
-constexpr int kTcNT = 64;  // max tokens per tile (MMA N <= 64)
+constexpr int kTcNT = 32;  // max tokens per tile: the MMA's N = 2 x tokens <= 64 TMEM columns
 
 // rows of an expert with n tokens in the padded tile space: full 64-token
 // tiles plus the last tile rounded up to a multiple of 16
