@@ -157,6 +157,27 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
     }
 }
 
+// Bounded wait for roles off the critical path (the epilogue waits a whole
+// item for its accumulators): polls are spaced by a short sleep so the
+// waiting warp leaves the issue slots to the dequant warps.
+__device__ __forceinline__ bool tc_wait_relaxed(uint64_t* bar, uint32_t parity, int* err,
+                                                volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (int i = 1;; i++) {
+        __nanosleep(128);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                atomicOr(err, kErrTimeout);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // Warp-wide form for the warps that go on to tcgen05.ld / tcgen05.st: those
 // are .sync.aligned, so every lane must leave the spin together and agree on
 // the outcome (each lane polls on its own and may exit at another iteration).
@@ -250,13 +271,13 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
 // tile x one block of 128 weight rows (gate/up: 64 gate + 64 up rows). Each
 // role walks the same item sequence, so the rings run on across items. Roles:
 //   warps 0-3   epilogue: thread = accumulator row = TMEM lane
-//   warps 4-7   dequant warpgroup 0 (even K steps of the CTA's stream)
-//   warps 8-11  dequant warpgroup 1 (odd K steps)
+//   warps 4-7   dequant warpgroup 0 (K steps 0, 1 of every weight stage)
+//   warps 8-11  dequant warpgroup 1 (K steps 2, 3)
 //   warp 12     weight producer: 6 stages of 4 K steps (17,408 B, one bulk copy)
 //   warp 13     activation producer: 2 stages of 32 KB (one bulk copy each)
-//   warps 14-15 MMA issuers: issuer w takes the K steps of parity w into its
-//               own accumulator; the epilogue adds the two in a fixed order
-// TMEM (512 columns): 8 A buffers of 32 columns (one 64-value K step each),
+//   warps 14-15 MMA issuers: issuer w takes the K-step pairs of parity w into
+//               its own accumulator; the epilogue adds the two in a fixed order
+// TMEM (512 columns): 4 A buffers of 64 columns (one pair of 64-value K steps),
 // then accumulators [issuer][buffer] of 2 x kTcNT columns; items alternate
 // buffers, so the epilogue of item i overlaps the main loop of item i + 1.
 // Two costs shape this: a bulk copy costs its issuing thread a few hundred
@@ -264,22 +285,22 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
 // and larger reach its HBM share), and a tcgen05.mma costs its issuing
 // thread tens of cycles whatever N is (issued from a converged warp through
 // elect.sync: a lone diverged lane issues about half as fast), while the
-// tensor core takes several issuers' MMAs at once. Every dequant thread
-// consumes every weight stage (warpgroup w takes its K steps of parity w); A
-// buffer b always serves K steps of parity b % 2, i.e. one warpgroup and one
-// issuer.
+// tensor core takes several issuers' MMAs at once. The hand-off from the
+// dequant warps (TMEM store, wait, fence, arrive) costs a few hundred cycles,
+// so it runs once per pair of K steps. A buffer b always serves pairs of
+// parity b % 2, i.e. one warpgroup and one issuer.
 constexpr int kPQK = 4;    // K steps per weight stage: one 17,408-byte bulk copy
 constexpr int kPQ = 6;     // weight stages
 constexpr int kPBBytes = 32 * 1024;  // activation stage: 8 / (N/16) K steps of 2N rows
 constexpr int kPB = 2;     // activation stages
-constexpr int kPA = 8;     // TMEM A buffers (one K step each)
+constexpr int kPA = 4;     // TMEM A buffers (one K-step pair, 64 columns, each)
 constexpr int kPI = 2;     // MMA issuers
 constexpr int kPAccCols = 2 * kTcNT;  // accumulator columns (hi + lo rows of a tile)
 constexpr int kPWarps = 14 + kPI;
 constexpr int kPThreads = kPWarps * 32;
 constexpr int kPStage = kPQK * kTcQ4Stage;
 // TMEM column of accumulator (issuer w, buffer b): after the A buffers
-__host__ __device__ constexpr int p_acc_col(int w, int b) { return kPA * 32 + (2 * w + b) * kPAccCols; }
+__host__ __device__ constexpr int p_acc_col(int w, int b) { return kPA * 64 + (2 * w + b) * kPAccCols; }
 static_assert(p_acc_col(kPI - 1, 1) + kPAccCols <= 512, "TMEM columns");
 
 struct PSmem {
@@ -381,7 +402,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const uint8_t* rec = store_l + (size_t)it.e * L.rec_bytes;
                 for (int j = 0; j < nq; j++, G++) {
                     const int s = G % kPQ;
-                    if (G >= kPQ && !tc_wait(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort)) {
+                    if (G >= kPQ && !tc_wait_relaxed(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort)) {
                         ok = false;
                         break;
                     }
@@ -405,7 +426,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const int kb = p_bsteps(it.N);
                 for (int c0 = 0; c0 < nk; c0 += kb, G++) {
                     const int s = G % kPB;
-                    if (G >= kPB && !tc_wait(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort)) {
+                    if (G >= kPB && !tc_wait_relaxed(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort)) {
                         ok = false;
                         break;
                     }
@@ -420,10 +441,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else if (warp >= 14) {
         // ---------------- MMA issuers (whole warps; one elected lane issues):
-        // issuer w runs the K steps of parity w of every item, 4 MMAs (K = 16
+        // issuer w runs the K-step pairs of parity w of every item, 8 MMAs (K = 16
         // each) of N = 2 x tokens (hi rows -> accumulator columns [0, N), lo
         // rows -> [N, 2N)) into accumulator (w, i % 2)
         const int w = warp - 14;
+        const int np = nk / 2;  // pairs per item (even: nk % 4 == 0)
         int G = 0;  // activation stages before the current item
         bool ok = true;
         for (int i = 0; ok && i < my_items; i++) {
@@ -431,20 +453,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const int ib = i & 1;
             if (i >= 2 && !tc_wait_warp(&sh.acc_empty[ib], ((i >> 1) - 1) & 1, ws.err, &sh.abort)) break;
             tc_fence_after();
-            const int kb = p_bsteps(it.N);
+            const int kb = p_bsteps(it.N);  // K steps per activation stage: 4 or 8
             const uint32_t idesc = umma_idesc_f16(2 * it.N);
             const uint64_t desc0 = umma_desc(b_ring, (uint32_t)it.N * 32, 128);
             const uint64_t kstep = (uint64_t)((2 * it.N * 32) >> 4);   // 16 K values of 2N rows
             const uint64_t cstep = (uint64_t)((it.N * 256) >> 4);      // one K step
             const uint32_t dacc = tmem + p_acc_col(w, ib);
-            for (int c = w; c < nk; c += kPI) {
-                const int g = i * nk + c, ab = g % kPA, cb = c % kb, Gs = G + c / kb, sb = Gs % kPB;
-                const int ns = min(kb, nk - (c - cb));  // K steps in this stage (a multiple of kPI)
-                if (cb == w && !tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort)) {
+            for (int pl = w; pl < np; pl += kPI) {
+                const int P = i * np + pl, ab = P % kPA;
+                const int c = 2 * pl, cb = c % kb, Gs = G + c / kb, sb = Gs % kPB;
+                const int ns = min(kb, nk - (c - cb));  // K steps in this stage (a multiple of 4)
+                if (cb == 2 * w && !tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort)) {
                     ok = false;
                     break;
                 }
-                if (!tc_wait_warp(&sh.a_full[ab], (g / kPA) & 1, ws.err, &sh.abort)) {
+                if (!tc_wait_warp(&sh.a_full[ab], (P / kPA) & 1, ws.err, &sh.abort)) {
                     ok = false;
                     break;
                 }
@@ -452,11 +475,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const uint64_t dsb = desc0 + (uint64_t)sb * (kPBBytes >> 4) + (uint64_t)cb * cstep;
                 if (elect_one()) {
 #pragma unroll
-                    for (int ks = 0; ks < 4; ks++)
-                        tc_mma_ts(dacc, tmem + ab * 32 + ks * 8, dsb + ks * kstep, idesc,
-                                  (c >= kPI || ks) ? 1u : 0u);
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int ks = 0; ks < 4; ks++)
+                            tc_mma_ts(dacc, tmem + ab * 64 + h * 32 + ks * 8, dsb + h * cstep + ks * kstep, idesc,
+                                      (pl >= kPI || h || ks) ? 1u : 0u);
                     tc_commit(&sh.a_empty[ab]);
-                    if (cb >= ns - kPI) tc_commit(&sh.b_empty[sb]);  // this issuer's last step of the stage
+                    if (cb >= ns - 4) tc_commit(&sh.b_empty[sb]);  // this issuer's last pair of the stage
                 }
                 __syncwarp();
             }
@@ -467,49 +492,49 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
         }
     } else if (warp >= 4) {
-        // ---------------- dequant warpgroups: thread = A row (TMEM lane)
+        // ---------------- dequant warpgroups: thread = A row (TMEM lane). Stage G
+        // holds K steps 4G .. 4G+3 = pairs 2G (warpgroup 0) and 2G + 1 (warpgroup 1).
         const int wg = (warp - 4) >> 2, wl = warp & 3;
         const int n_stages = my_steps / kPQK;
-        bool ok = true;
-        for (int G = 0; ok && G < n_stages; G++) {
-            const int s = G % kPQ;
+        for (int G = 0; G < n_stages; G++) {
+            const int s = G % kPQ, P = 2 * G + wg, ab = P % kPA;
             if (!tc_wait_warp(&sh.q4_full[s], (G / kPQ) & 1, ws.err, &sh.abort)) break;
             if (G < 8 && wg == 0) trace_point(tr, tk, 2 + G);
-            for (int ls = wg; ls < kPQK; ls += 2) {
-                const int g = G * kPQK + ls, ab = g % kPA;
-                const uint8_t* q = q4_ring + (size_t)s * kPStage + ls * kTcQ4Stage + wl * kTileRec;
-                const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
-                const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
-                const uint16_t sc = reinterpret_cast<const uint16_t*>(q + kTileBytes)[lane];
-                uint32_t a[32];
-                dequant_row_f16(q0, q1, __ushort_as_half(sc), a);
-                if (g >= kPA && !tc_wait_warp(&sh.a_empty[ab], ((g / kPA) - 1) & 1, ws.err, &sh.abort)) {
-                    ok = false;
-                    break;
-                }
-                // order this TMEM write after the MMAs that read the buffer (released by a_empty)
-                tc_fence_after();
-                tc_st32(tmem + ((uint32_t)(wl * 32) << 16) + ab * 32, a);
-                tc_wait_st();
-                tc_fence_before();
-                mbar_arrive(&sh.a_full[ab]);
-            }
+            const uint8_t* q = q4_ring + (size_t)s * kPStage + (2 * wg) * kTcQ4Stage + wl * kTileRec;
+            const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
+            const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
+            const uint16_t sc0 = reinterpret_cast<const uint16_t*>(q + kTileBytes)[lane];
+            const uint4 q2 = *reinterpret_cast<const uint4*>(q + kTcQ4Stage + lane * 16);
+            const uint4 q3 = *reinterpret_cast<const uint4*>(q + kTcQ4Stage + 512 + lane * 16);
+            const uint16_t sc1 = reinterpret_cast<const uint16_t*>(q + kTcQ4Stage + kTileBytes)[lane];
             // this thread's reads of the stage are done; the next bulk copy into it is
             // an async-proxy write, ordered after these plain loads by the proxy fence
             fence_proxy_async_smem();
             mbar_arrive(&sh.q4_empty[s]);
+            uint32_t a0[32], a1[32];
+            dequant_row_f16(q0, q1, __ushort_as_half(sc0), a0);
+            dequant_row_f16(q2, q3, __ushort_as_half(sc1), a1);
+            if (P >= kPA && !tc_wait_warp(&sh.a_empty[ab], ((P / kPA) - 1) & 1, ws.err, &sh.abort)) break;
+            // order these TMEM writes after the MMAs that read the buffer (released by a_empty)
+            tc_fence_after();
+            const uint32_t ta = tmem + ((uint32_t)(wl * 32) << 16) + ab * 64;
+            tc_st32(ta, a0);
+            tc_st32(ta + 32, a1);
+            tc_wait_st();
+            tc_fence_before();
+            mbar_arrive(&sh.a_full[ab]);
         }
     } else {
         // ---------------- epilogue warps 0-3: thread = accumulator row
         const int row = warp * 32 + lane;
-        float* up_s = reinterpret_cast<float*>(scr);                                 // [64 rows][kTcNT]
-        __half* act_s = reinterpret_cast<__half*>(scr + 64 * kTcNT * sizeof(float));  // [2][kTcNT][64]
+        float* up_s = reinterpret_cast<float*>(scr);  // [64 rows][kTcNT + 1] (odd stride: no bank conflicts)
+        __half* act_s = reinterpret_cast<__half*>(scr + 64 * (kTcNT + 1) * sizeof(float));  // [2][kTcNT][64]
         for (int i = 0; i < my_items; i++) {
             const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
             const int ib = i & 1;
             bool got = true;
             for (int w = 0; got && w < kPI; w++)
-                got = tc_wait_warp(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort);
+                got = __all_sync(0xffffffffu, tc_wait_relaxed(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort));
             if (!got) break;
             tc_fence_after();
             if (i == 0) trace_point(tr, tk, 10);
@@ -534,7 +559,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         float v[16];
                         tc_ld_acc16(acc0, acc1, N, t0, v);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) up_s[(row - 64) * kTcNT + t0 + j] = v[j];
+                        for (int j = 0; j < 16; j++) up_s[(row - 64) * (kTcNT + 1) + t0 + j] = v[j];
                     }
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 if (warp < 2) {
@@ -545,7 +570,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         tc_ld_acc16(acc0, acc1, N, t0, v);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            const float a = silu_mul(v[j], up_s[row * kTcNT + t0 + j]);
+                            const float a = silu_mul(v[j], up_s[row * (kTcNT + 1) + t0 + j]);
                             const __half h = __float2half_rn(a);
                             const __half l = __float2half_rn(a - __half2float(h));
                             act_s[(t0 + j) * 64 + kc * 8 + pp] = h;
