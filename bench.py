@@ -10,8 +10,12 @@ working set is far above the 126 MB L2 and no flush is needed.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
     python bench.py --impl reference ...   # the reference's CPU path, same metric
 
-Output: one JSON line on rank 0 (see the keys below). Multi-GPU (torchrun)
-runs one independent replica per GPU (weak scaling).
+The headline batch is B=64 (the tensor-core path); the sweep adds B=1 and
+B=8 (the exact CUDA-core path, bit-identical to the reference) and B=32 in
+`per_batch`. Output: one JSON line on rank 0 (see the keys below).
+Multi-GPU (torchrun, N > 1) runs the layer expert-parallel: each GPU serves
+its own B tokens and stores E/N experts; token rows and weighted outputs
+cross GPUs by NCCL all-to-all (weak scaling in tokens).
 """
 from __future__ import annotations
 
@@ -329,11 +333,119 @@ def cpu_model():
     return None
 
 
+def run_ep(a, ws, rank, local):
+    """N > 1: expert parallelism. Every rank serves its own B tokens (data
+    parallel) and stores E/N experts of each layer; each layer exchanges token
+    rows and weighted expert outputs with NCCL all-to-all. Same seeded model
+    as one GPU (each rank keeps its slice of the full weights)."""
+    import torch
+    import torch.distributed as dist
+    from joule_b200 import synth
+    from joule_b200.ep import CudaEPBackend, ExpertParallelMoE
+    from joule_b200.moe import make_cfg
+    d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    B = a.batch
+    cfg = make_cfg(L, d, E, k, m, SHAPE["norm"])
+    be = CudaEPBackend(cfg, B, rank, ws)
+    El = E // ws
+    sl = slice(rank * El, (rank + 1) * El)
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    t = time.time()
+    for l in range(L):
+        gw = synth.router_bf16(E, d, gen, dev)
+        w = [torch.randn(E, m, d, generator=gen, device=dev) * 0.02,
+             torch.randn(E, m, d, generator=gen, device=dev) * 0.02,
+             torch.randn(E, d, m, generator=gen, device=dev) * 0.02]
+        be.quantize_layer(l, gw, *[t_[sl].contiguous() for t_ in w])
+        del w
+    torch.cuda.synchronize()
+    setup_s = time.time() - t
+    ep = ExpertParallelMoE(be, E)
+    gx = torch.Generator(device=dev).manual_seed(100 + rank)
+    xs = torch.randn(L, B, d, generator=gx, device=dev)
+    recv = []
+
+    def step():
+        for l in range(L):
+            ep.forward(l, xs[l])
+            recv.append(sum(ep.last_counts))
+
+    for _ in range(a.warmup):
+        step()
+    be.check()
+    recv.clear()
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0.record()
+        for _ in range(a.steps):
+            step()
+        t1.record()
+        t1.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(ws, t0.elapsed_time(t1))
+    be.check()
+    rows = torch.tensor([float(np.mean(recv))], device=dev)
+    rows_all = [torch.zeros_like(rows) for _ in range(ws)]
+    dist.all_gather(rows_all, rows)
+    # end to end: host x in, host out back, per layer
+    xh = torch.randn(L, B, d, generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
+    oh = torch.empty(B, d).pin_memory()
+    n_e2e = max(2, a.steps // 4)
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n_e2e):
+        for l in range(L):
+            o = ep.forward(l, xh[l].to(dev, non_blocking=True))
+            oh.copy_(o, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    barrier(ws)
+    e2e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    val = ws * B * a.steps / (ms / 1e3)
+    if rank == 0:
+        line = dict(metric=METRIC, value=val, unit="tok/s", n_gpus=ws, steps=a.steps, warmup=a.warmup,
+                    ms_per_step=ms / a.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="f32 (Q4 weights, fp32 accumulate)",
+                    data="synthetic: seeded N(0,0.02) weights quantised to the reference Q4 format, "
+                         "x ~ N(0,1)",
+                    config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch "
+                                         f"{B} per GPU ({ws * B} total), expert parallel",
+                                batch_per_gpu=B, global_batch=ws * B, layers=L, d=d, E=E, topk=k,
+                                intermediate=m, norm_topk_prob=1, parallelism=f"ep{ws}",
+                                experts_per_gpu=El,
+                                exchange="NCCL all_to_all_single of token rows and weighted outputs "
+                                         "(torch.distributed), 3 per layer + counts",
+                                path="per rank: router (all E) then tensor-core or exact expert "
+                                     "kernels on received rows (JL_PATH_AUTO)",
+                                l2="not flushed: each step streams >= 1 GB of distinct expert weights",
+                                store_setup_s=round(setup_s, 1)),
+                    rows_received_per_layer=[round(float(r.item()), 1) for r in rows_all],
+                    clocks=clk.summary(),
+                    gpu_launches=L * a.steps * 6,  # route, dispatch, permute, gate/up, down, combine
+                    e2e=dict(value=ws * B * n_e2e / (e2e_ms / 1e3), unit="tok/s",
+                             h2d_bytes_per_step=L * B * d * 4, d2h_bytes_per_step=L * B * d * 4,
+                             api="ExpertParallelMoE.forward per layer, host x in / host out back"),
+                    roofline=None)
+        print(json.dumps(line), flush=True)
+    be.close()
+    dist.destroy_process_group()
+
+
 def run_ours(a):
     import torch
     from joule_b200.moe import MoELayers, make_cfg
     SHAPE["L"] = a.layers
     ws, rank, local = dist_init()
+    if ws > 1:
+        return run_ep(a, ws, rank, local)
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
     sweep = sorted(set(int(b) for b in a.sweep.split(",")) | {a.batch})
     Bmax = max(sweep)
@@ -363,6 +475,7 @@ def run_ours(a):
         layer_bytes = [u * rec_bytes(d, m) + E * d * 2 + 2 * B * d * 4 for u in U]
         gu_bytes = [u * 2 * (m * d // 2 + m * d // 32) + B * d * 4 + B * k * m * 4 for u in U]
         rec = dict(
+            path=path_of(B),
             tok_s=ws * B * a.steps / (total_ms / 1e3), ms_per_step=ms_step,
             us_per_layer=ms_step * 1e3 / L, mean_U=float(np.mean(U)),
             layer_gbs=sum(layer_bytes) / (ms_step / 1e3) / 1e9,
@@ -380,17 +493,25 @@ def run_ours(a):
                      "x ~ N(0,1)",
                 config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
                             batch=a.batch, layers=L, d=d, E=E, topk=k, intermediate=m,
-                            norm_topk_prob=1, path="exact (CUDA-core FP32, reference order)",
+                            norm_topk_prob=1,
+                            path=("exact (CUDA-core FP32 in the reference's order, bit-identical)"
+                                  if path_of(a.batch) == "exact" else
+                                  "tensor-core (tcgen05 grouped GEMM, fp16 weights x fp16 hi+lo "
+                                  "activations, fp32 accumulate; <= 1e-3 row-relative)"),
                             l2="not flushed: each step streams >= 1 GB of distinct expert weights "
                                "(store 15.4 GB) vs 126 MB L2",
                             parallelism=f"replicas x{ws}" if ws > 1 else "single GPU",
                             store_setup_s=round(setup_s, 1)),
                 per_batch=per_b)
-    line["roofline"] = dict(bound="hbm", kernel="k_gateup_exact (gate+up rows of the union experts)",
+    kern = "k_gateup_exact" if path_of(a.batch) == "exact" else "k_expert_tc<false>"
+    line["roofline"] = dict(bound="hbm",
+                            kernel=f"{kern} (gate + up rows of the union experts, SwiGLU fused; "
+                                   f"phase time includes {'nothing else' if kern == 'k_gateup_exact' else 'the token permute'})",
                             achieved=head["gateup_gbs"], peak=hbm, unit="GB/s",
                             frac=head["gateup_gbs"] / hbm, peak_kind=peak_kind,
-                            traffic=traffic_from_profiles(), layer_gbs=head["layer_gbs"],
-                            layer_frac=head["layer_gbs"] / hbm)
+                            traffic=traffic_from_profiles(kern, a.batch),
+                            algorithmic_bytes_per_launch=head["gateup_bytes_per_launch"],
+                            layer_gbs=head["layer_gbs"], layer_frac=head["layer_gbs"] / hbm)
     line["clocks"] = clocks
     line["gpu_launches"] = launches_per_step(a.batch) * a.steps
     if rank == 0 and a.e2e:
@@ -405,19 +526,26 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def path_of(B):
+    """The path jl_moe_forward takes (JL_PATH_AUTO) at batch B for this shape."""
+    return "exact" if B <= 8 else "tensor-core"
+
+
 def launches_per_step(B):
-    # per layer: router (+ top-k and dispatch kernels when B > 8), gate/up, down, combine
-    return SHAPE["L"] * (4 if B <= 8 else 6)
+    # per layer: the cluster router (routing + dispatch), then
+    #   exact: gate/up, down, combine; tensor-core: permute, gate/up, down, combine
+    return SHAPE["L"] * (1 + (3 if path_of(B) == "exact" else 4))
 
 
-def traffic_from_profiles():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+def traffic_from_profiles(kernel, B):
+    """DRAM bytes (read + write) per launch of `kernel` at batch B from the
+    committed ncu summary (profiles/traffic.txt lines `kernel B=<B> = <bytes>`)."""
     p = ROOT / "profiles" / "traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.startswith("k_gateup_exact_bytes_per_launch"):
-            return float(line.split("=")[1].split()[0])
+        if line.startswith(f"{kernel} B={B} "):
+            return float(line.split("=")[2].split()[0])
     return None
 
 
@@ -482,7 +610,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--sweep", default="1,8,32,64")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-layers", type=int, default=2)

@@ -140,6 +140,14 @@ typedef struct jl_moe jl_moe;
 int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out);
 int jl_moe_destroy(jl_moe* h);
 
+/* jl_moe_create with flags. JL_CREATE_ROUTER_ONLY allocates the router
+ * weights and the workspace but no expert store: such a handle serves
+ * jl_moe_upload_router and jl_moe_route only (the routing side of expert
+ * parallelism, where each rank stores a slice of the experts in a second
+ * handle). No counterpart in the reference, which runs on one host. */
+#define JL_CREATE_ROUTER_ONLY 1
+int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags, jl_moe** out);
+
 /* Upload layer l: router rows gate_w [E, d] bf16 and, for each part p in
  * (gate, up, down) and expert e, the Q4 record pk[p*E+e] / sc[p*E+e] in the
  * reference layout (the pointers decoder3.py:355-361 builds). Pointers may
@@ -179,6 +187,29 @@ int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out,
  * the reference. */
 int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, float* out,
                           int* top, float* tw, int mask, void* stream);
+
+/* Router weights of layer l only: gate_w [E, d] bf16, host or device
+ * (`src_on_device`). Synchronises `stream`. For JL_CREATE_ROUTER_ONLY
+ * handles this is the whole upload. */
+int jl_moe_upload_router(jl_moe* h, int l, const unsigned short* gate_w,
+                         int src_on_device, void* stream);
+
+/* Routing of layer l alone (decode_kernel.c:1424-1485): top [B, topk] int32
+ * expert ids, tw [B, topk] fp32 weights and, when comb is not NULL,
+ * comb [B, topk]: token b's slots b*topk + i in the union order the
+ * reference's combine adds them in (decode_kernel.c:1490-1507). Device
+ * buffers; enqueued on `stream`. */
+int jl_moe_route(jl_moe* h, int l, const float* x, int B, int* top, float* tw,
+                 int* comb, void* stream);
+
+/* The expert FFN and combine of layer l with routing supplied by the caller
+ * instead of the router: top [B, topk] (expert ids of this handle) and tw
+ * [B, topk] (device). out[b] = the combine of b's topk weighted expert
+ * outputs, as jl_moe_forward computes it after its own routing. With a
+ * topk = 1 handle holding a rank's slice of the experts, this is the
+ * remote half of expert parallelism: out[i] = tw[i] * FFN_top[i](x[i]). */
+int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, const int* top,
+                          const float* tw, float* out, void* stream);
 
 /* Debug / parity: copies (device) the router logits [B, E], the union
  * experts sel [U], offsets uh [U+1] and the slot map uidx/uw [B*topk] built

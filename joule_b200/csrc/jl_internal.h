@@ -70,6 +70,7 @@ constexpr int kTraceSlots = 4 * 16;
 struct jl_moe {
     int device;
     int sm_count;  // streaming multiprocessors of the device (persistent grids)
+    int router_only;  // JL_CREATE_ROUTER_ONLY: router weights and workspace, no expert store
     int L, d, E, k, m, norm;
     int max_tokens;
     int path;
@@ -118,6 +119,10 @@ int jl_router_topk_prepare();
 int jl_launch_router_topk(const jl_ws& ws, const unsigned short* gate_w, const float* x, int B, int E,
                           int d, int k, int norm, cudaStream_t s);
 
+// Dispatch (union, slot map, tile table) from the top/tw already in the
+// workspace, for callers that bring their own routing.
+int jl_launch_dispatch(const jl_moe* h, int B, cudaStream_t s);
+
 // jl_exact.cu: CUDA-core expert FFN in the reference's arithmetic order.
 int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
                            cudaStream_t s);
@@ -127,5 +132,5 @@ int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, c
 // jl_tc.cu: tensor-core expert FFN (permute -> gate/up+SwiGLU -> down).
 // The tile table is built at the end of the dispatch step (jl_tiles.cuh).
 size_t jl_tc_ws_bytes(int Bmax, int E, int k, int d, int m, size_t* xc_plane, size_t* ac_plane);
-int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
-                         cudaStream_t s);
+int jl_launch_gateup_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s);
+int jl_launch_down_tc(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);

@@ -70,7 +70,11 @@ ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
 extern "C" const char* jl_version(void) { return "joule_b200 0.1 sm_100a"; }
 
 extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out) {
-    if (!out) return JL_ERR_INVALID;
+    return jl_moe_create_ex(cfg, max_tokens, 0, out);
+}
+
+extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags, jl_moe** out) {
+    if (!out || (flags & ~JL_CREATE_ROUTER_ONLY)) return JL_ERR_INVALID;
     *out = nullptr;
     int rc = check_shape(cfg);
     if (rc) return rc;
@@ -98,14 +102,15 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
     h->lay.ngm = h->m / 64;
     h->lay.dn_off = (size_t)(h->m / 64) * h->lay.ngd * 4 * 1088;
     h->lay.rec_bytes = h->lay.dn_off + (size_t)(h->d / 128) * h->lay.ngm * 4 * 1088;
-    h->store_bytes = (size_t)h->L * h->E * h->lay.rec_bytes;
+    h->router_only = (flags & JL_CREATE_ROUTER_ONLY) ? 1 : 0;
+    h->store_bytes = h->router_only ? 0 : (size_t)h->L * h->E * h->lay.rec_bytes;
     const ws_plan wp = plan_ws(max_tokens, h->E, h->k, h->d, h->m);
     h->ws_bytes = wp.total;
     h->dev_stage_bytes = std::max(h->lay.rec_bytes, (size_t)h->E * h->d * 2);
     h->uploaded = (unsigned char*)calloc(h->L, 1);
     const size_t gw = (size_t)h->L * h->E * router_expert_halves(h->d) * 2;
     if (!h->uploaded || cudaMalloc(&h->gate_w, gw) != cudaSuccess ||
-        cudaMalloc(&h->store, h->store_bytes) != cudaSuccess ||
+        (!h->router_only && cudaMalloc(&h->store, h->store_bytes) != cudaSuccess) ||
         cudaMalloc(&h->ws_base, h->ws_bytes) != cudaSuccess ||
         cudaMalloc(&h->dev_stage, h->dev_stage_bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -207,7 +212,7 @@ static int part_cols(const jl_moe* h, int p) { return p < 2 ? h->d : h->m; }
 extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_w,
                                    const unsigned char* const* pk, const unsigned short* const* sc,
                                    int src_on_device, void* stream) {
-    if (!h || l < 0 || l >= h->L || !gate_w || !pk || !sc) return JL_ERR_INVALID;
+    if (!h || l < 0 || l >= h->L || !gate_w || !pk || !sc || h->router_only) return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
     const size_t gw = (size_t)h->E * h->d * 2;
     const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -240,7 +245,8 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
 extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
                                      const float* w_gate, const float* w_up, const float* w_down,
                                      void* stream) {
-    if (!h || l < 0 || l >= h->L || !gate_w || !w_gate || !w_up || !w_down) return JL_ERR_INVALID;
+    if (!h || l < 0 || l >= h->L || !gate_w || !w_gate || !w_up || !w_down || h->router_only)
+        return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
     int rc0 = jl_launch_repack_router(gate_w, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d), h->E,
                                       h->d, s);
@@ -270,6 +276,7 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
         return JL_ERR_INVALID;
     if (B > h->max_tokens) return JL_ERR_CAPACITY;
     if (!h->uploaded[l]) return JL_ERR_NOT_READY;
+    if (h->router_only && (mask & 6)) return JL_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
         return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
@@ -292,9 +299,9 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
     if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, tc, s);
     if (!rc) rc = mark(1);
     if (tc) {
-        // the tensor-core kernels run as one unit (permute, gate/up, down)
-        if (!rc && (mask & 2)) rc = jl_launch_experts_tc(h, store_l, x, B, s);
+        if (!rc && (mask & 2)) rc = jl_launch_gateup_tc(h, store_l, x, B, s);
         if (!rc) rc = mark(2);
+        if (!rc && (mask & 4)) rc = jl_launch_down_tc(h, store_l, B, s);
     } else {
         if (!rc && (mask & 2)) rc = jl_launch_gateup_exact(h, store_l, x, B, s);
         if (!rc) rc = mark(2);
@@ -310,6 +317,64 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
 extern "C" int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out, int* top,
                               float* tw, void* stream) {
     return jl_moe_forward_phases(h, l, x, B, out, top, tw, 7, stream);
+}
+
+extern "C" int jl_moe_upload_router(jl_moe* h, int l, const unsigned short* gate_w, int src_on_device,
+                                    void* stream) {
+    if (!h || l < 0 || l >= h->L || !gate_w) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint16_t* src = gate_w;
+    if (!src_on_device) {
+        JL_CUDA(cudaMemcpyAsync(h->dev_stage, gate_w, (size_t)h->E * h->d * 2, cudaMemcpyHostToDevice, s));
+        src = (const uint16_t*)h->dev_stage;
+    }
+    int rc = jl_launch_repack_router(src, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d), h->E,
+                                     h->d, s);
+    if (rc) return rc;
+    JL_CUDA(cudaStreamSynchronize(s));
+    if (h->router_only) h->uploaded[l] = 1;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_route(jl_moe* h, int l, const float* x, int B, int* top, float* tw, int* comb,
+                            void* stream) {
+    if (!h || !x || !top || !tw || l < 0 || l >= h->L || B < 1) return JL_ERR_INVALID;
+    if (B > h->max_tokens) return JL_ERR_CAPACITY;
+    if (!h->uploaded[l]) return JL_ERR_NOT_READY;
+    if (reinterpret_cast<uintptr_t>(x) & 15) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    const unsigned short* gw = h->gate_w + (size_t)l * h->E * router_expert_halves(h->d);
+    int rc = jl_launch_route(h, gw, x, B, false, s);
+    if (rc) return rc;
+    const size_t S = (size_t)B * h->k;
+    JL_CUDA(cudaMemcpyAsync(top, h->ws.top, S * 4, cudaMemcpyDeviceToDevice, s));
+    JL_CUDA(cudaMemcpyAsync(tw, h->ws.tw, S * 4, cudaMemcpyDeviceToDevice, s));
+    if (comb) JL_CUDA(cudaMemcpyAsync(comb, h->ws.comb, S * 4, cudaMemcpyDeviceToDevice, s));
+    h->last_B = B;
+    return JL_OK;
+}
+
+extern "C" int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, const int* top,
+                                     const float* tw, float* out, void* stream) {
+    if (!h || !x || !top || !tw || !out || l < 0 || l >= h->L || B < 1 || h->router_only)
+        return JL_ERR_INVALID;
+    if (B > h->max_tokens) return JL_ERR_CAPACITY;
+    if (!h->uploaded[l]) return JL_ERR_NOT_READY;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    const size_t S = (size_t)B * h->k;
+    JL_CUDA(cudaMemcpyAsync(h->ws.top, top, S * 4, cudaMemcpyDeviceToDevice, s));
+    JL_CUDA(cudaMemcpyAsync(h->ws.tw, tw, S * 4, cudaMemcpyDeviceToDevice, s));
+    const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
+    const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
+    int rc = jl_launch_dispatch(h, B, s);
+    if (!rc) rc = tc ? jl_launch_gateup_tc(h, store_l, x, B, s) : jl_launch_gateup_exact(h, store_l, x, B, s);
+    if (!rc) rc = tc ? jl_launch_down_tc(h, store_l, B, s) : jl_launch_down_exact(h, store_l, B, s);
+    if (!rc) rc = jl_launch_combine(h, B, out, nullptr, nullptr, s);
+    if (rc) return rc;
+    h->last_B = B;
+    return JL_OK;
 }
 
 extern "C" int jl_moe_debug_routing(jl_moe* h, int B, float* logits, int* sel, int* uh, int* uidx,

@@ -795,6 +795,19 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
                   h->ws);
 }
 
+int jl_launch_dispatch(const jl_moe* h, int B, cudaStream_t s) {
+    using namespace jl;
+    if (h->E > kMaxE || h->k > kMaxK) return JL_ERR_INVALID;
+    static bool attr = false;
+    if (!attr) {
+        JL_CUDA(cudaFuncSetAttribute(k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        attr = true;
+    }
+    const int T = 1024;
+    return launch(k_dispatch, dim3(1), dim3(T), (size_t)dispatch_smem_ints(h->E, T / 32) * 4, s, B, h->k,
+                  h->E, h->ws);
+}
+
 // Routing only, into buffers the caller chooses: k_router (no fused tail)
 // then k_topk. ws.logits ([B, E] fp32 scratch), ws.top / ws.tw (the outputs)
 // and ws.err are the only workspace fields these two kernels touch.

@@ -621,8 +621,7 @@ size_t jl_tc_ws_bytes(int Bmax, int E, int k, int d, int m, size_t* xc_plane, si
     return (*xc_plane + *ac_plane) * 2 * sizeof(__half) + (size_t)tiles * 4 * sizeof(int) + 16;
 }
 
-int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B,
-                         cudaStream_t s) {
+static int tc_attrs() {
     using namespace jl;
     static bool attr = false;
     if (!attr) {
@@ -632,14 +631,28 @@ int jl_launch_experts_tc(const jl_moe* h, const uint8_t* store_l, const float* x
                                      (int)kPSmemBytes));
         attr = true;
     }
+    return JL_OK;
+}
+
+int jl_launch_gateup_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s) {
+    using namespace jl;
+    int rc = tc_attrs();
+    if (rc) return rc;
     if (h->d % 512 || h->m % 256 || !h->ws.xc) return JL_ERR_INVALID;
     const int tiles = tc_max_tiles(B * h->k, h->E);
-    int rc = launch(k_tc_permute, dim3(tiles, h->d / 512), dim3(256), 0, s, x, h->d, h->k, h->ws);
+    rc = launch(k_tc_permute, dim3(tiles, h->d / 512), dim3(256), 0, s, x, h->d, h->k, h->ws);
     if (rc) return rc;
-    const int gu_items = tiles * (h->m / 64), dn_items = tiles * (h->d / 128);
-    rc = launch(k_expert_tc<false>, dim3(std::min(h->sm_count, gu_items)), dim3(kPThreads), kPSmemBytes, s,
-                store_l, h->lay, h->ws);
+    const int items = tiles * (h->m / 64);
+    return launch(k_expert_tc<false>, dim3(std::min(h->sm_count, items)), dim3(kPThreads), kPSmemBytes, s,
+                  store_l, h->lay, h->ws);
+}
+
+int jl_launch_down_tc(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s) {
+    using namespace jl;
+    int rc = tc_attrs();
     if (rc) return rc;
-    return launch(k_expert_tc<true>, dim3(std::min(h->sm_count, dn_items)), dim3(kPThreads), kPSmemBytes,
-                  s, store_l, h->lay, h->ws);
+    if (h->d % 512 || h->m % 256 || !h->ws.xc) return JL_ERR_INVALID;
+    const int items = tc_max_tiles(B * h->k, h->E) * (h->d / 128);
+    return launch(k_expert_tc<true>, dim3(std::min(h->sm_count, items)), dim3(kPThreads), kPSmemBytes, s,
+                  store_l, h->lay, h->ws);
 }

@@ -19,11 +19,11 @@ from typing import Sequence
 import numpy as np
 import torch
 
-from joule_b200.native import (PATH_AUTO, PATH_EXACT, PATH_TC, KernelCfg, KernelW, check,
-                               get_dll)
+from joule_b200.native import (CREATE_ROUTER_ONLY, PATH_AUTO, PATH_EXACT, PATH_TC, KernelCfg,
+                               KernelW, check, get_dll)
 
 __all__ = ["MoELayers", "KernelCfg", "KernelW", "layer_ffn_batch", "PATH_AUTO", "PATH_EXACT",
-           "PATH_TC", "make_cfg"]
+           "PATH_TC", "CREATE_ROUTER_ONLY", "make_cfg"]
 
 
 def make_cfg(L: int, d: int, E: int, topk: int, intermediate: int, norm_topk_prob: int,
@@ -56,12 +56,15 @@ def _stream(stream) -> int | None:
 class MoELayers:
     """All MoE layers of one model on the current CUDA device."""
 
-    def __init__(self, cfg: KernelCfg, max_tokens: int = 64):
+    def __init__(self, cfg: KernelCfg, max_tokens: int = 64, flags: int = 0):
+        """flags = CREATE_ROUTER_ONLY: router weights and workspace only (no
+        expert store): upload_router + route."""
         self._L = get_dll()
         self.cfg = cfg
         self.max_tokens = max_tokens
         h = ctypes.c_void_p()
-        check(self._L.jl_moe_create(ctypes.byref(cfg), max_tokens, ctypes.byref(h)), "jl_moe_create")
+        check(self._L.jl_moe_create_ex(ctypes.byref(cfg), max_tokens, flags, ctypes.byref(h)),
+              "jl_moe_create_ex")
         self.h = h
 
     # -- lifetime -----------------------------------------------------------
@@ -114,6 +117,37 @@ class MoELayers:
             out = torch.empty_like(x)
         check(self._L.jl_moe_forward(self.h, l, _ptr(x), B, _ptr(out), _ptr(top), _ptr(tw),
                                      _stream(stream)), "jl_moe_forward")
+        return out
+
+    def upload_router(self, l: int, gate_w, stream=None) -> None:
+        """Router weights [E, d] bf16 bits of layer l (numpy host or torch CUDA)."""
+        on_dev = isinstance(gate_w, torch.Tensor) and gate_w.is_cuda
+        check(self._L.jl_moe_upload_router(self.h, l, _ptr(gate_w), 1 if on_dev else 0,
+                                           _stream(stream)), "jl_moe_upload_router")
+
+    def route(self, l: int, x: torch.Tensor, stream=None):
+        """Routing alone: (top [B, k] int32, tw [B, k] fp32, comb [B, k] int32)
+        device tensors; comb lists token b's slots in the combine's order."""
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        B, k = x.shape[0], self.cfg.topk
+        top = torch.empty(B, k, dtype=torch.int32, device=x.device)
+        tw = torch.empty(B, k, dtype=torch.float32, device=x.device)
+        comb = torch.empty(B, k, dtype=torch.int32, device=x.device)
+        check(self._L.jl_moe_route(self.h, l, _ptr(x), B, _ptr(top), _ptr(tw), _ptr(comb),
+                                   _stream(stream)), "jl_moe_route")
+        return top, tw, comb
+
+    def forward_routed(self, l: int, x: torch.Tensor, top: torch.Tensor, tw: torch.Tensor,
+                       out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Expert FFN + combine with caller-given routing (top/tw [B, k] of
+        this handle's experts)."""
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        top = top.to(torch.int32).contiguous()
+        tw = tw.to(torch.float32).contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        check(self._L.jl_moe_forward_routed(self.h, l, _ptr(x), x.shape[0], _ptr(top), _ptr(tw),
+                                            _ptr(out), _stream(stream)), "jl_moe_forward_routed")
         return out
 
     def forward_phases(self, l: int, x: torch.Tensor, out: torch.Tensor, mask: int,

@@ -24,6 +24,7 @@ ERRORS = {
     -7: "JL_ERR_DEVICE: kernel reported a bad index/state",
 }
 PATH_AUTO, PATH_EXACT, PATH_TC = 0, 1, 2
+CREATE_ROUTER_ONLY = 1
 
 
 class JouleError(RuntimeError):
@@ -67,6 +68,10 @@ SIGNATURES = {
     "jl_q4_quantize": ([_P, _LL, _P, _P, _P], _I),
     "jl_moe_create": ([ctypes.POINTER(KernelCfg), _I, ctypes.POINTER(_P)], _I),
     "jl_moe_destroy": ([_P], _I),
+    "jl_moe_create_ex": ([ctypes.POINTER(KernelCfg), _I, _I, ctypes.POINTER(_P)], _I),
+    "jl_moe_upload_router": ([_P, _I, _P, _I, _P], _I),
+    "jl_moe_route": ([_P, _I, _P, _I, _P, _P, _P, _P], _I),
+    "jl_moe_forward_routed": ([_P, _I, _P, _I, _P, _P, _P, _P], _I),
     "jl_moe_upload_layer": ([_P, _I, _P, _P, _P, _I, _P], _I),
     "jl_moe_quantize_layer": ([_P, _I, _P, _P, _P, _P, _P], _I),
     "jl_moe_set_path": ([_P, _I], _I),

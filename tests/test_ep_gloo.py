@@ -1,0 +1,100 @@
+"""Expert parallelism on CPU: the exchange and combine of joule_b200.ep run as
+world_size 2 gloo ranks, with the expert compute done by the CPU oracle.
+
+Each rank owns half of the experts and routes its own tokens; the layer
+output of every rank must be bit-identical to the single-process oracle
+layer on the same tokens (the per-slot values and the union-order combine
+are the single-GPU ones; only where the rows are computed changes).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+SHAPE = dict(d=256, E=8, k=2, m=128, norm=1)
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+class OracleBackend:
+    """route / experts from the CPU restatement (tests only)."""
+
+    def __init__(self, lay, rank: int, world: int):
+        self.lay = lay
+        self.E_local = lay.E // world
+        self.e0 = rank * self.E_local
+
+    def route(self, l, x):
+        from oracle import restate
+        xn = x.numpy()
+        top, tw, _ = restate.route(restate.router_logits(self.lay, xn), self.lay.k,
+                                   self.lay.norm_topk_prob)
+        sel, _, _, _ = restate.dispatch(top, tw, self.lay.E)
+        upos = {int(e): u for u, e in enumerate(sel)}
+        B, k = top.shape
+        comb = np.empty((B, k), np.int32)
+        for b in range(B):
+            comb[b] = sorted(range(b * k, b * k + k), key=lambda s: upos[int(top.flat[s])])
+        return torch.from_numpy(top), torch.from_numpy(tw), torch.from_numpy(comb)
+
+    def experts(self, l, rows, eid, w):
+        from oracle import restate
+        lay, m, d = self.lay, self.lay.m, self.lay.d
+        X = rows.numpy()
+        y = np.empty_like(X)
+        expf = np.vectorize(lambda v: restate.expf_fast(float(v)), otypes=[np.float32])
+        for i in range(X.shape[0]):
+            e = self.e0 + int(eid[i])
+            g = restate.q4_gemm(X[i], lay.packed[0][e], lay.scales[0][e], m, d)[0]
+            u = restate.q4_gemm(X[i], lay.packed[1][e], lay.scales[1][e], m, d)[0]
+            act = ((g / (np.float32(1) + expf(-g))).astype(np.float32) * u).astype(np.float32)
+            dacc = restate.q4_gemm(act, lay.packed[2][e], lay.scales[2][e], d, m)[0]
+            y[i] = np.float32(0) + np.float32(w[i]) * dacc
+        return torch.from_numpy(y)
+
+
+def _rank(rank: int, world: int, port: int, B: int, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from joule_b200.ep import ExpertParallelMoE
+        from oracle import layer as olayer
+        from oracle import restate
+        lay = olayer.make_layer(SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["norm"],
+                                seed_router=3, seed_experts=4)
+        x = olayer.hidden(B, SHAPE["d"], 100 + rank)
+        ep = ExpertParallelMoE(OracleBackend(lay, rank, world), SHAPE["E"])
+        out = ep.forward(0, torch.from_numpy(x)).numpy()
+        ref, _, _ = restate.moe_layer(lay, x)
+        results[rank] = (bool(np.array_equal(out, ref)), float(np.abs(out - ref).max()),
+                         list(ep.last_counts))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("B", [1, 6])
+def test_ep_two_ranks_matches_single_process(B):
+    world = 2
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.start_processes(_rank, args=(world, _free_port(), B, results), nprocs=world,
+                           start_method="spawn", join=True)
+        res = dict(results)
+    assert sorted(res) == [0, 1]
+    for r, (same, err, counts) in res.items():
+        assert same, f"rank {r}: max abs diff {err}"
+    # every slot was computed somewhere: rows received over both ranks = 2 ranks x B x k
+    assert sum(sum(c) for _, _, c in res.values()) == world * B * SHAPE["k"]

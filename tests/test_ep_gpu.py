@@ -1,0 +1,71 @@
+"""Expert parallelism on 2 GPUs over NCCL (needs >= 2 GPUs; skipped otherwise).
+
+Each rank stores half of the Qwen3-shape layer's experts and routes its own
+tokens; with the exact expert path forced on the rank-local handles, every
+rank's layer output must equal the CPU oracle's bit for bit.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank(rank: int, world: int, port: int, B: int, results):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(__file__))
+        from conftest import seeded_layer
+        from joule_b200.ep import CudaEPBackend, ExpertParallelMoE
+        from joule_b200.moe import PATH_EXACT, make_cfg
+        from oracle import layer as olayer
+        from oracle import restate
+        lay = seeded_layer("qwen3")
+        be = CudaEPBackend(make_cfg(1, lay.d, lay.E, lay.k, lay.m, lay.norm_topk_prob), B, rank,
+                           world, path=PATH_EXACT)
+        be.upload_layer(0, lay.gate_w, lay.packed, lay.scales)
+        x = olayer.hidden(B, lay.d, 200 + rank)
+        ep = ExpertParallelMoE(be, lay.E)
+        out = ep.forward(0, torch.from_numpy(x).cuda()).cpu().numpy()
+        torch.cuda.synchronize()
+        be.check()
+        ref, _, _ = restate.moe_layer(lay, x)
+        results[rank] = (bool(np.array_equal(out, ref)), float(np.abs(out - ref).max()))
+        be.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("B", [1, 5])
+def test_ep_two_gpus_bit_exact(B):
+    import torch.multiprocessing as mp
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.start_processes(_rank, args=(2, _free_port(), B, results), nprocs=2, start_method="spawn",
+                           join=True)
+        res = dict(results)
+    assert sorted(res) == [0, 1]
+    for r, (same, err) in res.items():
+        assert same, f"rank {r}: max abs diff {err}"
