@@ -361,7 +361,11 @@ def run_ep(a, ws, rank, local):
         del w
     torch.cuda.synchronize()
     setup_s = time.time() - t
-    ep = ExpertParallelMoE(be, E)
+    if a.ep == "p2p":
+        from joule_b200.ep import P2PExpertParallelMoE
+        ep = P2PExpertParallelMoE(be, B)
+    else:
+        ep = ExpertParallelMoE(be, E)
     gx = torch.Generator(device=dev).manual_seed(100 + rank)
     xs = torch.randn(L, B, d, generator=gx, device=dev)
     recv = []
@@ -369,7 +373,8 @@ def run_ep(a, ws, rank, local):
     def step():
         for l in range(L):
             ep.forward(l, xs[l])
-            recv.append(sum(ep.last_counts))
+            if a.ep != "p2p":
+                recv.append(sum(ep.last_counts))
 
     for _ in range(a.warmup):
         step()
@@ -389,7 +394,7 @@ def run_ep(a, ws, rank, local):
     torch.cuda.synchronize()
     ms = max_over_ranks(ws, t0.elapsed_time(t1))
     be.check()
-    rows = torch.tensor([float(np.mean(recv))], device=dev)
+    rows = torch.tensor([float(np.mean(recv)) if recv else -1.0], device=dev)
     rows_all = [torch.zeros_like(rows) for _ in range(ws)]
     dist.all_gather(rows_all, rows)
     # end to end: host x in, host out back, per layer
@@ -421,20 +426,25 @@ def run_ep(a, ws, rank, local):
                                 batch_per_gpu=B, global_batch=ws * B, layers=L, d=d, E=E, topk=k,
                                 intermediate=m, norm_topk_prob=1, parallelism=f"ep{ws}",
                                 experts_per_gpu=El,
-                                exchange="NCCL all_to_all_single of token rows and weighted outputs "
-                                         "(torch.distributed), 3 per layer + counts",
+                                exchange=("library kernels over NVLink peer memory (CUDA IPC): "
+                                          "peer stores of token rows and weighted outputs, epoch "
+                                          "flags, no host sync" if a.ep == "p2p" else
+                                          "NCCL all_to_all_single of token rows and weighted outputs "
+                                          "(torch.distributed), 3 per layer + counts"),
                                 path="per rank: router (all E) then tensor-core or exact expert "
                                      "kernels on received rows (JL_PATH_AUTO)",
                                 l2="not flushed: each step streams >= 1 GB of distinct expert weights",
                                 store_setup_s=round(setup_s, 1)),
                     rows_received_per_layer=[round(float(r.item()), 1) for r in rows_all],
                     clocks=clk.summary(),
-                    gpu_launches=L * a.steps * 6,  # route, dispatch, permute, gate/up, down, combine
+                    gpu_launches=L * a.steps * (9 if a.ep == "p2p" else 6),
                     e2e=dict(value=ws * B * n_e2e / (e2e_ms / 1e3), unit="tok/s",
                              h2d_bytes_per_step=L * B * d * 4, d2h_bytes_per_step=L * B * d * 4,
                              api="ExpertParallelMoE.forward per layer, host x in / host out back"),
                     roofline=None)
         print(json.dumps(line), flush=True)
+    if a.ep == "p2p":
+        ep.close()
     be.close()
     dist.destroy_process_group()
 
@@ -617,6 +627,8 @@ def main():
     ap.add_argument("--layers", type=int, default=48, help="MoE layers per step (48 = the model)")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
+    ap.add_argument("--ep", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1 exchange: library peer-memory kernels or NCCL all-to-all")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3

@@ -211,6 +211,47 @@ int jl_moe_route(jl_moe* h, int l, const float* x, int B, int* top, float* tw,
 int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, const int* top,
                           const float* tw, float* out, void* stream);
 
+/* Expert-parallel bookkeeping for one layer on one rank (no counterpart in
+ * the reference, which runs on one host). The S = B*topk routed slots of
+ * the rank's tokens (top/tw [B, topk] from jl_moe_route, global expert ids)
+ * are grouped by owner rank top / E_local, keeping slot order within a
+ * group: pos[s] is slot s's row in send order, counts[w] the rows for rank
+ * w, rows [S, d] the token rows x[s / topk] in send order and meta [S, 2]
+ * their (local expert id, weight bits). dev_status (device int, 0 before the
+ * call) receives error bits for expert ids outside [0, E_local * world).
+ * Device buffers; x and rows 16-byte aligned. */
+int jl_ep_pack(const int* top, const float* tw, const float* x, int B, int topk,
+               int d, int E_local, int world, float* rows, int* meta, int* pos,
+               int* counts, int* dev_status, void* stream);
+
+/* out[b] = 0 + back[pos[comb[b*topk]]] + ... + back[pos[comb[b*topk+topk-1]]]
+ * in that order: the reference's union-order combine
+ * (decode_kernel.c:1490-1507) over rows that came back in send order. */
+int jl_ep_combine(const float* back, const int* pos, const int* comb, int B,
+                  int topk, int d, float* out, void* stream);
+
+/* Expert parallelism over NVLink peer memory, with no host round trip per
+ * layer (no counterpart in the reference). A jl_ep pairs this rank's
+ * topk = 1 expert handle `local` (experts [rank*E_local, (rank+1)*E_local),
+ * max_tokens >= world * max_tokens_per_rank * topk) with one exported
+ * device buffer. Set-up: jl_ep_create on every rank, exchange the 64-byte
+ * jl_ep_ipc_handle of every rank (rank order), then jl_ep_open_peers.
+ * jl_ep_forward(ep, router, l, x, B, out) runs layer l for this rank's B
+ * tokens: route (router: all E experts), send each routed slot's row to
+ * its owner's buffer, wait for every sender, run the local experts, return
+ * the weighted rows to their senders, wait for every owner, and combine in
+ * the batch's union order: out equals a single GPU's jl_moe_forward on the
+ * same tokens. Every rank must make the same sequence of calls. Waits on
+ * other ranks are bounded; jl_moe_check(local) reports JL_ERR_TIMEOUT. */
+typedef struct jl_ep jl_ep;
+int jl_ep_create(jl_moe* local, int rank, int world, int max_tokens_per_rank,
+                 int topk, jl_ep** out);
+int jl_ep_ipc_handle(jl_ep* ep, void* handle64);
+int jl_ep_open_peers(jl_ep* ep, const void* handles64);
+int jl_ep_forward(jl_ep* ep, jl_moe* router, int l, const float* x, int B,
+                  float* out, void* stream);
+int jl_ep_destroy(jl_ep* ep);
+
 /* Debug / parity: copies (device) the router logits [B, E], the union
  * experts sel [U], offsets uh [U+1] and the slot map uidx/uw [B*topk] built
  * by the last jl_moe_forward (decode_kernel.c:1424-1485). *U_out (host)

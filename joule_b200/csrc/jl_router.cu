@@ -123,7 +123,9 @@ __device__ void route_token_warp(const float* logits_b, int E, int k, int norm, 
 }
 
 // ---------------------------------------------------------------------------
-// Dispatch by one block (decode_kernel.c:1449-1485, same outputs):
+// Dispatch by one block (decode_kernel.c:1449-1485, same outputs). A slot
+// whose expert id is -1 is padding: it takes no place in the union or the
+// slot map (batches received by expert parallelism are padded).
 //   sel[u]      experts in first-appearance order over the slots s = b*k + i
 //   uh[u]       exclusive prefix of per-expert slot counts, uh[U] = B*k
 //   uidx/uw     slots grouped by union position, increasing slot order inside
@@ -177,6 +179,7 @@ __device__ __forceinline__ void dispatch_block(const int* top, const float* tw, 
     const int s_lo = min(S, warp * per), s_hi = min(S, s_lo + per);
     for (int s = s_lo + lane; s < s_hi; s += 32) {
         const int e0 = top[s];
+        if (e0 == -1) continue;  // padding slot (expert-parallel receive batches)
         if (e0 < 0 || e0 >= E) atomicOr(ws.err, kErrBadExpert);
         const int e = clamp_e(e0, E);
         atomicMin(&first[e], s);
@@ -251,7 +254,7 @@ __device__ __forceinline__ void dispatch_block(const int* top, const float* tw, 
     __syncthreads();
     for (int c0 = s_lo; c0 < s_hi; c0 += 32) {
         const int s = c0 + lane;
-        const bool valid = s < s_hi;
+        const bool valid = s < s_hi && top[s] != -1;
         const int e = valid ? clamp_e(top[s], E) : -1 - lane;
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         if (valid) {

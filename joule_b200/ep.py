@@ -17,10 +17,11 @@ ranks, as the reference's serving loop batches its own sequences). One layer:
    starting from 0: the single-GPU combine, so the layer output is the same
    bits as one GPU running the same batch.
 
-The exchange is host-orchestrated (torch.distributed with the NCCL backend
-on GPUs, gloo on CPU for the tests); the compute sits behind a small backend
-so the same orchestration runs against the CUDA library or, in the tests,
-against the CPU oracle.
+Two forms of the exchange: ExpertParallelMoE orchestrates it from the host
+(torch.distributed all-to-all: NCCL on GPUs, gloo on CPU for the tests; the
+compute sits behind a small backend so the same code runs against the CUDA
+library or the CPU oracle), and P2PExpertParallelMoE runs it entirely in
+the library's kernels over NVLink peer memory (jl_ep_forward).
 """
 from __future__ import annotations
 
@@ -29,15 +30,23 @@ from typing import Protocol
 import torch
 import torch.distributed as dist
 
-__all__ = ["EPBackend", "ExpertParallelMoE", "CudaEPBackend"]
+__all__ = ["EPBackend", "ExpertParallelMoE", "CudaEPBackend", "P2PExpertParallelMoE"]
 
 
 class EPBackend(Protocol):
     def route(self, l: int, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(top [B, k] global expert ids, tw [B, k] fp32, comb [B, k] slot ids)."""
 
+    def pack(self, top: torch.Tensor, tw: torch.Tensor, x: torch.Tensor, world: int, E_local: int):
+        """Slots grouped by owner rank (slot order kept): (rows [S, d] in send
+        order, meta [S, 2] int32 (local expert, weight bits), pos [S] = send
+        row of slot s, counts [world] int32)."""
+
     def experts(self, l: int, rows: torch.Tensor, eid: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """y [n, d] = w[i] * FFN_{eid[i]}(rows[i]) over this rank's experts."""
+
+    def combine(self, back: torch.Tensor, pos: torch.Tensor, comb: torch.Tensor) -> torch.Tensor:
+        """out [B, d]: token b adds back[pos[comb[b, j]]], j = 0..k-1, from +0."""
 
 
 class ExpertParallelMoE:
@@ -55,42 +64,24 @@ class ExpertParallelMoE:
 
     def forward(self, l: int, x: torch.Tensor) -> torch.Tensor:
         top, tw, comb = self.backend.route(l, x)
-        B, k = top.shape
-        d = x.shape[1]
-        S = B * k
-        dest = torch.div(top.reshape(S).long(), self.E_local, rounding_mode="floor")
-        order = torch.argsort(dest, stable=True)  # slots grouped by owner, slot order inside
-        send_counts = torch.bincount(dest, minlength=self.world)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        send_splits = send_counts.tolist()
-        recv_splits = recv_counts.tolist()
+        rows, meta, pos, counts = self.backend.pack(top, tw, x, self.world, self.E_local)
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        send_splits, recv_splits = torch.stack([counts, recv_counts]).tolist()  # the one host sync
         nrecv = int(sum(recv_splits))
         self.last_counts = recv_splits
-        # payload: token rows, and (local expert, weight bits) pairs
-        send_rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
-        ds = dest[order]
-        meta = torch.stack([(top.reshape(S).long()[order] - ds * self.E_local).to(torch.int32),
-                            tw.reshape(S)[order].contiguous().view(torch.int32)], dim=1)
-        recv_rows = x.new_empty(nrecv, d)
+        recv_rows = x.new_empty(nrecv, x.shape[1])
         recv_meta = meta.new_empty(nrecv, 2)
-        dist.all_to_all_single(recv_rows, send_rows, recv_splits, send_splits, group=self.group)
+        dist.all_to_all_single(recv_rows, rows, recv_splits, send_splits, group=self.group)
         dist.all_to_all_single(recv_meta, meta, recv_splits, send_splits, group=self.group)
         if nrecv:
             y = self.backend.experts(l, recv_rows, recv_meta[:, 0].contiguous(),
                                      recv_meta[:, 1].contiguous().view(torch.float32))
         else:
             y = recv_rows
-        back = x.new_empty(S, d)
-        dist.all_to_all_single(back, y.contiguous(), send_splits, recv_splits, group=self.group)
-        y_slot = torch.empty_like(back)
-        y_slot[order] = back
-        # combine in the batch's union order, from +0 (the reference's ye loop)
-        out = torch.zeros(B, d, dtype=torch.float32, device=x.device)
-        comb = comb.long()
-        for j in range(k):
-            out = out + y_slot.index_select(0, comb[:, j])
-        return out
+        back = torch.empty_like(rows)
+        dist.all_to_all_single(back, y, send_splits, recv_splits, group=self.group)
+        return self.backend.combine(back, pos, comb)
 
 
 class CudaEPBackend:
@@ -111,6 +102,7 @@ class CudaEPBackend:
                                         cfg.norm_topk_prob), self.max_rows)
         if path is not None:
             self.local.set_path(path)
+        self._status = None  # device error word of jl_ep_pack
 
     def upload_layer(self, l: int, gate_w, packed, scales) -> None:
         """gate_w [E, d] bf16 bits (all experts); packed[p][e] / scales[p][e]
@@ -133,13 +125,87 @@ class CudaEPBackend:
     def route(self, l: int, x: torch.Tensor):
         return self.router.route(l, x)
 
+    def pack(self, top, tw, x, world: int, E_local: int):
+        from joule_b200.moe import _ptr, _stream
+        from joule_b200.native import check, get_dll
+        B, k = top.shape
+        S, d = B * k, x.shape[1]
+        dev = x.device
+        rows = torch.empty(S, d, dtype=torch.float32, device=dev)
+        meta = torch.empty(S, 2, dtype=torch.int32, device=dev)
+        pos = torch.empty(S, dtype=torch.int32, device=dev)
+        counts = torch.empty(world, dtype=torch.int32, device=dev)
+        if self._status is None:
+            self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+        check(get_dll().jl_ep_pack(_ptr(top), _ptr(tw), _ptr(x), B, k, d, E_local, world, _ptr(rows),
+                                   _ptr(meta), _ptr(pos), _ptr(counts), _ptr(self._status),
+                                   _stream(None)), "jl_ep_pack")
+        return rows, meta, pos, counts
+
     def experts(self, l: int, rows: torch.Tensor, eid: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         return self.local.forward_routed(l, rows.contiguous(), eid.view(-1, 1), w.view(-1, 1))
+
+    def combine(self, back, pos, comb):
+        from joule_b200.moe import _ptr, _stream
+        from joule_b200.native import check, get_dll
+        B, k = comb.shape
+        out = torch.empty(B, back.shape[1], dtype=torch.float32, device=back.device)
+        check(get_dll().jl_ep_combine(_ptr(back), _ptr(pos), _ptr(comb), B, k, back.shape[1],
+                                      _ptr(out), _stream(None)), "jl_ep_combine")
+        return out
 
     def check(self) -> None:
         self.router.check()
         self.local.check()
+        if self._status is not None and int(self._status.item()):
+            raise RuntimeError("jl_ep_pack: expert id outside the ranks' experts")
 
     def close(self) -> None:
         self.router.close()
         self.local.close()
+
+
+class P2PExpertParallelMoE:
+    """The same layer with the exchange done by the library's own kernels
+    over NVLink peer memory (jl_ep_*): no host synchronisation and no NCCL
+    call per layer. Set-up exchanges one CUDA IPC handle per rank with an
+    NCCL all-gather; every rank must then call forward for the same layers
+    in the same order."""
+
+    def __init__(self, backend: CudaEPBackend, max_tokens: int, group=None):
+        import ctypes
+        from joule_b200.native import check, get_dll
+        self.backend = backend
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.max_tokens = max_tokens
+        self._L = get_dll()
+        ep = ctypes.c_void_p()
+        check(self._L.jl_ep_create(backend.local.h, self.rank, self.world, max_tokens,
+                                   backend.cfg.topk, ctypes.byref(ep)), "jl_ep_create")
+        self.ep = ep
+        mine = (ctypes.c_char * 64)()
+        check(self._L.jl_ep_ipc_handle(ep, mine), "jl_ep_ipc_handle")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        t = torch.frombuffer(bytearray(mine.raw), dtype=torch.uint8).to(dev)
+        allh = torch.empty(self.world * 64, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(allh, t, group=group)
+        hs = allh.cpu().numpy()
+        check(self._L.jl_ep_open_peers(ep, hs.ctypes.data), "jl_ep_open_peers")
+        dist.barrier(group=group)
+
+    def forward(self, l: int, x: torch.Tensor, out: torch.Tensor | None = None, stream=None):
+        from joule_b200.moe import _ptr, _stream
+        from joule_b200.native import check
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        check(self._L.jl_ep_forward(self.ep, self.backend.router.h, l, _ptr(x), x.shape[0], _ptr(out),
+                                    _stream(stream)), "jl_ep_forward")
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "ep", None) and self.ep.value:
+            self._L.jl_ep_destroy(self.ep)
+            self.ep = None

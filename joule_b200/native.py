@@ -83,6 +83,13 @@ SIGNATURES = {
     "jl_moe_set_phase_events": ([_P, _P, _I], _I),
     "jl_moe_trace": ([_P, _I, _P, _I, _P], _I),
     "jl_route_noalloc": ([_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P], _I),
+    "jl_ep_pack": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P], _I),
+    "jl_ep_combine": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
+    "jl_ep_create": ([_P, _I, _I, _I, _I, ctypes.POINTER(_P)], _I),
+    "jl_ep_ipc_handle": ([_P, _P], _I),
+    "jl_ep_open_peers": ([_P, _P], _I),
+    "jl_ep_forward": ([_P, _P, _I, _P, _I, _P, _P], _I),
+    "jl_ep_destroy": ([_P], _I),
     "jl_moe_device_bytes": ([_P], _LL),
     "jl_version": ([], ctypes.c_char_p),
 }

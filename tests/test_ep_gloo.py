@@ -49,6 +49,26 @@ class OracleBackend:
             comb[b] = sorted(range(b * k, b * k + k), key=lambda s: upos[int(top.flat[s])])
         return torch.from_numpy(top), torch.from_numpy(tw), torch.from_numpy(comb)
 
+    def pack(self, top, tw, x, world, E_local):
+        B, k = top.shape
+        S = B * k
+        dest = torch.div(top.reshape(S).long(), E_local, rounding_mode="floor")
+        order = torch.argsort(dest, stable=True)  # send row r holds slot order[r]
+        pos = torch.empty(S, dtype=torch.int64)
+        pos[order] = torch.arange(S)
+        rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+        meta = torch.stack([(top.reshape(S).long()[order] % E_local).to(torch.int32),
+                            tw.reshape(S)[order].contiguous().view(torch.int32)], dim=1)
+        counts = torch.bincount(dest, minlength=world).to(torch.int32)
+        return rows, meta, pos, counts
+
+    def combine(self, back, pos, comb):
+        B, k = comb.shape
+        out = torch.zeros(B, back.shape[1], dtype=torch.float32)
+        for j in range(k):
+            out = out + back.index_select(0, pos[comb[:, j].long()])
+        return out
+
     def experts(self, l, rows, eid, w):
         from oracle import restate
         lay, m, d = self.lay, self.lay.m, self.lay.d

@@ -1,4 +1,5 @@
-"""Expert parallelism on 2 GPUs over NCCL (needs >= 2 GPUs; skipped otherwise).
+"""Expert parallelism on 2 GPUs (needs >= 2 GPUs; skipped otherwise), with the
+host-orchestrated NCCL exchange and with the library's peer-memory exchange.
 
 Each rank stores half of the Qwen3-shape layer's experts and routes its own
 tokens; with the exact expert path forced on the rank-local handles, every
@@ -24,7 +25,7 @@ def _free_port() -> int:
     return port
 
 
-def _rank(rank: int, world: int, port: int, B: int, results):
+def _rank(rank: int, world: int, port: int, B: int, results, p2p: bool = False):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -46,25 +47,36 @@ def _rank(rank: int, world: int, port: int, B: int, results):
                            world, path=PATH_EXACT)
         be.upload_layer(0, lay.gate_w, lay.packed, lay.scales)
         x = olayer.hidden(B, lay.d, 200 + rank)
-        ep = ExpertParallelMoE(be, lay.E)
-        out = ep.forward(0, torch.from_numpy(x).cuda()).cpu().numpy()
+        if p2p:
+            from joule_b200.ep import P2PExpertParallelMoE
+            ep = P2PExpertParallelMoE(be, B)
+            xd = torch.from_numpy(x).cuda()
+            out = ep.forward(0, xd).cpu().numpy()
+            out2 = ep.forward(0, xd).cpu().numpy()  # a second call (next epoch) gives the same bits
+        else:
+            ep = ExpertParallelMoE(be, lay.E)
+            out = ep.forward(0, torch.from_numpy(x).cuda()).cpu().numpy()
+            out2 = out
         torch.cuda.synchronize()
         be.check()
         ref, _, _ = restate.moe_layer(lay, x)
-        results[rank] = (bool(np.array_equal(out, ref)), float(np.abs(out - ref).max()))
+        results[rank] = (bool(np.array_equal(out, ref) and np.array_equal(out2, ref)),
+                         float(np.abs(out - ref).max()))
+        if p2p:
+            ep.close()
         be.close()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("B", [1, 5])
-def test_ep_two_gpus_bit_exact(B):
+@pytest.mark.parametrize("B,p2p", [(1, False), (5, False), (1, True), (5, True)])
+def test_ep_two_gpus_bit_exact(B, p2p):
     import torch.multiprocessing as mp
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_rank, args=(2, _free_port(), B, results), nprocs=2, start_method="spawn",
-                           join=True)
+        mp.start_processes(_rank, args=(2, _free_port(), B, results, p2p), nprocs=2,
+                           start_method="spawn", join=True)
         res = dict(results)
     assert sorted(res) == [0, 1]
     for r, (same, err) in res.items():
