@@ -170,6 +170,9 @@ int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
 #define JL_PATH_AUTO 0  /* exact for B <= 8, tensor-core beyond (d % 512 == 0, m % 256 == 0) */
 #define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order */
 #define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
+#define JL_PATH_EXACT_FUSED 3 /* the exact path for B <= 8 as ONE persistent launch (router, top-k,
+                                dispatch, gate/up, down, combine), same results; larger B runs as
+                                JL_PATH_EXACT */
 int jl_moe_set_path(jl_moe* h, int path);
 
 /* One MoE FFN layer: out[B, d] = MoE(x[B, d]) for layer l (device fp32).
@@ -310,6 +313,11 @@ long long jl_moe_device_bytes(const jl_moe* h);
 
 /* Library version string, e.g. "joule_b200 0.1 sm_100a". */
 const char* jl_version(void);
+
+/* Text of the CUDA runtime error behind the most recent JL_ERR_CUDA of any
+ * call in this process ("" when none). No counterpart in the reference,
+ * whose calls return void. */
+const char* jl_last_cuda_error(void);
 
 #ifdef __cplusplus
 }

@@ -7,10 +7,13 @@
 
 #include "joule_moe.h"
 
+// Records a failed CUDA runtime call (jl_last_cuda_error) and returns JL_ERR_CUDA.
+int jl_note_cuda(cudaError_t e);
+
 #define JL_CUDA(call)                                   \
     do {                                                \
         cudaError_t _e = (call);                        \
-        if (_e != cudaSuccess) return JL_ERR_CUDA;      \
+        if (_e != cudaSuccess) return jl_note_cuda(_e); \
     } while (0)
 
 #define JL_LAUNCH_CHECK()                                   \
@@ -246,8 +249,8 @@ inline int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...) == cudaSuccess ? JL_OK
-                                                                                       : JL_ERR_CUDA;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    return e == cudaSuccess ? JL_OK : jl_note_cuda(e);
 }
 
 }  // namespace jl

@@ -6,6 +6,7 @@
 
 #include "jl_common.cuh"
 #include "jl_internal.h"
+#include "jl_route.cuh"
 #include "jl_tiles.cuh"
 
 #include <algorithm>
@@ -14,8 +15,6 @@ namespace jl {
 
 constexpr int kRouteEPB = 4;      // experts per router block
 constexpr int kRouteTB = 8;       // tokens per router block (one warp each)
-constexpr int kMaxK = 16;         // top-k capacity (the reference caps topk at 16, ws_init)
-constexpr int kMaxE = 256;
 
 // ---------------------------------------------------------------------------
 // Per-token softmax / top-k / renorm by one warp (decode_kernel.c:1425-1448).
@@ -137,22 +136,6 @@ __device__ void route_token_warp(const float* logits_b, int E, int k, int norm, 
 // chunks): O(B*k / threads + E) work, no quadratic search.
 __host__ __device__ inline int dispatch_smem_ints(int E, int W) { return 6 * E + 36 + W * E; }
 
-__device__ __forceinline__ int clamp_e(int e, int E) { return (e < 0 || e >= E) ? 0 : e; }
-
-// comb: token b's slots in the union order of their experts (stable for
-// equal positions). Slot s goes to position #{i2 : (u[i2], i2) < (u[i], i)}
-// of its token's k-slot list.
-__device__ __forceinline__ void comb_slot(const int* top, const int* upos, int s, int k, int E,
-                                          int* comb) {
-    const int b = s / k, i = s - b * k;
-    const int u = upos[clamp_e(top[s], E)];
-    int r = 0;
-    for (int i2 = 0; i2 < k; i2++) {
-        const int u2 = upos[clamp_e(top[b * k + i2], E)];
-        r += (u2 < u) || (u2 == u && i2 < i);
-    }
-    comb[b * k + r] = s;
-}
 
 __device__ __forceinline__ void dispatch_block(const int* top, const float* tw, int B, int k, int E,
                                const jl_ws& ws, int* sm) {
@@ -337,199 +320,6 @@ __global__ void k_router(const uint16_t* __restrict__ gate_w, const float* __res
     dispatch_block(ws.top, ws.tw, B, k, E, ws, reinterpret_cast<int*>(smem) + TB * kMaxE);
 }
 
-// ---------------------------------------------------------------------------
-// Routing of up to 8 tokens by one whole CTA (decode_kernel.c:1425-1448).
-// G = blockDim / next_pow2(nb) threads share a token and synchronise on
-// named barrier 1 + token. Same arithmetic as route_token_warp: max,
-// expf_fast, a SEQUENTIAL sum in expert order (one thread; loads run ahead of
-// the dependent adds), division, top-k, sequential renorm. The top-k ranks
-// every expert by a 64-bit key (p bits << 32 | ~e): p >= 0, so a larger key
-// means a larger p or, for equal p, a smaller index — the order in which the
-// reference's k strict-'>' argmax passes pick. With G >= 2E two threads
-// share an expert's comparisons.
-__device__ __forceinline__ void named_barrier(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-__host__ __device__ inline int route_scratch_bytes(int E) {
-    const int Ep = (E + 3) & ~3;
-    return Ep * 8 + Ep * 4 + 2 * Ep * 4 + 64 * 4;  // keys, p, rank halves, misc
-}
-
-__device__ __forceinline__ void route_tokens_cta(const float* lg_s, int nb, int b0, int E, int k, int norm,
-                                 const jl_ws& ws, uint8_t* scratch) {
-    const int T = blockDim.x, tid = threadIdx.x;
-    const int nbp = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8;
-    const int G = T / nbp, tb = tid / G, gl = tid % G;
-    const int Ep = (E + 3) & ~3;
-    uint8_t* base = scratch + (size_t)tb * route_scratch_bytes(E);
-    unsigned long long* key_s = reinterpret_cast<unsigned long long*>(base);
-    float* p_s = reinterpret_cast<float*>(base + Ep * 8);
-    int* rk_s = reinterpret_cast<int*>(p_s + Ep);  // [2][Ep] partial ranks
-    float* misc = reinterpret_cast<float*>(rk_s + 2 * Ep);  // [0..7] warp maxima, [8] sum, [16..31] top-k p
-    const int bar_id = 1 + tb;
-    if (tb < nb) {
-        const float* lg = lg_s + tb * E;
-        float mx = -1e30f;
-        for (int e = gl; e < E; e += G) mx = fmaxf(mx, lg[e]);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if ((gl & 31) == 0) misc[gl >> 5] = mx;
-        named_barrier(bar_id, G);
-        mx = misc[0];
-        for (int w = 1; w < G / 32; w++) mx = fmaxf(mx, misc[w]);
-        for (int e = gl; e < Ep; e += G) p_s[e] = (e < E) ? expf_fast(__fsub_rn(lg[e], mx)) : 0.0f;
-        named_barrier(bar_id, G);
-        if (gl == 0) {  // zeros past E leave the positive sum unchanged
-            const float4* q4 = reinterpret_cast<const float4*>(p_s);
-            const int n4 = Ep / 4;
-            float sum = 0.0f;
-            float4 cur[8], nxt[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) cur[i] = i < n4 ? q4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int c = 0; c < n4; c += 8) {
-#pragma unroll
-                for (int i = 0; i < 8; i++)
-                    nxt[i] = c + 8 + i < n4 ? q4[c + 8 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    sum = __fadd_rn(sum, cur[i].x);
-                    sum = __fadd_rn(sum, cur[i].y);
-                    sum = __fadd_rn(sum, cur[i].z);
-                    sum = __fadd_rn(sum, cur[i].w);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) cur[i] = nxt[i];
-            }
-            misc[8] = sum;
-        }
-        named_barrier(bar_id, G);
-        const float sum = misc[8];
-        for (int e = gl; e < E; e += G) {
-            const float pe = __fdiv_rn(p_s[e], sum);
-            p_s[e] = pe;
-            key_s[e] = ((unsigned long long)__float_as_uint(pe) << 32) | (0xFFFFFFFFu - (unsigned)e);
-        }
-        named_barrier(bar_id, G);
-        const int halves = G >= 2 * E ? 2 : 1;
-        const int span = E / halves;  // E is even when halves == 2 (E <= G / 2, G a power of 2)
-        for (int i = gl; i < E * halves; i += G) {
-            const int e = i % E, h = i / E;
-            const unsigned long long me = key_s[e];
-            const int lo = h * span, hi = h == halves - 1 ? E : lo + span;
-            int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
-            int e2 = lo;
-            for (; e2 + 4 <= hi; e2 += 4) {
-                r0 += key_s[e2] > me;
-                r1 += key_s[e2 + 1] > me;
-                r2 += key_s[e2 + 2] > me;
-                r3 += key_s[e2 + 3] > me;
-            }
-            for (; e2 < hi; e2++) r0 += key_s[e2] > me;
-            rk_s[h * Ep + e] = r0 + r1 + r2 + r3;
-        }
-        named_barrier(bar_id, G);
-        for (int e = gl; e < E; e += G) {
-            const int rank = rk_s[e] + (halves == 2 ? rk_s[Ep + e] : 0);
-            if (rank < k) {
-                ws.top[(b0 + tb) * k + rank] = e;
-                misc[16 + rank] = p_s[e];
-            }
-        }
-        named_barrier(bar_id, G);
-        if (gl < k) {
-            float w = misc[16 + gl];
-            if (norm) {
-                float ssum = 0.0f;
-                for (int i = 0; i < k; i++) ssum = __fadd_rn(ssum, misc[16 + i]);
-                w = __fdiv_rn(w, ssum);
-            }
-            ws.tw[(b0 + tb) * k + gl] = w;
-        }
-    }
-    __syncthreads();
-}
-
-// Dispatch for S = B*k <= 128 slots by warp 0 alone (no block barriers):
-// union positions in first-appearance order from __match_any_sync leaders,
-// offsets by a warp scan, ranks inside an expert by running counts.
-// Same outputs as dispatch_block. `sm` holds 4*E + 2 ints.
-__device__ __forceinline__ void dispatch_warp_small(const int* top, const float* tw, int B, int k, int E,
-                                    const jl_ws& ws, int* sm) {
-    const int lane = threadIdx.x & 31, S = B * k;
-    const unsigned lt = (1u << lane) - 1u;
-    int* upos = sm;          // [E]
-    int* cnt = upos + E;     // [E]
-    int* run = cnt + E;      // [E]
-    int* sel_s = run + E;    // [E]
-    for (int e = lane; e < E; e += 32) {
-        upos[e] = -1;
-        cnt[e] = 0;
-        run[e] = 0;
-    }
-    __syncwarp();
-    int U = 0;
-    for (int c0 = 0; c0 < S; c0 += 32) {
-        const int s = c0 + lane;
-        const bool valid = s < S;
-        int e = valid ? top[s] : -1 - lane;
-        if (valid && (e < 0 || e >= E)) {
-            atomicOr(ws.err, kErrBadExpert);
-            e = 0;
-        }
-        const unsigned peers = __match_any_sync(0xffffffffu, e);
-        const bool leader = valid && lane == __ffs(peers) - 1;
-        const bool fresh = leader && upos[e] < 0;
-        const unsigned bal = __ballot_sync(0xffffffffu, fresh);
-        if (fresh) {
-            const int u = U + __popc(bal & lt);
-            upos[e] = u;
-            sel_s[u] = e;
-            ws.sel[u] = e;
-        }
-        if (leader) cnt[e] += __popc(peers);
-        U += __popc(bal);
-        __syncwarp();
-    }
-    int acc = 0;
-    for (int u0 = 0; u0 < U; u0 += 32) {
-        const int u = u0 + lane;
-        const int c = u < U ? cnt[sel_s[u]] : 0;
-        int inc = c;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += t;
-        }
-        if (u < U) {
-            ws.uh[u] = acc + inc - c;
-            run[sel_s[u]] = acc + inc - c;  // start offset; ranks are added below
-        }
-        acc += __shfl_sync(0xffffffffu, inc, 31);
-    }
-    if (lane == 0) {
-        ws.uh[U] = acc;
-        *ws.U = U;
-    }
-    __syncwarp();
-    for (int c0 = 0; c0 < S; c0 += 32) {
-        const int s = c0 + lane;
-        const bool valid = s < S;
-        int e = valid ? top[s] : -1 - lane;
-        if (valid && (e < 0 || e >= E)) e = 0;
-        const unsigned peers = __match_any_sync(0xffffffffu, e);
-        if (valid) {
-            const int pos = run[e] + __popc(peers & lt);
-            ws.uidx[pos] = s;
-            ws.uw[pos] = tw[s];
-            ws.slot_pos[s] = pos;
-        }
-        __syncwarp();
-        if (valid && lane == __ffs(peers) - 1) run[e] += __popc(peers);
-        __syncwarp();
-    }
-    for (int s = lane; s < S; s += 32) comb_slot(top, upos, s, k, E, ws.comb);
-}
 
 // ---------------------------------------------------------------------------
 // Router on 8-CTA thread-block clusters, one cluster per group of TPC tokens
@@ -548,83 +338,6 @@ constexpr int kMaxTPC = 8;
 __host__ __device__ inline int route_tpc(int B) {  // tokens per cluster: 1, 2, 4 or 8
     const int t = (B + 31) / 32;
     return t <= 1 ? 1 : t <= 2 ? 2 : t <= 4 ? 4 : kMaxTPC;
-}
-
-// Shared-memory rows of the cluster router: router row (expert ee, lane j)
-// holds that lane's d/8 bf16 weights plus 8 halves of padding, exactly as the
-// lane-major HBM layout keeps them (one bulk copy per CTA); token row (tb, j)
-// holds x[tb][j + 8t] for t < d/8, padded by 4 floats. With rows 16 bytes
-// apart modulo 128, the 8 lanes x 4 experts of a warp read distinct banks.
-__host__ __device__ inline int router_gstride(int d) { return router_row_halves(d); }  // halves
-__host__ __device__ inline int router_xstride(int d) { return d / 8 + 4; }             // floats
-
-// Thread t < ne*8 owns lane j = t % 8 of expert ee = t / 8 for all NB tokens
-// of the cluster (nb <= NB live; the rest recompute token 0 and are not
-// stored). Each step reads the lane's next 8 weights (one 16-byte load,
-// shared by the NB tokens) and 8 activations per token (two), and the loads
-// of step t + 8 are issued before the FMAs of step t: the dependent FMA chain
-// of each (token, lane), in k order as the reference's lane j, sets the pace.
-template <int NB>
-__device__ __forceinline__ void cluster_logits(const uint16_t* g_s, const float* x_s, int d, int nb,
-                                               int E, int e0, int ne, int b0, float* lg_lead,
-                                               float* lg_glob) {
-    const int tid = threadIdx.x;
-    if ((tid & ~31) >= ne * 8) return;  // whole warp idle (warp-uniform)
-    const int gs = router_gstride(d), xs = router_xstride(d), c8 = d / 8;
-    const int live = tid < ne * 8;
-    const int j = tid & 7, ee = live ? tid >> 3 : 0;
-    const uint16_t* gp = g_s + (size_t)(ee * 8 + j) * gs;
-    const float* xp[NB];
-#pragma unroll
-    for (int r = 0; r < NB; r++) xp[r] = x_s + (size_t)((r < nb ? r : 0) * 8 + j) * xs;
-    float acc[NB];
-    float4 xc0[NB], xc1[NB];
-    uint4 gc = *reinterpret_cast<const uint4*>(gp);
-#pragma unroll
-    for (int r = 0; r < NB; r++) {
-        acc[r] = 0.0f;
-        xc0[r] = *reinterpret_cast<const float4*>(xp[r]);
-        xc1[r] = *reinterpret_cast<const float4*>(xp[r] + 4);
-    }
-    for (int t0 = 0; t0 < c8; t0 += 8) {
-        const int tn = (t0 + 8 < c8) ? t0 + 8 : t0;
-        const uint4 gn = *reinterpret_cast<const uint4*>(gp + tn);
-        float4 xn0[NB], xn1[NB];
-#pragma unroll
-        for (int r = 0; r < NB; r++) {
-            xn0[r] = *reinterpret_cast<const float4*>(xp[r] + tn);
-            xn1[r] = *reinterpret_cast<const float4*>(xp[r] + tn + 4);
-        }
-        const uint32_t w[4] = {gc.x, gc.y, gc.z, gc.w};
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const float lo = __uint_as_float(w[q] << 16), hi = __uint_as_float(w[q] & 0xFFFF0000u);
-#pragma unroll
-            for (int r = 0; r < NB; r++) {
-                const float x0 = q == 0 ? xc0[r].x : q == 1 ? xc0[r].z : q == 2 ? xc1[r].x : xc1[r].z;
-                const float x1 = q == 0 ? xc0[r].y : q == 1 ? xc0[r].w : q == 2 ? xc1[r].y : xc1[r].w;
-                acc[r] = __fmaf_rn(lo, x0, acc[r]);
-                acc[r] = __fmaf_rn(hi, x1, acc[r]);
-            }
-        }
-        gc = gn;
-#pragma unroll
-        for (int r = 0; r < NB; r++) {
-            xc0[r] = xn0[r];
-            xc1[r] = xn1[r];
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < NB; r++) {
-        float a = acc[r];
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        if (live && j == 0 && r < nb) {
-            lg_lead[r * E + e0 + ee] = a;
-            lg_glob[(size_t)(b0 + r) * E + e0 + ee] = a;
-        }
-    }
 }
 
 __host__ __device__ inline int dispatch_smem_bytes(int B, int k, int E) {
@@ -692,7 +405,12 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kClusterT
     if (rank != 0) return;
     trace_point(tr, kTraceRouter, 4);
     // leader: the staging area is free; routing scratch, then dispatch scratch
-    route_tokens_cta(lg_s, nb, b0, E, k, norm, ws, smem);
+    if ((int)(threadIdx.x >> 5) < nb) {  // one warp per token
+        const int w = threadIdx.x >> 5;
+        route_token_lean(lg_s + (size_t)w * E, E, k, norm, ws.top + (b0 + w) * k, ws.tw + (b0 + w) * k,
+                         reinterpret_cast<float*>(smem) + w * kMaxE);
+    }
+    __syncthreads();
     trace_point(tr, kTraceRouter, 5);
     if (!fuse_dispatch) return;  // k_dispatch follows
     if (nclusters > 1) {
@@ -756,16 +474,37 @@ __global__ void k_topk(const float* __restrict__ logits, int B, int E, int k, in
                      p_all + warp * kMaxE);
 }
 
-__global__ void k_dispatch(int B, int k, int E, jl_ws ws) {
+__global__ void k_dispatch(int B, int k, int E, jl_ws ws, int stage) {
     extern __shared__ __align__(16) int dsm[];
     griddep_wait();
     griddep_launch_dependents();
-    dispatch_block(ws.top, ws.tw, B, k, E, ws, dsm);
+    if (stage) {  // the routing in shared memory: the dispatch reads each slot several times
+        const int S = B * k;
+        int* top_s = dsm;
+        float* tw_s = reinterpret_cast<float*>(top_s + S);
+        for (int i = threadIdx.x; i < S; i += blockDim.x) {
+            top_s[i] = __ldcg(ws.top + i);
+            tw_s[i] = __ldcg(ws.tw + i);
+        }
+        __syncthreads();
+        dispatch_block(top_s, tw_s, B, k, E, ws, reinterpret_cast<int*>(tw_s + S));
+    } else {
+        dispatch_block(ws.top, ws.tw, B, k, E, ws, dsm);
+    }
     __syncthreads();
     if (threadIdx.x < 32) tc_build_tiles(ws);
 }
 
 }  // namespace jl
+
+// k_dispatch with the routing staged in shared memory when it fits.
+static int launch_dispatch(const jl_ws& ws, int B, int k, int E, cudaStream_t s) {
+    using namespace jl;
+    const int T = 1024;
+    const size_t base = (size_t)dispatch_smem_ints(E, T / 32) * 4, staged = base + (size_t)B * k * 8;
+    const int stage = staged <= 220 * 1024;
+    return launch(k_dispatch, dim3(1), dim3(T), stage ? staged : base, s, B, k, E, ws, stage);
+}
 
 int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float* x, int B,
                     bool tiles, cudaStream_t s) {
@@ -785,17 +524,15 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
     const size_t stage = (size_t)EPC * 8 * router_gstride(d) * 2 + (size_t)tpc * 8 * router_xstride(d) * 4;
     // the dispatch runs in the last leader when its scratch fits, else in k_dispatch
     const size_t dsp = (size_t)dispatch_smem_bytes(B, k, E);
-    const int fuse = dsp <= 64 * 1024;
-    const size_t tail = std::max((size_t)kMaxTPC * route_scratch_bytes(E), fuse ? dsp : (size_t)0);
+    const int fuse = dsp <= 64 * 1024 && B <= 32;
+    const size_t tail = std::max((size_t)kMaxTPC * kMaxE * 4, fuse ? dsp : (size_t)0);
     const size_t lg_off = (std::max(stage, tail) + 127) / 128 * 128;
     const size_t smem = lg_off + (size_t)tpc * E * 4;
     if (smem > 220 * 1024) return JL_ERR_INVALID;
     int rc = launch(k_router_cluster, dim3(kClusterCTAs * ncl), dim3(kClusterThreads), smem, s, gate_w_l,
                     x, B, E, d, k, h->norm, h->ws, tpc, (int)lg_off, fuse, tiles ? 1 : 0);
     if (rc || fuse) return rc;
-    const int T = 1024;
-    return launch(k_dispatch, dim3(1), dim3(T), (size_t)dispatch_smem_ints(E, T / 32) * 4, s, B, k, E,
-                  h->ws);
+    return launch_dispatch(h->ws, B, k, E, s);
 }
 
 int jl_launch_dispatch(const jl_moe* h, int B, cudaStream_t s) {
@@ -806,9 +543,7 @@ int jl_launch_dispatch(const jl_moe* h, int B, cudaStream_t s) {
         JL_CUDA(cudaFuncSetAttribute(k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
         attr = true;
     }
-    const int T = 1024;
-    return launch(k_dispatch, dim3(1), dim3(T), (size_t)dispatch_smem_ints(h->E, T / 32) * 4, s, B, h->k,
-                  h->E, h->ws);
+    return launch_dispatch(h->ws, B, h->k, h->E, s);
 }
 
 // Routing only, into buffers the caller chooses: k_router (no fused tail)

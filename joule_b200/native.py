@@ -23,13 +23,19 @@ ERRORS = {
     -6: "JL_ERR_NOT_READY: layer not uploaded",
     -7: "JL_ERR_DEVICE: kernel reported a bad index/state",
 }
-PATH_AUTO, PATH_EXACT, PATH_TC = 0, 1, 2
+PATH_AUTO, PATH_EXACT, PATH_TC, PATH_EXACT_FUSED = 0, 1, 2, 3
 CREATE_ROUTER_ONLY = 1
 
 
 class JouleError(RuntimeError):
     def __init__(self, code: int, where: str):
-        super().__init__(f"{where}: {ERRORS.get(code, f'error {code}')}")
+        msg = f"{where}: {ERRORS.get(code, f'error {code}')}"
+        if code == -3:  # JL_ERR_CUDA
+            try:
+                msg += f" ({get_dll().jl_last_cuda_error().decode()})"
+            except Exception:  # the message is best effort
+                pass
+        super().__init__(msg)
         self.code = code
 
 
@@ -92,6 +98,7 @@ SIGNATURES = {
     "jl_ep_destroy": ([_P], _I),
     "jl_moe_device_bytes": ([_P], _LL),
     "jl_version": ([], ctypes.c_char_p),
+    "jl_last_cuda_error": ([], ctypes.c_char_p),
 }
 
 
