@@ -476,8 +476,10 @@ __global__ void k_topk(const float* __restrict__ logits, int B, int E, int k, in
 
 __global__ void k_dispatch(int B, int k, int E, jl_ws ws, int stage) {
     extern __shared__ __align__(16) int dsm[];
+    trace_point(ws.trace, kTraceRouter, 10);
     griddep_wait();
     griddep_launch_dependents();
+    trace_point(ws.trace, kTraceRouter, 11);
     if (stage) {  // the routing in shared memory: the dispatch reads each slot several times
         const int S = B * k;
         int* top_s = dsm;
@@ -491,8 +493,188 @@ __global__ void k_dispatch(int B, int k, int E, jl_ws ws, int stage) {
     } else {
         dispatch_block(ws.top, ws.tw, B, k, E, ws, dsm);
     }
+    trace_point(ws.trace, kTraceRouter, 12);
     __syncthreads();
     if (threadIdx.x < 32) tc_build_tiles(ws);
+    trace_point(ws.trace, kTraceRouter, 13);
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch of router output (every token's k experts distinct) by one block
+// in a few barrier-separated steps, same outputs as dispatch_block plus the
+// tensor-core tile table (tc_build_tiles):
+//   1. per slot: first slot and slot count of its expert (shared atomics),
+//      and the token's bit in its expert's token mask
+//   2. per expert with slots: its first slot's bit in a slot mask; per
+//      expert, prefix popcounts of its token mask words
+//   3. prefix popcounts of the slot mask words: a union position is the
+//      number of experts whose first slot comes earlier (first appearance)
+//   4. one block scan over union positions of (slots, tiles, padded rows)
+//   5. per slot: its rank inside its expert = earlier tokens that chose the
+//      same expert (slot order, since each token holds an expert at most once)
+constexpr int kDfThreads = 512;
+
+__host__ __device__ inline size_t dispatch_fast_smem(int B, int k, int E) {
+    const size_t S = (size_t)B * k, NW = (B + 31) / 32, NF = (S + 31) / 32;
+    return (2 * S + 5 * (size_t)E + 2 * NF + 2 * (size_t)E * NW + 3 * 32 + 4) * 4;
+}
+
+__global__ void __launch_bounds__(kDfThreads) k_dispatch_fast(int B, int k, int E, jl_ws ws) {
+    extern __shared__ __align__(16) int sm[];
+    trace_point(ws.trace, kTraceRouter, 10);
+    griddep_wait();
+    griddep_launch_dependents();
+    trace_point(ws.trace, kTraceRouter, 11);
+    const int S = B * k, NW = (B + 31) >> 5, NF = (S + 31) >> 5;
+    const int T = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int* top = sm;
+    float* tw = reinterpret_cast<float*>(top + S);
+    int* first = reinterpret_cast<int*>(tw + S);
+    int* cnt = first + E;
+    int* upos = cnt + E;
+    int* sel = upos + E;
+    int* ustart = sel + E;
+    unsigned* fflag = reinterpret_cast<unsigned*>(ustart + E);
+    int* fpre = reinterpret_cast<int*>(fflag + NF);
+    unsigned* tmask = reinterpret_cast<unsigned*>(fpre + NF);
+    int* tpre = reinterpret_cast<int*>(tmask + (size_t)E * NW);
+    int* wsum = tpre + (size_t)E * NW;  // [3][32]
+    int* misc = wsum + 96;
+    for (int i = tid; i < S; i += T) {
+        top[i] = __ldcg(ws.top + i);
+        tw[i] = __ldcg(ws.tw + i);
+    }
+    for (int e = tid; e < E; e += T) {
+        first[e] = INT_MAX;
+        cnt[e] = 0;
+    }
+    for (int i = tid; i < NF; i += T) fflag[i] = 0u;
+    for (int i = tid; i < E * NW; i += T) tmask[i] = 0u;
+    __syncthreads();
+    for (int s = tid; s < S; s += T) {
+        int e = top[s];
+        if (e < 0 || e >= E) {
+            atomicOr(ws.err, kErrBadExpert);
+            e = 0;
+            top[s] = 0;
+        }
+        const int b = s / k;
+        atomicMin(&first[e], s);
+        atomicAdd(&cnt[e], 1);
+        atomicOr(&tmask[e * NW + (b >> 5)], 1u << (b & 31));
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += T) {
+        if (cnt[e] > 0) atomicOr(&fflag[first[e] >> 5], 1u << (first[e] & 31));
+        int run = 0;
+        for (int w = 0; w < NW; w++) {
+            tpre[e * NW + w] = run;
+            run += __popc(tmask[e * NW + w]);
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int run = 0;
+        for (int w0 = 0; w0 < NF; w0 += 32) {
+            const int w = w0 + lane;
+            const int c = w < NF ? __popc(fflag[w]) : 0;
+            int inc = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += a;
+            }
+            if (w < NF) fpre[w] = run + inc - c;
+            run += __shfl_sync(0xffffffffu, inc, 31);
+        }
+        if (lane == 0) misc[0] = run;
+    }
+    __syncthreads();
+    const int U = misc[0];
+    for (int e = tid; e < E; e += T) {
+        if (cnt[e] > 0) {
+            const int f = first[e];
+            const int u = fpre[f >> 5] + __popc(fflag[f >> 5] & ((1u << (f & 31)) - 1u));
+            upos[e] = u;
+            sel[u] = e;
+            ws.sel[u] = e;
+        } else {
+            upos[e] = -1;
+        }
+    }
+    __syncthreads();
+    // union-order scans (U <= E <= 256: warps 0..7 hold one position each)
+    {
+        const int u = tid;
+        int n = 0, t = 0, r = 0;
+        if (u < U) {
+            n = cnt[sel[u]];
+            t = (n + kTcNT - 1) / kTcNT;
+            r = tc_rows(n);
+        }
+        int ni = n, ti = t, ri = r;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xffffffffu, ni, o);
+            const int b2 = __shfl_up_sync(0xffffffffu, ti, o);
+            const int c2 = __shfl_up_sync(0xffffffffu, ri, o);
+            if (lane >= o) {
+                ni += a;
+                ti += b2;
+                ri += c2;
+            }
+        }
+        if (warp < 8 && lane == 31) {
+            wsum[warp] = ni;
+            wsum[32 + warp] = ti;
+            wsum[64 + warp] = ri;
+        }
+        __syncthreads();
+        if (warp == 0) {
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                const int v = lane < 8 ? wsum[32 * q + lane] : 0;
+                int inc = v;
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    const int a = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += a;
+                }
+                if (lane < 8) wsum[32 * q + lane] = inc - v;
+                if (lane == 7) misc[1 + q] = inc;
+            }
+        }
+        __syncthreads();
+        if (u < U) {
+            const int nex = wsum[warp] + ni - n, tex = wsum[32 + warp] + ti - t, rex = wsum[64 + warp] + ri - r;
+            ustart[u] = nex;
+            ws.uh[u] = nex;
+            const int e = sel[u];
+            for (int j = 0; j < t; j++) {
+                int* tt = ws.tc_tile + (size_t)(tex + j) * 4;
+                tt[0] = e;
+                tt[1] = min(kTcNT, n - j * kTcNT);
+                tt[2] = nex + j * kTcNT;
+                tt[3] = rex + j * kTcNT;
+            }
+        }
+        if (tid == 0) {
+            ws.uh[U] = misc[1];
+            *ws.U = U;
+            *ws.tc_ntiles = misc[2];
+        }
+    }
+    __syncthreads();
+    for (int s = tid; s < S; s += T) {
+        const int e = top[s], b = s / k, w = b >> 5;
+        const int rank = tpre[e * NW + w] + __popc(tmask[e * NW + w] & ((1u << (b & 31)) - 1u));
+        const int pos = ustart[upos[e]] + rank;
+        ws.uidx[pos] = s;
+        ws.uw[pos] = tw[s];
+        ws.slot_pos[s] = pos;
+        comb_slot(top, upos, s, k, E, ws.comb);
+    }
+    trace_point(ws.trace, kTraceRouter, 13);
 }
 
 }  // namespace jl
@@ -532,6 +714,15 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
     int rc = launch(k_router_cluster, dim3(kClusterCTAs * ncl), dim3(kClusterThreads), smem, s, gate_w_l,
                     x, B, E, d, k, h->norm, h->ws, tpc, (int)lg_off, fuse, tiles ? 1 : 0);
     if (rc || fuse) return rc;
+    const size_t fsm = dispatch_fast_smem(B, k, E);
+    if (fsm <= 200 * 1024) {
+        static int attr_f = 0;
+        if (!attr_f) {
+            JL_CUDA(cudaFuncSetAttribute(k_dispatch_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+            attr_f = 1;
+        }
+        return launch(k_dispatch_fast, dim3(1), dim3(kDfThreads), fsm, s, B, k, E, h->ws);
+    }
     return launch_dispatch(h->ws, B, k, E, s);
 }
 

@@ -240,29 +240,53 @@ __device__ __forceinline__ void split_chunk(const float (&x)[8], uint4& hi, uint
 // writes K chunks [64y, 64y + 64) of tile t as fp16 hi/lo in core layout.
 __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x, int d, int k,
                                                     jl_ws ws) {
+    long long* tr = (blockIdx.x == 0 && blockIdx.y == 0) ? ws.trace : nullptr;
+    trace_point(tr, kTraceCombine, 8);
     griddep_wait();
     griddep_launch_dependents();
+    trace_point(tr, kTraceCombine, 9);
     const int ti = blockIdx.x;
     if (ti >= *ws.tc_ntiles) return;
     const int n = ws.tc_tile[ti * 4 + 1], N = (n + 15) & ~15;
     const int pos0 = ws.tc_tile[ti * 4 + 2], row0 = ws.tc_tile[ti * 4 + 3];
     const int kc0 = blockIdx.y * 64, kcn = min(64, d / 8 - kc0);
-    // tile layout: [kc][2N rows: hi rows 0..N-1, lo rows N..2N-1][8 halves]
+    // the tile's token rows (at most kTcNT), read once
+    __shared__ int brow[kTcNT];
+    if (threadIdx.x < n) brow[threadIdx.x] = ws.uidx[pos0 + threadIdx.x] / k;
+    __syncthreads();
+    // tile layout: [kc][2N rows: hi rows 0..N-1, lo rows N..2N-1][8 halves].
+    // Each thread loads all of its chunks before converting and storing any,
+    // so the loads of one thread overlap.
     __half* base = ws.xc + (size_t)2 * row0 * d;
-    for (int i = threadIdx.x; i < N * kcn; i += blockDim.x) {
+    constexpr int kPer = kTcNT * 64 / 256;  // chunks per thread at the largest tile (N = kTcNT)
+    float4 va[kPer], vc[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; q++) {
+        const int i = threadIdx.x + q * 256;
         const int r = i % N, kc = kc0 + i / N;
-        uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
-        if (r < n) {
-            const int b = ws.uidx[pos0 + r] / k;
-            const float4 a = *reinterpret_cast<const float4*>(x + (size_t)b * d + kc * 8);
-            const float4 c = *reinterpret_cast<const float4*>(x + (size_t)b * d + kc * 8 + 4);
-            const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-            split_chunk(v, vh, vl);
+        va[q] = vc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < N * kcn && r < n) {
+            const float* src = x + (size_t)brow[r] * d + kc * 8;
+            va[q] = __ldg(reinterpret_cast<const float4*>(src));
+            vc[q] = __ldg(reinterpret_cast<const float4*>(src + 4));
         }
-        __half* blk = base + (size_t)kc * 2 * N * 8;
-        *reinterpret_cast<uint4*>(blk + r * 8) = vh;
-        *reinterpret_cast<uint4*>(blk + (N + r) * 8) = vl;
     }
+#pragma unroll
+    for (int q = 0; q < kPer; q++) {
+        const int i = threadIdx.x + q * 256;
+        if (i < N * kcn) {
+            const int r = i % N, kc = kc0 + i / N;
+            uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
+            if (r < n) {
+                const float v[8] = {va[q].x, va[q].y, va[q].z, va[q].w, vc[q].x, vc[q].y, vc[q].z, vc[q].w};
+                split_chunk(v, vh, vl);
+            }
+            __half* blk = base + (size_t)kc * 2 * N * 8;
+            *reinterpret_cast<uint4*>(blk + r * 8) = vh;
+            *reinterpret_cast<uint4*>(blk + (N + r) * 8) = vl;
+        }
+    }
+    trace_point(tr, kTraceCombine, 10);
 }
 
 // ---------------------------------------------------------------------------
