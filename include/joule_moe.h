@@ -276,12 +276,14 @@ int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l,
 
 /* Device-side trace (the counterpart of the reference's g_trace breadcrumbs,
  * decode_kernel.c:22-28): with enable = 1 the kernels of later forwards stamp
- * %globaltimer (ns) at phase boundaries into a 64-slot device buffer, 16
- * slots per kernel (router, gate/up, down, combine), written by thread 0 of
- * one block. out (host, n slots; nullable when n = 0) receives the buffer
- * (synchronises `stream`); enable = 0 stops later launches from tracing.
- * The buffer stays allocated until jl_moe_destroy, because CUDA graphs
- * captured while tracing keep writing to it. */
+ * %globaltimer (ns) at phase boundaries into a 128-slot device buffer: rows
+ * of 16 slots for the router, gate/up, down and combine kernels (thread 0 of
+ * one block), then rows 4 and 5 with the SM-clock cycles that block 0 of the
+ * tensor-core gate/up and down kernels spent in each of its waits (they add
+ * up over launches). out (host, n slots) receives the buffer (synchronises
+ * `stream`); enable = 1 with n = 0 zeroes it; enable = 0 stops later launches
+ * from tracing. The buffer stays allocated until jl_moe_destroy, because CUDA
+ * graphs captured while tracing keep writing to it. */
 int jl_moe_trace(jl_moe* h, int enable, long long* out, int n, void* stream);
 
 /* Phase timing: when n > 0, each jl_moe_forward[_phases] records events[0]

@@ -65,7 +65,7 @@ struct jl_ws {
 // Trace buffer layout: per kernel kind a row of 16 slots of %globaltimer
 // stamps (ns) taken by thread 0 of one chosen block.
 constexpr int kTraceRouter = 0, kTraceGateup = 1, kTraceDown = 2, kTraceCombine = 3;
-constexpr int kTraceSlots = 4 * 16;
+constexpr int kTraceSlots = 8 * 16;  // rows 4, 5: wait-cycle counters of the tensor-core kernels
 
 struct jl_moe {
     int device;

@@ -198,6 +198,7 @@ extern "C" int jl_moe_trace(jl_moe* h, int enable, long long* out, int n, void* 
     // earlier keep the pointer they captured, so the buffer is only freed by
     // jl_moe_destroy.
     h->ws.trace = enable ? h->trace_buf : nullptr;
+    if (enable && n == 0) JL_CUDA(cudaMemsetAsync(h->trace_buf, 0, kTraceSlots * sizeof(long long), s));
     if (n > 0 && h->trace_buf) {
         JL_CUDA(cudaMemcpyAsync(out, h->trace_buf, (size_t)std::min(n, kTraceSlots) * sizeof(long long),
                                 cudaMemcpyDeviceToHost, s));

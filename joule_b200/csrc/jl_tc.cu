@@ -38,7 +38,6 @@
 
 namespace jl {
 
-constexpr int kTcDqWarps = 4;        // dequant/epilogue warps = TMEM lanes 0..127
 constexpr int kTcQ4Stage = 4 * kTileRec;  // the 4 contiguous tile records of one K step
 // position p of an 8-value K chunk holds element kPerm[p] = {0,4,1,5,2,6,3,7}[p]
 
@@ -138,6 +137,16 @@ __device__ __forceinline__ uint64_t umma_desc(const void* smem, uint32_t lbo, ui
 __device__ __forceinline__ uint32_t umma_idesc_f16(int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
+
+// Role wait counters of CTA 0 when the device trace is on (rows 4 / 5 of
+// the trace buffer for gate/up / down): cycles spent in each wait.
+#define TC_TIMED(slot, wid, expr)                                          \
+    ([&]() {                                                              \
+        const long long _c0 = dg ? clock64() : 0;                         \
+        const bool _r = (expr);                                           \
+        if (dg && lane == 0 && warp == (wid)) dg[slot] += clock64() - _c0; \
+        return _r;                                                        \
+    }())
 
 // Bounded mbarrier wait that also gives up when another role aborted.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err,
@@ -414,6 +423,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sh.tmem_base;
+    // wait counters: [0] dequant q4_full, [1] dequant a_empty, [2] dequant TMEM store,
+    // [3] dequant total, [4] issuer a_full, [5] issuer b_full, [6] issuer acc_empty,
+    // [7] issuer total, [8] producer q4_empty, [9] producer total, [10] activation
+    // producer b_empty, [11] epilogue acc_full, [12] epilogue total, [13] items
+    long long* dg = (blockIdx.x == 0 && ws.trace != nullptr) ? ws.trace + (is_down ? 5 : 4) * 16 : nullptr;
+    const long long t_role = clock64();
+    if (dg && threadIdx.x == 0) dg[13] = my_items;
 
     if (warp == 12) {
         // ---------------- weight producer: stage G = K steps [4G, 4G + 4) of the stream
@@ -426,7 +442,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const uint8_t* rec = store_l + (size_t)it.e * L.rec_bytes;
                 for (int j = 0; j < nq; j++, G++) {
                     const int s = G % kPQ;
-                    if (G >= kPQ && !tc_wait_relaxed(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort)) {
+                    if (G >= kPQ && !TC_TIMED(8, 12, tc_wait_relaxed(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort))) {
                         ok = false;
                         break;
                     }
@@ -436,6 +452,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     bulk_g2s(q4_ring + (size_t)s * kPStage, rec + off, kPStage, &sh.q4_full[s]);
                 }
             }
+            if (dg) dg[9] = clock64() - t_role;
             for (int c = max(0, G - kPQ); c < G; c++)  // no copies left in flight
                 mbar_wait_bounded(&sh.q4_full[c % kPQ], (c / kPQ) & 1, ws.err);
         }
@@ -450,7 +467,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const int kb = p_bsteps(it.N);
                 for (int c0 = 0; c0 < nk; c0 += kb, G++) {
                     const int s = G % kPB;
-                    if (G >= kPB && !tc_wait_relaxed(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort)) {
+                    if (G >= kPB && !TC_TIMED(10, 13, tc_wait_relaxed(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort))) {
                         ok = false;
                         break;
                     }
@@ -475,7 +492,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int i = 0; ok && i < my_items; i++) {
             const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
             const int ib = i & 1;
-            if (i >= 2 && !tc_wait_warp(&sh.acc_empty[ib], ((i >> 1) - 1) & 1, ws.err, &sh.abort)) break;
+            if (i >= 2 && !TC_TIMED(6, 14, tc_wait_warp(&sh.acc_empty[ib], ((i >> 1) - 1) & 1, ws.err, &sh.abort)))
+                break;
             tc_fence_after();
             const int kb = p_bsteps(it.N);  // K steps per activation stage: 4 or 8
             const uint32_t idesc = umma_idesc_f16(2 * it.N);
@@ -487,11 +505,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const int P = i * np + pl, ab = P % kPA;
                 const int c = 2 * pl, cb = c % kb, Gs = G + c / kb, sb = Gs % kPB;
                 const int ns = min(kb, nk - (c - cb));  // K steps in this stage (a multiple of 4)
-                if (cb == 2 * w && !tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort)) {
+                if (cb == 2 * w && !TC_TIMED(5, 14, tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort))) {
                     ok = false;
                     break;
                 }
-                if (!tc_wait_warp(&sh.a_full[ab], (P / kPA) & 1, ws.err, &sh.abort)) {
+                if (!TC_TIMED(4, 14, tc_wait_warp(&sh.a_full[ab], (P / kPA) & 1, ws.err, &sh.abort))) {
                     ok = false;
                     break;
                 }
@@ -515,6 +533,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 __syncwarp();
             }
         }
+        if (dg && lane == 0 && warp == 14) dg[7] = clock64() - t_role;
     } else if (warp >= 4) {
         // ---------------- dequant warpgroups: thread = A row (TMEM lane). Stage G
         // holds K steps 4G .. 4G+3 = pairs 2G (warpgroup 0) and 2G + 1 (warpgroup 1).
@@ -522,8 +541,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int n_stages = my_steps / kPQK;
         for (int G = 0; G < n_stages; G++) {
             const int s = G % kPQ, P = 2 * G + wg, ab = P % kPA;
-            if (!tc_wait_warp(&sh.q4_full[s], (G / kPQ) & 1, ws.err, &sh.abort)) break;
-            if (G < 8 && wg == 0) trace_point(tr, tk, 2 + G);
+            if (!TC_TIMED(0, 4, tc_wait_warp(&sh.q4_full[s], (G / kPQ) & 1, ws.err, &sh.abort))) break;
             const uint8_t* q = q4_ring + (size_t)s * kPStage + (2 * wg) * kTcQ4Stage + wl * kTileRec;
             const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
             const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
@@ -538,16 +556,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
             uint32_t a0[32], a1[32];
             dequant_row_f16(q0, q1, __ushort_as_half(sc0), a0);
             dequant_row_f16(q2, q3, __ushort_as_half(sc1), a1);
-            if (P >= kPA && !tc_wait_warp(&sh.a_empty[ab], ((P / kPA) - 1) & 1, ws.err, &sh.abort)) break;
+            if (P >= kPA && !TC_TIMED(1, 4, tc_wait_warp(&sh.a_empty[ab], ((P / kPA) - 1) & 1, ws.err, &sh.abort))) break;
             // order these TMEM writes after the MMAs that read the buffer (released by a_empty)
             tc_fence_after();
             const uint32_t ta = tmem + ((uint32_t)(wl * 32) << 16) + ab * 64;
+            const long long c_st = dg ? clock64() : 0;
             tc_st32(ta, a0);
             tc_st32(ta + 32, a1);
             tc_wait_st();
+            if (dg && lane == 0 && warp == 4) dg[2] += clock64() - c_st;
             tc_fence_before();
             mbar_arrive(&sh.a_full[ab]);
         }
+        if (dg && lane == 0 && warp == 4) dg[3] = clock64() - t_role;
     } else {
         // ---------------- epilogue warps 0-3: thread = accumulator row
         const int row = warp * 32 + lane;
@@ -558,7 +579,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const int ib = i & 1;
             bool got = true;
             for (int w = 0; got && w < kPI; w++)
-                got = __all_sync(0xffffffffu, tc_wait_relaxed(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort));
+                got = TC_TIMED(11, 0, __all_sync(0xffffffffu, tc_wait_relaxed(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort)));
             if (!got) break;
             tc_fence_after();
             if (i == 0) trace_point(tr, tk, 10);
@@ -622,6 +643,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
         }
         trace_point(tr, tk, 11);
+        if (dg && lane == 0 && warp == 0) dg[12] = clock64() - t_role;
     }
     trace_point(tr, tk, 12);
     tc_fence_before();

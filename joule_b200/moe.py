@@ -158,11 +158,17 @@ class MoELayers:
         return out
 
     def trace(self, enable: bool = True) -> "np.ndarray | None":
-        """Turn the device trace on/off; returns the [4, 16] ns stamps when on."""
-        buf = np.zeros(64, np.int64)
+        """Turn the device trace on/off; returns the [8, 16] stamps when on: rows
+        0-3 %globaltimer ns per phase kernel, rows 4-5 wait-cycle counters of
+        the tensor-core gate/up and down kernels (block 0)."""
+        buf = np.zeros(128, np.int64)
         check(self._L.jl_moe_trace(self.h, 1 if enable else 0, buf.ctypes.data if enable else None,
-                                   64 if enable else 0, _stream(None)), "jl_moe_trace")
-        return buf.reshape(4, 16) if enable else None
+                                   128 if enable else 0, _stream(None)), "jl_moe_trace")
+        return buf.reshape(8, 16) if enable else None
+
+    def trace_reset(self) -> None:
+        """Turn the device trace on and zero its buffer."""
+        check(self._L.jl_moe_trace(self.h, 1, None, 0, _stream(None)), "jl_moe_trace")
 
     def check(self, stream=None) -> None:
         check(self._L.jl_moe_check(self.h, _stream(stream)), "jl_moe_check")
