@@ -10,12 +10,13 @@ working set is far above the 126 MB L2 and no flush is needed.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
     python bench.py --impl reference ...   # the reference's CPU path, same metric
 
-The headline batch is B=64 (the tensor-core path); the sweep adds B=1 and
-B=8 (the exact CUDA-core path, bit-identical to the reference) and B=32 in
+The headline batch is B=64 (the tensor-core path); the sweep adds B=1 (the
+exact CUDA-core path, bit-identical to the reference), B=8 and B=32 in
 `per_batch`. Output: one JSON line on rank 0 (see the keys below).
 Multi-GPU (torchrun, N > 1) runs the layer expert-parallel: each GPU serves
 its own B tokens and stores E/N experts; token rows and weighted outputs
-cross GPUs by NCCL all-to-all (weak scaling in tokens).
+cross GPUs as peer stores over NVLink by library kernels (--ep nccl: NCCL
+all-to-all instead); weak scaling in tokens.
 """
 from __future__ import annotations
 
@@ -538,13 +539,14 @@ def run_ours(a):
 
 def path_of(B):
     """The path jl_moe_forward takes (JL_PATH_AUTO) at batch B for this shape."""
-    return "exact" if B <= 8 else "tensor-core"
+    return "exact" if B <= 3 else "tensor-core"
 
 
 def launches_per_step(B):
-    # per layer: the cluster router (routing + dispatch), then
+    # per layer: the cluster router (routing, and the dispatch for B <= 32),
+    # k_dispatch_fast for B > 32, then
     #   exact: gate/up, down, combine; tensor-core: permute, gate/up, down, combine
-    return SHAPE["L"] * (1 + (3 if path_of(B) == "exact" else 4))
+    return SHAPE["L"] * (1 + (1 if B > 32 else 0) + (3 if path_of(B) == "exact" else 4))
 
 
 def traffic_from_profiles(kernel, B):

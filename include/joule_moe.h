@@ -167,7 +167,7 @@ int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
                           const float* w_down, void* stream);
 
 /* Path selection for jl_moe_forward. */
-#define JL_PATH_AUTO 0  /* exact for B <= 8, tensor-core beyond (d % 512 == 0, m % 256 == 0) */
+#define JL_PATH_AUTO 0  /* exact for B <= 3, tensor-core beyond (d % 512 == 0, m % 256 == 0) */
 #define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order */
 #define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
 #define JL_PATH_EXACT_FUSED 3 /* the exact path for B <= 8 as ONE persistent launch (router, top-k,
