@@ -140,12 +140,18 @@ __device__ __forceinline__ uint32_t umma_idesc_f16(int N) {
 
 // Role wait counters of CTA 0 when the device trace is on (rows 4 / 5 of
 // the trace buffer for gate/up / down): cycles spent in each wait.
+// Only the kTrace instance of the kernel (launched while tracing) reads the
+// clock; the other instance compiles the plain wait.
 #define TC_TIMED(slot, wid, expr)                                          \
     ([&]() {                                                              \
-        const long long _c0 = dg ? clock64() : 0;                         \
-        const bool _r = (expr);                                           \
-        if (dg && lane == 0 && warp == (wid)) dg[slot] += clock64() - _c0; \
-        return _r;                                                        \
+        if constexpr (kTrace) {                                           \
+            const long long _c0 = clock64();                              \
+            const bool _r = (expr);                                       \
+            if (dg && lane == 0 && warp == (wid)) dg[slot] += clock64() - _c0; \
+            return _r;                                                    \
+        } else {                                                          \
+            return (bool)(expr);                                          \
+        }                                                                 \
     }())
 
 // Bounded mbarrier wait that also gives up when another role aborted.
@@ -371,7 +377,7 @@ __device__ __forceinline__ PItem p_item(const int* tc_tile, int item, int MT) {
     return it;
 }
 
-template <bool is_down>
+template <bool is_down, bool kTrace>
 __global__ void __launch_bounds__(kPThreads, 1)
     k_expert_tc(const uint8_t* __restrict__ store_l, jl_layout L, jl_ws ws) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -427,8 +433,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // [3] dequant total, [4] issuer a_full, [5] issuer b_full, [6] issuer acc_empty,
     // [7] issuer total, [8] producer q4_empty, [9] producer total, [10] activation
     // producer b_empty, [11] epilogue acc_full, [12] epilogue total, [13] items
-    long long* dg = (blockIdx.x == 0 && ws.trace != nullptr) ? ws.trace + (is_down ? 5 : 4) * 16 : nullptr;
-    const long long t_role = clock64();
+    long long* dg = (kTrace && blockIdx.x == 0 && ws.trace != nullptr) ? ws.trace + (is_down ? 5 : 4) * 16 : nullptr;
+    const long long t_role = kTrace ? clock64() : 0;
     if (dg && threadIdx.x == 0) dg[13] = my_items;
 
     if (warp == 12) {
@@ -560,11 +566,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // order these TMEM writes after the MMAs that read the buffer (released by a_empty)
             tc_fence_after();
             const uint32_t ta = tmem + ((uint32_t)(wl * 32) << 16) + ab * 64;
-            const long long c_st = dg ? clock64() : 0;
+            const long long c_st = kTrace ? clock64() : 0;
             tc_st32(ta, a0);
             tc_st32(ta + 32, a1);
             tc_wait_st();
-            if (dg && lane == 0 && warp == 4) dg[2] += clock64() - c_st;
+            if (kTrace && dg && lane == 0 && warp == 4) dg[2] += clock64() - c_st;
             tc_fence_before();
             mbar_arrive(&sh.a_full[ab]);
         }
@@ -671,9 +677,13 @@ static int tc_attrs() {
     using namespace jl;
     static bool attr = false;
     if (!attr) {
-        JL_CUDA(cudaFuncSetAttribute(k_expert_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        JL_CUDA(cudaFuncSetAttribute(k_expert_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kPSmemBytes));
-        JL_CUDA(cudaFuncSetAttribute(k_expert_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        JL_CUDA(cudaFuncSetAttribute(k_expert_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kPSmemBytes));
+        JL_CUDA(cudaFuncSetAttribute(k_expert_tc<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kPSmemBytes));
+        JL_CUDA(cudaFuncSetAttribute(k_expert_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kPSmemBytes));
         attr = true;
     }
@@ -689,8 +699,8 @@ int jl_launch_gateup_tc(const jl_moe* h, const uint8_t* store_l, const float* x,
     rc = launch(k_tc_permute, dim3(tiles, h->d / 512), dim3(256), 0, s, x, h->d, h->k, h->ws);
     if (rc) return rc;
     const int items = tiles * (h->m / 64);
-    return launch(k_expert_tc<false>, dim3(std::min(h->sm_count, items)), dim3(kPThreads), kPSmemBytes, s,
-                  store_l, h->lay, h->ws);
+    return launch(h->ws.trace ? k_expert_tc<false, true> : k_expert_tc<false, false>,
+                  dim3(std::min(h->sm_count, items)), dim3(kPThreads), kPSmemBytes, s, store_l, h->lay, h->ws);
 }
 
 int jl_launch_down_tc(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s) {
@@ -699,6 +709,6 @@ int jl_launch_down_tc(const jl_moe* h, const uint8_t* store_l, int B, cudaStream
     if (rc) return rc;
     if (h->d % 512 || h->m % 256 || !h->ws.xc) return JL_ERR_INVALID;
     const int items = tc_max_tiles(B * h->k, h->E) * (h->d / 128);
-    return launch(k_expert_tc<true>, dim3(std::min(h->sm_count, items)), dim3(kPThreads), kPSmemBytes, s,
-                  store_l, h->lay, h->ws);
+    return launch(h->ws.trace ? k_expert_tc<true, true> : k_expert_tc<true, false>,
+                  dim3(std::min(h->sm_count, items)), dim3(kPThreads), kPSmemBytes, s, store_l, h->lay, h->ws);
 }
