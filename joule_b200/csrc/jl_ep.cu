@@ -1,6 +1,11 @@
-// Expert-parallel bookkeeping on the device: the per-layer packing of a
-// rank's routed slots by owner rank, and the combine of the rows that come
-// back. The exchange itself (NCCL all-to-all) is done by the caller.
+// Expert parallelism on the device. Two forms of the per-layer exchange:
+//  - with NCCL (the caller runs the all-to-alls): k_ep_order / k_ep_gather
+//    pack a rank's routed slots by owner rank, k_ep_combine adds the rows
+//    that come back (jl_ep_pack, jl_ep_combine);
+//  - over NVLink peer memory, no host round trip (jl_ep_forward): the
+//    kernels below the second banner store token rows into the owners'
+//    exported buffers and the weighted rows back, synchronised by epoch
+//    flags.
 #include <algorithm>
 #include <cstring>
 #include <new>
