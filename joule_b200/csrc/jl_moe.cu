@@ -456,6 +456,10 @@ struct dropin {
     jl_moe* h;
     float* xd;
     float* od;
+    float* xh;          // pinned host staging of x and out: the copies run at full link
+    float* oh;          // speed, and one synchronisation covers out and the error word
+    int* errh;          // pinned copy of the handle's device error word
+    cudaStream_t st;    // the drop-in's own stream
     int cap;
 };
 std::mutex g_dropin_mu;
@@ -494,8 +498,18 @@ extern "C" int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l, c
                 return rc;
             }
         }
-        if (cudaMalloc(&e.xd, (size_t)e.cap * c->d * 4) != cudaSuccess ||
-            cudaMalloc(&e.od, (size_t)e.cap * c->d * 4) != cudaSuccess) {
+        const size_t cb = (size_t)e.cap * c->d * 4;
+        if (cudaMalloc(&e.xd, cb) != cudaSuccess || cudaMalloc(&e.od, cb) != cudaSuccess ||
+            cudaHostAlloc(&e.xh, cb, cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc(&e.oh, cb, cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc(&e.errh, 16, cudaHostAllocDefault) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&e.st, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            if (e.xd) cudaFree(e.xd);
+            if (e.od) cudaFree(e.od);
+            if (e.xh) cudaFreeHost(e.xh);
+            if (e.oh) cudaFreeHost(e.oh);
+            if (e.errh) cudaFreeHost(e.errh);
             jl_moe_destroy(e.h);
             return JL_ERR_OOM;
         }
@@ -504,9 +518,14 @@ extern "C" int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l, c
     }
     if (B > ent->cap) return JL_ERR_CAPACITY;
     const size_t bytes = (size_t)B * c->d * 4;
-    JL_CUDA(cudaMemcpy(ent->xd, x, bytes, cudaMemcpyHostToDevice));
-    int rc = jl_moe_forward(ent->h, l, ent->xd, B, ent->od, nullptr, nullptr, nullptr);
+    memcpy(ent->xh, x, bytes);
+    JL_CUDA(cudaMemcpyAsync(ent->xd, ent->xh, bytes, cudaMemcpyHostToDevice, ent->st));
+    int rc = jl_moe_forward(ent->h, l, ent->xd, B, ent->od, nullptr, nullptr, ent->st);
     if (rc) return rc;
-    JL_CUDA(cudaMemcpy(out, ent->od, bytes, cudaMemcpyDeviceToHost));
-    return jl_moe_check(ent->h, nullptr);
+    JL_CUDA(cudaMemcpyAsync(ent->oh, ent->od, bytes, cudaMemcpyDeviceToHost, ent->st));
+    JL_CUDA(cudaMemcpyAsync(ent->errh, ent->h->ws.err, sizeof(int), cudaMemcpyDeviceToHost, ent->st));
+    JL_CUDA(cudaStreamSynchronize(ent->st));
+    if (*ent->errh) return jl_moe_check(ent->h, ent->st);  // reads, reports and clears the error
+    memcpy(out, ent->oh, bytes);
+    return JL_OK;
 }
