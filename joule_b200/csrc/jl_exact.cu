@@ -117,8 +117,8 @@ __device__ __forceinline__ void stage_region(uint8_t* w_s, const uint8_t* src, i
             mbar_init(&bars[tid], 1);
             mbar_fence_init();
             mbar_expect_tx(&bars[tid], bytes);
-            bulk_g2s(w_s + (size_t)g0 * kXRB * kTileRec, src + (size_t)g0 * kXRB * kTileRec, bytes,
-                     &bars[tid]);
+            bulk_g2s_hint(w_s + (size_t)g0 * kXRB * kTileRec, src + (size_t)g0 * kXRB * kTileRec, bytes,
+                          &bars[tid], l2_policy_evict_first());
         }
     }
 }

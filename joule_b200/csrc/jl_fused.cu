@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
             const uint32_t eb = (uint32_t)reh * 2;
             mbar_expect_tx(&sh.rbar, eb * nexp);
             for (int i = 0; i < nexp; i++)
-                bulk_g2s(g_s + (size_t)i * reh, gate_w_l + (size_t)(c + i * G) * reh, eb, &sh.rbar);
+                bulk_g2s_hint(g_s + (size_t)i * reh, gate_w_l + (size_t)(c + i * G) * reh, eb, &sh.rbar,
+                              l2_policy_evict_last());
         }
     }
     griddep_wait();  // x is the previous kernel's output
@@ -370,7 +371,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
                     const int gn = min(kFChunkGroups, ng - ch * kFChunkGroups);
                     const uint32_t bytes = (uint32_t)gn * 4 * kTileRec;
                     mbar_expect_tx(&sh.full[s], bytes);
-                    bulk_g2s(ring + (size_t)s * kFChunkBytes, base + (size_t)ch * kFChunkBytes, bytes, &sh.full[s]);
+                    bulk_g2s_hint(ring + (size_t)s * kFChunkBytes, base + (size_t)ch * kFChunkBytes, bytes, &sh.full[s],
+                                  l2_policy_evict_first());
                 }
             }
             // no copy may still be landing when the CTA leaves

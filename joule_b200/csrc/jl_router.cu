@@ -372,7 +372,7 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kClusterT
         if (ne > 0) {
             const uint32_t bytes = (uint32_t)(ne * router_expert_halves(d) * 2);
             mbar_expect_tx(&bar, bytes);
-            bulk_g2s(g_s, gate_w + (size_t)e0 * router_expert_halves(d), bytes, &bar);
+            bulk_g2s_hint(g_s, gate_w + (size_t)e0 * router_expert_halves(d), bytes, &bar, l2_policy_evict_last());
         } else {
             mbar_arrive(&bar);
         }

@@ -440,6 +440,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (warp == 12) {
         // ---------------- weight producer: stage G = K steps [4G, 4G + 4) of the stream
         if (lane == 0) {
+            const uint64_t wpol = l2_policy_evict_first();  // expert weights: read once per layer
             const int nq = nk / kPQK;
             int G = 0;
             bool ok = true;
@@ -455,7 +456,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     // the records of consecutive K steps of one row block are contiguous
                     const size_t off = is_down ? L.tile_off(2, it.mt * 4, j * kPQK) : L.tile_off(0, it.mt * 2, j * kPQK);
                     mbar_expect_tx(&sh.q4_full[s], kPStage);
-                    bulk_g2s(q4_ring + (size_t)s * kPStage, rec + off, kPStage, &sh.q4_full[s]);
+                    bulk_g2s_hint(q4_ring + (size_t)s * kPStage, rec + off, kPStage, &sh.q4_full[s], wpol);
                 }
             }
             if (dg) dg[9] = clock64() - t_role;
