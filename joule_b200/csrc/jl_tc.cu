@@ -139,15 +139,17 @@ __device__ __forceinline__ uint32_t umma_idesc_f16(int N) {
 }
 
 // Role wait counters of CTA 0 when the device trace is on (rows 4 / 5 of
-// the trace buffer for gate/up / down): cycles spent in each wait.
-// Only the kTrace instance of the kernel (launched while tracing) reads the
-// clock; the other instance compiles the plain wait.
-#define TC_TIMED(slot, wid, expr)                                          \
+// the trace buffer for gate/up / down): cycles spent in each wait, summed in
+// registers (dgl) and written once when the role ends, so that the counting
+// adds no memory round trip to the role it times. Only the kTrace instance of
+// the kernel (launched while tracing) reads the clock; the other instance
+// compiles the plain wait.
+#define TC_TIMED(slot, expr)                                              \
     ([&]() {                                                              \
         if constexpr (kTrace) {                                           \
             const long long _c0 = clock64();                              \
             const bool _r = (expr);                                       \
-            if (dg && lane == 0 && warp == (wid)) dg[slot] += clock64() - _c0; \
+            dgl[slot] += clock64() - _c0;                                 \
             return _r;                                                    \
         } else {                                                          \
             return (bool)(expr);                                          \
@@ -310,11 +312,11 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
 // tile x one block of 128 weight rows (gate/up: 64 gate + 64 up rows). Each
 // role walks the same item sequence, so the rings run on across items. Roles:
 //   warps 0-3   epilogue: thread = accumulator row = TMEM lane
-//   warps 4-7   dequant warpgroup 0 (K steps 0, 1 of every weight stage)
-//   warps 8-11  dequant warpgroup 1 (K steps 2, 3)
-//   warp 12     weight producer: 6 stages of 4 K steps (17,408 B, one bulk copy)
-//   warp 13     activation producer: 2 stages of 32 KB (one bulk copy each)
-//   warps 14-15 MMA issuers: issuer w takes the K-step pairs of parity w into
+//   warps 4-19  dequant warpgroups 0-3: warpgroup g dequantises the K-step
+//               pairs P = g (mod 4) into TMEM A buffer g
+//   warp 20     weight producer: 6 stages of 4 K steps (17,408 B, one bulk copy)
+//   warp 21     activation producer: 2 stages of 32 KB (one bulk copy each)
+//   warps 22-23 MMA issuers: issuer w takes the K-step pairs of parity w into
 //               its own accumulator; the epilogue adds the two in a fixed order
 // TMEM (512 columns): 4 A buffers of 64 columns (one pair of 64-value K steps),
 // then accumulators [issuer][buffer] of 2 x kTcNT columns; items alternate
@@ -326,16 +328,23 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
 // elect.sync: a lone diverged lane issues about half as fast), while the
 // tensor core takes several issuers' MMAs at once. The hand-off from the
 // dequant warps (TMEM store, wait, fence, arrive) costs a few hundred cycles,
-// so it runs once per pair of K steps. A buffer b always serves pairs of
-// parity b % 2, i.e. one warpgroup and one issuer.
+// so it runs once per pair of K steps. A buffer b always serves the pairs
+// P = b (mod 4), i.e. one warpgroup and one issuer (b % 2). Each dequant warp
+// arrives once on a barrier (after __syncwarp), not once per thread: 256
+// arrivals on one mbarrier per stage serialise in the shared-memory atomics.
 constexpr int kPQK = 4;    // K steps per weight stage: one 17,408-byte bulk copy
 constexpr int kPQ = 6;     // weight stages
 constexpr int kPBBytes = 32 * 1024;  // activation stage: 8 / (N/16) K steps of 2N rows
 constexpr int kPB = 2;     // activation stages
 constexpr int kPA = 4;     // TMEM A buffers (one K-step pair, 64 columns, each)
 constexpr int kPI = 2;     // MMA issuers
+constexpr int kPDq = 4;    // dequant warpgroups: warpgroup g fills TMEM A buffer g
 constexpr int kPAccCols = 2 * kTcNT;  // accumulator columns (hi + lo rows of a tile)
-constexpr int kPWarps = 14 + kPI;
+constexpr int kWProd = 4 + 4 * kPDq;  // weight producer warp
+constexpr int kWAct = kWProd + 1;     // activation producer warp
+constexpr int kWMma = kWProd + 2;     // first MMA issuer warp (it also owns the TMEM allocation)
+constexpr int kPWarps = kWMma + kPI;
+static_assert(kPA == kPDq && kPA % kPI == 0, "A buffer g belongs to warpgroup g and issuer g % kPI");
 constexpr int kPThreads = kPWarps * 32;
 constexpr int kPStage = kPQK * kTcQ4Stage;
 // TMEM column of accumulator (issuer w, buffer b): after the A buffers
@@ -354,12 +363,15 @@ static_assert(sizeof(PSmem) <= 512, "barrier block");
 constexpr size_t kPQ4Off = 512;
 constexpr size_t kPBOff = kPQ4Off + (size_t)kPQ * kPStage;
 constexpr size_t kPScrOff = kPBOff + (size_t)kPB * kPBBytes;
-constexpr size_t kPScratch = 32 * 1024;  // gate/up epilogue: up rows fp32 [64][64] + act hi/lo [2][64][64]
+constexpr size_t kPScratch = 32 * 1024;  // gate/up epilogue: gate + up rows fp32 [128][33] + act hi/lo [2][32][64]
 constexpr size_t kPSmemBytes = kPScrOff + kPScratch;
 
 // K steps per activation stage for a tile of N (16 or 32) token rows: a
 // multiple of kPI, so every issuer has steps in every stage
 __device__ __forceinline__ int p_bsteps(int N) { return 8 / (N >> 4); }
+__device__ __forceinline__ int p_lbsteps(int N) { return N == 16 ? 3 : 2; }  // log2(p_bsteps(N))
+static_assert(128 * (kTcNT + 1) * 4 + 2 * kTcNT * 64 * 2 <= kPScratch, "epilogue scratch");
+static_assert(kTcNT == 32 && kPA == 4 && kPB == 2, "tile N is 16 or 32; ring sizes are powers of two");
 
 struct PItem {
     int e, n, N, pos0, row0, mt;
@@ -403,23 +415,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
         sh.abort = 0;
         for (int s = 0; s < kPQ; s++) {
             mbar_init(&sh.q4_full[s], 1);
-            mbar_init(&sh.q4_empty[s], 256);  // both dequant warpgroups
+            mbar_init(&sh.q4_empty[s], 8);  // one arrival per dequant warp (both warpgroups)
         }
         for (int s = 0; s < kPB; s++) {
             mbar_init(&sh.b_full[s], 1);
             mbar_init(&sh.b_empty[s], kPI);  // every issuer releases a stage
         }
         for (int b = 0; b < kPA; b++) {
-            mbar_init(&sh.a_full[b], 128);
+            mbar_init(&sh.a_full[b], 4);  // one arrival per warp of a dequant warpgroup
             mbar_init(&sh.a_empty[b], 1);
         }
         for (int b = 0; b < 2; b++) {
             for (int w = 0; w < kPI; w++) mbar_init(&sh.acc_full[w][b], 1);
-            mbar_init(&sh.acc_empty[b], 128);
+            mbar_init(&sh.acc_empty[b], 4);  // one arrival per epilogue warp
         }
         mbar_fence_init();
     }
-    if (warp == 14) {
+    if (warp == kWMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&sh.tmem_base)),
                      "r"(512));
@@ -436,20 +448,30 @@ __global__ void __launch_bounds__(kPThreads, 1)
     long long* dg = (kTrace && blockIdx.x == 0 && ws.trace != nullptr) ? ws.trace + (is_down ? 5 : 4) * 16 : nullptr;
     const long long t_role = kTrace ? clock64() : 0;
     if (dg && threadIdx.x == 0) dg[13] = my_items;
+    long long dgl[16] = {};  // this thread's counters (kTrace only)
+    // lane 0 of the role's timed warp writes its slots [lo, hi) and the role total
+    auto dg_flush = [&](int wid, int lo, int hi, int total) {
+        if (kTrace && dg && lane == 0 && warp == wid) {
+            for (int i = lo; i < hi; i++) dg[i] += dgl[i];
+            dg[total] = clock64() - t_role;
+        }
+    };
 
-    if (warp == 12) {
+    if (warp == kWProd) {
         // ---------------- weight producer: stage G = K steps [4G, 4G + 4) of the stream
         if (lane == 0) {
             const uint64_t wpol = l2_policy_evict_first();  // expert weights: read once per layer
             const int nq = nk / kPQK;
             int G = 0;
             bool ok = true;
+            PItem nx = p_item(ws.tc_tile, (int)blockIdx.x, MT);  // the next item's record, loaded one item ahead
             for (int i = 0; ok && i < my_items; i++) {
-                const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+                const PItem it = nx;
+                if (i + 1 < my_items) nx = p_item(ws.tc_tile, (int)blockIdx.x + (i + 1) * (int)gridDim.x, MT);
                 const uint8_t* rec = store_l + (size_t)it.e * L.rec_bytes;
                 for (int j = 0; j < nq; j++, G++) {
                     const int s = G % kPQ;
-                    if (G >= kPQ && !TC_TIMED(8, 12, tc_wait_relaxed(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort))) {
+                    if (G >= kPQ && !TC_TIMED(8, tc_wait_relaxed(&sh.q4_empty[s], ((G / kPQ) - 1) & 1, ws.err, &sh.abort))) {
                         ok = false;
                         break;
                     }
@@ -459,22 +481,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     bulk_g2s_hint(q4_ring + (size_t)s * kPStage, rec + off, kPStage, &sh.q4_full[s], wpol);
                 }
             }
-            if (dg) dg[9] = clock64() - t_role;
+            dg_flush(kWProd, 8, 9, 9);
             for (int c = max(0, G - kPQ); c < G; c++)  // no copies left in flight
                 mbar_wait_bounded(&sh.q4_full[c % kPQ], (c / kPQ) & 1, ws.err);
         }
-    } else if (warp == 13) {
+    } else if (warp == kWAct) {
         // ---------------- activation producer: stage = kb K steps of one item's tile
         if (lane == 0) {
             int G = 0;
             bool ok = true;
+            PItem nx = p_item(ws.tc_tile, (int)blockIdx.x, MT);  // the next item's record, loaded one item ahead
             for (int i = 0; ok && i < my_items; i++) {
-                const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+                const PItem it = nx;
+                if (i + 1 < my_items) nx = p_item(ws.tc_tile, (int)blockIdx.x + (i + 1) * (int)gridDim.x, MT);
                 const __half* bsrc = is_down ? ws.ac + (size_t)2 * it.row0 * m : ws.xc + (size_t)2 * it.row0 * d;
                 const int kb = p_bsteps(it.N);
                 for (int c0 = 0; c0 < nk; c0 += kb, G++) {
                     const int s = G % kPB;
-                    if (G >= kPB && !TC_TIMED(10, 13, tc_wait_relaxed(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort))) {
+                    if (G >= kPB && !TC_TIMED(10, tc_wait_relaxed(&sh.b_empty[s], ((G / kPB) - 1) & 1, ws.err, &sh.abort))) {
                         ok = false;
                         break;
                     }
@@ -484,25 +508,28 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     bulk_g2s(b_ring + (size_t)s * kPBBytes, bsrc + (size_t)c0 * 16 * it.N * 8, bytes, &sh.b_full[s]);
                 }
             }
+            if (kTrace && dg && warp == kWAct) dg[10] += dgl[10];
             for (int c = max(0, G - kPB); c < G; c++)
                 mbar_wait_bounded(&sh.b_full[c % kPB], (c / kPB) & 1, ws.err);
         }
-    } else if (warp >= 14) {
+    } else if (warp >= kWMma) {
         // ---------------- MMA issuers (whole warps; one elected lane issues):
         // issuer w runs the K-step pairs of parity w of every item, 8 MMAs (K = 16
         // each) of N = 2 x tokens (hi rows -> accumulator columns [0, N), lo
         // rows -> [N, 2N)) into accumulator (w, i % 2)
-        const int w = warp - 14;
+        const int w = warp - kWMma;
         const int np = nk / 2;  // pairs per item (even: nk % 4 == 0)
         int G = 0;  // activation stages before the current item
         bool ok = true;
+        PItem nx = p_item(ws.tc_tile, (int)blockIdx.x, MT);  // the next item's record, loaded one item ahead
         for (int i = 0; ok && i < my_items; i++) {
-            const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+            const PItem it = nx;
+            if (i + 1 < my_items) nx = p_item(ws.tc_tile, (int)blockIdx.x + (i + 1) * (int)gridDim.x, MT);
             const int ib = i & 1;
-            if (i >= 2 && !TC_TIMED(6, 14, tc_wait_warp(&sh.acc_empty[ib], ((i >> 1) - 1) & 1, ws.err, &sh.abort)))
+            if (i >= 2 && !TC_TIMED(6, tc_wait_warp(&sh.acc_empty[ib], ((i >> 1) - 1) & 1, ws.err, &sh.abort)))
                 break;
             tc_fence_after();
-            const int kb = p_bsteps(it.N);  // K steps per activation stage: 4 or 8
+            const int lkb = p_lbsteps(it.N), kb = 1 << lkb;  // K steps per activation stage: 4 or 8
             const uint32_t idesc = umma_idesc_f16(2 * it.N);
             const uint64_t desc0 = umma_desc(b_ring, (uint32_t)it.N * 32, 128);
             const uint64_t kstep = (uint64_t)((2 * it.N * 32) >> 4);   // 16 K values of 2N rows
@@ -510,18 +537,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const uint32_t dacc = tmem + p_acc_col(w, ib);
             for (int pl = w; pl < np; pl += kPI) {
                 const int P = i * np + pl, ab = P % kPA;
-                const int c = 2 * pl, cb = c % kb, Gs = G + c / kb, sb = Gs % kPB;
+                const int c = 2 * pl, cb = c & (kb - 1), Gs = G + (c >> lkb), sb = Gs % kPB;
                 const int ns = min(kb, nk - (c - cb));  // K steps in this stage (a multiple of 4)
-                if (cb == 2 * w && !TC_TIMED(5, 14, tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort))) {
+                if (cb == 2 * w && !TC_TIMED(5, tc_wait_warp(&sh.b_full[sb], (Gs / kPB) & 1, ws.err, &sh.abort))) {
                     ok = false;
                     break;
                 }
-                if (!TC_TIMED(4, 14, tc_wait_warp(&sh.a_full[ab], (P / kPA) & 1, ws.err, &sh.abort))) {
+                if (!TC_TIMED(4, tc_wait_warp(&sh.a_full[ab], (P / kPA) & 1, ws.err, &sh.abort))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint64_t dsb = desc0 + (uint64_t)sb * (kPBBytes >> 4) + (uint64_t)cb * cstep;
+                const long long c_mma = kTrace ? clock64() : 0;
                 if (elect_one()) {
 #pragma unroll
                     for (int h = 0; h < 2; h++)
@@ -533,23 +561,29 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     if (cb >= ns - 4) tc_commit(&sh.b_empty[sb]);  // this issuer's last pair of the stage
                 }
                 __syncwarp();
+                if (kTrace) dgl[14] += clock64() - c_mma;
             }
-            G += (nk + kb - 1) / kb;
+            G += (nk + kb - 1) >> lkb;
             if (ok) {
                 if (elect_one()) tc_commit(&sh.acc_full[w][ib]);
                 __syncwarp();
             }
         }
-        if (dg && lane == 0 && warp == 14) dg[7] = clock64() - t_role;
+        dg_flush(kWMma, 4, 7, 7);
+        if (kTrace && dg && lane == 0 && warp == kWMma) dg[14] += dgl[14];
     } else if (warp >= 4) {
         // ---------------- dequant warpgroups: thread = A row (TMEM lane). Stage G
-        // holds K steps 4G .. 4G+3 = pairs 2G (warpgroup 0) and 2G + 1 (warpgroup 1).
-        const int wg = (warp - 4) >> 2, wl = warp & 3;
+        // holds K steps 4G .. 4G+3 = pairs 2G and 2G + 1; pair P goes to warpgroup
+        // P % kPDq and TMEM buffer P % kPA (the same number), so warpgroup g only
+        // sees stages G = g / 2 (mod 2) and one buffer: every barrier it waits on
+        // is released by itself or by a role that walks the same sequence, which
+        // keeps its phases at most one apart.
+        const int wg = (warp - 4) >> 2, wl = warp & 3, h = wg & 1;
         const int n_stages = my_steps / kPQK;
-        for (int G = 0; G < n_stages; G++) {
-            const int s = G % kPQ, P = 2 * G + wg, ab = P % kPA;
-            if (!TC_TIMED(0, 4, tc_wait_warp(&sh.q4_full[s], (G / kPQ) & 1, ws.err, &sh.abort))) break;
-            const uint8_t* q = q4_ring + (size_t)s * kPStage + (2 * wg) * kTcQ4Stage + wl * kTileRec;
+        for (int G = wg >> 1; G < n_stages; G += 2) {
+            const int s = G % kPQ, P = 2 * G + h, ab = wg;
+            if (!TC_TIMED(0, tc_wait_warp(&sh.q4_full[s], (G / kPQ) & 1, ws.err, &sh.abort))) break;
+            const uint8_t* q = q4_ring + (size_t)s * kPStage + (2 * h) * kTcQ4Stage + wl * kTileRec;
             const uint4 q0 = *reinterpret_cast<const uint4*>(q + lane * 16);
             const uint4 q1 = *reinterpret_cast<const uint4*>(q + 512 + lane * 16);
             const uint16_t sc0 = reinterpret_cast<const uint16_t*>(q + kTileBytes)[lane];
@@ -559,34 +593,50 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // this thread's reads of the stage are done; the next bulk copy into it is
             // an async-proxy write, ordered after these plain loads by the proxy fence
             fence_proxy_async_smem();
-            mbar_arrive(&sh.q4_empty[s]);
-            uint32_t a0[32], a1[32];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.q4_empty[s]);
+            const long long c_dq = kTrace ? clock64() : 0;
+            uint32_t a0[32];
             dequant_row_f16(q0, q1, __ushort_as_half(sc0), a0);
-            dequant_row_f16(q2, q3, __ushort_as_half(sc1), a1);
-            if (P >= kPA && !TC_TIMED(1, 4, tc_wait_warp(&sh.a_empty[ab], ((P / kPA) - 1) & 1, ws.err, &sh.abort))) break;
+            if (kTrace) dgl[15] += clock64() - c_dq;
+            if (P >= kPA && !TC_TIMED(1, tc_wait_warp(&sh.a_empty[ab], ((P / kPA) - 1) & 1, ws.err, &sh.abort))) break;
             // order these TMEM writes after the MMAs that read the buffer (released by a_empty)
             tc_fence_after();
             const uint32_t ta = tmem + ((uint32_t)(wl * 32) << 16) + ab * 64;
             const long long c_st = kTrace ? clock64() : 0;
             tc_st32(ta, a0);
+            uint32_t a1[32];
+            dequant_row_f16(q2, q3, __ushort_as_half(sc1), a1);
             tc_st32(ta + 32, a1);
             tc_wait_st();
-            if (kTrace && dg && lane == 0 && warp == 4) dg[2] += clock64() - c_st;
+            if (kTrace) dgl[2] += clock64() - c_st;
             tc_fence_before();
-            mbar_arrive(&sh.a_full[ab]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.a_full[ab]);
         }
-        if (dg && lane == 0 && warp == 4) dg[3] = clock64() - t_role;
+        dg_flush(4, 0, 3, 3);
+        if (kTrace && dg && lane == 0 && warp == 4) dg[15] += dgl[15];
     } else {
         // ---------------- epilogue warps 0-3: thread = accumulator row
         const int row = warp * 32 + lane;
-        float* up_s = reinterpret_cast<float*>(scr);  // [64 rows][kTcNT + 1] (odd stride: no bank conflicts)
-        __half* act_s = reinterpret_cast<__half*>(scr + 64 * (kTcNT + 1) * sizeof(float));  // [2][kTcNT][64]
+        float* gu_s = reinterpret_cast<float*>(scr);  // [128 rows][kTcNT + 1] (odd stride: no bank conflicts)
+        __half* act_s = reinterpret_cast<__half*>(scr + 128 * (kTcNT + 1) * sizeof(float));  // [2][kTcNT][64]
+        PItem nx = p_item(ws.tc_tile, (int)blockIdx.x, MT);  // the next item's record, loaded one item ahead
         for (int i = 0; i < my_items; i++) {
-            const PItem it = p_item(ws.tc_tile, (int)blockIdx.x + i * (int)gridDim.x, MT);
+            const PItem it = nx;
+            if (i + 1 < my_items) nx = p_item(ws.tc_tile, (int)blockIdx.x + (i + 1) * (int)gridDim.x, MT);
             const int ib = i & 1;
+            // down: the tile's token slots and weights, one token per lane (n <= 32),
+            // loaded before the wait so that the stores below never wait on them
+            int t_slot = 0;
+            float t_w = 0.0f;
+            if (is_down && lane < it.n) {
+                t_slot = ws.uidx[it.pos0 + lane];
+                t_w = ws.uw[it.pos0 + lane];
+            }
             bool got = true;
             for (int w = 0; got && w < kPI; w++)
-                got = TC_TIMED(11, 0, __all_sync(0xffffffffu, tc_wait_relaxed(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort)));
+                got = TC_TIMED(11, __all_sync(0xffffffffu, tc_wait_relaxed(&sh.acc_full[w][ib], (i >> 1) & 1, ws.err, &sh.abort)));
             if (!got) break;
             tc_fence_after();
             if (i == 0) trace_point(tr, tk, 10);
@@ -597,42 +647,42 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 for (int t0 = 0; t0 < N; t0 += 16) {
                     float v[16];
                     tc_ld_acc16(acc0, acc1, N, t0, v);
-                    for (int j = 0; j < 16 && t0 + j < n; j++) {
-                        const int pos = it.pos0 + t0 + j;
-                        ws.y[(size_t)ws.uidx[pos] * d + it.mt * 128 + row] = ws.uw[pos] * v[j];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int u = __shfl_sync(0xffffffffu, t_slot, t0 + j);
+                        const float wj = __shfl_sync(0xffffffffu, t_w, t0 + j);
+                        if (t0 + j < n) ws.y[(size_t)u * d + it.mt * 128 + row] = wj * v[j];
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&sh.acc_empty[ib]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.acc_empty[ib]);
             } else {
-                // up rows (warps 2,3) -> smem; gate rows (warps 0,1) apply SwiGLU
-                if (warp >= 2)
-                    for (int t0 = 0; t0 < N; t0 += 16) {
-                        float v[16];
-                        tc_ld_acc16(acc0, acc1, N, t0, v);
+                // gate rows (warps 0, 1) and up rows (warps 2, 3) -> smem; the
+                // accumulators go back to the MMA as soon as they are read
+                for (int t0 = 0; t0 < N; t0 += 16) {
+                    float v[16];
+                    tc_ld_acc16(acc0, acc1, N, t0, v);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) up_s[(row - 64) * (kTcNT + 1) + t0 + j] = v[j];
-                    }
+                    for (int j = 0; j < 16; j++) gu_s[row * (kTcNT + 1) + t0 + j] = v[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.acc_empty[ib]);
                 asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (warp < 2) {
-                    const int j8 = row & 7, kc = row >> 3;
+                // SwiGLU on all four warps: thread = (intermediate row r, half of the tokens)
+                {
+                    const int r = row & 63, j8 = r & 7, kc = r >> 3;
                     const int pp = j8 < 4 ? 2 * j8 : 2 * (j8 - 4) + 1;  // position of element j8 (kPerm inverse)
-                    for (int t0 = 0; t0 < N; t0 += 16) {
-                        float v[16];
-                        tc_ld_acc16(acc0, acc1, N, t0, v);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float a = silu_mul(v[j], up_s[row * (kTcNT + 1) + t0 + j]);
-                            const __half h = __float2half_rn(a);
-                            const __half l = __float2half_rn(a - __half2float(h));
-                            act_s[(t0 + j) * 64 + kc * 8 + pp] = h;
-                            act_s[kTcNT * 64 + (t0 + j) * 64 + kc * 8 + pp] = l;
-                        }
+                    const int th = N >> 1, tb = (row >> 6) * th;
+                    for (int t = tb; t < tb + th; t++) {
+                        const float a = silu_mul(gu_s[r * (kTcNT + 1) + t], gu_s[(64 + r) * (kTcNT + 1) + t]);
+                        const __half h = __float2half_rn(a);
+                        const __half l = __float2half_rn(a - __half2float(h));
+                        act_s[t * 64 + kc * 8 + pp] = h;
+                        act_s[kTcNT * 64 + t * 64 + kc * 8 + pp] = l;
                     }
                 }
-                // every TMEM read of the accumulators is done: hand them back to the MMA
-                tc_fence_before();
-                mbar_arrive(&sh.acc_empty[ib]);
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 // copy out: chunk (t, kc) of 8 halves -> ac tile layout [kc][2N][8]
                 __half* abase = ws.ac + (size_t)2 * it.row0 * m;
@@ -650,12 +700,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
         }
         trace_point(tr, tk, 11);
-        if (dg && lane == 0 && warp == 0) dg[12] = clock64() - t_role;
+        dg_flush(0, 11, 12, 12);
     }
     trace_point(tr, tk, 12);
     tc_fence_before();
     __syncthreads();
-    if (warp == 14) {
+    if (warp == kWMma) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
