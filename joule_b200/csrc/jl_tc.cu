@@ -444,7 +444,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // wait counters: [0] dequant q4_full, [1] dequant a_empty, [2] dequant TMEM store,
     // [3] dequant total, [4] issuer a_full, [5] issuer b_full, [6] issuer acc_empty,
     // [7] issuer total, [8] producer q4_empty, [9] producer total, [10] activation
-    // producer b_empty, [11] epilogue acc_full, [12] epilogue total, [13] items
+    // producer b_empty, [11] epilogue acc_full, [12] epilogue total, [13] items,
+    // [14] issuer MMA issue (elected lane's block), [15] dequant of the first row
     long long* dg = (kTrace && blockIdx.x == 0 && ws.trace != nullptr) ? ws.trace + (is_down ? 5 : 4) * 16 : nullptr;
     const long long t_role = kTrace ? clock64() : 0;
     if (dg && threadIdx.x == 0) dg[13] = my_items;
@@ -674,13 +675,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 {
                     const int r = row & 63, j8 = r & 7, kc = r >> 3;
                     const int pp = j8 < 4 ? 2 * j8 : 2 * (j8 - 4) + 1;  // position of element j8 (kPerm inverse)
-                    const int th = N >> 1, tb = (row >> 6) * th;
-                    for (int t = tb; t < tb + th; t++) {
-                        const float a = silu_mul(gu_s[r * (kTcNT + 1) + t], gu_s[(64 + r) * (kTcNT + 1) + t]);
-                        const __half h = __float2half_rn(a);
-                        const __half l = __float2half_rn(a - __half2float(h));
-                        act_s[t * 64 + kc * 8 + pp] = h;
-                        act_s[kTcNT * 64 + t * 64 + kc * 8 + pp] = l;
+                    const int th = N >> 1, tb = (row >> 6) * th;  // th = 8 or 16
+                    for (int t8 = tb; t8 < tb + th; t8 += 8) {
+                        // 8 independent SwiGLU chains in flight
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const int t = t8 + j;
+                            const float a = silu_mul(gu_s[r * (kTcNT + 1) + t], gu_s[(64 + r) * (kTcNT + 1) + t]);
+                            const __half h = __float2half_rn(a);
+                            const __half l = __float2half_rn(a - __half2float(h));
+                            act_s[t * 64 + kc * 8 + pp] = h;
+                            act_s[kTcNT * 64 + t * 64 + kc * 8 + pp] = l;
+                        }
                     }
                 }
                 asm volatile("bar.sync 1, 128;" ::: "memory");
