@@ -58,10 +58,12 @@ __device__ __forceinline__ float fp16_to_f32(uint32_t h) {
 }
 
 // The reference's own expf approximation (decode_kernel.c:94-108), with every
-// product and sum rounded separately as in its C source.
+// product and sum rounded separately as in its C source. Written without
+// branches (its early returns become selects, same results for every input,
+// NaN included), so that several calls interleave in one thread.
 __device__ __forceinline__ float expf_fast(float v) {
-    if (v < -17.0f) return 0.0f;
-    if (v > 88.0f) v = 88.0f;
+    const bool under = v < -17.0f;
+    v = v > 88.0f ? 88.0f : v;
     const float y = __fmul_rn(v, 1.4426950408889634f);
     const int k = __float2int_rz(__fadd_rn(y, y >= 0.0f ? 0.5f : -0.5f));
     const float f = __fsub_rn(y, __int2float_rn(k));
@@ -71,10 +73,9 @@ __device__ __forceinline__ float expf_fast(float v) {
     p = __fadd_rn(0.2402265f, __fmul_rn(f, p));
     p = __fadd_rn(0.6931472f, __fmul_rn(f, p));
     p = __fadd_rn(1.0f, __fmul_rn(f, p));
-    int kk = k + 127;
-    if (kk < 0) return 0.0f;
-    if (kk > 254) kk = 254;
-    return __fmul_rn(p, __uint_as_float((uint32_t)kk << 23));
+    const int kk = k + 127;
+    const float r = __fmul_rn(p, __uint_as_float((uint32_t)min(max(kk, 0), 254) << 23));
+    return (under || kk < 0) ? 0.0f : r;
 }
 
 // silu(g) * u as the reference writes it: (g / (1 + expf_fast(-g))) * u.

@@ -692,8 +692,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 // copy out: chunk (t, kc) of 8 halves -> ac tile layout [kc][2N][8]
                 __half* abase = ws.ac + (size_t)2 * it.row0 * m;
+                const int lN = N == 16 ? 4 : 5;  // log2(N)
                 for (int q = row; q < N * 8; q += 128) {
-                    const int t = q % N, kcl = q / N;
+                    const int t = q & (N - 1), kcl = q >> lN;
                     __half* blk = abase + (size_t)(it.mt * 8 + kcl) * 2 * N * 8;
                     uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
                     if (t < n) {
