@@ -254,7 +254,10 @@ __device__ __forceinline__ void split_chunk(const float (&x)[8], uint4& hi, uint
 
 // ---------------------------------------------------------------------------
 // Activation gather: grid = (max tiles, d / 512), block 256. Block (t, y)
-// writes K chunks [64y, 64y + 64) of tile t as fp16 hi/lo in core layout.
+// writes K chunks [64y, 64y + 64) of tile t's n token rows as fp16 hi/lo in
+// core layout. The pad rows n..N-1 are not written: an MMA column depends
+// only on its own B row, and the epilogues drop the pad columns, so whatever
+// the pad rows hold (left from earlier tiles) never reaches a result.
 __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x, int d, int k,
                                                     jl_ws ws) {
     long long* tr = (blockIdx.x == 0 && blockIdx.y == 0) ? ws.trace : nullptr;
@@ -291,13 +294,11 @@ __global__ void __launch_bounds__(256) k_tc_permute(const float* __restrict__ x,
 #pragma unroll
     for (int q = 0; q < kPer; q++) {
         const int i = threadIdx.x + q * 256;
-        if (i < N * kcn) {
-            const int r = i % N, kc = kc0 + i / N;
-            uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
-            if (r < n) {
-                const float v[8] = {va[q].x, va[q].y, va[q].z, va[q].w, vc[q].x, vc[q].y, vc[q].z, vc[q].w};
-                split_chunk(v, vh, vl);
-            }
+        const int r = i % N, kc = kc0 + i / N;
+        if (i < N * kcn && r < n) {
+            uint4 vh, vl;
+            const float v[8] = {va[q].x, va[q].y, va[q].z, va[q].w, vc[q].x, vc[q].y, vc[q].z, vc[q].w};
+            split_chunk(v, vh, vl);
             __half* blk = base + (size_t)kc * 2 * N * 8;
             *reinterpret_cast<uint4*>(blk + r * 8) = vh;
             *reinterpret_cast<uint4*>(blk + (N + r) * 8) = vl;
@@ -695,14 +696,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const int lN = N == 16 ? 4 : 5;  // log2(N)
                 for (int q = row; q < N * 8; q += 128) {
                     const int t = q & (N - 1), kcl = q >> lN;
+                    if (t >= n) continue;  // pad rows: never read into a kept result
                     __half* blk = abase + (size_t)(it.mt * 8 + kcl) * 2 * N * 8;
-                    uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
-                    if (t < n) {
-                        vh = *reinterpret_cast<const uint4*>(act_s + t * 64 + kcl * 8);
-                        vl = *reinterpret_cast<const uint4*>(act_s + kTcNT * 64 + t * 64 + kcl * 8);
-                    }
-                    *reinterpret_cast<uint4*>(blk + t * 8) = vh;
-                    *reinterpret_cast<uint4*>(blk + (N + t) * 8) = vl;
+                    *reinterpret_cast<uint4*>(blk + t * 8) = *reinterpret_cast<const uint4*>(act_s + t * 64 + kcl * 8);
+                    *reinterpret_cast<uint4*>(blk + (N + t) * 8) =
+                        *reinterpret_cast<const uint4*>(act_s + kTcNT * 64 + t * 64 + kcl * 8);
                 }
             }
         }
