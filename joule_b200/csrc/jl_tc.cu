@@ -649,6 +649,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 for (int t0 = 0; t0 < N; t0 += 16) {
                     float v[16];
                     tc_ld_acc16(acc0, acc1, N, t0, v);
+                    if (t0 + 16 >= N) {  // last TMEM read: hand the accumulators back before storing
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sh.acc_empty[ib]);
+                    }
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int u = __shfl_sync(0xffffffffu, t_slot, t0 + j);
@@ -656,9 +661,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         if (t0 + j < n) ws.y[(size_t)u * d + it.mt * 128 + row] = wj * v[j];
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.acc_empty[ib]);
             } else {
                 // gate rows (warps 0, 1) and up rows (warps 2, 3) -> smem; the
                 // accumulators go back to the MMA as soon as they are read
