@@ -279,7 +279,8 @@ int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l,
  * %globaltimer (ns) at phase boundaries into a 128-slot device buffer: rows
  * of 16 slots for the router, gate/up, down and combine kernels (thread 0 of
  * one block), then rows 4 and 5 with the SM-clock cycles that block 0 of the
- * tensor-core gate/up and down kernels spent in each of its waits (they add
+ * tensor-core gate/up and down kernels spent in each role's waits, MMA issue
+ * and dequantisation, and each role's total (they add
  * up over launches). out (host, n slots) receives the buffer (synchronises
  * `stream`); enable = 1 with n = 0 zeroes it; enable = 0 stops later launches
  * from tracing. The buffer stays allocated until jl_moe_destroy, because CUDA
