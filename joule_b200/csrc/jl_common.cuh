@@ -84,6 +84,14 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, den), u);
 }
 
+// The same with the division by __fdividef (within 2 ulp for den <= 2^126; den
+// >= 1, and above 2^126 it returns 0 where the exact quotient is below 1e-36),
+// for the tensor-core path, whose results are held to a relative tolerance.
+__device__ __forceinline__ float silu_mul_approx_div(float g, float u) {
+    const float den = __fadd_rn(1.0f, expf_fast(-g));
+    return __fmul_rn(__fdividef(g, den), u);
+}
+
 // Horizontal sum of an 8-lane AVX accumulator in the reference's order
 // (decode_kernel.c:843-846): ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)).
 __device__ __forceinline__ float hsum8(const float (&l)[8]) {

@@ -684,7 +684,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 8; j++) {
                             const int t = t8 + j;
-                            const float a = silu_mul(gu_s[r * (kTcNT + 1) + t], gu_s[(64 + r) * (kTcNT + 1) + t]);
+                            const float a = silu_mul_approx_div(gu_s[r * (kTcNT + 1) + t], gu_s[(64 + r) * (kTcNT + 1) + t]);
                             const __half h = __float2half_rn(a);
                             const __half l = __float2half_rn(a - __half2float(h));
                             act_s[t * 64 + kc * 8 + pp] = h;
