@@ -162,7 +162,12 @@ extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags,
         h->ws.tc_ntiles = (int*)t;
         h->ws.tc_tile = (int*)(t + 16);
     }
+    // The tensor-core token tiles start as fp16 NaN: the permute and the gate/up
+    // epilogue write only a tile's real rows, and the pad rows may feed only
+    // accumulator columns that the epilogues drop, so a pad that ever reached a
+    // result would show up as NaN in it.
     if (cudaMemset(h->ws_base, 0, h->ws_bytes) != cudaSuccess ||
+        (h->ws.xc && cudaMemset(h->ws.xc, 0xFF, (wp.xc_plane + wp.ac_plane) * 2 * sizeof(__half)) != cudaSuccess) ||
         cudaMemset(h->gate_w, 0, gw) != cudaSuccess) {
         jl_moe_destroy(h);
         return JL_ERR_CUDA;
