@@ -179,7 +179,11 @@ int jl_moe_set_path(jl_moe* h, int path);
  * Replaces layer_ffn_batch (decode_kernel.c:1387-1508) as called from
  * decode_layers_batch[_argmax] (decode_kernel.c:1535, 1577). top/tw
  * (nullable, device) receive the router's top-k ids [B, topk] int32 and
- * weights [B, topk] fp32. Enqueued on `stream`; returns after launch. */
+ * weights [B, topk] fp32. Enqueued on `stream`; returns after launch.
+ * B = 0 is an empty batch: JL_OK with nothing launched or written (x, out
+ * may then be NULL), as the reference's loops run zero times; B < 0 is
+ * JL_ERR_INVALID. jl_moe_forward_phases, jl_moe_route, jl_moe_forward_routed,
+ * jl_layer_ffn_batch and jl_route_noalloc treat B = 0 the same way. */
 int jl_moe_forward(jl_moe* h, int l, const float* x, int B, float* out,
                    int* top, float* tw, void* stream);
 

@@ -296,8 +296,9 @@ extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gat
 
 extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, float* out,
                                      int* top, float* tw, int mask, void* stream) {
-    if (!h || !x || !out || l < 0 || l >= h->L || B < 1 || mask < 1 || mask > 7)
-        return JL_ERR_INVALID;
+    if (!h || l < 0 || l >= h->L || B < 0 || mask < 1 || mask > 7) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;  // empty batch: nothing launched, nothing written (the reference's loops run zero times)
+    if (!x || !out) return JL_ERR_INVALID;
     if (B > h->max_tokens) return JL_ERR_CAPACITY;
     if (!h->uploaded[l]) return JL_ERR_NOT_READY;
     if (h->router_only && (mask & 6)) return JL_ERR_INVALID;
@@ -374,7 +375,9 @@ extern "C" int jl_moe_upload_router(jl_moe* h, int l, const unsigned short* gate
 
 extern "C" int jl_moe_route(jl_moe* h, int l, const float* x, int B, int* top, float* tw, int* comb,
                             void* stream) {
-    if (!h || !x || !top || !tw || l < 0 || l >= h->L || B < 1) return JL_ERR_INVALID;
+    if (!h || l < 0 || l >= h->L || B < 0) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;
+    if (!x || !top || !tw) return JL_ERR_INVALID;
     if (B > h->max_tokens) return JL_ERR_CAPACITY;
     if (!h->uploaded[l]) return JL_ERR_NOT_READY;
     if (reinterpret_cast<uintptr_t>(x) & 15) return JL_ERR_INVALID;
@@ -392,8 +395,9 @@ extern "C" int jl_moe_route(jl_moe* h, int l, const float* x, int B, int* top, f
 
 extern "C" int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, const int* top,
                                      const float* tw, float* out, void* stream) {
-    if (!h || !x || !top || !tw || !out || l < 0 || l >= h->L || B < 1 || h->router_only)
-        return JL_ERR_INVALID;
+    if (!h || l < 0 || l >= h->L || B < 0 || h->router_only) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;
+    if (!x || !top || !tw || !out) return JL_ERR_INVALID;
     if (B > h->max_tokens) return JL_ERR_CAPACITY;
     if (!h->uploaded[l]) return JL_ERR_NOT_READY;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return JL_ERR_INVALID;
@@ -473,7 +477,9 @@ std::vector<dropin> g_dropins;
 
 extern "C" int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l, const float* x,
                                   int B, float* out) {
-    if (!c || !W || !x || !out || B < 1 || l < 0 || l >= c->L) return JL_ERR_INVALID;
+    if (!c || !W || B < 0 || l < 0 || l >= c->L) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;  // as the reference: zero tokens, out untouched
+    if (!x || !out) return JL_ERR_INVALID;
     if (!W->gate_w || !W->expert_pk[0] || !W->expert_sc[0]) return JL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(g_dropin_mu);
     dropin* ent = nullptr;

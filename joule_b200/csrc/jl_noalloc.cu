@@ -73,8 +73,9 @@ int scratch_for_device(int dev, float** out) {
 extern "C" int jl_route_noalloc(const unsigned short* gate_w, const float* x, int B, int E, int d,
                                 int topk, int norm_topk_prob, int* top, float* tw, int* dev_status,
                                 void* stream) {
+    if (B < 0) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;  // empty batch: nothing to route
     if (!gate_w || !x || !top || !tw) return JL_ERR_INVALID;
-    if (B < 1) return JL_ERR_INVALID;
     if (B > kNoAllocMaxB) return JL_ERR_CAPACITY;
     if (E < 1 || E > kNoAllocMaxE || topk < 1 || topk > kNoAllocMaxK || topk > E) return JL_ERR_INVALID;
     if (d < 8 || d % 8) return JL_ERR_INVALID;

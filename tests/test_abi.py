@@ -75,3 +75,16 @@ def test_loader_fails_loudly_without_library(tmp_path, monkeypatch):
     monkeypatch.setattr(native, "_DLL_CACHE", {})
     with pytest.raises(RuntimeError, match="not built"):
         native.get_dll()
+
+
+def test_empty_batch_is_a_no_op(dll):
+    """B = 0 returns JL_OK before any CUDA call and touches no buffer (the
+    reference's layer_ffn_batch runs its token loops zero times); B < 0 is
+    rejected. Runs without a GPU."""
+    c = native.KernelCfg(L=2, d=2048, E=128, topk=8, intermediate=768, norm_topk_prob=1)
+    w = native.KernelW()
+    assert dll.jl_layer_ffn_batch(ctypes.byref(c), ctypes.byref(w), 0, None, 0, None) == 0
+    assert dll.jl_layer_ffn_batch(ctypes.byref(c), ctypes.byref(w), 0, None, -1, None) == -1
+    assert dll.jl_layer_ffn_batch(ctypes.byref(c), ctypes.byref(w), 2, None, 0, None) == -1  # l out of range
+    assert dll.jl_route_noalloc(None, None, 0, 128, 2048, 8, 1, None, None, None, None) == 0
+    assert dll.jl_route_noalloc(None, None, -1, 128, 2048, 8, 1, None, None, None, None) == -1
