@@ -2,24 +2,26 @@
 //
 // Per layer, after routing:
 //   tc_build_tiles (end of the dispatch step) cuts every union expert's
-//                 tokens into tiles of <= 64 (padded to a multiple of 16).
+//                 tokens into tiles of <= kTcNT = 32 (padded to 16 or 32).
 //   k_tc_permute  gathers each tile's tokens and writes them as fp16 hi/lo
 //                 pairs (x = hi + lo, ~22 significant bits) in the UMMA
 //                 K-major "interleaved" core layout, hi rows then lo rows, so
 //                 one MMA of N = 2 x tokens covers both (the epilogue adds the
-//                 two accumulator halves).
-//   k_gateup_tc   one CTA per (tile, 64 gate rows + the matching 64 up rows):
-//                 two producer warps stream the Q4 tiles (8-stage ring) and
-//                 the token tiles (4-stage ring) with 1-D bulk copies;
-//                 4 dequant warps turn each 64-value group into fp16
+//                 two accumulator halves). Pad rows are left unwritten.
+//   k_expert_tc<false> (gate/up) a persistent grid, one CTA per SM walking
+//                 items (tile, 64 gate rows + the matching 64 up rows): a
+//                 producer warp streams the Q4 tiles (6-stage ring of 17 KB
+//                 bulk copies), another the token tiles (2-stage ring); four
+//                 dequant warpgroups turn each 64-value group into fp16
 //                 (n - 8) * scale (correctly rounded) and store it straight
 //                 into tensor memory as the MMA's A operand (lane = weight
-//                 row); one thread issues tcgen05.mma (M=128, N=2 x tokens,
-//                 K=16, fp32 accumulate in TMEM). The epilogue
-//                 reads the accumulator with tcgen05.ld, applies SwiGLU and
-//                 writes the activations (hi/lo, same core layout) for down.
-//   k_down_tc     the same pipeline over the down matrix (M=128 rows of d,
-//                 K = intermediate); the epilogue writes y[slot] = w * acc.
+//                 row); two issuer warps run tcgen05.mma (M=128, N=2 x tokens,
+//                 K=16, fp32 accumulate in TMEM). The epilogue reads the
+//                 accumulators with tcgen05.ld, applies SwiGLU and writes the
+//                 activations (hi/lo, same core layout) for down.
+//   k_expert_tc<true> (down) the same pipeline over the down matrix (M=128
+//                 rows of d, K = intermediate); the epilogue writes
+//                 y[slot] = w * acc.
 //   k_combine     (jl_exact.cu) sums y in the reference's union order.
 //
 // K order inside each 8-value chunk is permuted identically in A and B
