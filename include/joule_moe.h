@@ -249,7 +249,10 @@ int jl_ep_combine(const float* back, const int* pos, const int* comb, int B,
  * the weighted rows to their senders, wait for every owner, and combine in
  * the batch's union order: out equals a single GPU's jl_moe_forward on the
  * same tokens. Every rank must make the same sequence of calls. Waits on
- * other ranks are bounded; jl_moe_check(local) reports JL_ERR_TIMEOUT. */
+ * other ranks are bounded; jl_moe_check(local) reports JL_ERR_TIMEOUT.
+ * B >= 1 on every rank: a rank takes part in the exchange even when no
+ * token of its own routes anywhere, so unlike jl_moe_forward an empty batch
+ * is JL_ERR_INVALID here (the caller pads it with one token). */
 typedef struct jl_ep jl_ep;
 int jl_ep_create(jl_moe* local, int rank, int world, int max_tokens_per_rank,
                  int topk, jl_ep** out);
