@@ -1,10 +1,12 @@
 """Expert parallelism on CPU: the exchange and combine of joule_b200.ep run as
-world_size 2 gloo ranks, with the expert compute done by the CPU oracle.
+world_size 2 and 4 gloo ranks, with the expert compute done by the CPU oracle.
 
-Each rank owns half of the experts and routes its own tokens; the layer
+Each rank owns E / world of the experts and routes its own tokens; the layer
 output of every rank must be bit-identical to the single-process oracle
 layer on the same tokens (the per-slot values and the union-order combine
-are the single-GPU ones; only where the rows are computed changes).
+are the single-GPU ones; only where the rows are computed changes). The
+4-rank case gives the ranks different batch sizes, so the all-to-all splits
+are ragged and a rank may receive no rows at all.
 """
 from __future__ import annotations
 
@@ -85,7 +87,7 @@ class OracleBackend:
         return torch.from_numpy(y)
 
 
-def _rank(rank: int, world: int, port: int, B: int, results):
+def _rank(rank: int, world: int, port: int, B: int, ragged: bool, results):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -95,26 +97,25 @@ def _rank(rank: int, world: int, port: int, B: int, results):
         from oracle import restate
         lay = olayer.make_layer(SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["norm"],
                                 seed_router=3, seed_experts=4)
-        x = olayer.hidden(B, SHAPE["d"], 100 + rank)
+        x = olayer.hidden(B + (rank if ragged else 0), SHAPE["d"], 100 + rank)
         ep = ExpertParallelMoE(OracleBackend(lay, rank, world), SHAPE["E"])
         out = ep.forward(0, torch.from_numpy(x)).numpy()
         ref, _, _ = restate.moe_layer(lay, x)
         results[rank] = (bool(np.array_equal(out, ref)), float(np.abs(out - ref).max()),
-                         list(ep.last_counts))
+                         list(ep.last_counts), x.shape[0])
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("B", [1, 6])
-def test_ep_two_ranks_matches_single_process(B):
-    world = 2
+@pytest.mark.parametrize("world,B,ragged", [(2, 1, False), (2, 6, False), (4, 1, True)])
+def test_ep_ranks_match_single_process(world, B, ragged):
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_rank, args=(world, _free_port(), B, results), nprocs=world,
+        mp.start_processes(_rank, args=(world, _free_port(), B, ragged, results), nprocs=world,
                            start_method="spawn", join=True)
         res = dict(results)
-    assert sorted(res) == [0, 1]
-    for r, (same, err, counts) in res.items():
+    assert sorted(res) == list(range(world))
+    for r, (same, err, counts, _) in res.items():
         assert same, f"rank {r}: max abs diff {err}"
-    # every slot was computed somewhere: rows received over both ranks = 2 ranks x B x k
-    assert sum(sum(c) for _, _, c in res.values()) == world * B * SHAPE["k"]
+    # every slot was computed somewhere: rows received over all ranks = the ranks' tokens x k
+    assert sum(sum(c) for _, _, c, _ in res.values()) == sum(n for *_, n in res.values()) * SHAPE["k"]
