@@ -323,3 +323,215 @@ void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
     free(y);
     free(slot_u);
 }
+
+/* ------------------------------------------------------------------------
+ * The rest of the decode step (attention, norms, lm_head) for the greedy
+ * parity pin of a full decode step. Same rounding rules as above: every
+ * scalar product and sum rounds on its own (-ffp-contract=off), the AVX2
+ * dot products are 8 fmaf lanes plus hsum8.
+ * ------------------------------------------------------------------------ */
+
+/* decode_kernel.c:88-93: halve the exponent for a first estimate, then one
+ * Newton step y' = (y + x / y) / 2. */
+float jo_sqrtf_fast(float x) {
+    bits32 v;
+    v.f = x;
+    v.u = (v.u + 0x3F800000u) >> 1;
+    const float q = x / v.f;
+    const float s = v.f + q;
+    return 0.5f * s;
+}
+
+/* decode_kernel.c:224-230: sum of squares in index order, one reciprocal of
+ * the root, then (x * inv) * w per element. */
+void jo_rms_norm(float* out, const float* x, const uint16_t* w, int d, float eps) {
+    float ss = 0.0f;
+    for (int i = 0; i < d; i++) {
+        const float sq = x[i] * x[i];
+        ss = ss + sq;
+    }
+    const float mean = ss / (float)d;
+    const float inv = 1.0f / jo_sqrtf_fast(mean + eps);
+    for (int i = 0; i < d; i++) {
+        const float t = x[i] * inv;
+        out[i] = t * jo_bf16_to_f32(w[i]);
+    }
+}
+
+/* decode_kernel.c:259-266: rotate-half RoPE with the first hd/2 entries of
+ * the position's cos / sin rows. */
+void jo_rope(float* q, const float* cs, const float* sn, int hd) {
+    const int h = hd / 2;
+    for (int i = 0; i < h; i++) {
+        const float a = q[i], b = q[i + h];
+        const float ac = a * cs[i], bs = b * sn[i], as = a * sn[i], bc = b * cs[i];
+        q[i] = ac - bs;
+        q[i + h] = as + bc;
+    }
+}
+
+/* decode_kernel.c:969-995 (lm_B_worker) and 1021-1047 (lm_A_worker): an fp32
+ * weight row against B rows, 8 fmaf lanes + hsum8, scalar tail. */
+void jo_matvec_f32w(const float* W, const float* x, int B, int n, int d, float* out) {
+    for (int b = 0; b < B; b++) {
+        const float* xb = x + (size_t)b * d;
+        for (int i = 0; i < n; i++) {
+            const float* row = W + (size_t)i * d;
+            float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int k = 0;
+            for (; k + 8 <= d; k += 8)
+                for (int j = 0; j < 8; j++) lane[j] = fmaf(row[k + j], xb[k + j], lane[j]);
+            float acc = hsum8(lane);
+            for (; k < d; k++) {
+                const float t = row[k] * xb[k];
+                acc = acc + t;
+            }
+            out[(size_t)b * n + i] = acc;
+        }
+    }
+}
+
+/* Root-mean-square norm of a vector in place with bf16 weights, the QK-norm
+ * form of decode_kernel.c:1155-1189 (n = H*hd whole-vector, or hd per head). */
+static void qk_norm(float* v, const uint16_t* w, int n, float eps) {
+    float ss = 0.0f;
+    for (int i = 0; i < n; i++) {
+        const float sq = v[i] * v[i];
+        ss = ss + sq;
+    }
+    const float mean = ss / (float)n;
+    const float inv = 1.0f / jo_sqrtf_fast(mean + eps);
+    for (int i = 0; i < n; i++) {
+        const float t = v[i] * inv;
+        v[i] = t * jo_bf16_to_f32(w[i]);
+    }
+}
+
+/* layer_attn_batch (decode_kernel.c:1120-1234), bf16 projections: q/k/v,
+ * optional bias, QK-norm (1 = per head, 2 = whole vector), RoPE, append to
+ * the KV cache, softmax attention over positions 0..pos, o_proj. */
+static void attn_layer(const jo_decoder* M, int l, float* const* kc, float* const* vc,
+                       const int* positions, const float* x, int B, float* out) {
+    const int d = M->d, H = M->H, KH = M->KH, hd = M->hd;
+    const int qn = H * hd, kn = KH * hd;
+    float* q = (float*)malloc(sizeof(float) * (size_t)B * qn);
+    float* kx = (float*)malloc(sizeof(float) * (size_t)B * kn);
+    float* vx = (float*)malloc(sizeof(float) * (size_t)B * kn);
+    float* att = (float*)malloc(sizeof(float) * (size_t)B * qn);
+    float* sc = (float*)malloc(sizeof(float) * (size_t)M->maxT);
+    jo_router_logits(M->wq + (size_t)l * qn * d, x, B, qn, d, q);
+    jo_router_logits(M->wk + (size_t)l * kn * d, x, B, kn, d, kx);
+    jo_router_logits(M->wv + (size_t)l * kn * d, x, B, kn, d, vx);
+    if (M->bias_qkv)
+        for (int b = 0; b < B; b++) {
+            for (int i = 0; i < qn; i++) q[(size_t)b * qn + i] += M->bq[(size_t)l * qn + i];
+            for (int i = 0; i < kn; i++) {
+                kx[(size_t)b * kn + i] += M->bk[(size_t)l * kn + i];
+                vx[(size_t)b * kn + i] += M->bv[(size_t)l * kn + i];
+            }
+        }
+    if (M->qk_norm_type == 2)
+        for (int b = 0; b < B; b++) {
+            qk_norm(q + (size_t)b * qn, M->qn + (size_t)l * qn, qn, M->eps);
+            qk_norm(kx + (size_t)b * kn, M->kn + (size_t)l * kn, kn, M->eps);
+        }
+    for (int b = 0; b < B; b++) {
+        float* qb = q + (size_t)b * qn;
+        float* kb = kx + (size_t)b * kn;
+        const float* vb = vx + (size_t)b * kn;
+        if (M->qk_norm_type == 1) {
+            for (int h = 0; h < H; h++) qk_norm(qb + (size_t)h * hd, M->qn + (size_t)l * hd, hd, M->eps);
+            for (int h = 0; h < KH; h++) qk_norm(kb + (size_t)h * hd, M->kn + (size_t)l * hd, hd, M->eps);
+        }
+        const int pos = positions[b];
+        const float* cs = M->cos + (size_t)pos * hd;
+        const float* sn = M->sin + (size_t)pos * hd;
+        for (int h = 0; h < H; h++) jo_rope(qb + (size_t)h * hd, cs, sn, hd);
+        for (int h = 0; h < KH; h++) jo_rope(kb + (size_t)h * hd, cs, sn, hd);
+        float* K = kc[(size_t)b * M->L + l];
+        float* V = vc[(size_t)b * M->L + l];
+        memcpy(K + (size_t)pos * kn, kb, sizeof(float) * (size_t)kn);
+        memcpy(V + (size_t)pos * kn, vb, sizeof(float) * (size_t)kn);
+        const int T = pos + 1;
+        const float scale = jo_sqrtf_fast((float)hd);
+        for (int h = 0; h < H; h++) {
+            const float* qh = qb + (size_t)h * hd;
+            const int g = h / (H / KH);
+            float smax = -1e30f;
+            for (int t = 0; t < T; t++) {
+                const float* kt = K + (size_t)t * kn + (size_t)g * hd;
+                float s = 0.0f;
+                for (int i = 0; i < hd; i++) {
+                    const float p = qh[i] * kt[i];
+                    s = s + p;
+                }
+                sc[t] = s / scale;
+                if (sc[t] > smax) smax = sc[t];
+            }
+            float sum = 0.0f;
+            for (int t = 0; t < T; t++) {
+                sc[t] = jo_expf_fast(sc[t] - smax);
+                sum = sum + sc[t];
+            }
+            float* oh = att + (size_t)b * qn + (size_t)h * hd;
+            for (int i = 0; i < hd; i++) oh[i] = 0.0f;
+            for (int t = 0; t < T; t++) {
+                const float* vt = V + (size_t)t * kn + (size_t)g * hd;
+                const float p = sc[t] / sum;
+                for (int i = 0; i < hd; i++) {
+                    const float pv = p * vt[i];
+                    oh[i] = oh[i] + pv;
+                }
+            }
+        }
+    }
+    jo_router_logits(M->wo + (size_t)l * d * qn, att, B, d, qn, out);
+    free(q);
+    free(kx);
+    free(vx);
+    free(att);
+    free(sc);
+}
+
+/* decode_layers_batch / decode_layers_batch_argmax (decode_kernel.c:1518-1586)
+ * on the Q4 MoE layers: per layer h += attn(norm1(h)), h += moe(norm2(h));
+ * then the final norm and the fp32 lm_head. */
+void jo_decode_step(const jo_decoder* M, float* const* kc, float* const* vc, const int* positions,
+                    const float* x, int B, int* out_tok, float* logits) {
+    const int d = M->d, E = M->E;
+    float* h = (float*)malloc(sizeof(float) * (size_t)B * d);
+    float* t = (float*)malloc(sizeof(float) * (size_t)B * d);
+    float* h2 = (float*)malloc(sizeof(float) * (size_t)B * d);
+    float* lg = (float*)malloc(sizeof(float) * (size_t)B * M->V);
+    memcpy(h, x, sizeof(float) * (size_t)B * d);
+    for (int l = 0; l < M->L; l++) {
+        for (int b = 0; b < B; b++)
+            jo_rms_norm(t + (size_t)b * d, h + (size_t)b * d, M->norm1 + (size_t)l * d, d, M->eps);
+        attn_layer(M, l, kc, vc, positions, t, B, h2);
+        for (size_t i = 0; i < (size_t)B * d; i++) h[i] = h[i] + h2[i];
+        for (int b = 0; b < B; b++)
+            jo_rms_norm(t + (size_t)b * d, h + (size_t)b * d, M->norm2 + (size_t)l * d, d, M->eps);
+        jo_moe_layer(d, E, M->k, M->m, M->norm_topk_prob, M->gate_w + (size_t)l * E * d,
+                     M->pk + (size_t)l * 3 * E, M->sc + (size_t)l * 3 * E, t, B, h2, NULL, NULL);
+        for (size_t i = 0; i < (size_t)B * d; i++) h[i] = h[i] + h2[i];
+    }
+    for (int b = 0; b < B; b++)
+        jo_rms_norm(t + (size_t)b * d, h + (size_t)b * d, M->final_norm, d, M->eps);
+    jo_matvec_f32w(M->lm_head, t, B, M->V, d, lg);
+    for (int b = 0; b < B; b++) {
+        const float* r = lg + (size_t)b * M->V;
+        int best = 0;
+        float bv = -1e30f;
+        for (int v = 0; v < M->V; v++)
+            if (r[v] > bv) {
+                bv = r[v];
+                best = v;
+            }
+        if (out_tok) out_tok[b] = best;
+    }
+    if (logits) memcpy(logits, lg, sizeof(float) * (size_t)B * M->V);
+    free(h);
+    free(t);
+    free(h2);
+    free(lg);
+}

@@ -60,6 +60,40 @@ void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
                   const uint16_t* const* sc, const float* x, int B,
                   float* out, int* top, float* tw);
 
+/* ---- the rest of the decode step (greedy parity pin) ---- */
+
+/* decode_kernel.c:88-93 */
+float jo_sqrtf_fast(float x);
+/* decode_kernel.c:224-230: out[d] = rms_norm(x) * bf16 w */
+void jo_rms_norm(float* out, const float* x, const uint16_t* w, int d, float eps);
+/* decode_kernel.c:259-266: rotate-half RoPE of one head in place */
+void jo_rope(float* q, const float* cs, const float* sn, int hd);
+/* out[B, n] = fp32 W[n, d] @ x[B, d]^T: decode_kernel.c:969-995, 1021-1047 */
+void jo_matvec_f32w(const float* W, const float* x, int B, int n, int d, float* out);
+
+/* A decoder in the reference's weight layout (KernelW, decode_kernel.c:288-325)
+ * with Q4 MoE layers. bf16 weights: embed [V, d], norm1/norm2 [L, d],
+ * final_norm [d], wq [L, H*hd, d], wk/wv [L, KH*hd, d], wo [L, d, H*hd],
+ * qn/kn [L, hd] (qk_norm_type 1) or [L, H*hd] / [L, KH*hd] (type 2),
+ * gate_w [L, E, d]. fp32: lm_head [V, d], bq/bk/bv [L, H*hd / KH*hd],
+ * cos/sin [maxT, hd]. pk/sc: index (l*3 + p)*E + e, p = gate, up, down. */
+typedef struct {
+    int L, d, H, KH, hd, E, k, m, V, maxT, qk_norm_type, bias_qkv, norm_topk_prob;
+    float eps;
+    const uint16_t *embed, *final_norm, *norm1, *norm2, *wq, *wk, *wv, *wo, *qn, *kn, *gate_w;
+    const float *lm_head, *bq, *bk, *bv, *cos, *sin;
+    const uint8_t* const* pk;
+    const uint16_t* const* sc;
+} jo_decoder;
+
+/* One batched decode step (decode_layers_batch[_argmax], decode_kernel.c:
+ * 1518-1586): x [B, d] embedded inputs at positions[b]; kc/vc: B*L caches
+ * kc[b*L + l] = [maxT, KH, hd] fp32 (the reference's kv[b*L + l]), appended
+ * at positions[b]. out_tok [B] (argmax, lowest index on ties) and logits
+ * [B, V] are nullable. */
+void jo_decode_step(const jo_decoder* M, float* const* kc, float* const* vc, const int* positions,
+                    const float* x, int B, int* out_tok, float* logits);
+
 #ifdef __cplusplus
 }
 #endif

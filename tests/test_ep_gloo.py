@@ -109,7 +109,7 @@ def _rank(rank: int, world: int, port: int, B: int, ragged: bool, results):
 
 @pytest.mark.parametrize("world,B,ragged", [(2, 1, False), (2, 6, False), (4, 1, True)])
 def test_ep_ranks_match_single_process(world, B, ragged):
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # no fork of a threaded process
         results = mgr.dict()
         mp.start_processes(_rank, args=(world, _free_port(), B, ragged, results), nprocs=world,
                            start_method="spawn", join=True)
