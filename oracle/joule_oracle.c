@@ -233,11 +233,26 @@ static inline float silu_mul(float g, float u) {
     return sg * u;
 }
 
-void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
-                  const uint16_t* gate_w, const uint8_t* const* pk,
-                  const uint16_t* const* sc, const float* x, int B,
-                  float* out, int* top_out, float* tw_out) {
-    const int nb = d / 2, ng = d / 64, nb_d = m / 2, ng_d = m / 64;
+/* One expert row against one activation row: the Q4 row dot
+ * (decode_kernel.c:770-858) or, for the bf16 tier, bf16_row_dot_B
+ * (decode_kernel.c:934-963), whose 8 FMA lanes + hsum8 + scalar tail are the
+ * order of jo_router_logits. */
+static float expert_row_dot(int bf16, const void* w, const uint16_t* sc, int row, int ncols,
+                            const float* x) {
+    float acc;
+    if (bf16) {
+        jo_router_logits((const uint16_t*)w + (size_t)row * ncols, x, 1, 1, ncols, &acc);
+    } else {
+        jo_q4_row_dot_B((const uint8_t*)w + (size_t)row * (ncols / 2), sc + (size_t)row * (ncols / 64),
+                        x, 1, ncols, ncols, &acc);
+    }
+    return acc;
+}
+
+static void moe_layer(int bf16, int d, int E, int k, int m, int norm_topk_prob,
+                      const uint16_t* gate_w, const void* const* pk,
+                      const uint16_t* const* sc, const float* x, int B,
+                      float* out, int* top_out, float* tw_out) {
     const int S = B * k;
     float* logits = (float*)malloc(sizeof(float) * (size_t)B * E);
     int* top = (int*)malloc(sizeof(int) * (size_t)S);
@@ -254,33 +269,32 @@ void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
     jo_route(logits, B, E, k, norm_topk_prob, top, tw, NULL);
     const int U = jo_dispatch(top, tw, B, k, E, sel, uh, uidx, uw);
 
-    /* ffn_expert_worker, Q4 branch (decode_kernel.c:1365-1384): for each
-     * union expert and each of its slots (token b = slot / k), the gate and
-     * up rows give act = silu(g) * u, then down rows give
-     * y = w * dacc (the reference's `ye += uw * dacc` onto a zeroed ye). */
+    /* ffn_expert_worker, Q4 branch (decode_kernel.c:1365-1384) and bf16
+     * branch (1276-1301): for each union expert and each of its slots
+     * (token b = slot / k), the gate and up rows give act = silu(g) * u, then
+     * down rows give y = w * dacc (the reference's `ye += uw * dacc` onto a
+     * zeroed ye). */
     for (int u = 0; u < U; u++) {
         const int e = sel[u];
-        const uint8_t* pkg = pk[0 * E + e];
-        const uint8_t* pku = pk[1 * E + e];
-        const uint8_t* pkd = pk[2 * E + e];
-        const uint16_t* scg = sc[0 * E + e];
-        const uint16_t* scu = sc[1 * E + e];
-        const uint16_t* scd = sc[2 * E + e];
+        const void* pkg = pk[0 * E + e];
+        const void* pku = pk[1 * E + e];
+        const void* pkd = pk[2 * E + e];
+        const uint16_t* scg = bf16 ? NULL : sc[0 * E + e];
+        const uint16_t* scu = bf16 ? NULL : sc[1 * E + e];
+        const uint16_t* scd = bf16 ? NULL : sc[2 * E + e];
         for (int s = uh[u]; s < uh[u + 1]; s++) {
             const int slot = uidx[s];
             const int b = slot / k;
             const float* xb = x + (size_t)b * d;
             slot_u[slot] = u;
             for (int i = 0; i < m; i++) {
-                float g, up;
-                jo_q4_row_dot_B(pkg + (size_t)i * nb, scg + (size_t)i * ng, xb, 1, d, d, &g);
-                jo_q4_row_dot_B(pku + (size_t)i * nb, scu + (size_t)i * ng, xb, 1, d, d, &up);
+                const float g = expert_row_dot(bf16, pkg, scg, i, d, xb);
+                const float up = expert_row_dot(bf16, pku, scu, i, d, xb);
                 act[i] = silu_mul(g, up);
             }
             float* ys = y + (size_t)slot * d;
             for (int i = 0; i < d; i++) {
-                float dacc;
-                jo_q4_row_dot_B(pkd + (size_t)i * nb_d, scd + (size_t)i * ng_d, act, 1, m, m, &dacc);
+                const float dacc = expert_row_dot(bf16, pkd, scd, i, m, act);
                 const float t = uw[s] * dacc;
                 ys[i] = 0.0f + t;
             }
@@ -322,6 +336,21 @@ void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
     free(act);
     free(y);
     free(slot_u);
+}
+
+void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
+                  const uint16_t* gate_w, const uint8_t* const* pk,
+                  const uint16_t* const* sc, const float* x, int B,
+                  float* out, int* top_out, float* tw_out) {
+    moe_layer(0, d, E, k, m, norm_topk_prob, gate_w, (const void* const*)pk, sc, x, B, out,
+              top_out, tw_out);
+}
+
+void jo_moe_layer_bf16(int d, int E, int k, int m, int norm_topk_prob,
+                       const uint16_t* gate_w, const uint16_t* const* bw, const float* x, int B,
+                       float* out, int* top_out, float* tw_out) {
+    moe_layer(1, d, E, k, m, norm_topk_prob, gate_w, (const void* const*)bw, NULL, x, B, out,
+              top_out, tw_out);
 }
 
 /* ------------------------------------------------------------------------

@@ -60,6 +60,13 @@ void jo_moe_layer(int d, int E, int k, int m, int norm_topk_prob,
                   const uint16_t* const* sc, const float* x, int B,
                   float* out, int* top, float* tw);
 
+/* The bf16 expert tier of the same layer (decode_kernel.c:1276-1301, taken
+ * when KernelCfg.expert_bf16 is set): bw[p*E + e] points at expert e's part p
+ * as a bf16 matrix, gate/up [m, d] and down [d, m]; no scales. */
+void jo_moe_layer_bf16(int d, int E, int k, int m, int norm_topk_prob,
+                       const uint16_t* gate_w, const uint16_t* const* bw, const float* x, int B,
+                       float* out, int* top_out, float* tw_out);
+
 /* ---- the rest of the decode step (greedy parity pin) ---- */
 
 /* decode_kernel.c:88-93 */

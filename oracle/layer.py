@@ -64,3 +64,33 @@ def make_layer(d: int, E: int, k: int, m: int, norm_topk_prob: int,
             lay.scales[p][e] = s
             lay.packed[p][e] = pk
     return lay
+
+
+@dataclass
+class BF16Layer:
+    """The bf16 expert tier (decode_kernel.c:1276-1301): experts as bf16
+    matrices, no scales. weights[p][e]: gate/up [m, d], down [d, m] uint16."""
+    d: int
+    E: int
+    k: int
+    m: int
+    norm_topk_prob: int
+    gate_w: np.ndarray
+    weights: list = field(default_factory=list)
+
+    def shape(self, p: int) -> tuple[int, int]:
+        return (self.m, self.d) if p < 2 else (self.d, self.m)
+
+
+def make_layer_bf16(d: int, E: int, k: int, m: int, norm_topk_prob: int,
+                    seed_router: int = 0, seed_experts: int = 1, std: float = 0.02) -> BF16Layer:
+    """Router as make_layer; expert e part p drawn fp32 N(0, std) in the order
+    e = 0..E-1, p = gate, up, down from one generator, rounded to bf16."""
+    lay = BF16Layer(d, E, k, m, norm_topk_prob, router_weights(E, d, seed_router),
+                    [[None] * E for _ in range(3)])
+    g = torch.Generator().manual_seed(seed_experts)
+    for e in range(E):
+        for p in range(3):
+            w = torch.randn(*lay.shape(p), generator=g, dtype=torch.float32) * std
+            lay.weights[p][e] = w.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16).copy()
+    return lay

@@ -140,6 +140,46 @@ class RefLayer:
         return out
 
 
+class RefLayerBF16:
+    """The reference's layer_ffn_batch on its bf16 expert tier (KernelCfg.expert_bf16 = 1,
+    decode_kernel.c:1276-1301): expert_pk[p][e] points at the bf16 matrix; the
+    scale tables are read as pointers but never dereferenced on this tier."""
+
+    def __init__(self, lay):
+        self.lay = lay
+        E = lay.E
+        self.cfg = KernelCfg(L=1, d=lay.d, n_heads=1, n_kv=1, hd=lay.d, E=E, topk=lay.k, V=1,
+                             eps=1e-6, maxT=1, intermediate=lay.m, qk_norm_type=0,
+                             bias_qkv=0, norm_topk_prob=lay.norm_topk_prob,
+                             expert_i8=0, expert_bf16=1)
+        self._pk = [(_P * E)(*[lay.weights[p][e].ctypes.data for e in range(E)]) for p in range(3)]
+        self._sc = [(_P * E)() for _ in range(3)]
+        self.W = KernelW()
+        self.W.gate_w = lay.gate_w.ctypes.data
+        for p in range(3):
+            self.W.expert_pk[p] = ctypes.cast(self._pk[p], _P)
+            self.W.expert_sc[p] = ctypes.cast(self._sc[p], _P)
+        self.L = lib()
+
+    def ffn_debug(self, x: np.ndarray) -> dict:
+        """One call (B <= 16): output, top-k ids and weights."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, self.lay.d)
+        B, k, E = x.shape[0], self.lay.k, self.lay.E
+        assert B <= BMAX
+        out = np.empty_like(x)
+        top = np.empty(B * k, np.int32)
+        tw = np.empty(B * k, np.float32)
+        sel = np.empty(E, np.int32)
+        uh = np.empty(E + 1, np.int32)
+        uidx = np.empty(B * k, np.int32)
+        uw = np.empty(B * k, np.float32)
+        U = ctypes.c_int(0)
+        self.L.oracle_ffn_debug(ctypes.byref(self.cfg), ctypes.byref(self.W), 0, x.ctypes.data, B,
+                                out.ctypes.data, top.ctypes.data, tw.ctypes.data, sel.ctypes.data,
+                                uh.ctypes.data, uidx.ctypes.data, uw.ctypes.data, ctypes.byref(U))
+        return dict(out=out, top=top.reshape(B, k), tw=tw.reshape(B, k))
+
+
 def q4_gemv_scalar(x, packed, scales, m, d) -> np.ndarray:
     """quant_gemv.c:35-57 (the scalar statement of the Q4 GEMV)."""
     out = np.empty(m, np.float32)

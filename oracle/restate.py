@@ -39,7 +39,8 @@ def lib() -> ctypes.CDLL:
         L.jo_dispatch.argtypes = [_P, _P, _I, _I, _I, _P, _P, _P, _P]
         L.jo_dispatch.restype = _I
         L.jo_moe_layer.argtypes = [_I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P]
-        for f in (L.jo_q4_gemm, L.jo_router_logits, L.jo_route, L.jo_moe_layer):
+        L.jo_moe_layer_bf16.argtypes = [_I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P]
+        for f in (L.jo_q4_gemm, L.jo_router_logits, L.jo_route, L.jo_moe_layer, L.jo_moe_layer_bf16):
             f.restype = None
         _LIB = L
     return _LIB
@@ -117,4 +118,17 @@ def moe_layer(lay: Q4Layer, x: np.ndarray):
     lib().jo_moe_layer(lay.d, lay.E, lay.k, lay.m, lay.norm_topk_prob,
                        _ptr(lay.gate_w), ctypes.cast(t.pk, _P), ctypes.cast(t.sc, _P),
                        _ptr(x), B, _ptr(out), _ptr(top), _ptr(tw))
+    return out, top, tw
+
+
+def moe_layer_bf16(lay, x: np.ndarray):
+    """The bf16 expert tier of the layer (jo_moe_layer_bf16): (out, top, tw)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, lay.d)
+    B, E, k = x.shape[0], lay.E, lay.k
+    bw = (_P * (3 * E))(*[lay.weights[p][e].ctypes.data for p in range(3) for e in range(E)])
+    out = np.empty_like(x)
+    top = np.empty((B, k), np.int32)
+    tw = np.empty((B, k), np.float32)
+    lib().jo_moe_layer_bf16(lay.d, E, k, lay.m, lay.norm_topk_prob, _ptr(lay.gate_w), bw,
+                            _ptr(x), B, _ptr(out), _ptr(top), _ptr(tw))
     return out, top, tw

@@ -132,3 +132,23 @@ def test_restatement_vs_compiled_reference_random(shape):
     out, top, tw = restate.moe_layer(lay, x)
     assert np.array_equal(out, dbg["out"]) and np.array_equal(top, dbg["top"])
     assert np.array_equal(tw, dbg["tw"])
+
+
+BF16 = ["moe_bf16_small_b1", "moe_bf16_small_b5", "moe_bf16_small_b16", "moe_bf16_mid_b5",
+        "moe_bf16_wide_b16"]
+
+
+@pytest.mark.parametrize("name", BF16)
+def test_moe_layer_bf16_tier_bit_exact(name):
+    """The bf16 expert tier (expert_bf16 = 1, decode_kernel.c:1276-1301) restated:
+    output, top-k ids and weights bit-identical to the reference's layer_ffn_batch."""
+    from oracle import layer as olayer
+    g = golden(name)
+    d, E, k, m, norm = (int(v) for v in g["cfg"])
+    lay = olayer.make_layer_bf16(d, E, k, m, norm, seed_router=int(g["seeds"][0]),
+                                 seed_experts=int(g["seeds"][1]))
+    x = olayer.hidden(g["out"].shape[0], d, int(g["seeds"][2]))
+    out, top, tw = restate.moe_layer_bf16(lay, x)
+    assert np.array_equal(top, g["top"])
+    assert np.array_equal(tw.view(np.uint32), g["tw"].view(np.uint32))
+    assert np.array_equal(out.view(np.uint32), g["out"].view(np.uint32))
