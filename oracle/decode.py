@@ -236,6 +236,23 @@ class RefDecoder:
                                      xs.ctypes.data, B, logits.ctypes.data)
         return np.argmax(logits, axis=1).astype(np.int32), logits
 
+    def prefill(self, tokens) -> np.ndarray:
+        """prefill_layers (decode_kernel.c:1606-1615) of one prompt on fresh
+        caches: one decode step per position, last-token logits [V]."""
+        s = self.model.shape
+        self.lib.prefill_layers.argtypes = [_P, _P, _P, _P, _I, _P]
+        self.lib.prefill_layers.restype = None
+        caches = _Caches(s, 1)
+        kv = (_P * (2 * s.L))()
+        for i in range(s.L):
+            kv[2 * i] = caches.k[i].ctypes.data
+            kv[2 * i + 1] = caches.v[i].ctypes.data
+        tok = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(s.V, np.float32)
+        self.lib.prefill_layers(ctypes.byref(self.cfg), ctypes.byref(self.W), kv, tok.ctypes.data,
+                                len(tok), logits.ctypes.data)
+        return logits
+
     def argmax_entry(self, caches: _Caches, b0: int, x: np.ndarray, positions) -> np.ndarray:
         """decode_layers_batch_argmax on the same step (it appends the same K/V rows)."""
         B = x.shape[0]
@@ -283,3 +300,13 @@ def greedy(dec, prompts: list[list[int]], n_new: int):
         cur = nxt
         pos = pos + 1
     return toks, logits
+
+
+def prefill(dec, tokens) -> np.ndarray:
+    """One prompt through ``dec`` a position at a time on fresh caches, as
+    prefill_layers does: the logits [V] of the last token."""
+    caches = _Caches(dec.model.shape, 1)
+    lg = None
+    for t, token in enumerate(tokens):
+        _, lg = dec.step(caches, 0, embed(dec.model, [token]), [t])
+    return lg[0]
