@@ -25,27 +25,43 @@ def record_views(mm: np.ndarray, rec: dict) -> tuple[np.ndarray, np.ndarray]:
     return mm[o:o + sb].view(np.uint16), mm[o + sb:o + sb + pb]
 
 
+class StoreReader:
+    """The index and a read-only memory map of one ``experts_q4.bin``."""
+
+    def __init__(self, store_dir: str | Path):
+        store_dir = Path(store_dir)
+        self.index = json.loads((store_dir / "experts_q4.json").read_text())
+        self.mm = np.memmap(store_dir / "experts_q4.bin", dtype=np.uint8, mode="r")
+
+    def layer(self, l: int, E: int, d: int, m: int) -> tuple[list, list]:
+        """(packed[p][e], scales[p][e]) of layer l, contiguous copies in the
+        reference record layout; p = gate, up, down. A record whose shape is
+        not gate/up [m, d] or down [d, m] raises ValueError."""
+        packed = [[None] * E for _ in range(3)]
+        scales = [[None] * E for _ in range(3)]
+        for e in range(E):
+            for p, part in enumerate(PARTS):
+                key = f"{l}.{e}.{part}"
+                if key not in self.index:
+                    raise ValueError(f"record {key} missing from the store index")
+                rec = self.index[key]
+                want = (m, d) if p < 2 else (d, m)
+                if tuple(rec["shape"]) != want:
+                    raise ValueError(f"record {key} has shape {rec['shape']}, expected {list(want)}")
+                s, pk = record_views(self.mm, rec)
+                scales[p][e] = np.ascontiguousarray(s)
+                packed[p][e] = np.ascontiguousarray(pk)
+        return packed, scales
+
+
 def load_store(moe, store_dir: str | Path, gate_w: np.ndarray, layers=None) -> None:
     """Upload layers (default: all) of the store in ``store_dir`` into ``moe``.
 
     gate_w: the router weights [L, E, d] as bf16 bit patterns (uint16), which
     the reference keeps with the fixed weights rather than in the Q4 store.
     """
-    store_dir = Path(store_dir)
-    index = json.loads((store_dir / "experts_q4.json").read_text())
-    mm = np.memmap(store_dir / "experts_q4.bin", dtype=np.uint8, mode="r")
+    reader = StoreReader(store_dir)
     cfg = moe.cfg
     for l in (range(cfg.L) if layers is None else layers):
-        packed = [[None] * cfg.E for _ in range(3)]
-        scales = [[None] * cfg.E for _ in range(3)]
-        for e in range(cfg.E):
-            for p, part in enumerate(PARTS):
-                rec = index[f"{l}.{e}.{part}"]
-                rows, cols = rec["shape"]
-                want = (cfg.intermediate, cfg.d) if p < 2 else (cfg.d, cfg.intermediate)
-                if (rows, cols) != want:
-                    raise ValueError(f"record {l}.{e}.{part} has shape {rec['shape']}, expected {want}")
-                s, pk = record_views(mm, rec)
-                scales[p][e] = np.ascontiguousarray(s)
-                packed[p][e] = np.ascontiguousarray(pk)
+        packed, scales = reader.layer(l, cfg.E, cfg.d, cfg.intermediate)
         moe.upload_layer(l, np.ascontiguousarray(gate_w[l]), packed, scales)
