@@ -63,9 +63,8 @@ class Clocks:
 
     def __enter__(self):
         try:
-            out = ROOT / "gpurun_out"
-            out.mkdir(exist_ok=True)
-            self.path = out / f"clocks_gpu{self.gpu}.csv"
+            import tempfile
+            self.path = Path(tempfile.mkdtemp(prefix="joule_clocks_")) / f"clocks_gpu{self.gpu}.csv"
             self.f = open(self.path, "w")
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
                                        "--format=csv,noheader,nounits", "-lms", "100"],

@@ -116,6 +116,32 @@ int jl_q4_gemm_f32(float* out, const float* X, int T,
                    int m, int d, int group, void* stream);
 
 /* ------------------------------------------------------------------ */
+/* The reference's own symbols, with its signatures (host pointers, void,
+ * synchronous), so that its unmodified Python binds this library through
+ * get_dll (src/jouleai/native/backend.py:32-42). Inputs are copied to device
+ * buffers the library caches per device, the kernel runs on the current
+ * device, and the result is back in `out` when the call returns. A failed
+ * call (bad argument, no device, CUDA error) fills `out` with NaN and
+ * jl_compat_status() returns its JL_ERR_* code. */
+
+/* quant_gemv.c:35-57 (bound by kernel.py:15-41 and ScalarBackend,
+ * backend.py:72-91): out[m] = dequant(packed, scales) @ x[d], the scalar
+ * loop's order (per byte gacc += lo*x0 + hi*x1; acc += gacc*s per group).
+ * group must be 64 and d a multiple of 64. */
+void q4_gemv_f32(float* out, const float* x, const unsigned char* packed,
+                 const unsigned short* scales, int m, int d, int group);
+
+/* expert_ffn.c:200-215 (bound by kernel.py:43-62 and AVX2Backend,
+ * backend.py:94-116): out[T, m] = X[T, d] @ dequant(W)^T in the AVX2 row
+ * dot's order, as jl_q4_gemm_f32. T = 0 does nothing. */
+void q4_gemm_f32(float* out, const float* X, int T, const unsigned char* packed,
+                 const unsigned short* scales, int m, int d, int group);
+
+/* Status of this thread's last q4_gemv_f32 / q4_gemm_f32 call (JL_OK or a
+ * JL_ERR_* code). No counterpart in the reference, whose calls return void. */
+int jl_compat_status(void);
+
+/* ------------------------------------------------------------------ */
 /* Q4 store: on-device quantiser and repack. */
 
 /* Quantise n fp32 values (device) into the reference's Q4 record format:
@@ -170,9 +196,6 @@ int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
 #define JL_PATH_AUTO 0  /* exact for B <= 3, tensor-core beyond (d % 512 == 0, m % 256 == 0) */
 #define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order */
 #define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
-#define JL_PATH_EXACT_FUSED 3 /* the exact path for B <= 8 as ONE persistent launch (router, top-k,
-                                dispatch, gate/up, down, combine), same results; larger B runs as
-                                JL_PATH_EXACT */
 int jl_moe_set_path(jl_moe* h, int path);
 
 /* One MoE FFN layer: out[B, d] = MoE(x[B, d]) for layer l (device fp32).
@@ -311,9 +334,10 @@ int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n);
  * B > 64 returns JL_ERR_CAPACITY and E > 256 JL_ERR_INVALID; calls on one
  * device must not overlap (one stream, or ordered by events); the first call
  * on a device performs a one-time setup that must precede any stream
- * capture. dev_status (nullable, device int) must hold 0 before the call;
- * the kernels OR bit 1 into it when a bounded wait runs out. For hosts that
- * must not allocate per request. */
+ * capture. dev_status (device int, required; NULL is JL_ERR_INVALID) must
+ * hold 0 before the call; the kernels OR bit 1 into it when a bounded wait
+ * runs out, and top/tw are then not valid. For hosts that must not allocate
+ * per request. */
 int jl_route_noalloc(const unsigned short* gate_w, const float* x, int B, int E,
                      int d, int topk, int norm_topk_prob, int* top, float* tw,
                      int* dev_status, void* stream);

@@ -232,6 +232,7 @@ __global__ void k_ep_send(const float* __restrict__ x, const int* __restrict__ t
     griddep_launch_dependents();
     for (int s = blockIdx.x; s < S; s += gridDim.x) {
         const int e = top[s], q = e / E_local;
+        if (e < 0 || q >= world) continue;  // k_ep_order flagged it; store nothing
         int base = 0;
         for (int w = 0; w < q; w++) base += counts[w];
         const int i = pos[s] - base;
@@ -330,7 +331,8 @@ __global__ void k_ep_gather_out(const uint8_t* __restrict__ buf, ep_layout o, co
     const float* ret = reinterpret_cast<const float*>(buf + o.ret);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < k; j++) {
-        const int s = comb[b * k + j], q = top[s] / E_local;
+        const int s = comb[b * k + j], e = top[s], q = e / E_local;
+        if (e < 0 || q >= world) continue;  // k_ep_order flagged it; the term is dropped
         int base = 0;
         for (int w = 0; w < q; w++) base += counts[w];
         const float4 v = __ldcv(reinterpret_cast<const float4*>(ret + ((size_t)q * cap + pos[s] - base) * d + c));

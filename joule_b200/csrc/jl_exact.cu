@@ -320,14 +320,11 @@ size_t down_smem(int m) {
 }  // namespace jl
 
 static int exact_attrs() {
-    using namespace jl;
-    static bool attr = false;
-    if (!attr) {
-        JL_CUDA(cudaFuncSetAttribute(k_gateup_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        JL_CUDA(cudaFuncSetAttribute(k_down_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        attr = true;
-    }
-    return JL_OK;
+    return jl_device_once(kOnceExact, [] {
+        JL_CUDA(cudaFuncSetAttribute(jl::k_gateup_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        JL_CUDA(cudaFuncSetAttribute(jl::k_down_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        return JL_OK;
+    });
 }
 
 int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float* x, int B,

@@ -51,7 +51,6 @@ struct jl_ws {
     float* act;      // [Bmax*k, m] SwiGLU output per slot
     float* y;        // [Bmax*k, d] weighted expert output per slot
     int* counter;    // [1] last-block counter of the router kernel
-    int* fsync;      // [8 + 256 + d/128] counters of the single-launch small-batch layer (jl_fused.cu)
     int* err;        // [1] device error word (jl::kErr* bits)
     long long* trace;  // [kTraceSlots] phase timestamps, nullptr when tracing is off
     // tensor-core path
@@ -95,6 +94,16 @@ struct jl_moe {
 
 // ---- launchers (return JL_OK or JL_ERR_*) --------------------------------
 
+// Runs `setup` once per (current device, key) and returns its status (JL_OK
+// on later calls). Kernel attributes such as the dynamic shared-memory limit
+// are per device, so a process that drives several GPUs sets them on each;
+// callers from several host threads are serialised. key < 32.
+enum {
+    kOnceExact = 0, kOnceRouter, kOnceRouterFast, kOnceDispatch, kOnceGemm, kOnceTc, kOnceGemv,
+    kOnceDecode, kOnceEp
+};
+int jl_device_once(int key, int (*setup)());
+
 // jl_store.cu
 int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, const jl_layout& L,
                           uint8_t* rec, cudaStream_t s);
@@ -128,16 +137,6 @@ int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float*
                            cudaStream_t s);
 int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
 int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s);
-
-// jl_fused.cu: the whole layer in one persistent launch for B <= 8 (same
-// results as route + gate/up + down + combine of the exact path).
-bool jl_layer_small_ok(const jl_moe* h, int B);
-int jl_launch_layer_small(const jl_moe* h, const unsigned short* gate_w_l, const uint8_t* store_l,
-                          const float* x, int B, float* out, int* top, float* tw, cudaStream_t s);
-// ws.fsync layout (ints): [0, 8) counters of the single-launch layer; [8, 264)
-// its per-expert finished gate/up units; [264, 264 + d/128) its finished
-// down units per 128-row block.
-size_t jl_fsync_bytes(int d);
 
 // jl_tc.cu: tensor-core expert FFN (permute -> gate/up+SwiGLU -> down).
 // The tile table is built at the end of the dispatch step (jl_tiles.cuh).

@@ -54,7 +54,7 @@ ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
         S * d * 4,             // y
         16,                    // counter
         16,                    // err
-        jl_fsync_bytes(d),     // fsync
+        16,                    // (unused)
         tc_bytes,              // tensor-core path: xc, ac, tile table, tile count
     };
     ws_plan p;
@@ -80,6 +80,27 @@ std::atomic<int> g_last_cuda{0};
 int jl_note_cuda(cudaError_t e) {
     g_last_cuda.store((int)e);
     return JL_ERR_CUDA;
+}
+
+namespace {
+constexpr int kOnceDevices = 128;
+std::mutex g_once_mu;
+std::atomic<uint32_t> g_once[kOnceDevices];
+}  // namespace
+
+int jl_device_once(int key, int (*setup)()) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return jl_note_cuda(e);
+    if (dev < 0 || dev >= kOnceDevices || key < 0 || key >= 32) return JL_ERR_INVALID;
+    const uint32_t bit = 1u << key;
+    if (g_once[dev].load(std::memory_order_acquire) & bit) return JL_OK;
+    std::lock_guard<std::mutex> lk(g_once_mu);
+    if (g_once[dev].load(std::memory_order_relaxed) & bit) return JL_OK;
+    const int rc = setup();
+    if (rc) return rc;
+    g_once[dev].fetch_or(bit, std::memory_order_release);
+    return JL_OK;
 }
 
 extern "C" const char* jl_last_cuda_error(void) {
@@ -150,7 +171,6 @@ extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags,
     h->ws.y = (float*)(b + wp.off[11]);
     h->ws.counter = (int*)(b + wp.off[12]);
     h->ws.err = (int*)(b + wp.off[13]);
-    h->ws.fsync = (int*)(b + wp.off[14]);
     {
         uint8_t* t = b + wp.off[15];
         h->ws.xc_plane = wp.xc_plane;
@@ -190,7 +210,7 @@ extern "C" int jl_moe_destroy(jl_moe* h) {
 }
 
 extern "C" int jl_moe_set_path(jl_moe* h, int path) {
-    if (!h || path < JL_PATH_AUTO || path > JL_PATH_EXACT_FUSED) return JL_ERR_INVALID;
+    if (!h || path < JL_PATH_AUTO || path > JL_PATH_TC) return JL_ERR_INVALID;
     h->path = path;
     return JL_OK;
 }
@@ -321,18 +341,6 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
     int rc = mark(0);
     const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
     const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
-    // (phase events time the separate kernels, so they select the split form)
-    if (!rc && !tc && mask == 7 && h->path == JL_PATH_EXACT_FUSED && h->n_phase_ev == 0 &&
-        jl_layer_small_ok(h, B)) {
-        // the whole layer in one launch (same results as the phases below)
-        rc = jl_launch_layer_small(h, gw, store_l, x, B, out, top, tw, s);
-        if (!rc) rc = mark(1);
-        if (!rc) rc = mark(2);
-        if (!rc) rc = mark(3);
-        if (rc) return rc;
-        h->last_B = B;
-        return JL_OK;
-    }
     if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, tc, s);
     if (!rc) rc = mark(1);
     if (tc) {
@@ -443,11 +451,7 @@ extern "C" int jl_moe_check(jl_moe* h, void* stream) {
     int err = 0;
     JL_CUDA(cudaMemcpyAsync(&err, h->ws.err, sizeof(int), cudaMemcpyDeviceToHost, s));
     JL_CUDA(cudaStreamSynchronize(s));
-    if (err) {
-        // a kernel that gave up may have left the small-batch layer's counters mid-way
-        JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
-        JL_CUDA(cudaMemsetAsync(h->ws.fsync, 0, jl_fsync_bytes(h->d), s));
-    }
+    if (err) JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
     JL_CUDA(cudaStreamSynchronize(s));
     if (err & jl::kErrTimeout) return JL_ERR_TIMEOUT;
     if (err) return JL_ERR_DEVICE;

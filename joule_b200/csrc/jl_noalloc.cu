@@ -19,8 +19,10 @@
 //    router kernel's shared-memory limit. That first call must come before any
 //    stream capture is begun on the device;
 //  - the scratch needs no clearing: every logit the top-k step reads was
-//    written earlier in the same call. The optional caller-owned status word
-//    must hold zero before the call; kernels only OR error bits into it;
+//    written earlier in the same call. The caller-owned status word is
+//    required (a bounded wait that runs out leaves this call's logits
+//    unwritten, and the status word is the only place that says so); it must
+//    hold zero before the call, and the kernels only OR error bits into it;
 //  - one scratch array per device is shared by all callers, so two calls on
 //    the same device must not overlap in time: issue them on one stream, or
 //    order them with events. Overlapping calls race on the logits.
@@ -38,9 +40,8 @@ constexpr int kNoAllocMaxK = 16;
 constexpr int kNoAllocDevices = 64;
 constexpr int kNoAllocLogits = kNoAllocMaxB * kNoAllocMaxE;
 
-// [kNoAllocLogits] fp32 logits, then one int used as the error sink when
-// the caller passes no status word (64 floats keep the tail 256-B aligned).
-__device__ __align__(256) float g_noalloc_scratch[kNoAllocLogits + 64];
+// [kNoAllocLogits] fp32 router logits.
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocLogits];
 
 std::atomic<float*> g_scratch_dev[kNoAllocDevices];
 std::mutex g_setup_mu;
@@ -75,7 +76,7 @@ extern "C" int jl_route_noalloc(const unsigned short* gate_w, const float* x, in
                                 void* stream) {
     if (B < 0) return JL_ERR_INVALID;
     if (B == 0) return JL_OK;  // empty batch: nothing to route
-    if (!gate_w || !x || !top || !tw) return JL_ERR_INVALID;
+    if (!gate_w || !x || !top || !tw || !dev_status) return JL_ERR_INVALID;
     if (B > kNoAllocMaxB) return JL_ERR_CAPACITY;
     if (E < 1 || E > kNoAllocMaxE || topk < 1 || topk > kNoAllocMaxK || topk > E) return JL_ERR_INVALID;
     if (d < 8 || d % 8) return JL_ERR_INVALID;
@@ -95,7 +96,7 @@ extern "C" int jl_route_noalloc(const unsigned short* gate_w, const float* x, in
     ws.logits = scratch;
     ws.top = top;
     ws.tw = tw;
-    ws.err = dev_status ? dev_status : reinterpret_cast<int*>(scratch + kNoAllocLogits);
+    ws.err = dev_status;
     return jl_launch_router_topk(ws, gate_w, x, B, E, d, topk, norm_topk_prob ? 1 : 0,
                                  (cudaStream_t)stream);
 }

@@ -1,6 +1,5 @@
-// Routing device code shared by the router kernels (jl_router.cu) and the
-// single-launch small-batch layer (jl_fused.cu): per-token softmax / top-k /
-// renorm by a whole CTA and the warp-level dispatch for up to 128 slots.
+// Routing device code of the router kernels (jl_router.cu): per-token
+// softmax / top-k / renorm and the warp-level dispatch for up to 128 slots.
 #pragma once
 
 #include <climits>

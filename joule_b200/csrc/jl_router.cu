@@ -693,12 +693,12 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
     using namespace jl;
     const int E = h->E, d = h->d, k = h->k;
     if (E > kMaxE || k > kMaxK || k < 1 || E < k) return JL_ERR_INVALID;
-    static bool attr = false;
-    if (!attr) {
-        JL_CUDA(cudaFuncSetAttribute(k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        JL_CUDA(cudaFuncSetAttribute(k_router_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        attr = true;
-    }
+    int rc0 = jl_device_once(kOnceRouter, [] {
+        JL_CUDA(cudaFuncSetAttribute(jl::k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        JL_CUDA(cudaFuncSetAttribute(jl::k_router_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        return JL_OK;
+    });
+    if (rc0) return rc0;
     if (d % 128) return JL_ERR_INVALID;
     const int tpc = route_tpc(B);
     const int ncl = (B + tpc - 1) / tpc;
@@ -716,11 +716,11 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
     if (rc || fuse) return rc;
     const size_t fsm = dispatch_fast_smem(B, k, E);
     if (fsm <= 200 * 1024) {
-        static int attr_f = 0;
-        if (!attr_f) {
-            JL_CUDA(cudaFuncSetAttribute(k_dispatch_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-            attr_f = 1;
-        }
+        rc = jl_device_once(kOnceRouterFast, [] {
+            JL_CUDA(cudaFuncSetAttribute(jl::k_dispatch_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+            return JL_OK;
+        });
+        if (rc) return rc;
         return launch(k_dispatch_fast, dim3(1), dim3(kDfThreads), fsm, s, B, k, E, h->ws);
     }
     return launch_dispatch(h->ws, B, k, E, s);
@@ -729,11 +729,11 @@ int jl_launch_route(const jl_moe* h, const unsigned short* gate_w_l, const float
 int jl_launch_dispatch(const jl_moe* h, int B, cudaStream_t s) {
     using namespace jl;
     if (h->E > kMaxE || h->k > kMaxK) return JL_ERR_INVALID;
-    static bool attr = false;
-    if (!attr) {
-        JL_CUDA(cudaFuncSetAttribute(k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        attr = true;
-    }
+    const int rc = jl_device_once(kOnceDispatch, [] {
+        JL_CUDA(cudaFuncSetAttribute(jl::k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        return JL_OK;
+    });
+    if (rc) return rc;
     return launch_dispatch(h->ws, B, h->k, h->E, s);
 }
 

@@ -215,12 +215,12 @@ static int q4_gemm_common(float* out, const float* X, int T, const unsigned char
         return JL_ERR_INVALID;
     const size_t smem = (size_t)jl::kGemvTok * d * sizeof(float);
     if (smem > 200 * 1024) return JL_ERR_INVALID;
-    static bool attr_set = false;
-    if (!attr_set) {
+    const int rc = jl_device_once(kOnceGemm, [] {
         JL_CUDA(cudaFuncSetAttribute(jl::k_q4_gemm_ref, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      200 * 1024));
-        attr_set = true;
-    }
+        return JL_OK;
+    });
+    if (rc) return rc;
     dim3 grid((m + jl::kGemvRows - 1) / jl::kGemvRows, (T + jl::kGemvTok - 1) / jl::kGemvTok);
     jl::k_q4_gemm_ref<<<grid, jl::kGemvRows, smem, (cudaStream_t)stream>>>(out, X, T, packed,
                                                                           scales, m, d);

@@ -734,9 +734,8 @@ size_t jl_tc_ws_bytes(int Bmax, int E, int k, int d, int m, size_t* xc_plane, si
 }
 
 static int tc_attrs() {
-    using namespace jl;
-    static bool attr = false;
-    if (!attr) {
+    return jl_device_once(kOnceTc, [] {
+        using namespace jl;
         JL_CUDA(cudaFuncSetAttribute(k_expert_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kPSmemBytes));
         JL_CUDA(cudaFuncSetAttribute(k_expert_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -745,9 +744,8 @@ static int tc_attrs() {
                                      (int)kPSmemBytes));
         JL_CUDA(cudaFuncSetAttribute(k_expert_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kPSmemBytes));
-        attr = true;
-    }
-    return JL_OK;
+        return JL_OK;
+    });
 }
 
 int jl_launch_gateup_tc(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s) {

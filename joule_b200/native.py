@@ -23,7 +23,7 @@ ERRORS = {
     -6: "JL_ERR_NOT_READY: layer not uploaded",
     -7: "JL_ERR_DEVICE: kernel reported a bad index/state",
 }
-PATH_AUTO, PATH_EXACT, PATH_TC, PATH_EXACT_FUSED = 0, 1, 2, 3
+PATH_AUTO, PATH_EXACT, PATH_TC = 0, 1, 2
 CREATE_ROUTER_ONLY = 1
 
 
@@ -97,6 +97,9 @@ SIGNATURES = {
     "jl_ep_forward": ([_P, _P, _I, _P, _I, _P, _P], _I),
     "jl_ep_destroy": ([_P], _I),
     "jl_moe_device_bytes": ([_P], _LL),
+    "q4_gemv_f32": ([_P, _P, _P, _P, _I, _I, _I], None),
+    "q4_gemm_f32": ([_P, _P, _I, _P, _P, _I, _I, _I], None),
+    "jl_compat_status": ([], _I),
     "jl_version": ([], ctypes.c_char_p),
     "jl_last_cuda_error": ([], ctypes.c_char_p),
 }

@@ -125,6 +125,31 @@ void jo_q4_gemm(float* out, const float* X, int T, const uint8_t* packed,
         }
 }
 
+/* quant_gemv.c:35-57 (the scalar GEMV that ScalarBackend and kernel.q4_gemv
+ * bind): per group, a sequential per-byte chain gacc += lo*x0 + hi*x1 (each
+ * product and sum rounded), then acc += gacc * s. */
+void jo_q4_gemv_scalar(float* out, const float* x, const uint8_t* packed,
+                       const uint16_t* scales, int m, int d) {
+    const int nb = d / 2, ng = d / 64;
+    for (int i = 0; i < m; i++) {
+        const uint8_t* row = packed + (size_t)i * nb;
+        float acc = 0.0f;
+        for (int g = 0; g < ng; g++) {
+            const float s = jo_fp16_to_f32(scales[(size_t)i * ng + g]);
+            float gacc = 0.0f;
+            for (int b = g * 32; b < g * 32 + 32; b++) {
+                const float lo = (float)((int)(row[b] & 0x0Fu) - 8) * x[2 * b];
+                const float hi = (float)((int)(row[b] >> 4) - 8) * x[2 * b + 1];
+                const float t = lo + hi;
+                gacc = gacc + t;
+            }
+            const float p = gacc * s;
+            acc = acc + p;
+        }
+        out[i] = acc;
+    }
+}
+
 /* decode_kernel.c:234-256 / 693-718: lane j sums k = j mod 8 by FMA in k
  * order, then hsum8; the scalar tail (d % 8) is a separate mul and add. */
 void jo_router_logits(const uint16_t* gate_w, const float* x, int B, int E,

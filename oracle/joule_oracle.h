@@ -34,6 +34,10 @@ void jo_q4_row_dot_B(const uint8_t* row, const uint16_t* sc, const float* x,
 void jo_q4_gemm(float* out, const float* X, int T, const uint8_t* packed,
                 const uint16_t* scales, int m, int d);
 
+/* out[m] = dequant(W[m, d]) @ x[d] in quant_gemv.c:35-57's scalar order. */
+void jo_q4_gemv_scalar(float* out, const float* x, const uint8_t* packed,
+                       const uint16_t* scales, int m, int d);
+
 /* scores[B, E] = bf16 gate[E, d] @ x[B, d]^T: decode_kernel.c:234-256 and
  * 693-718 (identical lane order for B == 1 and B > 1). */
 void jo_router_logits(const uint16_t* gate_w, const float* x, int B, int E,

@@ -34,6 +34,8 @@ def lib() -> ctypes.CDLL:
         L.jo_expf_fast.argtypes = [ctypes.c_float]
         L.jo_expf_fast.restype = ctypes.c_float
         L.jo_q4_gemm.argtypes = [_P, _P, _I, _P, _P, _I, _I]
+        L.jo_q4_gemv_scalar.argtypes = [_P, _P, _P, _P, _I, _I]
+        L.jo_q4_gemv_scalar.restype = None
         L.jo_router_logits.argtypes = [_P, _P, _I, _I, _I, _P]
         L.jo_route.argtypes = [_P, _I, _I, _I, _I, _P, _P, _P]
         L.jo_dispatch.argtypes = [_P, _P, _I, _I, _I, _P, _P, _P, _P]
@@ -63,6 +65,16 @@ def q4_gemm(X: np.ndarray, packed: np.ndarray, scales: np.ndarray, m: int, d: in
     out = np.empty((X.shape[0], m), np.float32)
     lib().jo_q4_gemm(_ptr(out), _ptr(X), X.shape[0], _ptr(np.ascontiguousarray(packed)),
                      _ptr(np.ascontiguousarray(scales)), m, d)
+    return out
+
+
+def q4_gemv_scalar(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, m: int,
+                   d: int) -> np.ndarray:
+    """quant_gemv.c:35-57's scalar GEMV (restated in joule_oracle.c)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(d)
+    out = np.empty(m, np.float32)
+    lib().jo_q4_gemv_scalar(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(packed)),
+                            _ptr(np.ascontiguousarray(scales)), m, d)
     return out
 
 

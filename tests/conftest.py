@@ -21,6 +21,16 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
+def reference_root() -> Path | None:
+    """The reference checkout, when present: $JOULE_REFERENCE, else a
+    `reference` directory beside this repository. Only CPU tests use it; GPU
+    tests and the bench never read it."""
+    import os
+    cand = os.environ.get("JOULE_REFERENCE")
+    p = Path(cand) if cand else ROOT.parent / "reference"
+    return p if (p / "src" / "jouleai" / "native" / "backend.py").exists() else None
+
+
 def golden(name: str) -> dict:
     with np.load(GOLDEN / f"{name}.npz") as z:
         return {k: z[k] for k in z.files}

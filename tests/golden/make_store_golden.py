@@ -1,7 +1,7 @@
 """Generate tests/golden/q4_store_tiny/ with the REFERENCE's own store converter.
 
 Run once in a container that has the reference checkout (default
-``/root/reference``, or ``$JOULE_REFERENCE``):
+``$JOULE_REFERENCE``, else a ``reference`` directory beside this repository):
 
     python tests/golden/make_store_golden.py
 
@@ -22,7 +22,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("JOULE_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("JOULE_REFERENCE") or Path(__file__).resolve().parents[3] / "reference")
 OUT = HERE / "q4_store_tiny"
 L, E, D, M, SEED = 2, 4, 128, 64, 11
 

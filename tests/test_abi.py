@@ -22,13 +22,13 @@ def dll():
 
 def header_symbols() -> list[str]:
     txt = (ROOT / "include" / "joule_moe.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|long long|const char\*)\s+(jl_\w+)\s*\(", txt, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:void|int|long long|const char\*)\s+(\w+)\s*\(", txt, re.M)))
 
 
 def test_header_declares_expected_entry_points():
     syms = header_symbols()
     for s in ("jl_q4_gemv_f32", "jl_q4_gemm_f32", "jl_moe_create", "jl_moe_forward",
-              "jl_layer_ffn_batch", "jl_q4_quantize"):
+              "jl_layer_ffn_batch", "jl_q4_quantize", "q4_gemv_f32", "q4_gemm_f32"):
         assert s in syms
 
 

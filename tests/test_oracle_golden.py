@@ -50,6 +50,8 @@ def test_q4_gemm_matches_reference_avx2_and_scalar():
     # quant_gemv.c's scalar loop sums in another order: fp32 tolerance
     ref = g["gemv_scalar"]
     assert np.abs(out[0] - ref).max() <= 1e-5 * np.abs(ref).max()
+    # ... and the restatement of that scalar loop is bit-exact with it
+    assert np.array_equal(restate.q4_gemv_scalar(g["X"][0], g["packed"], g["scales"], m, d), ref)
 
 
 def _check_layer(lay, g, x):
