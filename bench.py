@@ -36,6 +36,10 @@ sys.path.insert(0, str(ROOT))
 
 SHAPE = dict(d=2048, E=128, k=8, m=768, norm=1, L=48)
 METRIC = "Qwen3-30B-A3B-shape Q4 MoE decode tok/s (48 MoE layers per step)"
+TOL = 1e-3  # max row-relative error of expert outputs (north star)
+DTYPE_TC = ("fp16 x fp16 -> fp32: Q4 weights dequantised to fp16 ((n-8)*s rounded), activations "
+            "as fp16 hi + lo pairs, fp32 accumulate")
+DTYPE_EXACT = "f32: Q4 weights, fp32 arithmetic in the reference's order"
 
 
 def rec_bytes(d, m):
@@ -202,14 +206,22 @@ def capture_step(moe, xs, outs, B, mask, stream, layers):
     return g
 
 
-def replay_ms(g, reps, warmup, stream, ws=1):
-    """Mean ms per replay of graph g: warm-up replays, then `reps` replays
-    back to back between two events (barrier + synchronize on both sides)."""
+def replay_ms(g, reps, warmup, stream, ws=1, preroll_s=0.0):
+    """Mean ms per replay of graph g: warm-up replays (at least `preroll_s`
+    seconds of them, so that a clock sampler running over the warm-up and
+    the timed region sees the GPU under this load), then `reps` replays back
+    to back between two events (barrier + synchronize on both sides)."""
     import torch
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             g.replay()
     stream.synchronize()
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < preroll_s:
+        with torch.cuda.stream(stream):
+            for _ in range(4):
+                g.replay()
+        stream.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -225,7 +237,7 @@ def replay_ms(g, reps, warmup, stream, ws=1):
     return t0.elapsed_time(t1) / reps
 
 
-def time_batch(moe, xs, outs, B, steps, warmup, ws):
+def time_batch(moe, xs, outs, B, steps, warmup, ws, phases=True, preroll_s=0.0):
     """The timed region: `steps` replays of the 48-layer step graph. Then each
     phase alone (48 back-to-back launches of one kernel, reading the routing
     the last full layer left) to attribute the time."""
@@ -237,10 +249,10 @@ def time_batch(moe, xs, outs, B, steps, warmup, ws):
             moe.forward(l, xs[l, :B], outs[l, :B], stream=stream)
     stream.synchronize()
     g = capture_step(moe, xs, outs, B, 7, stream, range(L))
-    step_ms = replay_ms(g, steps, warmup, stream, ws)
+    step_ms = replay_ms(g, steps, warmup, stream, ws, preroll_s)
     moe.check()
     phase = {}
-    for name, mask in (("router", 1), ("gateup", 2), ("down_combine", 4)):
+    for name, mask in ((("router", 1), ("gateup", 2), ("down_combine", 4)) if phases else ()):
         gp = capture_step(moe, xs, outs, B, mask, stream, range(L))
         phase[name] = replay_ms(gp, max(3, steps // 2), 2, stream) / L
         del gp
@@ -333,16 +345,28 @@ def cpu_model():
     return None
 
 
+def row_rel_err(out, ref) -> float:
+    """max over rows of max|out - ref| / max|ref| (the north star's bar)."""
+    import torch
+    num = (out - ref).abs().amax(dim=1)
+    den = ref.abs().amax(dim=1).clamp_min(1e-30)
+    return float((num / den).max().item())
+
+
 def run_ep(a, ws, rank, local):
     """N > 1: expert parallelism. Every rank serves its own B tokens (data
     parallel) and stores E/N experts of each layer; each layer exchanges token
-    rows and weighted expert outputs with NCCL all-to-all. Same seeded model
-    as one GPU (each rank keeps its slice of the full weights)."""
+    rows and weighted expert outputs with the experts' owners (library
+    kernels over NVLink peer memory, or NCCL all-to-all with --ep nccl). Same
+    seeded model as one GPU (each rank keeps its slice of the full weights).
+    Before timing, layer 0's output on every rank is checked against a
+    single-GPU forward of the same tokens on the exact path (the reference's
+    arithmetic order): the run fails above 1e-3 max row-relative error."""
     import torch
     import torch.distributed as dist
     from joule_b200 import synth
     from joule_b200.ep import CudaEPBackend, ExpertParallelMoE
-    from joule_b200.moe import make_cfg
+    from joule_b200.moe import PATH_EXACT, MoELayers, make_cfg
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
     B = a.batch
     cfg = make_cfg(L, d, E, k, m, SHAPE["norm"])
@@ -352,12 +376,15 @@ def run_ep(a, ws, rank, local):
     dev = torch.device("cuda", local)
     gen = torch.Generator(device=dev).manual_seed(1)
     t = time.time()
+    full0 = MoELayers(make_cfg(1, d, E, k, m, SHAPE["norm"]), B)  # layer 0, all experts: parity
     for l in range(L):
         gw = synth.router_bf16(E, d, gen, dev)
         w = [torch.randn(E, m, d, generator=gen, device=dev) * 0.02,
              torch.randn(E, m, d, generator=gen, device=dev) * 0.02,
              torch.randn(E, d, m, generator=gen, device=dev) * 0.02]
         be.quantize_layer(l, gw, *[t_[sl].contiguous() for t_ in w])
+        if l == 0:
+            full0.quantize_layer(0, gw, *w)
         del w
     torch.cuda.synchronize()
     setup_s = time.time() - t
@@ -368,6 +395,27 @@ def run_ep(a, ws, rank, local):
         ep = ExpertParallelMoE(be, E)
     gx = torch.Generator(device=dev).manual_seed(100 + rank)
     xs = torch.randn(L, B, d, generator=gx, device=dev)
+
+    # parity of the configuration timed below (layer 0, this rank's tokens)
+    o_ep = ep.forward(0, xs[0]).clone()
+    full0.set_path(PATH_EXACT)
+    o_ref = full0.forward(0, xs[0])
+    torch.cuda.synchronize()
+    be.check()
+    full0.check()
+    err = torch.tensor([row_rel_err(o_ep, o_ref)], dtype=torch.float64, device=dev)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    parity = dict(max_row_rel_err=float(err.item()), tokens_checked=ws * B, layer=0, tol=TOL,
+                  against="single-GPU jl_moe_forward on the same tokens, exact path "
+                          "(the reference's arithmetic order, bit-exact with its goldens)")
+    full0.close()
+    del o_ep, o_ref
+    if parity["max_row_rel_err"] > TOL:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "error": "expert-parallel parity failed",
+                              "parity": parity}), flush=True)
+        dist.barrier()
+        raise SystemExit(1)
     recv = []
 
     def step():
@@ -380,11 +428,22 @@ def run_ep(a, ws, rank, local):
         step()
     be.check()
     recv.clear()
+    if a.ep == "p2p":
+        ep.stats()  # reset the counters: only the timed steps count
     barrier(ws)
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        tw0 = time.perf_counter()   # pre-roll: the sampler sees >= 1 s of this load
+        while time.perf_counter() - tw0 < 1.0:
+            step()
+            torch.cuda.synchronize()
+        barrier(ws)
+        torch.cuda.synchronize()
+        if a.ep == "p2p":
+            ep.stats()
+        recv.clear()
         t0.record()
         for _ in range(a.steps):
             step()
@@ -394,9 +453,60 @@ def run_ep(a, ws, rank, local):
     torch.cuda.synchronize()
     ms = max_over_ranks(ws, t0.elapsed_time(t1))
     be.check()
-    rows = torch.tensor([float(np.mean(recv)) if recv else -1.0], device=dev)
+    if a.ep == "p2p":
+        nrows, ncalls = ep.stats()
+        mean_rows = nrows / max(1, ncalls)
+    else:
+        mean_rows = float(np.mean(recv)) if recv else -1.0
+    rows = torch.tensor([mean_rows], device=dev)
     rows_all = [torch.zeros_like(rows) for _ in range(ws)]
     dist.all_gather(rows_all, rows)
+
+    # attribution (untimed): per-phase event times and the local union size of
+    # every layer; bytes each rank streams from HBM and sends over NVLink
+    phases = ["route", "order_send", "recv_wait", "dispatch", "gateup", "down", "return",
+              "combine_wait"]
+    Ul = []
+    breakdown = None
+    if a.ep == "p2p":
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(9)] for _ in range(L)]
+        for l in range(L):
+            ep.set_phase_events(evs[l])
+            ep.forward(l, xs[l])
+        ep.set_phase_events([])
+        torch.cuda.synchronize()
+        acc = np.zeros(8)
+        for l in range(L):
+            acc += [evs[l][i].elapsed_time(evs[l][i + 1]) * 1e3 for i in range(8)]
+        mine = torch.tensor(acc / L, dtype=torch.float64, device=dev)
+        allb = [torch.zeros_like(mine) for _ in range(ws)]
+        dist.all_gather(allb, mine)
+        breakdown = dict(unit="us per layer (mean over the 48 layers; CUDA events between "
+                              "jl_ep_forward's kernels, untimed pass)",
+                         phases=phases,
+                         per_rank=[[round(float(v), 2) for v in b_.tolist()] for b_ in allb])
+        Bpad = ws * B * k
+        for l in range(L):
+            ep.forward(l, xs[l])
+            Ul.append(be.local.union_size(Bpad))
+        be.check()
+    e_bytes = (float(np.mean(Ul)) * rec_bytes(d, m) if Ul else None)
+    us_layer = ms / a.steps * 1e3 / L
+    roof = None
+    if e_bytes is not None:
+        hbm, peak_kind = peaks()
+        layer_bytes = e_bytes + E * d * 2 + 2 * B * d * 4
+        u_all = torch.tensor([layer_bytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(u_all, op=dist.ReduceOp.MAX)
+        gbs = float(u_all.item()) / (us_layer * 1e-6) / 1e9
+        nv = 2 * B * k * d * 4 * (ws - 1) / ws  # rows out and weighted rows back, remote share
+        roof = dict(bound="hbm", kernel="whole expert-parallel layer on the busiest rank "
+                                        "(its local experts' Q4 records + router rows + x/out)",
+                    achieved=gbs, peak=hbm, unit="GB/s", frac=gbs / hbm, peak_kind=peak_kind,
+                    traffic=None, algorithmic_bytes_per_layer=float(u_all.item()),
+                    mean_local_union=float(np.mean(Ul)),
+                    nvlink_bytes_per_layer_per_rank=nv,
+                    nvlink_gbs=nv / (us_layer * 1e-6) / 1e9, nvlink_peak_gbs=770.0)
     # end to end: host x in, host out back, per layer
     xh = torch.randn(L, B, d, generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
     oh = torch.empty(B, d).pin_memory()
@@ -415,10 +525,11 @@ def run_ep(a, ws, rank, local):
     barrier(ws)
     e2e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
     val = ws * B * a.steps / (ms / 1e3)
+    per_layer_launches = (2 if B > 32 else 1) + 6 + (3 if ws * B * k > 8 else 2)
     if rank == 0:
         line = dict(metric=METRIC, value=val, unit="tok/s", n_gpus=ws, steps=a.steps, warmup=a.warmup,
                     ms_per_step=ms / a.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
-                    dtype="f32 (Q4 weights, fp32 accumulate)",
+                    dtype=DTYPE_TC,
                     data="synthetic: seeded N(0,0.02) weights quantised to the reference Q4 format, "
                          "x ~ N(0,1)",
                     config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch "
@@ -435,18 +546,71 @@ def run_ep(a, ws, rank, local):
                                      "kernels on received rows (JL_PATH_AUTO)",
                                 l2="not flushed: each step streams >= 1 GB of distinct expert weights",
                                 store_setup_s=round(setup_s, 1)),
+                    us_per_layer=us_layer,
+                    parity=parity,
                     rows_received_per_layer=[round(float(r.item()), 1) for r in rows_all],
+                    ep_breakdown=breakdown,
                     clocks=clk.summary(),
-                    gpu_launches=L * a.steps * (9 if a.ep == "p2p" else 6),
+                    gpu_launches=L * a.steps * per_layer_launches,
                     e2e=dict(value=ws * B * n_e2e / (e2e_ms / 1e3), unit="tok/s",
                              h2d_bytes_per_step=L * B * d * 4, d2h_bytes_per_step=L * B * d * 4,
                              api="ExpertParallelMoE.forward per layer, host x in / host out back"),
-                    roofline=None)
+                    roofline=roof)
         print(json.dumps(line), flush=True)
     if a.ep == "p2p":
+        dist.barrier()
         ep.close()
     be.close()
     dist.destroy_process_group()
+
+
+def microbench(moe, a, hbm, peak_kind):
+    """grouped expert microbenchmark. Tokens per step T in
+    {1, 8, 64, 512, 4096}, Qwen3 MoE shape; routing logits log p + Gumbel
+    with Zipf(1.2) popularity over a seeded permutation, fed through the
+    router unchanged by router rows [I | 0] (logit_e = x_e). Each step runs
+    the 48 layers (distinct expert weights; the routers are replaced)."""
+    import torch
+    from joule_b200 import synth
+    d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    Ts = [int(t) for t in a.micro.split(",")]
+    Tmax = max(Ts)
+    eye = synth.identity_router(E, d, dev)
+    for l in range(L):
+        moe.upload_router(l, eye)
+    xs = torch.empty(L, Tmax, d, device=dev)
+    g = torch.Generator(device=dev).manual_seed(300)
+    for l in range(L):
+        xs[l] = torch.randn(Tmax, d, generator=g, device=dev)
+        xs[l, :, :E] = torch.from_numpy(synth.zipf_logits(Tmax, E, 1.2, seed=l)).to(dev)
+    outs = torch.empty_like(xs)
+    tensor_peak = tensor_peak_tflops()
+    res = {}
+    for T in Ts:
+        U = routing_unions(moe, xs, T)
+        total_ms, _ = time_batch(moe, xs, outs, T, max(3, a.steps // 2), 3, 1, phases=False)
+        t_step = total_ms / max(3, a.steps // 2) / 1e3
+        byts = sum(U) * rec_bytes(d, m) + L * (E * d * 2 + 2 * T * d * 4)
+        flops = L * 2.0 * T * k * 3 * d * m
+        t_hbm = byts / (hbm * 1e9)
+        t_tc = flops / (tensor_peak * 1e12)
+        res[str(T)] = dict(path=path_of(T), us_per_layer=t_step * 1e6 / L, tok_s=T / t_step,
+                           mean_U=float(np.mean(U)), bytes_per_layer=byts / L, flops_per_layer=flops / L,
+                           hbm_frac=t_hbm / t_step, tensor_frac=t_tc / t_step,
+                           bound="hbm" if t_hbm >= t_tc else "tensor",
+                           roofline_frac=max(t_hbm, t_tc) / t_step)
+    return dict(config="BASELINE config 5: grouped expert microbenchmark, Zipf(1.2) routing "
+                       "via router rows [I|0], 48 layers per step",
+                peaks=dict(hbm_gbs=hbm, bf16_tflops=tensor_peak, kind=peak_kind),
+                per_T=res)
+
+
+def tensor_peak_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
 
 
 def run_ours(a):
@@ -458,47 +622,50 @@ def run_ours(a):
         return run_ep(a, ws, rank, local)
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
     sweep = sorted(set(int(b) for b in a.sweep.split(",")) | {a.batch})
-    Bmax = max(sweep)
+    Bmax = max(sweep + ([max(int(t) for t in a.micro.split(","))] if a.micro else []))
     moe = MoELayers(make_cfg(L, d, E, k, m, SHAPE["norm"]), Bmax)
-    host_layers = L if (a.e2e and rank == 0) else (1 if rank == 0 else 0)
+    host_layers = L if a.e2e else 1
     t = time.time()
     host = build_store(moe, host_layers)
     setup_s = time.time() - t
     gen = torch.Generator(device="cuda").manual_seed(100 + rank)
-    xs = torch.randn(L, Bmax, d, generator=gen, device="cuda")
+    Bs = max(sweep)
+    xs = torch.randn(L, Bs, d, generator=gen, device="cuda")
     outs = torch.empty_like(xs)
     hbm, peak_kind = peaks()
     per_b = {}
     head = None
     clocks = None
-    # the headline batch runs last, with the clocks sampled over its timed region
+    # the headline batch runs last, with the clocks sampled over >= 1 s of
+    # warm-up replays and then its timed region
     for B in [b for b in sweep if b != a.batch] + [a.batch]:
         U = routing_unions(moe, xs, B)
         if B == a.batch:
             with Clocks(local) as clk:
-                total_ms, phase = time_batch(moe, xs, outs, B, a.steps, a.warmup, ws)
+                total_ms, phase = time_batch(moe, xs, outs, B, a.steps, a.warmup, ws, preroll_s=1.0)
             clocks = clk.summary()
         else:
             total_ms, phase = time_batch(moe, xs, outs, B, a.steps, a.warmup, ws)
-        total_ms = max_over_ranks(ws, total_ms)
         ms_step = total_ms / a.steps
         layer_bytes = [u * rec_bytes(d, m) + E * d * 2 + 2 * B * d * 4 for u in U]
         gu_bytes = [u * 2 * (m * d // 2 + m * d // 32) + B * d * 4 + B * k * m * 4 for u in U]
         rec = dict(
             path=path_of(B),
-            tok_s=ws * B * a.steps / (total_ms / 1e3), ms_per_step=ms_step,
+            tok_s=B * a.steps / (total_ms / 1e3), ms_per_step=ms_step,
             us_per_layer=ms_step * 1e3 / L, mean_U=float(np.mean(U)),
             layer_gbs=sum(layer_bytes) / (ms_step / 1e3) / 1e9,
             phase_us={k: v * 1e3 for k, v in phase.items()},
             gateup_gbs=float(np.mean(gu_bytes)) / (phase["gateup"] / 1e3) / 1e9,
             gateup_bytes_per_launch=float(np.mean(gu_bytes)))
         rec["layer_frac_of_hbm"] = rec["layer_gbs"] / hbm
+        rec["gateup_frac_of_hbm"] = rec["gateup_gbs"] / hbm
         per_b[str(B)] = rec
         if B == a.batch:
             head = rec
     line = dict(metric=METRIC, value=head["tok_s"], unit="tok/s", n_gpus=ws, steps=a.steps,
                 warmup=a.warmup, ms_per_step=head["ms_per_step"], higher_is_better=True,
-                scaling="weak", vs_baseline=None, dtype="f32 (Q4 weights, fp32 accumulate)",
+                scaling="weak", vs_baseline=None,
+                dtype=DTYPE_EXACT if path_of(a.batch) == "exact" else DTYPE_TC,
                 data="synthetic: seeded N(0,0.02) weights quantised to the reference Q4 format, "
                      "x ~ N(0,1)",
                 config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
@@ -510,7 +677,7 @@ def run_ours(a):
                                   "activations, fp32 accumulate; <= 1e-3 row-relative)"),
                             l2="not flushed: each step streams >= 1 GB of distinct expert weights "
                                "(store 15.4 GB) vs 126 MB L2",
-                            parallelism=f"replicas x{ws}" if ws > 1 else "single GPU",
+                            parallelism="single GPU",
                             store_setup_s=round(setup_s, 1)),
                 per_batch=per_b)
     kern = "k_gateup_exact" if path_of(a.batch) == "exact" else "k_expert_tc<false>"
@@ -524,16 +691,23 @@ def run_ours(a):
                             layer_gbs=head["layer_gbs"], layer_frac=head["layer_gbs"] / hbm)
     line["clocks"] = clocks
     line["gpu_launches"] = launches_per_step(a.batch) * a.steps
-    if rank == 0 and a.e2e:
+    if a.e2e:
         e2e, keep = e2e_dropin(host, a.batch, max(2, a.steps // 4), 1)
         line["e2e"] = e2e
-    if rank == 0 and a.cpu:
-        line["cpu_baseline"] = cpu_baseline_ref(host[0], a.batch)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if ws > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    if a.cpu:
+        cb = {}
+        for B in sorted({1, a.batch}):
+            c = cpu_baseline_ref(host[0], B)
+            if c is not None:
+                cb[str(B)] = c
+                if str(B) in per_b:
+                    per_b[str(B)]["cpu_tok_s"] = c["value"]
+                    per_b[str(B)]["gpu_over_cpu"] = per_b[str(B)]["tok_s"] / c["value"]
+        line["cpu_baseline"] = cb.get(str(a.batch))
+        line["cpu_baseline_per_batch"] = cb
+    if a.micro:
+        line["microbench"] = microbench(moe, a, hbm, peak_kind)
+    print(json.dumps(line), flush=True)
 
 
 def path_of(B):
@@ -602,7 +776,7 @@ def run_reference(a):
     cores = 1 if a.batch == 1 else nthreads + 1
     line = dict(metric=METRIC, value=val, unit="tok/s", n_gpus=ws, steps=a.steps, warmup=a.warmup,
                 ms_per_step=step * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None,
-                dtype="f32 (Q4 weights, fp32 accumulate)", impl="reference",
+                dtype=DTYPE_EXACT, impl="reference",
                 data="synthetic: seeded N(0,0.02) weights in the reference Q4 format, x ~ N(0,1)",
                 config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
                             batch=a.batch, layers=L, d=d, E=E, topk=k, intermediate=m,
@@ -628,6 +802,8 @@ def main():
     ap.add_argument("--layers", type=int, default=48, help="MoE layers per step (48 = the model)")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
+    ap.add_argument("--micro", default="1,8,64,512,4096",
+                    help="config 5 token counts ('' to skip the microbenchmark)")
     ap.add_argument("--ep", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1 exchange: library peer-memory kernels or NCCL all-to-all")
     a = ap.parse_args()

@@ -285,6 +285,29 @@ int jl_ep_forward(jl_ep* ep, jl_moe* router, int l, const float* x, int B,
                   float* out, void* stream);
 int jl_ep_destroy(jl_ep* ep);
 
+/* Peer r of `ep` is `peer`, a jl_ep of the same world created in this
+ * process (ranks driven from one process: no IPC handle; on another device
+ * peer access is enabled). In place of jl_ep_open_peers for that rank. */
+int jl_ep_attach(jl_ep* ep, int r, jl_ep* peer);
+
+/* Bound of each device-side wait on other ranks, in nanoseconds (default
+ * about 2 s). A wait that runs out sets JL_ERR_TIMEOUT on the local expert
+ * handle (jl_moe_check), the layer's output is then not valid, and the
+ * rank's epochs no longer match its peers': destroy and recreate every
+ * rank's jl_ep before the next layer. */
+int jl_ep_set_wait_limit(jl_ep* ep, long long ns);
+
+/* Phase timing of jl_ep_forward: events (cudaEvent_t, n <= 9) recorded on
+ * the call's stream before routing, then after routing, the send, the
+ * receive (its wait included), the dispatch, gate/up, down, the return and
+ * the final combine (its wait included). n = 0 turns it off. */
+int jl_ep_set_phase_events(jl_ep* ep, void* const* events, int n);
+
+/* Rows this rank received as an owner (summed over calls) and the number of
+ * calls, since the previous jl_ep_stats; resets both. Synchronises
+ * `stream`. */
+int jl_ep_stats(jl_ep* ep, long long* rows, long long* calls, void* stream);
+
 /* Debug / parity: copies (device) the router logits [B, E], the union
  * experts sel [U], offsets uh [U+1] and the slot map uidx/uw [B*topk] built
  * by the last jl_moe_forward (decode_kernel.c:1424-1485). *U_out (host)

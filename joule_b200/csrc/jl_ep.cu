@@ -202,14 +202,15 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-// Bounded wait until flags[f][0..world) all reached `epoch`.
+// Bounded wait until flags[f][0..world) all reached `epoch`; gives up after
+// `limit` SM clock cycles in total.
 __device__ bool ep_wait_flags(const uint8_t* buf, ep_layout o, int world, int f,
-                              unsigned long long epoch, int* err) {
+                              unsigned long long epoch, long long limit, int* err) {
     const unsigned long long* fl = reinterpret_cast<const unsigned long long*>(buf + o.fl) + f * world;
     const long long t0 = clock64();
     for (int r = 0; r < world; r++) {
         while (ld_acquire_sys(fl + r) < epoch) {
-            if (clock64() - t0 > kWaitLimitCycles) {
+            if (clock64() - t0 > limit) {
                 atomicOr(err, kErrTimeout);
                 return false;
             }
@@ -267,17 +268,24 @@ __global__ void k_ep_send(const float* __restrict__ x, const int* __restrict__ t
 // Owner side: wait for every sender, then turn the received rows into a
 // padded routed batch for the topk = 1 expert handle: slot r*cap + i is row
 // i from rank r (expert id -1 past that rank's count).
+// stats[0] accumulates the rows received, stats[1] the calls.
 __global__ void k_ep_recv(const uint8_t* __restrict__ buf, ep_layout o, int world, int cap,
-                          unsigned long long epoch, int* __restrict__ top, float* __restrict__ tw,
-                          int* err) {
+                          unsigned long long epoch, long long limit, int* __restrict__ top,
+                          float* __restrict__ tw, unsigned long long* stats, int* err) {
     __shared__ int ok;
     griddep_wait();
     griddep_launch_dependents();
-    if (threadIdx.x == 0) ok = ep_wait_flags(buf, o, world, 0, epoch, err);
+    if (threadIdx.x == 0) ok = ep_wait_flags(buf, o, world, 0, epoch, limit, err);
     __syncthreads();
     // peers wrote these: read them past L1 (__ldcv)
     const int* cnt = reinterpret_cast<const int*>(buf + o.rc);
     const int* meta = reinterpret_cast<const int*>(buf + o.rm);
+    if (threadIdx.x == 0 && ok) {
+        unsigned long long n = 0;
+        for (int r = 0; r < world; r++) n += (unsigned long long)min(max(__ldcv(cnt + r), 0), cap);
+        atomicAdd(stats, n);
+        atomicAdd(stats + 1, 1ull);
+    }
     for (int s = threadIdx.x; s < world * cap; s += blockDim.x) {
         const int r = s / cap, i = s % cap;
         const bool valid = ok && i < __ldcv(cnt + r);
@@ -318,11 +326,12 @@ __global__ void k_ep_return(const uint8_t* __restrict__ buf, const float* __rest
 __global__ void k_ep_gather_out(const uint8_t* __restrict__ buf, ep_layout o, const int* __restrict__ top,
                                 const int* __restrict__ pos, const int* __restrict__ counts,
                                 const int* __restrict__ comb, int k, int d, int E_local, int world,
-                                int cap, unsigned long long epoch, float* __restrict__ out, int* err) {
+                                int cap, unsigned long long epoch, long long limit, float* __restrict__ out,
+                                int* err) {
     __shared__ int ok;
     griddep_wait();
     griddep_launch_dependents();
-    if (threadIdx.x == 0) ok = ep_wait_flags(buf, o, world, 1, epoch, err);
+    if (threadIdx.x == 0) ok = ep_wait_flags(buf, o, world, 1, epoch, limit, err);
     __syncthreads();
     if (!ok) return;
     const int b = blockIdx.y;
@@ -353,8 +362,12 @@ struct jl_ep {
     uint8_t* peer[jl::kEpMaxWorld];
     bool opened[jl::kEpMaxWorld];
     int* scratch;  // pos [cap], counts [world], done [2], err [1]
+    unsigned long long* stats;  // [2] rows received, calls (k_ep_recv)
     unsigned long long epoch;
+    long long wait_cycles;  // bound of each wait on other ranks, SM clock cycles
     jl_moe* local;
+    cudaEvent_t ev[9];  // optional phase events (jl_ep_set_phase_events)
+    int n_ev;
 };
 
 extern "C" int jl_ep_create(jl_moe* local, int rank, int world, int max_tokens, int topk, jl_ep** out) {
@@ -377,13 +390,17 @@ extern "C" int jl_ep_create(jl_moe* local, int rank, int world, int max_tokens, 
     ep->max_tokens = max_tokens;
     ep->local = local;
     ep->o = ep_offsets(world, cap, local->d);
+    ep->wait_cycles = kWaitLimitCycles;
     if (cudaMalloc(&ep->buf, ep->o.bytes) != cudaSuccess ||
         cudaMalloc(&ep->scratch, ((size_t)cap + world + 3) * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&ep->stats, 2 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(ep->stats, 0, 2 * sizeof(unsigned long long)) != cudaSuccess ||
         cudaMemset(ep->buf, 0, ep->o.bytes) != cudaSuccess ||
         cudaMemset(ep->scratch, 0, ((size_t)cap + world + 3) * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         if (ep->buf) cudaFree(ep->buf);
         if (ep->scratch) cudaFree(ep->scratch);
+        if (ep->stats) cudaFree(ep->stats);
         delete ep;
         return JL_ERR_OOM;
     }
@@ -414,12 +431,58 @@ extern "C" int jl_ep_open_peers(jl_ep* ep, const void* handles) {
     return JL_OK;
 }
 
+extern "C" int jl_ep_attach(jl_ep* ep, int r, jl_ep* peer) {
+    if (!ep || !peer || r < 0 || r >= ep->world || r == ep->rank || ep->opened[r]) return JL_ERR_INVALID;
+    if (peer->rank != r || peer->world != ep->world || peer->cap != ep->cap || peer->d != ep->d)
+        return JL_ERR_INVALID;
+    if (peer->device != ep->device) {
+        int can = 0;
+        JL_CUDA(cudaDeviceCanAccessPeer(&can, ep->device, peer->device));
+        if (!can) return JL_ERR_INVALID;
+        const cudaError_t e = cudaDeviceEnablePeerAccess(peer->device, 0);
+        if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) return jl_note_cuda(e);
+        cudaGetLastError();
+    }
+    ep->peer[r] = peer->buf;
+    return JL_OK;
+}
+
+extern "C" int jl_ep_set_wait_limit(jl_ep* ep, long long ns) {
+    if (!ep || ns < 1) return JL_ERR_INVALID;
+    // clock64 counts SM cycles; 2 cycles per ns bounds the wait by at least
+    // `ns` at any SM clock up to 2 GHz (a B200 runs at most 1.965 GHz)
+    ep->wait_cycles = ns > (1ll << 61) ? (1ll << 62) : 2 * ns;
+    return JL_OK;
+}
+
+extern "C" int jl_ep_set_phase_events(jl_ep* ep, void* const* events, int n) {
+    if (!ep || n < 0 || n > 9 || (n > 0 && !events)) return JL_ERR_INVALID;
+    for (int i = 0; i < n; i++)
+        if (!events[i]) return JL_ERR_INVALID;
+    for (int i = 0; i < n; i++) ep->ev[i] = (cudaEvent_t)events[i];
+    ep->n_ev = n;
+    return JL_OK;
+}
+
+extern "C" int jl_ep_stats(jl_ep* ep, long long* rows, long long* calls, void* stream) {
+    if (!ep || !rows || !calls) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned long long h[2] = {0, 0};
+    JL_CUDA(cudaMemcpyAsync(h, ep->stats, sizeof(h), cudaMemcpyDeviceToHost, s));
+    JL_CUDA(cudaMemsetAsync(ep->stats, 0, sizeof(h), s));
+    JL_CUDA(cudaStreamSynchronize(s));
+    *rows = (long long)h[0];
+    *calls = (long long)h[1];
+    return JL_OK;
+}
+
 extern "C" int jl_ep_destroy(jl_ep* ep) {
     if (!ep) return JL_OK;
     for (int r = 0; r < ep->world; r++)
         if (ep->opened[r]) cudaIpcCloseMemHandle(ep->peer[r]);
     if (ep->buf) cudaFree(ep->buf);
     if (ep->scratch) cudaFree(ep->scratch);
+    if (ep->stats) cudaFree(ep->stats);
     delete ep;
     return JL_OK;
 }
@@ -444,9 +507,22 @@ extern "C" int jl_ep_forward(jl_ep* ep, jl_moe* router, int l, const float* x, i
     int* err = h->ws.err;
     ep_peers peers;
     for (int r = 0; r < kEpMaxWorld; r++) peers.p[r] = r < world ? ep->peer[r] : nullptr;
+    // optional phase events (an event record inside stream capture must be an
+    // external node to be timed when the graph replays)
+    cudaStreamCaptureStatus cap_st = cudaStreamCaptureStatusNone;
+    if (ep->n_ev > 0 && cudaStreamIsCapturing(s, &cap_st) != cudaSuccess) return JL_ERR_CUDA;
+    auto mark = [&](int i) -> int {
+        if (i >= ep->n_ev) return JL_OK;
+        const cudaError_t e = (cap_st == cudaStreamCaptureStatusActive)
+                                  ? cudaEventRecordWithFlags(ep->ev[i], s, cudaEventRecordExternal)
+                                  : cudaEventRecord(ep->ev[i], s);
+        return e == cudaSuccess ? JL_OK : jl_note_cuda(e);
+    };
     // 1. route this rank's tokens (all E experts)
     const unsigned short* gw = router->gate_w + (size_t)l * router->E * router_expert_halves(router->d);
-    int rc = jl_launch_route(router, gw, x, B, false, s);
+    int rc = mark(0);
+    if (!rc) rc = jl_launch_route(router, gw, x, B, false, s);
+    if (!rc) rc = mark(1);
     if (rc) return rc;
     // 2. group the slots by owner, 3. send them
     rc = launch(k_ep_order, dim3(1), dim3(kEpThreads), 0, s, (const int*)router->ws.top, S, E_local, world, pos,
@@ -455,28 +531,35 @@ extern "C" int jl_ep_forward(jl_ep* ep, jl_moe* router, int l, const float* x, i
         rc = launch(k_ep_send, dim3(std::min(S, 4 * h->sm_count)), dim3(128), 0, s, x, (const int*)router->ws.top,
                     (const float*)router->ws.tw, (const int*)pos, (const int*)counts, S, ep->k, ep->d, E_local,
                     ep->rank, world, cap, peers, ep->o, epoch, done);
+    if (!rc) rc = mark(2);
     // 4. owner: receive, run the local experts on the padded batch
     const int Bpad = world * cap;
     if (!rc)
         rc = launch(k_ep_recv, dim3(1), dim3(1024), 0, s, (const uint8_t*)ep->buf, ep->o, world, cap, epoch,
-                    h->ws.top, h->ws.tw, err);
+                    ep->wait_cycles, h->ws.top, h->ws.tw, ep->stats, err);
+    if (!rc) rc = mark(3);
     const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
     const float* xr = reinterpret_cast<const float*>(ep->buf + ep->o.rr);
     const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
     const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && Bpad > 8 && tc_ok);
     if (!rc) rc = jl_launch_dispatch(h, Bpad, s);
+    if (!rc) rc = mark(4);
     if (!rc) rc = tc ? jl_launch_gateup_tc(h, store_l, xr, Bpad, s) : jl_launch_gateup_exact(h, store_l, xr, Bpad, s);
+    if (!rc) rc = mark(5);
     if (!rc) rc = tc ? jl_launch_down_tc(h, store_l, Bpad, s) : jl_launch_down_exact(h, store_l, Bpad, s);
+    if (!rc) rc = mark(6);
     // 5. return the weighted rows, 6. combine
     if (!rc)
         rc = launch(k_ep_return, dim3(std::min(Bpad, 4 * h->sm_count)), dim3(128), 0, s, (const uint8_t*)ep->buf,
                     (const float*)h->ws.y, ep->d, ep->rank, world, cap, peers, ep->o, epoch, done + 1);
+    if (!rc) rc = mark(7);
     if (!rc) {
         const int tpb = 128;
         rc = launch(k_ep_gather_out, dim3((ep->d / 4 + tpb - 1) / tpb, B), dim3(tpb), 0, s,
                     (const uint8_t*)ep->buf, ep->o, (const int*)router->ws.top, (const int*)pos,
                     (const int*)counts, (const int*)router->ws.comb, ep->k, ep->d, E_local, world, cap, epoch,
-                    out, err);
+                    ep->wait_cycles, out, err);
     }
+    if (!rc) rc = mark(8);
     return rc;
 }

@@ -205,6 +205,28 @@ class P2PExpertParallelMoE:
                                     _stream(stream)), "jl_ep_forward")
         return out
 
+    def set_wait_limit(self, ns: int) -> None:
+        """Bound of each wait on another rank (jl_ep_set_wait_limit)."""
+        from joule_b200.native import check
+        check(self._L.jl_ep_set_wait_limit(self.ep, int(ns)), "jl_ep_set_wait_limit")
+
+    def set_phase_events(self, events) -> None:
+        """torch.cuda.Event objects (enable_timing), up to 9; [] turns it off."""
+        import ctypes
+        from joule_b200.native import check
+        arr = (ctypes.c_void_p * max(1, len(events)))(*[e.cuda_event for e in events])
+        check(self._L.jl_ep_set_phase_events(self.ep, arr, len(events)), "jl_ep_set_phase_events")
+
+    def stats(self, stream=None) -> tuple[int, int]:
+        """(rows received as an owner, calls) since the last call; resets."""
+        import ctypes
+        from joule_b200.moe import _stream
+        from joule_b200.native import check
+        rows, calls = ctypes.c_longlong(), ctypes.c_longlong()
+        check(self._L.jl_ep_stats(self.ep, ctypes.byref(rows), ctypes.byref(calls), _stream(stream)),
+              "jl_ep_stats")
+        return rows.value, calls.value
+
     def close(self) -> None:
         if getattr(self, "ep", None) and self.ep.value:
             self._L.jl_ep_destroy(self.ep)

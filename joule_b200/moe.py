@@ -190,6 +190,13 @@ class MoELayers:
         u = U.value
         return dict(logits=logits, sel=sel[:u], uh=uh[:u + 1], uidx=uidx, uw=uw, U=u)
 
+    def union_size(self, B: int, stream=None) -> int:
+        """Experts the last forward's B tokens used (synchronises)."""
+        U = ctypes.c_int(0)
+        check(self._L.jl_moe_debug_routing(self.h, B, None, None, None, None, None, ctypes.byref(U),
+                                           _stream(stream)), "jl_moe_debug_routing")
+        return U.value
+
 
 def layer_ffn_batch(cfg: KernelCfg, W: KernelW, l: int, x: np.ndarray, B: int,
                     out: np.ndarray) -> None:

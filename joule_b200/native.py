@@ -96,6 +96,10 @@ SIGNATURES = {
     "jl_ep_open_peers": ([_P, _P], _I),
     "jl_ep_forward": ([_P, _P, _I, _P, _I, _P, _P], _I),
     "jl_ep_destroy": ([_P], _I),
+    "jl_ep_attach": ([_P, _I, _P], _I),
+    "jl_ep_set_wait_limit": ([_P, _LL], _I),
+    "jl_ep_set_phase_events": ([_P, _P, _I], _I),
+    "jl_ep_stats": ([_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), _P], _I),
     "jl_moe_device_bytes": ([_P], _LL),
     "q4_gemv_f32": ([_P, _P, _P, _P, _I, _I, _I], None),
     "q4_gemm_f32": ([_P, _P, _I, _P, _P, _I, _I, _I], None),

@@ -55,3 +55,12 @@ def test_peaks_measured_file_else_fallback(tmp_path, monkeypatch):
 def test_algorithmic_bytes_per_expert(d, m, bytes_):
     """Qwen3 and OLMoE: gate + up + down Q4 records (4.25 bits per weight)."""
     assert bench.rec_bytes(d, m) == bytes_
+
+
+def test_row_rel_err_is_the_per_row_max_relative_error():
+    import torch
+    ref = torch.tensor([[1.0, -2.0], [0.5, 0.25]])
+    out = ref.clone()
+    out[0, 1] += 2e-3   # row 0: 2e-3 / 2
+    out[1, 0] -= 1e-4   # row 1: 1e-4 / 0.5
+    assert abs(bench.row_rel_err(out, ref) - 1e-3) < 1e-6

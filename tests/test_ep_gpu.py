@@ -25,7 +25,10 @@ def _free_port() -> int:
     return port
 
 
-def _rank(rank: int, world: int, port: int, B: int, results, p2p: bool = False):
+TOL = 1e-3  # max relative error per token row on the tensor-core expert path
+
+
+def _rank(rank: int, world: int, port: int, B: int, results, p2p: bool = False, exact: bool = True):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -39,12 +42,12 @@ def _rank(rank: int, world: int, port: int, B: int, results, p2p: bool = False):
         sys.path.insert(0, os.path.dirname(__file__))
         from conftest import seeded_layer
         from joule_b200.ep import CudaEPBackend, ExpertParallelMoE
-        from joule_b200.moe import PATH_EXACT, make_cfg
+        from joule_b200.moe import PATH_AUTO, PATH_EXACT, make_cfg
         from oracle import layer as olayer
         from oracle import restate
         lay = seeded_layer("qwen3")
         be = CudaEPBackend(make_cfg(1, lay.d, lay.E, lay.k, lay.m, lay.norm_topk_prob), B, rank,
-                           world, path=PATH_EXACT)
+                           world, path=PATH_EXACT if exact else PATH_AUTO)
         be.upload_layer(0, lay.gate_w, lay.packed, lay.scales)
         x = olayer.hidden(B, lay.d, 200 + rank)
         if p2p:
@@ -60,8 +63,9 @@ def _rank(rank: int, world: int, port: int, B: int, results, p2p: bool = False):
         torch.cuda.synchronize()
         be.check()
         ref, _, _ = restate.moe_layer(lay, x)
-        results[rank] = (bool(np.array_equal(out, ref) and np.array_equal(out2, ref)),
-                         float(np.abs(out - ref).max()))
+        rel = max(float((np.abs(o - ref).max(axis=1) / np.abs(ref).max(axis=1)).max()) for o in (out, out2))
+        same = (np.array_equal(out, ref) and np.array_equal(out2, ref)) if exact else rel <= TOL
+        results[rank] = (bool(same), rel)
         if p2p:
             ep.close()
         be.close()
@@ -69,15 +73,29 @@ def _rank(rank: int, world: int, port: int, B: int, results, p2p: bool = False):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("B,p2p", [(1, False), (5, False), (1, True), (5, True)])
-def test_ep_two_gpus_bit_exact(B, p2p):
+def _run(B, p2p, exact):
     import torch.multiprocessing as mp
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_rank, args=(2, _free_port(), B, results, p2p), nprocs=2,
+        mp.start_processes(_rank, args=(2, _free_port(), B, results, p2p, exact), nprocs=2,
                            start_method="spawn", join=True)
         res = dict(results)
     assert sorted(res) == [0, 1]
     for r, (same, err) in res.items():
-        assert same, f"rank {r}: max abs diff {err}"
+        assert same, f"rank {r}: max row-relative error {err}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("B,p2p", [(1, False), (5, False), (1, True), (5, True)])
+def test_ep_two_gpus_bit_exact(B, p2p):
+    """Exact expert path on the owners: the layer output is the reference's bits."""
+    _run(B, p2p, True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("p2p", [True, False])
+def test_ep_two_gpus_auto_path_b64(p2p):
+    """The configuration the scaling bench runs: B = 64 tokens per rank with
+    JL_PATH_AUTO, so the owners run the tensor-core kernels on the rows they
+    received (peer-exchanged, padded to world x cap slots): <= 1e-3 per row."""
+    _run(64, p2p, False)
