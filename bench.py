@@ -606,6 +606,92 @@ def microbench(moe, a, hbm, peak_kind):
                 per_T=res)
 
 
+def full_decode(a, hbm):
+    """the whole decode step of the Qwen3-30B-A3B shape on
+    one GPU (attention, norms, the 48 Q4 MoE layers, the lm_head and the
+    argmax), seeded random-init weights built on the device. Context: every
+    sequence's 512-token prompt of uniform-random ids runs through the same
+    decode step first (all sequences batched, one step per position). Then
+    greedy decode at each B: a step embeds the previous step's token, runs the
+    decoder and takes the argmax, captured once as a CUDA graph (positions
+    advance inside the graph). e2e: the token ids cross host <-> device every
+    step (pinned host memory) with a synchronisation per step."""
+    import torch
+    from joule_b200.decoder import Decoder, qwen3_cfg
+    Bs = sorted(set(int(b) for b in a.decode_sweep.split(",")))
+    Bmax, ctx = max(Bs), a.ctx
+    steps, warm = a.steps, a.warmup
+    cfg = qwen3_cfg(maxT=ctx + warm + steps + 16)
+    t0 = time.time()
+    dec = Decoder.random(cfg, Bmax, Bmax)
+    build_s = time.time() - t0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    V, d, L = cfg.V, cfg.d, cfg.L
+    prompt = torch.randint(0, V, (Bmax, ctx), generator=torch.Generator().manual_seed(0),
+                           dtype=torch.int32).to(dev)
+    slots = torch.arange(Bmax, dtype=torch.int32, device=dev)
+    x = torch.empty(Bmax, d, device=dev)
+    tok0 = torch.empty(Bmax, dtype=torch.int32, device=dev)
+    t0 = time.time()
+    for p in range(ctx):
+        pos = torch.full((Bmax,), p, dtype=torch.int32, device=dev)
+        dec.embed(prompt[:, p].contiguous(), x)
+        dec.step(slots, pos, x, tok=tok0 if p == ctx - 1 else None)
+    torch.cuda.synchronize()
+    dec.check()
+    prefill_s = time.time() - t0
+    res = {}
+    stream = torch.cuda.Stream()
+    for B in Bs:
+        pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+        tok = tok0[:B].clone()
+        xb = torch.empty(B, d, device=dev)
+        sl = slots[:B].contiguous()
+        with torch.cuda.stream(stream):  # eager once (sets kernel attributes outside capture)
+            dec.embed(tok, xb, stream=stream)
+            dec.step(sl, pos, xb, tok=tok, stream=stream)
+        stream.synchronize()
+        pos.fill_(ctx)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                dec.embed(tok, xb, stream=stream)
+                dec.step(sl, pos, xb, tok=tok, stream=stream)
+                pos.add_(1)
+        ms = replay_ms(g, steps, warm, stream)
+        dec.check(stream)
+        # end to end: token ids host -> device -> host each step
+        tok_h = torch.empty(B, dtype=torch.int32).pin_memory()
+        tok_h.copy_(tok.cpu())
+        pos.fill_(ctx)
+        n_e2e = max(3, steps // 2)
+        stream.synchronize()
+        e0 = time.perf_counter()
+        for _ in range(n_e2e):
+            with torch.cuda.stream(stream):
+                tok.copy_(tok_h, non_blocking=True)
+                g.replay()
+                tok_h.copy_(tok, non_blocking=True)
+            stream.synchronize()
+        e2e_s = (time.perf_counter() - e0) / n_e2e
+        dec.check(stream)
+        del g
+        res[str(B)] = dict(tok_s=B / (ms / 1e3), ms_per_step=ms,
+                           e2e=dict(value=B / e2e_s, unit="tok/s", h2d_bytes_per_step=B * 4,
+                                    d2h_bytes_per_step=B * 4, ms_per_step=e2e_s * 1e3,
+                                    api="Decoder.embed + Decoder.step (jl_dec_embed, jl_dec_step) as one "
+                                        "CUDA graph, token ids host->device and back every step"))
+    dec.close()
+    torch.cuda.synchronize()
+    return dict(config="BASELINE config 3: Qwen3-30B-A3B architecture, random-init (bf16 dense N(0,0.02), "
+                       "fp32 lm_head, Q4 experts), 48 layers, GQA 32/4 x 128, per-head QK-norm, RoPE theta "
+                       "1e6, eps 1e-6, vocab 151936; context 512 uniform-random ids (seed 0) then greedy decode",
+                context=ctx, build_s=round(build_s, 1), prefill_s=round(prefill_s, 1),
+                path="norms, attention, projections and lm_head in the reference's fp32 order on CUDA cores; "
+                     "MoE layers JL_PATH_AUTO (exact for B <= 3, tensor cores above)",
+                per_batch=res)
+
+
 def tensor_peak_tflops():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -707,6 +793,11 @@ def run_ours(a):
         line["cpu_baseline_per_batch"] = cb
     if a.micro:
         line["microbench"] = microbench(moe, a, hbm, peak_kind)
+    if a.decode_sweep:
+        moe.close()
+        del xs, outs
+        torch.cuda.empty_cache()
+        line["full_decode"] = full_decode(a, hbm)
     print(json.dumps(line), flush=True)
 
 
@@ -804,6 +895,9 @@ def main():
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
     ap.add_argument("--micro", default="1,8,64,512,4096",
                     help="config 5 token counts ('' to skip the microbenchmark)")
+    ap.add_argument("--decode-sweep", default="1,8,32,64",
+                    help="full-model decode batch sizes (config 3; '' to skip)")
+    ap.add_argument("--ctx", type=int, default=512, help="context before the timed decode steps")
     ap.add_argument("--ep", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1 exchange: library peer-memory kernels or NCCL all-to-all")
     a = ap.parse_args()

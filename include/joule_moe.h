@@ -193,9 +193,11 @@ int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
                           const float* w_down, void* stream);
 
 /* Path selection for jl_moe_forward. */
-#define JL_PATH_AUTO 0  /* exact for B <= 3, tensor-core beyond (d % 512 == 0, m % 256 == 0) */
-#define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order */
+#define JL_PATH_AUTO 0  /* GEMV for B <= 4, tensor-core beyond (d % 512 == 0, m % 256 == 0), else exact */
+#define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order (bit-identical outputs) */
 #define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
+#define JL_PATH_GEMV 3  /* B <= 4: warp-per-row GEMVs over every warp of the GPU, fp32 in another
+                           order (<= 1e-3 row-relative); larger B runs as JL_PATH_AUTO */
 int jl_moe_set_path(jl_moe* h, int path);
 
 /* One MoE FFN layer: out[B, d] = MoE(x[B, d]) for layer l (device fp32).
@@ -364,6 +366,102 @@ int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n);
 int jl_route_noalloc(const unsigned short* gate_w, const float* x, int B, int E,
                      int d, int topk, int norm_topk_prob, int* top, float* tw,
                      int* dev_status, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* The whole decode step on the GPU: norms, attention, the MoE layers, the
+ * lm_head and the argmax, in the reference's arithmetic order. */
+
+/* The reference's KV cache entry (decode_kernel.c:328-331): kv[b*L + l] holds
+ * sequence b's layer-l keys and values, each [maxT, n_kv, hd] fp32. */
+typedef struct {
+    float* k;
+    float* v;
+} KVCache;
+
+typedef struct jl_dec jl_dec;
+
+/* A decoder on the current device: uploads every weight KernelW names (host
+ * memory, or device memory when src_on_device; lm_head is fp32 [V, d] as
+ * decoder3.py:218-230 stores it) into the device layout, creates the MoE
+ * handle (its Q4 layers from W's expert tables; when expert_pk[0] is NULL
+ * they are left for jl_dec_moe + jl_moe_upload_layer / jl_moe_quantize_layer)
+ * and KV caches of `slots` sequences x L layers x maxT rows. max_batch is the
+ * most sequences one step may run. Replaces what NativeDecoder.__init__
+ * (decoder3.py:86-163) and ws_init (decode_kernel.c:382-424) set up. */
+int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch, int slots,
+                  int src_on_device, jl_dec** out);
+int jl_dec_destroy(jl_dec* h);
+
+/* The decoder's MoE handle (to upload experts, or set its path). */
+int jl_dec_moe(jl_dec* h, jl_moe** moe);
+
+/* Device base pointers of the K and V caches, [slots][L][maxT][n_kv*hd] fp32. */
+int jl_dec_kv(jl_dec* h, float** k, float** v);
+
+/* x[b] = bf16 embed[tokens[b]] as fp32 (embed_lookup, decode_kernel.c:1597-1600);
+ * tokens [B] and x [B, d] device. */
+int jl_dec_embed(jl_dec* h, const int* tokens, int B, float* x, void* stream);
+
+/* One batched decode step (decode_layers_batch[_argmax], decode_kernel.c:
+ * 1518-1586) for B sequences: sequence b is KV slot slots[b] at position
+ * positions[b] (its rows [0, positions[b]) already in the cache; this step
+ * appends row positions[b] of every layer), input x[b] (embedded, fp32 [d]).
+ * logits [B, V] and tok [B] (argmax, lowest index on ties) are nullable
+ * device outputs. All pointers device; enqueued on `stream`. With the MoE
+ * handle on JL_PATH_EXACT the logits equal the reference's bit for bit. */
+int jl_dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B,
+                float* logits, int* tok, void* stream);
+
+/* Read and clear the decoder's error word and its MoE handle's
+ * (synchronises): JL_ERR_INVALID for a position outside [0, maxT). */
+int jl_dec_check(jl_dec* h, void* stream);
+
+/* The reference's own decode entry points with its signatures (host
+ * buffers, void, synchronous), bound through get_dll("decode_kernel") by
+ * NativeDecoder (decoder3.py:32, 490-629). One decoder per (cfg, W) is
+ * created on first use (weights uploaded from W, MoE on the exact path) for
+ * up to 32 sequences per call. The library keeps a device copy of each
+ * sequence's KV cache (a sequence is identified by its kv[b*L].k pointer):
+ * a call at position p uses that copy when it holds exactly p rows, and
+ * otherwise first copies the host rows [0, p) of every layer over; after
+ * the step the new row of every layer is written back to the host caches.
+ * A failed call fills logits with NaN (out_tok with -1) and
+ * jl_decode_status() returns its JL_ERR_* code.
+ *   decode_layers_batch: decode_kernel.c:1518-1556 (logits [B, V] host)
+ *   decode_layers_batch_argmax: decode_kernel.c:1560-1586 (out_tok [B]; the
+ *     argmax of the logits, lowest index on ties)
+ *   decode_layers: decode_kernel.c:1588-1595 (B = 1)
+ *   embed_lookup: decode_kernel.c:1597-1600 */
+void decode_layers_batch(const KernelCfg* c, const KernelW* W, KVCache* kv,
+                         const int* positions, const float* xin, int B, float* logits);
+void decode_layers_batch_argmax(const KernelCfg* c, const KernelW* W, KVCache* kv,
+                                const int* positions, const float* xin, int B, int* out_tok);
+void decode_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, int pos,
+                   const float* xin, float* logits);
+void embed_lookup(const KernelW* W, const KernelCfg* c, int token, float* out);
+
+/* prefill_layers (decode_kernel.c:1606-1615): one B = 1 step per position
+ * 0..T-1 of one sequence; logits [V] (host) of the last position. */
+void prefill_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* tokens,
+                    int T, float* logits);
+
+/* debug_decode_layers (decode_kernel.c:1764-1790): one B = 1 step at pos;
+ * out (host) receives per layer 7 rows of max(E, d) floats: norm1 output,
+ * attention output, h after attention, norm2 output, router logits, MoE
+ * output, h after the MoE layer. */
+void debug_decode_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, int pos,
+                         const float* xin, float* out);
+
+/* The reference's host thread-pool controls (decode_kernel.c:631, 1843),
+ * called by NativeDecoder at start-up (decoder3.py:133-145). This library
+ * has no host pool: spin_pool_init returns 1 (success) and set_lm_threads
+ * does nothing. */
+int spin_pool_init(int n_workers);
+void set_lm_threads(int n);
+
+/* Status of this thread's last reference-signature decode call. No
+ * counterpart in the reference. */
+int jl_decode_status(void);
 
 /* Bytes of device memory the handle holds (store + workspace). */
 long long jl_moe_device_bytes(const jl_moe* h);

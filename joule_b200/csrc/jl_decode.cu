@@ -1,0 +1,1115 @@
+// The decode step around the MoE layer on the GPU: RMSNorm, bf16 QKV and
+// o_proj, QKV bias, QK-norm (per head or whole vector), RoPE, attention over
+// per-sequence KV caches, the fp32 lm_head and the argmax, in the reference's
+// arithmetic order (decode_layers_batch, decode_kernel.c:1518-1556, with
+// layer_attn_batch 1120-1234, rms_norm 224-230, rope_apply 259-266,
+// sqrtf_fast 88-93, matvec_B_worker 693-718, lm_B_worker 969-995), so that a
+// decode step gives the reference's logits bit for bit when the MoE layer runs
+// on its exact path.
+//
+// Per layer: k_rms (h += previous residual, norm1) -> k_mv (QKV, + bias) ->
+// k_attn (QK-norm, RoPE, KV append, softmax attention) -> k_mv (o_proj) ->
+// k_rms (h += o, norm2) -> the MoE layer (jl_moe_forward) -> next layer.
+// Then k_rms (final norm) -> k_mv (fp32 lm_head) -> k_argmax.
+//
+// Every sum the reference forms sequentially stays one sequential chain here
+// (the norms' sums of squares, the attention's score, softmax and value sums);
+// the parallelism is across rows, heads, positions and sequences. The matvecs
+// use the reference's 8-lane FMA order: lane j of a row sums the products of
+// columns j, j+8, j+16, ... by fused multiply-add, then the AVX tree
+// ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7)).
+//
+// Weight layout for the matvecs (coalesced 16-byte loads): matrix W [N, K] is
+// stored as W'[c][n][j][u] = W[n][j + 8*(U*c + u)] with U = 8 values per
+// 16 bytes for bf16 (4 for fp32); thread (row n, lane j) reads chunk c as one
+// 16-byte load and a warp (4 rows x 8 lanes) reads 512 contiguous bytes.
+#include <algorithm>
+#include <climits>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <unordered_map>
+#include <vector>
+
+#include "jl_common.cuh"
+#include "jl_internal.h"
+
+namespace jl {
+
+constexpr int kMvRows = 32;           // rows per matvec block (x 8 lanes = 256 threads)
+constexpr int kMvTok = 8;             // tokens per pass of a matvec block
+constexpr int kAttnThreads = 128;     // attention block (head dim <= 128)
+constexpr int kNormThreads = 256;
+constexpr int kErrPosition = 8;       // a position outside [0, maxT) (error word bit)
+
+// decode_kernel.c:88-93: halve the exponent for a first estimate, then one
+// Newton step 0.5 * (y + x / y).
+__device__ __forceinline__ float sqrtf_fast(float x) {
+    const float y = __uint_as_float((__float_as_uint(x) + 0x3F800000u) >> 1);
+    return __fmul_rn(0.5f, __fadd_rn(y, __fdiv_rn(x, y)));
+}
+
+// 1 / sqrtf_fast(ss / n + eps) (decode_kernel.c:227, 1168, 1181)
+__device__ __forceinline__ float rms_inv(float ss, int n, float eps) {
+    return __fdiv_rn(1.0f, sqrtf_fast(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+// Sequential sum of v[0..n) in index order by the calling thread (n % 4 == 0,
+// v 16-byte aligned): loads run ahead of the one dependent add chain.
+__device__ __forceinline__ float chain_sum(const float* v, int n) {
+    float s = 0.0f;
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+#pragma unroll 8
+    for (int i = 0; i < n / 4; i++) {
+        const float4 q = v4[i];
+        s = __fadd_rn(s, q.x);
+        s = __fadd_rn(s, q.y);
+        s = __fadd_rn(s, q.z);
+        s = __fadd_rn(s, q.w);
+    }
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// Residual add + RMSNorm (decode_kernel.c:224-230, 1528-1535). One block per
+// sequence b: h[b] += add[b] (when add != null), then t[b] = (h * inv) * w
+// with inv from the sum of squares in index order.
+__global__ void __launch_bounds__(kNormThreads) k_rms(float* __restrict__ h, const float* __restrict__ add,
+                                                      const uint16_t* __restrict__ w, float eps, int d,
+                                                      float* __restrict__ t) {
+    extern __shared__ __align__(16) float sq[];  // [d]
+    __shared__ float inv_s;
+    griddep_wait();
+    griddep_launch_dependents();
+    const int b = blockIdx.x;
+    float* hb = h + (size_t)b * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        float v = hb[i];
+        if (add) {
+            v = __fadd_rn(v, add[(size_t)b * d + i]);
+            hb[i] = v;
+        }
+        sq[i] = __fmul_rn(v, v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) inv_s = rms_inv(chain_sum(sq, d), d, eps);
+    __syncthreads();
+    const float inv = inv_s;
+    for (int i = threadIdx.x; i < d; i += blockDim.x)
+        t[(size_t)b * d + i] = __fmul_rn(__fmul_rn(hb[i], inv), bf16_to_f32(w[i]));
+}
+
+// ---------------------------------------------------------------------------
+// out[b, n] = W[n, :] . x[b, :] (+ bias[n], a separate add as the reference's
+// `q[i] += bq[i]`), W in the chunked lane-major layout above. Block: 32 rows x
+// 8 lanes; it runs the B tokens in passes of kMvTok, with the pass's token
+// rows staged lane-major in shared memory (x_s[t][j][i] = x[b0+t][j + 8i], rows
+// padded by 4 floats so the 8 lanes' float4 reads hit distinct banks). The
+// block's weight rows are re-read from L2 on later passes.
+template <typename WT>
+struct mv_traits;
+template <>
+struct mv_traits<uint16_t> {
+    static constexpr int U = 8;  // values per 16-byte chunk
+};
+template <>
+struct mv_traits<float> {
+    static constexpr int U = 4;
+};
+
+__device__ __forceinline__ void fma_chunk(const uint4 w, const float* xp, float& acc, uint16_t) {
+    const float4 x0 = *reinterpret_cast<const float4*>(xp);
+    const float4 x1 = *reinterpret_cast<const float4*>(xp + 4);
+    acc = __fmaf_rn(__uint_as_float(w.x << 16), x0.x, acc);
+    acc = __fmaf_rn(__uint_as_float(w.x & 0xFFFF0000u), x0.y, acc);
+    acc = __fmaf_rn(__uint_as_float(w.y << 16), x0.z, acc);
+    acc = __fmaf_rn(__uint_as_float(w.y & 0xFFFF0000u), x0.w, acc);
+    acc = __fmaf_rn(__uint_as_float(w.z << 16), x1.x, acc);
+    acc = __fmaf_rn(__uint_as_float(w.z & 0xFFFF0000u), x1.y, acc);
+    acc = __fmaf_rn(__uint_as_float(w.w << 16), x1.z, acc);
+    acc = __fmaf_rn(__uint_as_float(w.w & 0xFFFF0000u), x1.w, acc);
+}
+__device__ __forceinline__ void fma_chunk(const uint4 w, const float* xp, float& acc, float) {
+    const float4 x0 = *reinterpret_cast<const float4*>(xp);
+    acc = __fmaf_rn(__uint_as_float(w.x), x0.x, acc);
+    acc = __fmaf_rn(__uint_as_float(w.y), x0.y, acc);
+    acc = __fmaf_rn(__uint_as_float(w.z), x0.z, acc);
+    acc = __fmaf_rn(__uint_as_float(w.w), x0.w, acc);
+}
+
+__host__ __device__ inline int mv_xstride(int K) { return K / 8 + 4; }
+
+template <typename WT, int NT>
+__global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, const float* __restrict__ x,
+                                                    int N, int K, int B, const float* __restrict__ bias,
+                                                    float* __restrict__ out) {
+    constexpr int U = mv_traits<WT>::U;
+    constexpr int P = 8;  // chunks per load group; the next group is in flight while one is used
+    extern __shared__ __align__(16) float x_s[];  // [NT][8][K/8 + 4]
+    const int tid = threadIdx.x, j = tid & 7;
+    const int n = blockIdx.x * kMvRows + (tid >> 3);
+    const bool live = n < N;
+    const int nc = K / (8 * U), xs = mv_xstride(K);
+    const uint4* wp = reinterpret_cast<const uint4*>(W) + (size_t)(live ? n : 0) * 8 + j;
+    const size_t cstride = (size_t)N * 8;  // uint4 per chunk
+    auto load_group = [&](int c0, uint4 (&w)[P]) {
+#pragma unroll
+        for (int i = 0; i < P; i++)
+            w[i] = (live && c0 + i < nc) ? __ldg(wp + (size_t)(c0 + i) * cstride) : make_uint4(0, 0, 0, 0);
+    };
+    uint4 first[P];
+    load_group(0, first);  // weights do not depend on the previous kernel: fetch before the wait
+    griddep_wait();
+    griddep_launch_dependents();
+    for (int b0 = 0; b0 < B; b0 += NT) {
+        const int nt = min(NT, B - b0);
+        __syncthreads();
+        for (int i = tid; i < nt * K; i += blockDim.x) {
+            const int t = i / K, c = i % K;
+            x_s[(t * 8 + (c & 7)) * xs + (c >> 3)] = x[(size_t)(b0 + t) * K + c];
+        }
+        __syncthreads();
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+        uint4 cur[P], nxt[P];
+#pragma unroll
+        for (int i = 0; i < P; i++) cur[i] = first[i];
+        for (int c0 = 0; c0 < nc; c0 += P) {
+            if (c0 + P < nc) load_group(c0 + P, nxt);
+#pragma unroll
+            for (int i = 0; i < P; i++) {
+                if (c0 + i < nc) {
+#pragma unroll
+                    for (int t = 0; t < NT; t++)
+                        if (t < nt) fma_chunk(cur[i], x_s + (size_t)(t * 8 + j) * xs + (c0 + i) * U, acc[t], WT());
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < P; i++) cur[i] = nxt[i];
+        }
+        if (b0 + NT < B) load_group(0, first);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            float a = acc[t];
+            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+            a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+            if (live && j == 0 && t < nt) {
+                if (bias) a = __fadd_rn(a, bias[n]);
+                out[(size_t)(b0 + t) * N + n] = a;
+            }
+        }
+    }
+}
+
+// W [N, K] (row-major, device) -> the chunked lane-major layout.
+template <typename WT>
+__global__ void k_repack_mv(const WT* __restrict__ src, WT* __restrict__ dst, int N, int K) {
+    constexpr int U = mv_traits<WT>::U;
+    const size_t total = (size_t)N * K;
+    for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
+        // o = ((c * N + n) * 8 + j) * U + u
+        const int u = (int)(o % U);
+        const int j = (int)((o / U) % 8);
+        const size_t cn = o / (8 * U);
+        const int n = (int)(cn % N);
+        const int c = (int)(cn / N);
+        dst[o] = src[(size_t)n * K + j + 8 * (U * c + u)];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Attention of one (head h, sequence b) (decode_kernel.c:1150-1231): QK-norm,
+// RoPE, the KV append, scores q.k_t for t <= pos (each a sequential sum over
+// the head dimension), scaled by 1/sqrtf_fast(hd), softmax with expf_fast and
+// a sequential sum over t, and att[i] = sum over t of (p_t * v_t[i]) in t
+// order. The block of the first q head of each KV group writes the group's K
+// and V rows at pos; the other blocks of the group use the row they computed
+// themselves for t = pos, so no block reads a row another block is writing.
+struct attn_args {
+    const float* qkv;        // [B][qn + 2 kn] (bias added)
+    float* att;              // [B][qn]
+    const int* positions;    // [B]
+    const int* slots;        // [B] KV cache slot of each sequence
+    float* kc;               // [slots][L][maxT][kn]
+    float* vc;
+    const uint16_t* qnw;     // QK-norm weights of this layer (per head [hd] or whole [qn]/[kn])
+    const uint16_t* knw;
+    const float* cosb;       // [maxT][hd]
+    const float* sinb;
+    int l, L, H, KH, hd, maxT, qk_type;
+    int sqn;                 // floats per squares buffer: max(qn, kn) for whole-vector norms, else hd
+    float eps;
+    int* err;
+};
+
+__global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
+    extern __shared__ __align__(16) float sm[];
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, gsz = a.H / a.KH, g = h / gsz;
+    const int kTile = kAttnThreads;
+    // shared layout: q, k, v [hd]; sq [max(qn, kn)] (squares for the norms);
+    // ks [kTile][hd + 1]; sc [maxT]
+    float* q_s = sm;
+    float* k_s = q_s + 128;
+    float* v_s = k_s + 128;
+    const int sqn = a.sqn;
+    float* sq = v_s + 128;                       // [2][sqn] (q and k squares)
+    float* ks = sq + 2 * sqn;                    // [kTile][hd + 1]
+    float* sc = ks + kTile * (hd + 1);           // [maxT]
+    __shared__ float red[kAttnThreads / 32];
+    __shared__ float inv_q, inv_k, smax_s, sum_s;
+    griddep_wait();
+    griddep_launch_dependents();
+    const int pos = a.positions[b];
+    if (pos < 0 || pos >= a.maxT) {
+        if (tid == 0) atomicOr(a.err, kErrPosition);
+        return;
+    }
+    const int slot = a.slots[b];
+    const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
+    if (tid < hd) {
+        q_s[tid] = row[h * hd + tid];
+        k_s[tid] = row[qn + g * hd + tid];
+        v_s[tid] = row[qn + kn + g * hd + tid];
+    }
+    // QK-norm
+    if (a.qk_type == 2) {  // whole vectors q [qn], k [kn] (decode_kernel.c:1162-1174)
+        for (int i = tid; i < qn; i += blockDim.x) sq[i] = __fmul_rn(row[i], row[i]);
+        for (int i = tid; i < kn; i += blockDim.x) sq[sqn + i] = __fmul_rn(row[qn + i], row[qn + i]);
+        __syncthreads();
+        if (tid == 0) inv_q = rms_inv(chain_sum(sq, qn), qn, a.eps);
+        if (tid == 32) inv_k = rms_inv(chain_sum(sq + sqn, kn), kn, a.eps);
+        __syncthreads();
+        if (tid < hd) {
+            q_s[tid] = __fmul_rn(__fmul_rn(q_s[tid], inv_q), bf16_to_f32(a.qnw[h * hd + tid]));
+            k_s[tid] = __fmul_rn(__fmul_rn(k_s[tid], inv_k), bf16_to_f32(a.knw[g * hd + tid]));
+        }
+    } else if (a.qk_type == 1) {  // per head, weights [hd] (decode_kernel.c:1180-1193)
+        __syncthreads();
+        if (tid < hd) {
+            sq[tid] = __fmul_rn(q_s[tid], q_s[tid]);
+            sq[sqn + tid] = __fmul_rn(k_s[tid], k_s[tid]);
+        }
+        __syncthreads();
+        if (tid == 0) inv_q = rms_inv(chain_sum(sq, hd), hd, a.eps);
+        if (tid == 32) inv_k = rms_inv(chain_sum(sq + sqn, hd), hd, a.eps);
+        __syncthreads();
+        if (tid < hd) {
+            q_s[tid] = __fmul_rn(__fmul_rn(q_s[tid], inv_q), bf16_to_f32(a.qnw[tid]));
+            k_s[tid] = __fmul_rn(__fmul_rn(k_s[tid], inv_k), bf16_to_f32(a.knw[tid]));
+        }
+    }
+    __syncthreads();
+    // RoPE, rotate-half (decode_kernel.c:259-266, 1195-1199)
+    const int half = hd / 2;
+    float qa = 0.f, qb = 0.f, ka = 0.f, kb = 0.f;
+    if (tid < half) {
+        const float cs = a.cosb[(size_t)pos * hd + tid], sn = a.sinb[(size_t)pos * hd + tid];
+        const float x0 = q_s[tid], x1 = q_s[tid + half];
+        qa = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        qb = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        const float y0 = k_s[tid], y1 = k_s[tid + half];
+        ka = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+        kb = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+    }
+    __syncthreads();
+    if (tid < half) {
+        q_s[tid] = qa;
+        q_s[tid + half] = qb;
+        k_s[tid] = ka;
+        k_s[tid + half] = kb;
+    }
+    __syncthreads();
+    const size_t cache_off = ((size_t)slot * a.L + a.l) * a.maxT * kn;
+    float* K = a.kc + cache_off;
+    float* V = a.vc + cache_off;
+    if (h % gsz == 0 && tid < hd) {  // KV append (decode_kernel.c:1200-1205)
+        K[(size_t)pos * kn + g * hd + tid] = k_s[tid];
+        V[(size_t)pos * kn + g * hd + tid] = v_s[tid];
+    }
+    // scores (decode_kernel.c:1212-1218), tiles of kTile positions
+    const int T = pos + 1;
+    const float scale = sqrtf_fast((float)hd);
+    float mx = -1e30f;
+    for (int t0 = 0; t0 < T; t0 += kTile) {
+        const int nt = min(kTile, T - t0);
+        __syncthreads();
+        for (int i = tid; i < nt * hd; i += blockDim.x) {
+            const int r = i / hd, c = i % hd, t = t0 + r;
+            ks[r * (hd + 1) + c] = (t == pos) ? k_s[c] : K[(size_t)t * kn + g * hd + c];
+        }
+        __syncthreads();
+        if (tid < nt) {
+            const float* kr = ks + tid * (hd + 1);
+            float s = 0.0f;
+            for (int i = 0; i < hd; i++) s = __fadd_rn(s, __fmul_rn(q_s[i], kr[i]));
+            const float v = __fdiv_rn(s, scale);
+            sc[t0 + tid] = v;
+            if (v > mx) mx = v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = red[0];
+        for (int w = 1; w < kAttnThreads / 32; w++) m = fmaxf(m, red[w]);
+        smax_s = m;
+    }
+    __syncthreads();
+    const float smax = smax_s;
+    for (int t = tid; t < T; t += blockDim.x) sc[t] = expf_fast(__fsub_rn(sc[t], smax));
+    __syncthreads();
+    if (tid == 0) {  // sequential sum over t (decode_kernel.c:1220)
+        float s = 0.0f;
+        int t = 0;
+        for (; t + 4 <= T; t += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(sc + t);
+            s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+        }
+        for (; t < T; t++) s = __fadd_rn(s, sc[t]);
+        sum_s = s;
+    }
+    __syncthreads();
+    const float sum = sum_s;
+    for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
+    __syncthreads();
+    if (tid < hd) {  // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229)
+        const float* vp = V + g * hd + tid;
+        float o = 0.0f;
+        int t = 0;
+        for (; t + 4 <= T; t += 4) {
+            const float v0 = (t == pos) ? v_s[tid] : vp[(size_t)t * kn];
+            const float v1 = (t + 1 == pos) ? v_s[tid] : vp[(size_t)(t + 1) * kn];
+            const float v2 = (t + 2 == pos) ? v_s[tid] : vp[(size_t)(t + 2) * kn];
+            const float v3 = (t + 3 == pos) ? v_s[tid] : vp[(size_t)(t + 3) * kn];
+            o = __fadd_rn(o, __fmul_rn(sc[t], v0));
+            o = __fadd_rn(o, __fmul_rn(sc[t + 1], v1));
+            o = __fadd_rn(o, __fmul_rn(sc[t + 2], v2));
+            o = __fadd_rn(o, __fmul_rn(sc[t + 3], v3));
+        }
+        for (; t < T; t++) {
+            const float v0 = (t == pos) ? v_s[tid] : vp[(size_t)t * kn];
+            o = __fadd_rn(o, __fmul_rn(sc[t], v0));
+        }
+        a.att[(size_t)b * qn + h * hd + tid] = o;
+    }
+}
+
+// squares buffer size (floats, a multiple of 4) for the QK-norm of a type
+int attn_sqn(int qk_type, int H, int KH, int hd) {
+    const int n = qk_type == 2 ? std::max(H * hd, KH * hd) : hd;
+    return (n + 3) / 4 * 4;
+}
+
+size_t attn_smem(int sqn, int hd, int maxT) {
+    return (size_t)(3 * 128 + 2 * sqn + kAttnThreads * (hd + 1) + maxT) * sizeof(float);
+}
+
+// ---------------------------------------------------------------------------
+// argmax over each logits row, lowest index on ties (the first maximum of an
+// ascending scan with strict '>', as the greedy pick over the reference's
+// logits).
+__global__ void k_argmax(const float* __restrict__ logits, int V, int* __restrict__ tok) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    griddep_wait();
+    griddep_launch_dependents();
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const float* r = logits + (size_t)b * V;
+    float best = -__int_as_float(0x7f800000);
+    int idx = INT_MAX;
+    for (int v = tid; v < V; v += blockDim.x) {
+        const float x = r[v];
+        if (x > best) {  // ascending per thread: the first maximum stays
+            best = x;
+            idx = v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ob > best || (ob == best && oi < idx)) {
+            best = ob;
+            idx = oi;
+        }
+    }
+    if ((tid & 31) == 0) {
+        bv[tid >> 5] = best;
+        bi[tid >> 5] = idx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+                best = bv[w];
+                idx = bi[w];
+            }
+        tok[b] = idx == INT_MAX ? 0 : idx;
+    }
+}
+
+// embed_lookup (decode_kernel.c:1597-1600): x[b] = bf16 embed[tok[b]] as fp32.
+__global__ void k_embed(const uint16_t* __restrict__ embed, const int* __restrict__ tok, int V, int d,
+                        float* __restrict__ x, int* err) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int b = blockIdx.y;
+    const int t = tok[b];
+    if (t < 0 || t >= V) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, kErrBadExpert);
+        return;
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x)
+        x[(size_t)b * d + i] = bf16_to_f32(embed[(size_t)t * d + i]);
+}
+
+}  // namespace jl
+
+// ---------------------------------------------------------------------------
+// The handle.
+
+struct jl_dec {
+    int device;
+    int L, d, H, KH, hd, E, k, m, V, maxT, qk_type, bias;
+    float eps;
+    int qn, kn, nqkv;
+    int max_batch, slots;
+    jl_moe* moe;
+    uint16_t* embed;   // [V, d]
+    uint16_t* norm1;   // [L, d]
+    uint16_t* norm2;   // [L, d]
+    uint16_t* fnorm;   // [d]
+    uint16_t* qnw;     // [L, hd] (per head) or [L, qn] (whole)
+    uint16_t* knw;     // [L, hd] or [L, kn]
+    uint16_t* wqkv;    // per layer: [nqkv, d] chunked lane-major
+    uint16_t* wo;      // per layer: [d, qn] chunked lane-major
+    float* bqkv;       // [L, nqkv] or null
+    float* lm;         // [V, d] fp32 chunked lane-major
+    float* cosb;       // [maxT, hd]
+    float* sinb;
+    float* kc;         // [slots][L][maxT][kn]
+    float* vc;
+    // workspace
+    float* h;          // [max_batch, d]
+    float* t;          // [max_batch, d]
+    float* h2;         // [max_batch, d]
+    float* qkv;        // [max_batch, nqkv]
+    float* att;        // [max_batch, qn]
+    float* logits;     // [max_batch, V]
+    int* tok;          // [max_batch]
+    int* err;          // [1]
+    void* stage;       // device staging for uploads
+    size_t stage_bytes;
+};
+
+namespace {
+
+int dec_attrs() {
+    return jl_device_once(kOnceDecode, [] {
+        using namespace jl;
+        const int big = 200 * 1024;
+        JL_CUDA(cudaFuncSetAttribute(k_mv<uint16_t, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<uint16_t, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<uint16_t, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<uint16_t, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<float, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<float, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_mv<float, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        return JL_OK;
+    });
+}
+
+template <typename WT>
+int launch_mv(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, cudaStream_t s) {
+    using namespace jl;
+    const int nt = B >= 8 ? 8 : B >= 4 ? 4 : B >= 2 ? 2 : 1;
+    const size_t smem = (size_t)nt * 8 * mv_xstride(K) * sizeof(float);
+    if (smem > 200 * 1024) return JL_ERR_INVALID;
+    const dim3 grid((N + kMvRows - 1) / kMvRows), block(kMvRows * 8);
+    switch (nt) {
+        case 8: return launch(k_mv<WT, 8>, grid, block, smem, s, W, x, N, K, B, bias, out);
+        case 4: return launch(k_mv<WT, 4>, grid, block, smem, s, W, x, N, K, B, bias, out);
+        case 2: return launch(k_mv<WT, 2>, grid, block, smem, s, W, x, N, K, B, bias, out);
+        default: return launch(k_mv<WT, 1>, grid, block, smem, s, W, x, N, K, B, bias, out);
+    }
+}
+
+template <typename WT>
+int repack_mv(const WT* src, WT* dst, int N, int K, cudaStream_t s) {
+    const size_t total = (size_t)N * K;
+    const int tpb = 256;
+    const unsigned blocks = (unsigned)std::min<size_t>((total + tpb - 1) / tpb, 65535u * 16);
+    jl::k_repack_mv<WT><<<blocks, tpb, 0, s>>>(src, dst, N, K);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? JL_OK : jl_note_cuda(e);
+}
+
+int check_dec_cfg(const KernelCfg* c) {
+    if (!c || c->L < 1 || c->d < 64 || c->n_heads < 1 || c->n_kv < 1 || c->hd < 2 || c->V < 1 || c->maxT < 1)
+        return JL_ERR_INVALID;
+    if (c->n_heads % c->n_kv || c->hd > 128 || c->hd % 4) return JL_ERR_INVALID;
+    if (c->d % 64 || (c->n_heads * c->hd) % 64 || (c->n_kv * c->hd) % 8) return JL_ERR_INVALID;
+    if (c->qk_norm_type < 0 || c->qk_norm_type > 2) return JL_ERR_INVALID;
+    return JL_OK;
+}
+
+// Copy `bytes` from src (host or device) into dst (device).
+int put(void* dst, const void* src, size_t bytes, int on_dev, cudaStream_t s) {
+    if (!src) return JL_ERR_INVALID;
+    JL_CUDA(cudaMemcpyAsync(dst, src, bytes, on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+    return JL_OK;
+}
+
+}  // namespace
+
+extern "C" int jl_dec_destroy(jl_dec* h) {
+    if (!h) return JL_OK;
+    if (h->moe) jl_moe_destroy(h->moe);
+    void* ptrs[] = {h->embed, h->norm1, h->norm2, h->fnorm, h->qnw, h->knw, h->wqkv, h->wo, h->bqkv, h->lm,
+                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->logits,
+                    h->tok, h->err, h->stage};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    delete h;
+    return JL_OK;
+}
+
+extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch, int slots, int src_on_device,
+                             jl_dec** out) {
+    using namespace jl;
+    if (!out || !W || max_batch < 1 || slots < max_batch) return JL_ERR_INVALID;
+    *out = nullptr;
+    int rc = check_dec_cfg(c);
+    if (rc) return rc;
+    if (c->qk_norm_type && (!W->qn || !W->kn)) return JL_ERR_INVALID;
+    if (c->bias_qkv && (!W->bq || !W->bk || !W->bv)) return JL_ERR_INVALID;
+    if (!W->embed || !W->lm_head || !W->final_norm || !W->norm1 || !W->norm2 || !W->wq || !W->wk || !W->wv ||
+        !W->wo || !W->gate_w || !W->cos || !W->sin)
+        return JL_ERR_INVALID;
+    rc = dec_attrs();
+    if (rc) return rc;
+    jl_dec* h = new (std::nothrow) jl_dec();
+    if (!h) return JL_ERR_OOM;
+    memset(h, 0, sizeof(*h));
+    cudaGetDevice(&h->device);
+    h->L = c->L, h->d = c->d, h->H = c->n_heads, h->KH = c->n_kv, h->hd = c->hd, h->E = c->E, h->k = c->topk;
+    h->m = c->intermediate, h->V = c->V, h->maxT = c->maxT, h->qk_type = c->qk_norm_type, h->bias = c->bias_qkv;
+    h->eps = c->eps;
+    h->qn = h->H * h->hd, h->kn = h->KH * h->hd, h->nqkv = h->qn + 2 * h->kn;
+    h->max_batch = max_batch, h->slots = slots;
+    rc = jl_moe_create(c, max_batch, &h->moe);
+    if (rc) {
+        delete h;
+        return rc;
+    }
+    const size_t L = h->L, d = h->d, V = h->V;
+    const size_t qnw_n = h->qk_type == 2 ? (size_t)h->qn : h->hd, knw_n = h->qk_type == 2 ? (size_t)h->kn : h->hd;
+    const size_t kvb = (size_t)slots * L * h->maxT * h->kn * sizeof(float);
+    h->stage_bytes = std::max({V * d * sizeof(float), (size_t)h->nqkv * d * 2, d * (size_t)h->qn * 2});
+    struct alloc { void** p; size_t n; } al[] = {
+        {(void**)&h->embed, V * d * 2},
+        {(void**)&h->norm1, L * d * 2},
+        {(void**)&h->norm2, L * d * 2},
+        {(void**)&h->fnorm, d * 2},
+        {(void**)&h->qnw, h->qk_type ? L * qnw_n * 2 : 0},
+        {(void**)&h->knw, h->qk_type ? L * knw_n * 2 : 0},
+        {(void**)&h->wqkv, L * h->nqkv * d * 2},
+        {(void**)&h->wo, L * d * h->qn * 2},
+        {(void**)&h->bqkv, h->bias ? L * h->nqkv * 4 : 0},
+        {(void**)&h->lm, V * d * 4},
+        {(void**)&h->cosb, (size_t)h->maxT * h->hd * 4},
+        {(void**)&h->sinb, (size_t)h->maxT * h->hd * 4},
+        {(void**)&h->kc, kvb},
+        {(void**)&h->vc, kvb},
+        {(void**)&h->h, (size_t)max_batch * d * 4},
+        {(void**)&h->t, (size_t)max_batch * d * 4},
+        {(void**)&h->h2, (size_t)max_batch * d * 4},
+        {(void**)&h->qkv, (size_t)max_batch * h->nqkv * 4},
+        {(void**)&h->att, (size_t)max_batch * h->qn * 4},
+        {(void**)&h->logits, (size_t)max_batch * V * 4},
+        {(void**)&h->tok, (size_t)max_batch * 4},
+        {(void**)&h->err, 16},
+        {&h->stage, h->stage_bytes},
+    };
+    for (auto& a : al) {
+        if (!a.n) continue;
+        if (cudaMalloc(a.p, a.n) != cudaSuccess) {
+            cudaGetLastError();
+            jl_dec_destroy(h);
+            return JL_ERR_OOM;
+        }
+    }
+    cudaStream_t s = nullptr;
+    const int od = src_on_device;
+    auto fail = [&](int r) {
+        cudaStreamSynchronize(s);
+        jl_dec_destroy(h);
+        return r;
+    };
+    if (cudaMemsetAsync(h->err, 0, 16, s) != cudaSuccess || cudaMemsetAsync(h->kc, 0, kvb, s) != cudaSuccess ||
+        cudaMemsetAsync(h->vc, 0, kvb, s) != cudaSuccess)
+        return fail(JL_ERR_CUDA);
+    if ((rc = put(h->embed, W->embed, V * d * 2, od, s)) || (rc = put(h->norm1, W->norm1, L * d * 2, od, s)) ||
+        (rc = put(h->norm2, W->norm2, L * d * 2, od, s)) || (rc = put(h->fnorm, W->final_norm, d * 2, od, s)) ||
+        (rc = put(h->cosb, W->cos, (size_t)h->maxT * h->hd * 4, od, s)) ||
+        (rc = put(h->sinb, W->sin, (size_t)h->maxT * h->hd * 4, od, s)))
+        return fail(rc);
+    if (h->qk_type && ((rc = put(h->qnw, W->qn, L * qnw_n * 2, od, s)) || (rc = put(h->knw, W->kn, L * knw_n * 2, od, s))))
+        return fail(rc);
+    uint16_t* st16 = static_cast<uint16_t*>(h->stage);
+    for (int l = 0; l < h->L; l++) {
+        const size_t qrows = (size_t)h->qn * d, krows = (size_t)h->kn * d;
+        if ((rc = put(st16, W->wq + l * qrows, qrows * 2, od, s)) ||
+            (rc = put(st16 + qrows, W->wk + l * krows, krows * 2, od, s)) ||
+            (rc = put(st16 + qrows + krows, W->wv + l * krows, krows * 2, od, s)) ||
+            (rc = repack_mv<uint16_t>(st16, h->wqkv + (size_t)l * h->nqkv * d, h->nqkv, (int)d, s)))
+            return fail(rc);
+        if ((rc = put(st16, W->wo + (size_t)l * d * h->qn, d * h->qn * 2, od, s)) ||
+            (rc = repack_mv<uint16_t>(st16, h->wo + (size_t)l * d * h->qn, (int)d, h->qn, s)))
+            return fail(rc);
+        if (h->bias) {
+            float* bl = h->bqkv + (size_t)l * h->nqkv;
+            if ((rc = put(bl, W->bq + (size_t)l * h->qn, h->qn * 4, od, s)) ||
+                (rc = put(bl + h->qn, W->bk + (size_t)l * h->kn, h->kn * 4, od, s)) ||
+                (rc = put(bl + h->qn + h->kn, W->bv + (size_t)l * h->kn, h->kn * 4, od, s)))
+                return fail(rc);
+        }
+    }
+    // lm_head: declared unsigned short* in KernelW but fp32 [V, d] (decoder3.py:218-230)
+    if ((rc = put(h->stage, W->lm_head, V * d * 4, od, s)) ||
+        (rc = repack_mv<float>(static_cast<float*>(h->stage), h->lm, (int)V, (int)d, s)))
+        return fail(rc);
+    if (cudaStreamSynchronize(s) != cudaSuccess) return fail(JL_ERR_CUDA);
+    cudaFree(h->stage);  // the staging buffer is only needed while uploading
+    h->stage = nullptr;
+    // the MoE layers (expert tables may be absent: upload them later through jl_dec_moe)
+    if (W->expert_pk[0] && W->expert_sc[0]) {
+        std::vector<const unsigned char*> pk(3 * h->E);
+        std::vector<const unsigned short*> sc(3 * h->E);
+        for (int l = 0; l < h->L; l++) {
+            for (int p = 0; p < 3; p++)
+                for (int e = 0; e < h->E; e++) {
+                    pk[p * h->E + e] = W->expert_pk[p][(size_t)l * h->E + e];
+                    sc[p * h->E + e] = W->expert_sc[p][(size_t)l * h->E + e];
+                }
+            rc = jl_moe_upload_layer(h->moe, l, W->gate_w + (size_t)l * h->E * d, pk.data(), sc.data(), od, s);
+            if (rc) return fail(rc);
+        }
+    }
+    *out = h;
+    return JL_OK;
+}
+
+extern "C" int jl_dec_moe(jl_dec* h, jl_moe** moe) {
+    if (!h || !moe) return JL_ERR_INVALID;
+    *moe = h->moe;
+    return JL_OK;
+}
+
+extern "C" int jl_dec_kv(jl_dec* h, float** k, float** v) {
+    if (!h || !k || !v) return JL_ERR_INVALID;
+    *k = h->kc;
+    *v = h->vc;
+    return JL_OK;
+}
+
+extern "C" int jl_dec_embed(jl_dec* h, const int* tokens, int B, float* x, void* stream) {
+    using namespace jl;
+    if (!h || B < 0) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;
+    if (!tokens || !x) return JL_ERR_INVALID;
+    return launch(k_embed, dim3((h->d + 255) / 256, B), dim3(256), 0, (cudaStream_t)stream, (const uint16_t*)h->embed,
+                  tokens, h->V, h->d, x, h->err);
+}
+
+// dbg (device, B = 1 only): per layer 7 rows of max(E, d) floats, as the
+// reference's debug_decode_layers (decode_kernel.c:1764-1790) writes them:
+// norm1 output, attention output, h after attention, norm2 output, router
+// logits, MoE output, h after the MoE layer.
+static int dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B, float* logits,
+                    int* tok, float* dbg, cudaStream_t s);
+
+extern "C" int jl_dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B,
+                           float* logits, int* tok, void* stream) {
+    return dec_step(h, slots, positions, x, B, logits, tok, nullptr, (cudaStream_t)stream);
+}
+
+static int dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B, float* logits,
+                    int* tok, float* dbg, cudaStream_t s) {
+    using namespace jl;
+    if (!h || B < 0) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;
+    if (!slots || !positions || !x) return JL_ERR_INVALID;
+    if (B > h->max_batch) return JL_ERR_CAPACITY;
+    if (dbg && B != 1) return JL_ERR_INVALID;
+    int rc = dec_attrs();
+    if (rc) return rc;
+    const int d = h->d;
+    const size_t rowlen = (size_t)std::max(h->E, d);
+    auto snap = [&](int l, int r, const float* src, int n) -> int {
+        if (!dbg) return JL_OK;
+        const cudaError_t e = cudaMemcpyAsync(dbg + ((size_t)l * 7 + r) * rowlen, src, (size_t)n * 4,
+                                              cudaMemcpyDeviceToDevice, s);
+        return e == cudaSuccess ? JL_OK : jl_note_cuda(e);
+    };
+    JL_CUDA(cudaMemcpyAsync(h->h, x, (size_t)B * d * 4, cudaMemcpyDeviceToDevice, s));
+    const size_t nsm = (size_t)d * sizeof(float);
+    attn_args aa;
+    aa.qkv = h->qkv, aa.att = h->att, aa.positions = positions, aa.slots = slots, aa.kc = h->kc, aa.vc = h->vc;
+    aa.cosb = h->cosb, aa.sinb = h->sinb, aa.L = h->L, aa.H = h->H, aa.KH = h->KH, aa.hd = h->hd, aa.maxT = h->maxT;
+    aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err;
+    aa.sqn = attn_sqn(h->qk_type, h->H, h->KH, h->hd);
+    const size_t asm_ = attn_smem(aa.sqn, h->hd, h->maxT);
+    if (asm_ > 200 * 1024) return JL_ERR_INVALID;
+    for (int l = 0; l < h->L; l++) {
+        // norm1 (adding the previous layer's MoE output to the residual)
+        rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)(l ? h->h2 : nullptr),
+                    (const uint16_t*)(h->norm1 + (size_t)l * d), h->eps, d, h->t);
+        if (!rc && l > 0) rc = snap(l - 1, 6, h->h, d);
+        if (!rc) rc = snap(l, 0, h->t, d);
+        if (!rc)
+            rc = launch_mv<uint16_t>(h->wqkv + (size_t)l * h->nqkv * d, h->t, h->nqkv, d, B,
+                                     h->bias ? h->bqkv + (size_t)l * h->nqkv : nullptr, h->qkv, s);
+        if (!rc) {
+            aa.l = l;
+            const size_t qs = h->qk_type == 2 ? (size_t)h->qn : h->hd, ks = h->qk_type == 2 ? (size_t)h->kn : h->hd;
+            aa.qnw = h->qk_type ? h->qnw + l * qs : nullptr;
+            aa.knw = h->qk_type ? h->knw + l * ks : nullptr;
+            rc = launch(k_attn, dim3(h->H, B), dim3(kAttnThreads), asm_, s, aa);
+        }
+        if (!rc) rc = launch_mv<uint16_t>(h->wo + (size_t)l * d * h->qn, h->att, d, h->qn, B, nullptr, h->h2, s);
+        if (!rc) rc = snap(l, 1, h->h2, d);
+        // norm2 (adding the attention output to the residual), then the MoE layer
+        if (!rc)
+            rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)h->h2,
+                        (const uint16_t*)(h->norm2 + (size_t)l * d), h->eps, d, h->t);
+        if (!rc) rc = snap(l, 2, h->h, d);
+        if (!rc) rc = snap(l, 3, h->t, d);
+        if (!rc) rc = jl_moe_forward(h->moe, l, h->t, B, h->h2, nullptr, nullptr, s);
+        if (!rc) rc = snap(l, 4, h->moe->ws.logits, h->E);
+        if (!rc) rc = snap(l, 5, h->h2, d);
+        if (rc) return rc;
+    }
+    rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)h->h2, (const uint16_t*)h->fnorm,
+                h->eps, d, h->t);
+    if (!rc) rc = snap(h->L - 1, 6, h->h, d);
+    if (rc) return rc;
+    if (logits || tok) {
+        rc = launch_mv<float>(h->lm, h->t, h->V, d, B, nullptr, h->logits, s);
+        if (!rc && tok) rc = launch(k_argmax, dim3(B), dim3(1024), 0, s, (const float*)h->logits, h->V, tok);
+        if (!rc && logits)
+            rc = cudaMemcpyAsync(logits, h->logits, (size_t)B * h->V * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess
+                     ? JL_OK
+                     : JL_ERR_CUDA;
+    }
+    return rc;
+}
+
+extern "C" int jl_dec_check(jl_dec* h, void* stream) {
+    if (!h) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    int err = 0;
+    JL_CUDA(cudaMemcpyAsync(&err, h->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    JL_CUDA(cudaStreamSynchronize(s));
+    if (err) JL_CUDA(cudaMemsetAsync(h->err, 0, sizeof(int), s));
+    const int rc = jl_moe_check(h->moe, stream);
+    if (err & jl::kErrPosition) return JL_ERR_INVALID;
+    if (err) return JL_ERR_DEVICE;
+    return rc;
+}
+
+// ---------------------------------------------------------------------------
+// The reference's own decode entry points (decode_kernel.c:1518-1600), host
+// buffers and KVCache pointers, backed by one cached jl_dec per (cfg, W).
+//
+// KV caches: the reference keeps them in the caller's host arrays
+// (kv[b*L + l].k / .v, each [maxT, KH, hd] fp32). The library keeps a device
+// copy of each sequence (identified by its layer-0 K pointer) and its row
+// count n. A call at position p uses the device copy when p == n; otherwise it
+// first copies the host rows [0, p) of every layer to the device. After the
+// step the new row of every layer is written back to the host arrays, so the
+// caller's caches hold what the reference would have written.
+
+namespace {
+
+struct dec_entry {
+    KernelCfg cfg;
+    const void* key_embed;
+    const void* key_pk;
+    uint64_t fp;  // jl_weights_fingerprint at upload
+    jl_dec* h;
+    cudaStream_t st;
+    int* slots_d;
+    int* pos_d;
+    float* x_d;
+    int* tok_d;
+    float* k_pin;   // pinned staging of one step's new K/V rows [B][L][kn] x 2
+    float* v_pin;
+    std::unordered_map<const float*, int> seq_slot;  // layer-0 K pointer -> slot
+    std::vector<int> slot_rows;                      // rows held per slot
+    std::vector<const float*> slot_key;
+    std::vector<long long> slot_used;                // last call that used the slot (eviction)
+    long long calls;
+};
+
+std::mutex g_dec_mu;
+std::vector<dec_entry*> g_decs;
+thread_local int t_dec_status = JL_OK;
+
+constexpr int kDropinBatch = 32;  // sequences per call and KV slots held (the reference caps a call at 16)
+
+void dec_entry_free(dec_entry* e) {
+    cudaStreamSynchronize(e->st);
+    cudaFree(e->slots_d);
+    cudaFree(e->pos_d);
+    cudaFree(e->x_d);
+    cudaFree(e->tok_d);
+    cudaFreeHost(e->k_pin);
+    cudaFreeHost(e->v_pin);
+    cudaStreamDestroy(e->st);
+    jl_dec_destroy(e->h);
+    delete e;
+}
+
+dec_entry* dec_for(const KernelCfg* c, const KernelW* W, int* rc) {
+    const uint64_t fp = jl_weights_fingerprint(c, W, true);
+    for (size_t i = 0; i < g_decs.size(); i++) {
+        dec_entry* e = g_decs[i];
+        if (e->key_embed != W->embed || e->key_pk != W->expert_pk[0] || memcmp(&e->cfg, c, sizeof(*c))) continue;
+        if (e->fp == fp) return e;
+        dec_entry_free(e);  // same addresses, other weights: drop the stale copy
+        g_decs.erase(g_decs.begin() + i);
+        break;
+    }
+    auto* e = new (std::nothrow) dec_entry();
+    if (!e) {
+        *rc = JL_ERR_OOM;
+        return nullptr;
+    }
+    e->cfg = *c;
+    e->key_embed = W->embed;
+    e->key_pk = W->expert_pk[0];
+    e->fp = fp;
+    e->calls = 0;
+    const int slots = kDropinBatch;
+    *rc = jl_dec_create(c, W, kDropinBatch, slots, 0, &e->h);
+    if (*rc) {
+        delete e;
+        return nullptr;
+    }
+    jl_moe_set_path(e->h->moe, JL_PATH_EXACT);  // the reference's arithmetic: bit-identical layers
+    const size_t rows = (size_t)kDropinBatch * c->L * e->h->kn;
+    if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&e->slots_d, kDropinBatch * 4) != cudaSuccess || cudaMalloc(&e->pos_d, kDropinBatch * 4) != cudaSuccess ||
+        cudaMalloc(&e->x_d, (size_t)kDropinBatch * c->d * 4) != cudaSuccess ||
+        cudaMalloc(&e->tok_d, kDropinBatch * 4) != cudaSuccess ||
+        cudaHostAlloc(&e->k_pin, rows * 4, cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc(&e->v_pin, rows * 4, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        *rc = JL_ERR_OOM;
+        jl_dec_destroy(e->h);
+        delete e;
+        return nullptr;
+    }
+    e->slot_rows.assign(slots, -1);
+    e->slot_key.assign(slots, nullptr);
+    e->slot_used.assign(slots, -1);
+    g_decs.push_back(e);
+    return e;
+}
+
+// One batched step through the drop-in: logits (host, [B, V]) and/or tokens.
+int dropin_step(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* positions, const float* xin,
+                int B, float* logits, int* out_tok, float* dbg_host = nullptr) {
+    if (!c || !W || !kv || !positions || !xin || B < 0) return JL_ERR_INVALID;
+    if (B == 0) return JL_OK;
+    std::lock_guard<std::mutex> lk(g_dec_mu);
+    int rc = JL_OK;
+    dec_entry* e = dec_for(c, W, &rc);
+    if (!e) return rc;
+    jl_dec* h = e->h;
+    if (B > h->max_batch) return JL_ERR_CAPACITY;
+    const int L = c->L, kn = h->kn;
+    const size_t row_b = (size_t)kn * 4, lay_b = (size_t)h->maxT * row_b;
+    e->calls++;
+    std::vector<int> slot(B);
+    for (int b = 0; b < B; b++) {
+        if (positions[b] < 0 || positions[b] >= h->maxT) return JL_ERR_INVALID;
+        const float* key = kv[(size_t)b * L].k;
+        if (!key) return JL_ERR_INVALID;
+        auto it = e->seq_slot.find(key);
+        int sl;
+        if (it != e->seq_slot.end()) {
+            sl = it->second;
+        } else {  // a free slot, else the least recently used one not in this call
+            sl = -1;
+            for (int i = 0; i < h->slots; i++)
+                if (!e->slot_key[i]) {
+                    sl = i;
+                    break;
+                }
+            if (sl < 0) {
+                long long best = LLONG_MAX;
+                for (int i = 0; i < h->slots; i++)
+                    if (e->slot_used[i] < e->calls && e->slot_used[i] < best) {
+                        best = e->slot_used[i];
+                        sl = i;
+                    }
+                if (sl < 0) return JL_ERR_CAPACITY;
+                e->seq_slot.erase(e->slot_key[sl]);
+            }
+            e->seq_slot[key] = sl;
+            e->slot_key[sl] = key;
+            e->slot_rows[sl] = -1;
+        }
+        e->slot_used[sl] = e->calls;
+        slot[b] = sl;
+        const int p = positions[b];
+        if (e->slot_rows[sl] != p) {  // bring the host rows [0, p) of every layer over
+            for (int l = 0; l < L; l++) {
+                const KVCache& cl = kv[(size_t)b * L + l];
+                if (!cl.k || !cl.v) return JL_ERR_INVALID;
+                const size_t off = ((size_t)sl * L + l) * h->maxT * kn;
+                if (p > 0) {
+                    JL_CUDA(cudaMemcpyAsync(h->kc + off, cl.k, (size_t)p * row_b, cudaMemcpyHostToDevice, e->st));
+                    JL_CUDA(cudaMemcpyAsync(h->vc + off, cl.v, (size_t)p * row_b, cudaMemcpyHostToDevice, e->st));
+                }
+            }
+        }
+        e->slot_rows[sl] = p + 1;
+    }
+    (void)lay_b;
+    JL_CUDA(cudaMemcpyAsync(e->slots_d, slot.data(), (size_t)B * 4, cudaMemcpyHostToDevice, e->st));
+    JL_CUDA(cudaMemcpyAsync(e->pos_d, positions, (size_t)B * 4, cudaMemcpyHostToDevice, e->st));
+    JL_CUDA(cudaMemcpyAsync(e->x_d, xin, (size_t)B * c->d * 4, cudaMemcpyHostToDevice, e->st));
+    float* dbg_d = nullptr;
+    const size_t dbg_n = (size_t)L * 7 * std::max(h->E, c->d);
+    if (dbg_host) {
+        if (B != 1) return JL_ERR_INVALID;
+        if (cudaMallocAsync(reinterpret_cast<void**>(&dbg_d), dbg_n * 4, e->st) != cudaSuccess) return JL_ERR_OOM;
+        JL_CUDA(cudaMemsetAsync(dbg_d, 0, dbg_n * 4, e->st));
+    }
+    rc = dec_step(h, e->slots_d, e->pos_d, e->x_d, B, nullptr, out_tok ? e->tok_d : nullptr, dbg_d, e->st);
+    if (dbg_d) {
+        if (!rc && cudaMemcpyAsync(dbg_host, dbg_d, dbg_n * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+            rc = JL_ERR_CUDA;
+        cudaFreeAsync(dbg_d, e->st);
+    }
+    if (!rc && logits)
+        rc = launch_mv<float>(h->lm, h->t, h->V, c->d, B, nullptr, h->logits, e->st);
+    if (rc) return rc;
+    // the new K/V row of every layer back into the caller's caches
+    for (int b = 0; b < B; b++)
+        for (int l = 0; l < L; l++) {
+            const size_t off = (((size_t)slot[b] * L + l) * h->maxT + positions[b]) * kn;
+            JL_CUDA(cudaMemcpyAsync(e->k_pin + ((size_t)b * L + l) * kn, h->kc + off, row_b, cudaMemcpyDeviceToHost, e->st));
+            JL_CUDA(cudaMemcpyAsync(e->v_pin + ((size_t)b * L + l) * kn, h->vc + off, row_b, cudaMemcpyDeviceToHost, e->st));
+        }
+    if (logits) JL_CUDA(cudaMemcpyAsync(logits, h->logits, (size_t)B * h->V * 4, cudaMemcpyDeviceToHost, e->st));
+    if (out_tok) JL_CUDA(cudaMemcpyAsync(out_tok, e->tok_d, (size_t)B * 4, cudaMemcpyDeviceToHost, e->st));
+    JL_CUDA(cudaStreamSynchronize(e->st));
+    rc = jl_dec_check(h, e->st);
+    if (rc) {
+        for (int b = 0; b < B; b++) e->slot_rows[slot[b]] = -1;  // resync these sequences next time
+        return rc;
+    }
+    for (int b = 0; b < B; b++)
+        for (int l = 0; l < L; l++) {
+            const KVCache& cl = kv[(size_t)b * L + l];
+            memcpy(cl.k + (size_t)positions[b] * kn, e->k_pin + ((size_t)b * L + l) * kn, row_b);
+            memcpy(cl.v + (size_t)positions[b] * kn, e->v_pin + ((size_t)b * L + l) * kn, row_b);
+        }
+    return JL_OK;
+}
+
+void nan_fill(float* p, size_t n) {
+    if (!p) return;
+    const float q = __builtin_nanf("");
+    for (size_t i = 0; i < n; i++) p[i] = q;
+}
+
+}  // namespace
+
+extern "C" void decode_layers_batch(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* positions,
+                                    const float* xin, int B, float* logits) {
+    t_dec_status = dropin_step(c, W, kv, positions, xin, B, logits, nullptr);
+    if (t_dec_status && c && B > 0) nan_fill(logits, (size_t)B * c->V);
+}
+
+extern "C" void decode_layers_batch_argmax(const KernelCfg* c, const KernelW* W, KVCache* kv,
+                                           const int* positions, const float* xin, int B, int* out_tok) {
+    t_dec_status = dropin_step(c, W, kv, positions, xin, B, nullptr, out_tok);
+    if (t_dec_status && out_tok)
+        for (int b = 0; b < B; b++) out_tok[b] = -1;
+}
+
+extern "C" void decode_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, int pos, const float* xin,
+                              float* logits) {
+    const int p[1] = {pos};
+    decode_layers_batch(c, W, kv, p, xin, 1, logits);
+}
+
+extern "C" void embed_lookup(const KernelW* W, const KernelCfg* c, int token, float* out) {
+    t_dec_status = JL_ERR_INVALID;
+    if (!W || !c || !out || !W->embed) return;
+    if (token < 0 || token >= c->V) {
+        nan_fill(out, (size_t)c->d);
+        return;
+    }
+    std::lock_guard<std::mutex> lk(g_dec_mu);
+    int rc = JL_OK;
+    dec_entry* e = dec_for(c, W, &rc);
+    if (e) {
+        if (cudaMemcpyAsync(e->tok_d, &token, 4, cudaMemcpyHostToDevice, e->st) != cudaSuccess) rc = JL_ERR_CUDA;
+        if (!rc) rc = jl_dec_embed(e->h, e->tok_d, 1, e->x_d, e->st);
+        if (!rc && cudaMemcpyAsync(out, e->x_d, (size_t)c->d * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+            rc = JL_ERR_CUDA;
+        if (!rc && cudaStreamSynchronize(e->st) != cudaSuccess) rc = JL_ERR_CUDA;
+    }
+    t_dec_status = rc;
+    if (rc) nan_fill(out, (size_t)c->d);
+}
+
+extern "C" void prefill_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* tokens, int T,
+                               float* logits) {
+    // decode_kernel.c:1606-1615: one B = 1 step per position, logits at the last
+    t_dec_status = JL_OK;
+    if (!c || !W || !tokens || T < 0) {
+        t_dec_status = JL_ERR_INVALID;
+        return;
+    }
+    std::vector<float> x((size_t)c->d);
+    for (int t = 0; t < T && t_dec_status == JL_OK; t++) {
+        embed_lookup(W, c, tokens[t], x.data());
+        if (t_dec_status) break;
+        const int p[1] = {t};
+        t_dec_status = dropin_step(c, W, kv, p, x.data(), 1, t == T - 1 ? logits : nullptr, nullptr);
+    }
+    if (t_dec_status && logits) nan_fill(logits, (size_t)c->V);
+}
+
+extern "C" void debug_decode_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, int pos, const float* xin,
+                                    float* out) {
+    const int p[1] = {pos};
+    t_dec_status = dropin_step(c, W, kv, p, xin, 1, nullptr, nullptr, out);
+    if (t_dec_status && c && out) nan_fill(out, (size_t)c->L * 7 * std::max(c->E, c->d));
+}
+
+// The reference's CPU thread-pool controls, which its Python calls at start-up
+// (decoder3.py:133-145): the GPU library has no host pool, so they only
+// report success.
+extern "C" int spin_pool_init(int n_workers) {
+    (void)n_workers;
+    return 1;
+}
+extern "C" void set_lm_threads(int n) { (void)n; }
+
+extern "C" int jl_decode_status(void) { return t_dec_status; }

@@ -59,6 +59,11 @@ struct jl_ws {
     __half* xc;        // token tiles: per tile [d/8][2N rows: hi, lo][8] fp16 (UMMA core layout)
     __half* ac;        // SwiGLU activations of the tiles, same layout over m
     size_t xc_plane, ac_plane;  // halves per plane
+    // small-batch GEMV path (jl_gemv.cu): per-M-tile partial sums and arrival counters
+    float* gv_parts;     // gate/up pieces [U x m/64 tiles][64][4 x 4 x 32]
+    float* gv_parts_dn;  // down pieces [U x d/128 tiles][64][4 x 4 x 32]
+    int* gv_count;       // [U x m/64] gate/up arrivals (0 between launches)
+    int* gv_count_dn;    // [U x d/128] down arrivals
 };
 
 // Trace buffer layout: per kernel kind a row of 16 slots of %globaltimer
@@ -104,6 +109,14 @@ enum {
 };
 int jl_device_once(int key, int (*setup)());
 
+// Fingerprint of the host weights a (cfg, W) pair points at: leading bytes of
+// the router rows and of the first and last expert records, the expert
+// pointer tables' first and last entries, and with `dense` the embedding, the
+// first q projection and the lm_head. The host-buffer drop-ins cache a device
+// copy per (cfg, W) and compare it on every call, so a model loaded into
+// reused addresses is not mistaken for the cached one.
+uint64_t jl_weights_fingerprint(const KernelCfg* c, const KernelW* W, bool dense);
+
 // jl_store.cu
 int jl_launch_repack_part(const uint8_t* pk_ref, const uint16_t* sc_ref, int p, const jl_layout& L,
                           uint8_t* rec, cudaStream_t s);
@@ -137,6 +150,12 @@ int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float*
                            cudaStream_t s);
 int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
 int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s);
+
+// jl_gemv.cu: small-batch (B <= 4) expert FFN, stream-K GEMVs over all warps.
+size_t jl_gemv_ws_floats(int E, int k, int d, int m, size_t* dn_off, size_t* count_off);
+bool jl_gemv_ok(const jl_moe* h, int B);
+int jl_launch_gateup_gemv(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s);
+int jl_launch_down_gemv(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
 
 // jl_tc.cu: tensor-core expert FFN (permute -> gate/up+SwiGLU -> down).
 // The tile table is built at the end of the dispatch step (jl_tiles.cuh).

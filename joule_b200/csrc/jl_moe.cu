@@ -13,10 +13,12 @@ namespace {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// JL_PATH_AUTO: CUDA-core exact path up to this batch, tensor cores above.
-// Measured on B200 at the Qwen3 shape (us per layer, exact / tensor-core):
-// B = 1: 26.8 / 34.1, 2: 45.9 / 48.4, 4: 66.1 / 62.5, 8: 101 / 86.
+// JL_PATH_AUTO: the GEMV path up to kGemvMaxB tokens, tensor cores above
+// (exact where the tensor-core shape rules fail). Measured on B200 at the
+// Qwen3 shape (us per layer, exact / tensor-core): B = 1: 26.8 / 34.1,
+// 2: 45.9 / 48.4, 4: 66.1 / 62.5, 8: 101 / 86.
 constexpr int kExactMaxB = 3;
+constexpr int kGemvMaxB = 4;
 
 int check_shape(const KernelCfg* c) {
     if (!c) return JL_ERR_INVALID;
@@ -30,16 +32,19 @@ int check_shape(const KernelCfg* c) {
 }
 
 struct ws_plan {
-    size_t off[16];
+    size_t off[17];
     size_t total;
     size_t xc_plane, ac_plane;
+    size_t gv_dn, gv_cnt;  // float offsets of the GEMV path's down pieces and counters
 };
 
 ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
     const size_t S = (size_t)Bmax * k;
     size_t xc_plane = 0, ac_plane = 0;
     const size_t tc_bytes = jl_tc_ws_bytes(Bmax, E, k, d, m, &xc_plane, &ac_plane);
-    const size_t sizes[16] = {
+    size_t gv_dn = 0, gv_cnt = 0;
+    const size_t gv_floats = jl_gemv_ws_floats(E, k, d, m, &gv_dn, &gv_cnt);
+    const size_t sizes[17] = {
         (size_t)Bmax * E * 4,  // logits
         S * 4,                 // top
         S * 4,                 // tw
@@ -56,12 +61,15 @@ ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
         16,                    // err
         16,                    // (unused)
         tc_bytes,              // tensor-core path: xc, ac, tile table, tile count
+        gv_floats * 4,         // GEMV path: pieces and counters
     };
     ws_plan p;
     p.xc_plane = xc_plane;
     p.ac_plane = ac_plane;
     size_t o = 0;
-    for (int i = 0; i < 16; i++) {
+    p.gv_dn = gv_dn;
+    p.gv_cnt = gv_cnt;
+    for (int i = 0; i < 17; i++) {
         p.off[i] = o;
         o = align_up(o + sizes[i], 256);
     }
@@ -101,6 +109,34 @@ int jl_device_once(int key, int (*setup)()) {
     if (rc) return rc;
     g_once[dev].fetch_or(bit, std::memory_order_release);
     return JL_OK;
+}
+
+uint64_t jl_weights_fingerprint(const KernelCfg* c, const KernelW* W, bool dense) {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](const void* p, size_t n) {
+        const unsigned char* b = static_cast<const unsigned char*>(p);
+        for (size_t i = 0; i < n; i++) h = (h ^ b[i]) * 1099511628211ull;
+    };
+    auto mixp = [&](const void* p) { mix(&p, sizeof(p)); };
+    const size_t LE = (size_t)c->L * c->E;
+    const size_t rec = (size_t)c->intermediate * c->d / 2;
+    if (W->gate_w) mix(W->gate_w, std::min<size_t>(256, (size_t)c->E * c->d * 2));
+    for (int p = 0; p < 3; p++) {
+        if (!W->expert_pk[p] || !W->expert_sc[p] || LE == 0) continue;
+        const unsigned char* first = W->expert_pk[p][0];
+        const unsigned char* last = W->expert_pk[p][LE - 1];
+        mixp(first);
+        mixp(last);
+        mixp(W->expert_sc[p][0]);
+        if (first) mix(first, std::min<size_t>(256, rec));
+        if (last) mix(last, std::min<size_t>(256, rec));
+    }
+    if (dense) {
+        if (W->embed) mix(W->embed, std::min<size_t>(256, (size_t)c->V * c->d * 2));
+        if (W->wq) mix(W->wq, std::min<size_t>(256, (size_t)c->d * 2));
+        if (W->lm_head) mix(W->lm_head, std::min<size_t>(256, (size_t)c->V * c->d * 4));
+    }
+    return h;
 }
 
 extern "C" const char* jl_last_cuda_error(void) {
@@ -182,6 +218,14 @@ extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags,
         h->ws.tc_ntiles = (int*)t;
         h->ws.tc_tile = (int*)(t + 16);
     }
+    {
+        float* g = (float*)(b + wp.off[16]);
+        h->ws.gv_parts = g;
+        h->ws.gv_parts_dn = g + wp.gv_dn;
+        h->ws.gv_count = (int*)(g + wp.gv_cnt);
+        const int Ug = std::min(h->E, 4 * h->k);
+        h->ws.gv_count_dn = h->ws.gv_count + (size_t)Ug * (h->m / 64);
+    }
     // The tensor-core token tiles start as fp16 NaN: the permute and the gate/up
     // epilogue write only a tile's real rows, and the pad rows may feed only
     // accumulator columns that the epilogues drop, so a pad that ever reached a
@@ -210,7 +254,7 @@ extern "C" int jl_moe_destroy(jl_moe* h) {
 }
 
 extern "C" int jl_moe_set_path(jl_moe* h, int path) {
-    if (!h || path < JL_PATH_AUTO || path > JL_PATH_TC) return JL_ERR_INVALID;
+    if (!h || path < JL_PATH_AUTO || path > JL_PATH_GEMV) return JL_ERR_INVALID;
     h->path = path;
     return JL_OK;
 }
@@ -340,10 +384,15 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
     };
     int rc = mark(0);
     const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
-    const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
+    const bool gemv = (h->path == JL_PATH_GEMV || (h->path == JL_PATH_AUTO && B <= kGemvMaxB)) && jl_gemv_ok(h, B);
+    const bool tc = !gemv && (h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok));
     if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, tc, s);
     if (!rc) rc = mark(1);
-    if (tc) {
+    if (gemv) {
+        if (!rc && (mask & 2)) rc = jl_launch_gateup_gemv(h, store_l, x, B, s);
+        if (!rc) rc = mark(2);
+        if (!rc && (mask & 4)) rc = jl_launch_down_gemv(h, store_l, B, s);
+    } else if (tc) {
         if (!rc && (mask & 2)) rc = jl_launch_gateup_tc(h, store_l, x, B, s);
         if (!rc) rc = mark(2);
         if (!rc && (mask & 4)) rc = jl_launch_down_tc(h, store_l, B, s);
@@ -415,7 +464,7 @@ extern "C" int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, co
     JL_CUDA(cudaMemcpyAsync(h->ws.top, top, S * 4, cudaMemcpyDeviceToDevice, s));
     JL_CUDA(cudaMemcpyAsync(h->ws.tw, tw, S * 4, cudaMemcpyDeviceToDevice, s));
     const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
-    const bool tc = h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok);
+    const bool tc = h->path == JL_PATH_TC || ((h->path == JL_PATH_AUTO || h->path == JL_PATH_GEMV) && B > kExactMaxB && tc_ok);
     int rc = jl_launch_dispatch(h, B, s);
     if (!rc) rc = tc ? jl_launch_gateup_tc(h, store_l, x, B, s) : jl_launch_gateup_exact(h, store_l, x, B, s);
     if (!rc) rc = tc ? jl_launch_down_tc(h, store_l, B, s) : jl_launch_down_exact(h, store_l, B, s);
@@ -451,7 +500,12 @@ extern "C" int jl_moe_check(jl_moe* h, void* stream) {
     int err = 0;
     JL_CUDA(cudaMemcpyAsync(&err, h->ws.err, sizeof(int), cudaMemcpyDeviceToHost, s));
     JL_CUDA(cudaStreamSynchronize(s));
-    if (err) JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
+    if (err) {
+        JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
+        // a launch that failed part-way may have left GEMV arrival counters behind
+        const int Ug = std::min(h->E, 4 * h->k);
+        JL_CUDA(cudaMemsetAsync(h->ws.gv_count, 0, (size_t)Ug * (h->m / 64 + h->d / 128) * sizeof(int), s));
+    }
     JL_CUDA(cudaStreamSynchronize(s));
     if (err & jl::kErrTimeout) return JL_ERR_TIMEOUT;
     if (err) return JL_ERR_DEVICE;
@@ -466,6 +520,7 @@ struct dropin {
     KernelCfg cfg;
     const void* key_gate;
     const void* key_pk;
+    uint64_t fp;        // jl_weights_fingerprint at upload
     jl_moe* h;
     float* xd;
     float* od;
@@ -487,14 +542,32 @@ extern "C" int jl_layer_ffn_batch(const KernelCfg* c, const KernelW* W, int l, c
     if (!W->gate_w || !W->expert_pk[0] || !W->expert_sc[0]) return JL_ERR_INVALID;
     std::lock_guard<std::mutex> lk(g_dropin_mu);
     dropin* ent = nullptr;
-    for (auto& e : g_dropins)
-        if (e.key_gate == W->gate_w && e.key_pk == W->expert_pk[0] && !memcmp(&e.cfg, c, sizeof(*c)))
+    const uint64_t fp = jl_weights_fingerprint(c, W, false);
+    for (size_t i = 0; i < g_dropins.size(); i++) {
+        dropin& e = g_dropins[i];
+        if (e.key_gate != W->gate_w || e.key_pk != W->expert_pk[0] || memcmp(&e.cfg, c, sizeof(*c))) continue;
+        if (e.fp == fp) {
             ent = &e;
+            break;
+        }
+        // same addresses, other weights: drop the stale copy
+        cudaStreamSynchronize(e.st);
+        cudaFree(e.xd);
+        cudaFree(e.od);
+        cudaFreeHost(e.xh);
+        cudaFreeHost(e.oh);
+        cudaFreeHost(e.errh);
+        cudaStreamDestroy(e.st);
+        jl_moe_destroy(e.h);
+        g_dropins.erase(g_dropins.begin() + i);
+        break;
+    }
     if (!ent) {
         dropin e{};
         e.cfg = *c;
         e.key_gate = W->gate_w;
         e.key_pk = W->expert_pk[0];
+        e.fp = fp;
         e.cap = std::max(B, 64);
         int rc = jl_moe_create(c, e.cap, &e.h);
         if (rc) return rc;

@@ -19,11 +19,11 @@ from typing import Sequence
 import numpy as np
 import torch
 
-from joule_b200.native import (CREATE_ROUTER_ONLY, PATH_AUTO, PATH_EXACT, PATH_TC, KernelCfg,
+from joule_b200.native import (CREATE_ROUTER_ONLY, PATH_AUTO, PATH_EXACT, PATH_GEMV, PATH_TC, KernelCfg,
                                KernelW, check, get_dll)
 
 __all__ = ["MoELayers", "KernelCfg", "KernelW", "layer_ffn_batch", "PATH_AUTO", "PATH_EXACT",
-           "PATH_TC", "CREATE_ROUTER_ONLY", "make_cfg"]
+           "PATH_TC", "PATH_GEMV", "CREATE_ROUTER_ONLY", "make_cfg"]
 
 
 def make_cfg(L: int, d: int, E: int, topk: int, intermediate: int, norm_topk_prob: int,

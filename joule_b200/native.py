@@ -23,7 +23,7 @@ ERRORS = {
     -6: "JL_ERR_NOT_READY: layer not uploaded",
     -7: "JL_ERR_DEVICE: kernel reported a bad index/state",
 }
-PATH_AUTO, PATH_EXACT, PATH_TC = 0, 1, 2
+PATH_AUTO, PATH_EXACT, PATH_TC, PATH_GEMV = 0, 1, 2, 3
 CREATE_ROUTER_ONLY = 1
 
 
@@ -104,6 +104,23 @@ SIGNATURES = {
     "q4_gemv_f32": ([_P, _P, _P, _P, _I, _I, _I], None),
     "q4_gemm_f32": ([_P, _P, _I, _P, _P, _I, _I, _I], None),
     "jl_compat_status": ([], _I),
+    "jl_dec_create": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _I, _I, _I, ctypes.POINTER(_P)], _I),
+    "jl_dec_destroy": ([_P], _I),
+    "jl_dec_moe": ([_P, ctypes.POINTER(_P)], _I),
+    "jl_dec_kv": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I),
+    "jl_dec_embed": ([_P, _P, _I, _P, _P], _I),
+    "jl_dec_step": ([_P, _P, _P, _P, _I, _P, _P, _P], _I),
+    "jl_dec_check": ([_P, _P], _I),
+    "decode_layers_batch": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _P, _P, _I, _P], None),
+    "decode_layers_batch_argmax": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _P, _P, _I, _P],
+                                   None),
+    "decode_layers": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _I, _P, _P], None),
+    "embed_lookup": ([ctypes.POINTER(KernelW), ctypes.POINTER(KernelCfg), _I, _P], None),
+    "prefill_layers": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _P, _I, _P], None),
+    "debug_decode_layers": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _I, _P, _P], None),
+    "spin_pool_init": ([_I], _I),
+    "set_lm_threads": ([_I], None),
+    "jl_decode_status": ([], _I),
     "jl_version": ([], ctypes.c_char_p),
     "jl_last_cuda_error": ([], ctypes.c_char_p),
 }

@@ -88,3 +88,23 @@ def test_empty_batch_is_a_no_op(dll):
     assert dll.jl_layer_ffn_batch(ctypes.byref(c), ctypes.byref(w), 2, None, 0, None) == -1  # l out of range
     assert dll.jl_route_noalloc(None, None, 0, 128, 2048, 8, 1, None, None, None, None) == 0
     assert dll.jl_route_noalloc(None, None, -1, 128, 2048, 8, 1, None, None, None, None) == -1
+
+
+def test_decode_exports_validate_before_any_device_work(dll):
+    """The reference-signature decode entries return void: a bad call fills
+    its outputs (NaN logits, -1 tokens) and reports through jl_decode_status;
+    the host thread-pool controls succeed (the library has no host pool)."""
+    import numpy as np
+    assert dll.spin_pool_init(8) == 1
+    dll.set_lm_threads(8)
+    logits = np.zeros(4, np.float32)
+    dll.decode_layers_batch(None, None, None, None, None, 1, logits.ctypes.data)
+    assert dll.jl_decode_status() == -1
+    tok = np.zeros(2, np.int32)
+    dll.decode_layers_batch_argmax(None, None, None, None, None, 2, tok.ctypes.data)
+    assert dll.jl_decode_status() == -1 and (tok == -1).all()
+    h = ctypes.c_void_p()
+    bad = native.KernelCfg(L=1, d=2048, n_heads=3, n_kv=2, hd=128, E=8, topk=2, V=100, maxT=16,
+                           intermediate=768)  # heads not a multiple of kv heads
+    assert dll.jl_dec_create(ctypes.byref(bad), ctypes.byref(native.KernelW()), 4, 4, 0,
+                             ctypes.byref(h)) == -1
