@@ -206,7 +206,7 @@ def capture_step(moe, xs, outs, B, mask, stream, layers):
     return g
 
 
-def replay_ms(g, reps, warmup, stream, ws=1, preroll_s=0.0):
+def replay_ms(g, reps, warmup, stream, ws=1, preroll_s=0.0, reset=None):
     """Mean ms per replay of graph g: warm-up replays (at least `preroll_s`
     seconds of them, so that a clock sampler running over the warm-up and
     the timed region sees the GPU under this load), then `reps` replays back
@@ -218,9 +218,16 @@ def replay_ms(g, reps, warmup, stream, ws=1, preroll_s=0.0):
     stream.synchronize()
     t_start = time.perf_counter()
     while time.perf_counter() - t_start < preroll_s:
+        if reset is not None:  # a graph with state that must not run past its buffers
+            with torch.cuda.stream(stream):
+                reset()
         with torch.cuda.stream(stream):
             for _ in range(4):
                 g.replay()
+        stream.synchronize()
+    if reset is not None:
+        with torch.cuda.stream(stream):
+            reset()
         stream.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
@@ -303,19 +310,19 @@ def e2e_dropin(host, B, steps, warmup, seed=11):
                 host_layers=nl), keep
 
 
-def cpu_baseline_ref(host_layer, B, budget_s=12.0):
-    """The reference's layer_ffn_batch (oracle/_ref) on this host's cores, one
-    layer (bounded sample), extrapolated to the 48-layer step."""
+def cpu_moe_sample(B, budget_s=12.0):
+    """The reference's layer_ffn_batch (oracle/_ref) on this host's cores: one
+    seeded Qwen3-shape layer (bounded sample), extrapolated to the 48-layer
+    step. Runs in a process of its own (run_isolated): the reference's thread
+    pool cannot be started twice in one process."""
+    from oracle import layer as olayer
     from oracle import ref
-    from oracle.layer import Q4Layer
     if not ref.available():
         return None
-    gwh, pk, sc = host_layer
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
-    lay = Q4Layer(d, E, k, m, SHAPE["norm"], gwh, sc, pk)
+    lay = olayer.make_layer(d, E, k, m, SHAPE["norm"], seed_router=10, seed_experts=20)
     R = ref.RefLayer(lay)
-    ncores = os.cpu_count() or 1
-    nthreads = max(1, min(16, ncores - 1))
+    nthreads = ref_threads()
     R.L.spin_pool_init(nthreads)
     x = np.random.default_rng(5).standard_normal((B, d)).astype(np.float32)
     R.ffn(x)
@@ -324,15 +331,102 @@ def cpu_baseline_ref(host_layer, B, budget_s=12.0):
         R.ffn(x)
         reps += 1
     t_layer = (time.perf_counter() - t0) / reps
-    R.L.spin_pool_shutdown()
     cores = 1 if B == 1 else nthreads + 1
     return dict(value=B / (t_layer * L), unit="tok/s", cores=cores, kind="reference",
-                sample=f"1 Qwen3-shape layer x {reps} calls at B={B} (16-token chunks), "
-                       f"{t_layer * 1e3:.2f} ms/layer, x48 layers",
+                sample=f"1 Qwen3-shape MoE layer x {reps} calls of the reference's layer_ffn_batch at B={B} "
+                       f"(16-token chunks), {t_layer * 1e3:.2f} ms/layer, x48 layers",
                 threads_note="B=1 runs on one thread by the reference's design "
                              "(decode_kernel.c:1495-1497)" if B == 1 else
                              f"spin_pool_init({nthreads}) + main thread",
                 cpu=cpu_model())
+
+
+def cpu_decode_sample(B, budget_s=20.0, ctx=512, layers=2):
+    """The reference's decode_layers_batch (oracle/_ref) on this host's cores:
+    the Qwen3-30B-A3B shape with `layers` layers (seeded random weights, fp32
+    lm_head of the full vocabulary), every sequence at position ctx over KV
+    caches holding ctx rows (seeded random values, in place of a prefill of the
+    reference's own, which would take minutes), B > 16 as 16-sequence calls
+    (its BMAX). Timed with and without the lm_head (logits NULL), extrapolated
+    to 48 layers + one lm_head per step. Runs in a process of its own."""
+    import ctypes
+    from oracle import decode as dec
+    from oracle import ref
+    if not ref.available():
+        return None
+    shape = dec.DecodeShape("qwen3_bench", layers, 2048, 32, 4, 128, 128, 8, 768, 151936, ctx + 8, 1, 0, 1,
+                            1e-6, 1e6)
+    model = dec.make_model(shape, 3)
+    nthreads = ref_threads()
+    r = dec.RefDecoder(model, threads=nthreads)
+    caches = dec._Caches(shape, B)
+    rng = np.random.default_rng(0)
+    for arr in caches.k + caches.v:
+        arr[:ctx] = rng.standard_normal((ctx, arr.shape[1]), dtype=np.float32)
+    x = dec.embed(model, rng.integers(0, shape.V, B))
+    logits = np.empty((16, shape.V), np.float32)
+    P = ctypes.c_void_p
+
+    def step(with_logits):
+        for b0 in range(0, B, ref.BMAX):
+            nb = min(ref.BMAX, B - b0)
+            kv = (P * (2 * nb * layers))()
+            for i in range(nb * layers):
+                kv[2 * i] = caches.k[b0 * layers + i].ctypes.data
+                kv[2 * i + 1] = caches.v[b0 * layers + i].ctypes.data
+            pos = np.full(nb, ctx, np.int32)
+            xs = np.ascontiguousarray(x[b0:b0 + nb])
+            r.lib.decode_layers_batch(ctypes.byref(r.cfg), ctypes.byref(r.W), kv, pos.ctypes.data,
+                                      xs.ctypes.data, nb, logits.ctypes.data if with_logits else None)
+
+    def timed(with_logits):
+        step(with_logits)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s / 2 and reps < 100:
+            step(with_logits)
+            reps += 1
+        return (time.perf_counter() - t0) / reps, reps
+
+    t_nolm, n1 = timed(False)
+    t_lm, n2 = timed(True)
+    t_layer = t_nolm / layers
+    t_head = max(0.0, t_lm - t_nolm)
+    t_step = SHAPE["L"] * t_layer + t_head
+    return dict(value=B / t_step, unit="tok/s", cores=nthreads + 1, kind="reference",
+                sample=f"the reference's decode_layers_batch, Qwen3 shape with {layers} layers, B={B} at "
+                       f"position {ctx} (16-sequence calls): {t_layer * 1e3:.1f} ms per layer ({n1} steps), "
+                       f"lm_head {t_head * 1e3:.1f} ms ({n2} steps); step = 48 layers + lm_head "
+                       f"= {t_step * 1e3:.0f} ms",
+                threads_note=f"spin_pool_init({nthreads}) + main thread", cpu=cpu_model())
+
+
+def ref_threads() -> int:
+    return max(1, min(16, (os.cpu_count() or 1) - 1))
+
+
+def _isolated_child(fn_name, kwargs, q):
+    sys.path.insert(0, str(ROOT))
+    try:
+        q.put(("ok", globals()[fn_name](**kwargs)))
+    except Exception as e:  # reported, not raised: the baseline is optional
+        q.put(("error", f"{type(e).__name__}: {e}"))
+
+
+def run_isolated(fn_name, timeout_s=600, **kwargs):
+    """Run one of this module's CPU-baseline functions in a spawned process."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_isolated_child, args=(fn_name, kwargs, q))
+    p.start()
+    try:
+        status, res = q.get(timeout=timeout_s)
+    except Exception:
+        status, res = "error", "timed out"
+    p.join(timeout=30)
+    if p.is_alive():
+        p.kill()
+    return res if status == "ok" else {"unavailable": res}
 
 
 def cpu_model():
@@ -621,7 +715,7 @@ def full_decode(a, hbm):
     Bs = sorted(set(int(b) for b in a.decode_sweep.split(",")))
     Bmax, ctx = max(Bs), a.ctx
     steps, warm = a.steps, a.warmup
-    cfg = qwen3_cfg(maxT=ctx + warm + steps + 16)
+    cfg = qwen3_cfg(maxT=ctx + warm + steps + 64)
     t0 = time.time()
     dec = Decoder.random(cfg, Bmax, Bmax)
     build_s = time.time() - t0
@@ -641,8 +735,9 @@ def full_decode(a, hbm):
     dec.check()
     prefill_s = time.time() - t0
     res = {}
+    clocks = None
     stream = torch.cuda.Stream()
-    for B in Bs:
+    for B in [b for b in Bs if b != a.batch] + ([a.batch] if a.batch in Bs else []):
         pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
         tok = tok0[:B].clone()
         xb = torch.empty(B, d, device=dev)
@@ -658,7 +753,12 @@ def full_decode(a, hbm):
                 dec.embed(tok, xb, stream=stream)
                 dec.step(sl, pos, xb, tok=tok, stream=stream)
                 pos.add_(1)
-        ms = replay_ms(g, steps, warm, stream)
+        if B == a.batch:  # the headline: clocks sampled over >= 1 s of replays, then the timed region
+            with Clocks(torch.cuda.current_device()) as clk:
+                ms = replay_ms(g, steps, warm, stream, preroll_s=1.0, reset=lambda: pos.fill_(ctx))
+            clocks = clk.summary()
+        else:
+            ms = replay_ms(g, steps, warm, stream)
         dec.check(stream)
         # end to end: token ids host -> device -> host each step
         tok_h = torch.empty(B, dtype=torch.int32).pin_memory()
@@ -683,7 +783,7 @@ def full_decode(a, hbm):
                                         "CUDA graph, token ids host->device and back every step"))
     dec.close()
     torch.cuda.synchronize()
-    return dict(config="BASELINE config 3: Qwen3-30B-A3B architecture, random-init (bf16 dense N(0,0.02), "
+    return dict(clocks=clocks, config="BASELINE config 3: Qwen3-30B-A3B architecture, random-init (bf16 dense N(0,0.02), "
                        "fp32 lm_head, Q4 experts), 48 layers, GQA 32/4 x 128, per-head QK-norm, RoPE theta "
                        "1e6, eps 1e-6, vocab 151936; context 512 uniform-random ids (seed 0) then greedy decode",
                 context=ctx, build_s=round(build_s, 1), prefill_s=round(prefill_s, 1),
@@ -783,8 +883,8 @@ def run_ours(a):
     if a.cpu:
         cb = {}
         for B in sorted({1, a.batch}):
-            c = cpu_baseline_ref(host[0], B)
-            if c is not None:
+            c = run_isolated("cpu_moe_sample", B=B)
+            if c is not None and "value" in c:
                 cb[str(B)] = c
                 if str(B) in per_b:
                     per_b[str(B)]["cpu_tok_s"] = c["value"]
@@ -797,8 +897,58 @@ def run_ours(a):
         moe.close()
         del xs, outs
         torch.cuda.empty_cache()
-        line["full_decode"] = full_decode(a, hbm)
+        fd = full_decode(a, hbm)
+        if str(a.batch) in fd["per_batch"]:
+            line = decode_headline(a, line, fd)
     print(json.dumps(line), flush=True)
+
+
+METRIC_DECODE = ("Qwen3-30B-A3B-shape Q4 decode tok/s (full model: 48 layers of attention + Q4 MoE, "
+                 "lm_head, greedy argmax)")
+
+
+def decode_headline(a, line, fd):
+    """The full-model decode step is the headline (BASELINE metric: decode
+    tok/s); the MoE-layer measurements move under `moe_layer`, and the roofline
+    stays on the dominant kernel (the MoE gate/up kernel)."""
+    moe_keys = ("metric", "value", "ms_per_step", "dtype", "config", "per_batch", "e2e", "cpu_baseline",
+                "cpu_baseline_per_batch", "clocks", "gpu_launches")
+    moe = {k: line.pop(k) for k in moe_keys if k in line}
+    head = fd["per_batch"][str(a.batch)]
+    L = SHAPE["L"]
+    moe_launches = launches_per_step(a.batch) // L
+    out = dict(metric=METRIC_DECODE, value=head["tok_s"], unit="tok/s", n_gpus=1, steps=a.steps,
+               warmup=a.warmup, ms_per_step=head["ms_per_step"], higher_is_better=True, scaling="weak",
+               vs_baseline=None,
+               dtype=("f32 (attention, norms, projections, lm_head in the reference's fp32 order); MoE: "
+                      + (DTYPE_EXACT if path_of(a.batch) == "exact" else DTYPE_TC)),
+               data="synthetic: seeded random-init weights (bf16 dense N(0,0.02), fp32 lm_head, Q4 experts "
+                    "quantised from N(0,0.02)), 512-token contexts of uniform-random ids",
+               config=dict(workload=f"Qwen3-30B-A3B decode step, batch B={a.batch} at context {a.ctx}",
+                           model="Qwen3-30B-A3B architecture, random init (BASELINE config 3)",
+                           batch=a.batch, context=a.ctx, layers=L,
+                           l2="not flushed: each step streams the 3.7 GB of dense weights and the active "
+                              "experts of 48 layers vs 126 MB L2",
+                           parallelism="single GPU"),
+               e2e=head["e2e"], clocks=fd.get("clocks"),
+               gpu_launches=(L * (5 + moe_launches) + 4) * a.steps,
+               full_decode=fd)
+    for k in ("roofline", "microbench"):
+        if k in line:
+            out[k] = line.pop(k)
+    moe.update(line)
+    out["moe_layer"] = moe
+    if a.cpu:
+        cb = {}
+        for B in sorted({1, a.batch}):
+            c = run_isolated("cpu_decode_sample", timeout_s=900, B=B, ctx=a.ctx)
+            if c is not None and "value" in c:
+                cb[str(B)] = c
+                if str(B) in fd["per_batch"]:
+                    fd["per_batch"][str(B)]["cpu_tok_s"] = c["value"]
+        out["cpu_baseline"] = cb.get(str(a.batch))
+        out["cpu_baseline_per_batch"] = cb
+    return out
 
 
 def path_of(B):
@@ -840,6 +990,22 @@ def run_reference(a):
                           "oracle/_ref/libjoule_ref.so not built (needs the reference sources)"}))
         return
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
+    if ws == 1 and a.decode_sweep:
+        # the headline metric at N = 1: the whole decode step (our arm's full_decode)
+        budget = min(240.0, max(20.0, 4.0 * (a.steps + a.warmup)))
+        c = cpu_decode_sample(a.batch, budget_s=budget, ctx=a.ctx)
+        line = dict(metric=METRIC_DECODE, value=c["value"], unit="tok/s", n_gpus=1, steps=a.steps,
+                    warmup=a.warmup, ms_per_step=a.batch / c["value"] * 1e3, higher_is_better=True,
+                    scaling="weak", vs_baseline=None, dtype=DTYPE_EXACT, impl="reference",
+                    data="synthetic: seeded random-init weights in the reference's layout (bf16 dense, fp32 "
+                         "lm_head, Q4 experts), KV caches of 512 seeded random rows",
+                    config=dict(workload=f"Qwen3-30B-A3B decode step, batch B={a.batch} at context {a.ctx}",
+                                model="Qwen3-30B-A3B architecture, random init (BASELINE config 3)",
+                                batch=a.batch, context=a.ctx, layers=L),
+                    cpu_baseline=c,
+                    e2e=dict(value=c["value"], unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+        print(json.dumps(line), flush=True)
+        return
     nl = a.ref_layers
     t = time.time()
     lays = [olayer.make_layer(d, E, k, m, SHAPE["norm"], seed_router=10 + i, seed_experts=20 + i)

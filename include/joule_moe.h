@@ -412,6 +412,17 @@ int jl_dec_embed(jl_dec* h, const int* tokens, int B, float* x, void* stream);
 int jl_dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B,
                 float* logits, int* tok, void* stream);
 
+/* Batched prefill of one sequence: tokens [T] (device ids) at positions
+ * pos0 .. pos0+T-1 of KV slot `slot`, max_batch positions per pass (each
+ * pass appends its K/V rows before its attention reads them; the MoE
+ * layers add each token's experts in its own top-k order). The logits [V]
+ * and argmax tok [1] (nullable, device) are the last position's. With the
+ * MoE handle on JL_PATH_EXACT every position gets the bits of the
+ * reference's one-position steps (prefill_layers, decode_kernel.c:
+ * 1606-1615); decoder3.py:512-571 (prefill_batch) runs prompts this way. */
+int jl_dec_prefill(jl_dec* h, int slot, const int* tokens, int T, int pos0, float* logits,
+                   int* tok, void* stream);
+
 /* Read and clear the decoder's error word and its MoE handle's
  * (synchronises): JL_ERR_INVALID for a position outside [0, maxT). */
 int jl_dec_check(jl_dec* h, void* stream);

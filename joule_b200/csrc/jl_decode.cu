@@ -239,6 +239,8 @@ struct attn_args {
     const float* cosb;       // [maxT][hd]
     const float* sinb;
     int l, L, H, KH, hd, maxT, qk_type;
+    int nslots;              // KV cache slots held
+    int from_cache;          // 1: this position's K/V rows are already in the cache (k_kv_append ran)
     int sqn;                 // floats per squares buffer: max(qn, kn) for whole-vector norms, else hd
     float eps;
     int* err;
@@ -263,11 +265,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
     griddep_wait();
     griddep_launch_dependents();
     const int pos = a.positions[b];
-    if (pos < 0 || pos >= a.maxT) {
+    const int slot = a.slots[b];
+    if (pos < 0 || pos >= a.maxT || slot < 0 || slot >= a.nslots) {
         if (tid == 0) atomicOr(a.err, kErrPosition);
         return;
     }
-    const int slot = a.slots[b];
     const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
     if (tid < hd) {
         q_s[tid] = row[h * hd + tid];
@@ -325,7 +327,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
     const size_t cache_off = ((size_t)slot * a.L + a.l) * a.maxT * kn;
     float* K = a.kc + cache_off;
     float* V = a.vc + cache_off;
-    if (h % gsz == 0 && tid < hd) {  // KV append (decode_kernel.c:1200-1205)
+    // The position whose K/V rows this block holds in registers (-1: every row
+    // comes from the cache, where k_kv_append put this step's rows).
+    const int own = a.from_cache ? -1 : pos;
+    if (!a.from_cache && h % gsz == 0 && tid < hd) {  // KV append (decode_kernel.c:1200-1205)
         K[(size_t)pos * kn + g * hd + tid] = k_s[tid];
         V[(size_t)pos * kn + g * hd + tid] = v_s[tid];
     }
@@ -338,7 +343,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
         __syncthreads();
         for (int i = tid; i < nt * hd; i += blockDim.x) {
             const int r = i / hd, c = i % hd, t = t0 + r;
-            ks[r * (hd + 1) + c] = (t == pos) ? k_s[c] : K[(size_t)t * kn + g * hd + c];
+            ks[r * (hd + 1) + c] = (t == own) ? k_s[c] : K[(size_t)t * kn + g * hd + c];
         }
         __syncthreads();
         if (tid < nt) {
@@ -382,20 +387,78 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
         float o = 0.0f;
         int t = 0;
         for (; t + 4 <= T; t += 4) {
-            const float v0 = (t == pos) ? v_s[tid] : vp[(size_t)t * kn];
-            const float v1 = (t + 1 == pos) ? v_s[tid] : vp[(size_t)(t + 1) * kn];
-            const float v2 = (t + 2 == pos) ? v_s[tid] : vp[(size_t)(t + 2) * kn];
-            const float v3 = (t + 3 == pos) ? v_s[tid] : vp[(size_t)(t + 3) * kn];
+            const float v0 = (t == own) ? v_s[tid] : vp[(size_t)t * kn];
+            const float v1 = (t + 1 == own) ? v_s[tid] : vp[(size_t)(t + 1) * kn];
+            const float v2 = (t + 2 == own) ? v_s[tid] : vp[(size_t)(t + 2) * kn];
+            const float v3 = (t + 3 == own) ? v_s[tid] : vp[(size_t)(t + 3) * kn];
             o = __fadd_rn(o, __fmul_rn(sc[t], v0));
             o = __fadd_rn(o, __fmul_rn(sc[t + 1], v1));
             o = __fadd_rn(o, __fmul_rn(sc[t + 2], v2));
             o = __fadd_rn(o, __fmul_rn(sc[t + 3], v3));
         }
         for (; t < T; t++) {
-            const float v0 = (t == pos) ? v_s[tid] : vp[(size_t)t * kn];
+            const float v0 = (t == own) ? v_s[tid] : vp[(size_t)t * kn];
             o = __fadd_rn(o, __fmul_rn(sc[t], v0));
         }
         a.att[(size_t)b * qn + h * hd + tid] = o;
+    }
+}
+
+// K/V append for a batch of positions of one or more sequences (batched
+// prefill, where one launch's positions of a sequence attend to each other):
+// per (KV head g, row b) the K row gets its QK-norm and RoPE exactly as in
+// k_attn, and both rows go into the cache at positions[b]. k_attn then runs
+// with from_cache = 1.
+__global__ void __launch_bounds__(kAttnThreads) k_kv_append(attn_args a) {
+    extern __shared__ __align__(16) float sm[];
+    const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd;
+    float* k_s = sm;
+    float* sq = sm + 128;  // [a.sqn]
+    __shared__ float inv_k;
+    griddep_wait();
+    griddep_launch_dependents();
+    const int pos = a.positions[b];
+    const int slot = a.slots[b];
+    if (pos < 0 || pos >= a.maxT || slot < 0 || slot >= a.nslots) {
+        if (tid == 0) atomicOr(a.err, kErrPosition);
+        return;
+    }
+    const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
+    if (tid < hd) k_s[tid] = row[qn + g * hd + tid];
+    if (a.qk_type == 2) {
+        for (int i = tid; i < kn; i += blockDim.x) sq[i] = __fmul_rn(row[qn + i], row[qn + i]);
+        __syncthreads();
+        if (tid == 0) inv_k = rms_inv(chain_sum(sq, kn), kn, a.eps);
+        __syncthreads();
+        if (tid < hd) k_s[tid] = __fmul_rn(__fmul_rn(k_s[tid], inv_k), bf16_to_f32(a.knw[g * hd + tid]));
+    } else if (a.qk_type == 1) {
+        __syncthreads();
+        if (tid < hd) sq[tid] = __fmul_rn(k_s[tid], k_s[tid]);
+        __syncthreads();
+        if (tid == 0) inv_k = rms_inv(chain_sum(sq, hd), hd, a.eps);
+        __syncthreads();
+        if (tid < hd) k_s[tid] = __fmul_rn(__fmul_rn(k_s[tid], inv_k), bf16_to_f32(a.knw[tid]));
+    }
+    __syncthreads();
+    const int half = hd / 2;
+    float ka = 0.f, kb = 0.f;
+    if (tid < half) {
+        const float cs = a.cosb[(size_t)pos * hd + tid], sn = a.sinb[(size_t)pos * hd + tid];
+        const float y0 = k_s[tid], y1 = k_s[tid + half];
+        ka = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+        kb = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+    }
+    __syncthreads();
+    if (tid < half) {
+        k_s[tid] = ka;
+        k_s[tid + half] = kb;
+    }
+    __syncthreads();
+    const size_t off = (((size_t)slot * a.L + a.l) * a.maxT + pos) * kn + g * hd;
+    if (tid < hd) {
+        a.kc[off + tid] = k_s[tid];
+        a.vc[off + tid] = row[qn + kn + g * hd + tid];
     }
 }
 
@@ -502,6 +565,8 @@ struct jl_dec {
     float* att;        // [max_batch, qn]
     float* logits;     // [max_batch, V]
     int* tok;          // [max_batch]
+    int* pre_pos;      // [max_batch] positions of a prefill chunk
+    int* pre_slot;     // [max_batch] its slot, repeated
     int* err;          // [1]
     void* stage;       // device staging for uploads
     size_t stage_bytes;
@@ -575,7 +640,7 @@ extern "C" int jl_dec_destroy(jl_dec* h) {
     if (h->moe) jl_moe_destroy(h->moe);
     void* ptrs[] = {h->embed, h->norm1, h->norm2, h->fnorm, h->qnw, h->knw, h->wqkv, h->wo, h->bqkv, h->lm,
                     h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->logits,
-                    h->tok, h->err, h->stage};
+                    h->tok, h->pre_pos, h->pre_slot, h->err, h->stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete h;
@@ -636,6 +701,8 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
         {(void**)&h->att, (size_t)max_batch * h->qn * 4},
         {(void**)&h->logits, (size_t)max_batch * V * 4},
         {(void**)&h->tok, (size_t)max_batch * 4},
+        {(void**)&h->pre_pos, (size_t)max_batch * 4},
+        {(void**)&h->pre_slot, (size_t)max_batch * 4},
         {(void**)&h->err, 16},
         {&h->stage, h->stage_bytes},
     };
@@ -734,8 +801,12 @@ extern "C" int jl_dec_embed(jl_dec* h, const int* tokens, int B, float* x, void*
 // reference's debug_decode_layers (decode_kernel.c:1764-1790) writes them:
 // norm1 output, attention output, h after attention, norm2 output, router
 // logits, MoE output, h after the MoE layer.
+// prefill = 1: the B rows are consecutive positions of one sequence (one
+// launch's rows attend to each other: K/V rows are appended first, then the
+// attention reads every row from the cache); the MoE layers combine in each
+// token's own order; logits/tok are of the last row only.
 static int dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B, float* logits,
-                    int* tok, float* dbg, cudaStream_t s);
+                    int* tok, float* dbg, cudaStream_t s, int prefill = 0);
 
 extern "C" int jl_dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B,
                            float* logits, int* tok, void* stream) {
@@ -743,7 +814,7 @@ extern "C" int jl_dec_step(jl_dec* h, const int* slots, const int* positions, co
 }
 
 static int dec_step(jl_dec* h, const int* slots, const int* positions, const float* x, int B, float* logits,
-                    int* tok, float* dbg, cudaStream_t s) {
+                    int* tok, float* dbg, cudaStream_t s, int prefill) {
     using namespace jl;
     if (!h || B < 0) return JL_ERR_INVALID;
     if (B == 0) return JL_OK;
@@ -767,6 +838,7 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     aa.cosb = h->cosb, aa.sinb = h->sinb, aa.L = h->L, aa.H = h->H, aa.KH = h->KH, aa.hd = h->hd, aa.maxT = h->maxT;
     aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err;
     aa.sqn = attn_sqn(h->qk_type, h->H, h->KH, h->hd);
+    aa.nslots = h->slots;
     const size_t asm_ = attn_smem(aa.sqn, h->hd, h->maxT);
     if (asm_ > 200 * 1024) return JL_ERR_INVALID;
     for (int l = 0; l < h->L; l++) {
@@ -783,7 +855,11 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
             const size_t qs = h->qk_type == 2 ? (size_t)h->qn : h->hd, ks = h->qk_type == 2 ? (size_t)h->kn : h->hd;
             aa.qnw = h->qk_type ? h->qnw + l * qs : nullptr;
             aa.knw = h->qk_type ? h->knw + l * ks : nullptr;
-            rc = launch(k_attn, dim3(h->H, B), dim3(kAttnThreads), asm_, s, aa);
+            aa.from_cache = prefill;
+            if (prefill)
+                rc = launch(k_kv_append, dim3(h->KH, B), dim3(kAttnThreads), (size_t)(128 + aa.sqn) * sizeof(float),
+                            s, aa);
+            if (!rc) rc = launch(k_attn, dim3(h->H, B), dim3(kAttnThreads), asm_, s, aa);
         }
         if (!rc) rc = launch_mv<uint16_t>(h->wo + (size_t)l * d * h->qn, h->att, d, h->qn, B, nullptr, h->h2, s);
         if (!rc) rc = snap(l, 1, h->h2, d);
@@ -793,7 +869,11 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
                         (const uint16_t*)(h->norm2 + (size_t)l * d), h->eps, d, h->t);
         if (!rc) rc = snap(l, 2, h->h, d);
         if (!rc) rc = snap(l, 3, h->t, d);
-        if (!rc) rc = jl_moe_forward(h->moe, l, h->t, B, h->h2, nullptr, nullptr, s);
+        if (!rc) {
+            h->moe->comb_token_order = prefill;
+            rc = jl_moe_forward(h->moe, l, h->t, B, h->h2, nullptr, nullptr, s);
+            h->moe->comb_token_order = 0;
+        }
         if (!rc) rc = snap(l, 4, h->moe->ws.logits, h->E);
         if (!rc) rc = snap(l, 5, h->h2, d);
         if (rc) return rc;
@@ -803,14 +883,50 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     if (!rc) rc = snap(h->L - 1, 6, h->h, d);
     if (rc) return rc;
     if (logits || tok) {
-        rc = launch_mv<float>(h->lm, h->t, h->V, d, B, nullptr, h->logits, s);
-        if (!rc && tok) rc = launch(k_argmax, dim3(B), dim3(1024), 0, s, (const float*)h->logits, h->V, tok);
+        const int nb = prefill ? 1 : B;
+        const float* tx = prefill ? h->t + (size_t)(B - 1) * d : h->t;
+        rc = launch_mv<float>(h->lm, tx, h->V, d, nb, nullptr, h->logits, s);
+        if (!rc && tok) rc = launch(k_argmax, dim3(nb), dim3(1024), 0, s, (const float*)h->logits, h->V, tok);
         if (!rc && logits)
-            rc = cudaMemcpyAsync(logits, h->logits, (size_t)B * h->V * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess
+            rc = cudaMemcpyAsync(logits, h->logits, (size_t)nb * h->V * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess
                      ? JL_OK
                      : JL_ERR_CUDA;
     }
     return rc;
+}
+
+namespace jl {
+__global__ void k_prefill_rows(int* pos, int* slot, int p0, int s, int n) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int i = threadIdx.x + blockIdx.x * blockDim.x;
+    if (i < n) {
+        pos[i] = p0 + i;
+        slot[i] = s;
+    }
+}
+}  // namespace jl
+
+extern "C" int jl_dec_prefill(jl_dec* h, int slot, const int* tokens, int T, int pos0, float* logits, int* tok,
+                              void* stream) {
+    using namespace jl;
+    if (!h || T < 0 || slot < 0 || slot >= h->slots || pos0 < 0) return JL_ERR_INVALID;
+    if (T == 0) return JL_OK;
+    if (!tokens || pos0 + T > h->maxT) return JL_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int Bm = h->max_batch;
+    for (int c0 = 0; c0 < T; c0 += Bm) {
+        const int n = std::min(Bm, T - c0);
+        const bool last = c0 + n == T;
+        int rc = launch(k_prefill_rows, dim3((n + 127) / 128), dim3(128), 0, s, h->pre_pos, h->pre_slot, pos0 + c0,
+                        slot, n);
+        if (!rc) rc = jl_dec_embed(h, tokens + c0, n, h->t, s);
+        if (!rc)
+            rc = dec_step(h, h->pre_slot, h->pre_pos, h->t, n, last ? logits : nullptr, last ? tok : nullptr,
+                          nullptr, s, 1);
+        if (rc) return rc;
+    }
+    return JL_OK;
 }
 
 extern "C" int jl_dec_check(jl_dec* h, void* stream) {
@@ -926,6 +1042,59 @@ dec_entry* dec_for(const KernelCfg* c, const KernelW* W, int* rc) {
     return e;
 }
 
+// The device slot of the sequence whose layer caches are kvb[0..L): found by
+// its layer-0 K pointer, else a free slot or the least recently used one not
+// in this call. Unless the slot holds exactly p rows, the host rows [0, p)
+// of every layer are copied over first. Afterwards it counts rows_after rows.
+int acquire_slot(dec_entry* e, const KVCache* kvb, int L, int p, int rows_after, int* out) {
+    jl_dec* h = e->h;
+    const int kn = h->kn;
+    const size_t row_b = (size_t)kn * 4;
+    if (p < 0 || rows_after > h->maxT) return JL_ERR_INVALID;
+    const float* key = kvb[0].k;
+    if (!key) return JL_ERR_INVALID;
+    auto it = e->seq_slot.find(key);
+    int sl;
+    if (it != e->seq_slot.end()) {
+        sl = it->second;
+    } else {
+        sl = -1;
+        for (int i = 0; i < h->slots; i++)
+            if (!e->slot_key[i]) {
+                sl = i;
+                break;
+            }
+        if (sl < 0) {
+            long long best = LLONG_MAX;
+            for (int i = 0; i < h->slots; i++)
+                if (e->slot_used[i] < e->calls && e->slot_used[i] < best) {
+                    best = e->slot_used[i];
+                    sl = i;
+                }
+            if (sl < 0) return JL_ERR_CAPACITY;
+            e->seq_slot.erase(e->slot_key[sl]);
+        }
+        e->seq_slot[key] = sl;
+        e->slot_key[sl] = key;
+        e->slot_rows[sl] = -1;
+    }
+    e->slot_used[sl] = e->calls;
+    if (e->slot_rows[sl] != p) {  // bring the host rows [0, p) of every layer over
+        for (int l = 0; l < L; l++) {
+            const KVCache& cl = kvb[l];
+            if (!cl.k || !cl.v) return JL_ERR_INVALID;
+            const size_t off = ((size_t)sl * L + l) * h->maxT * kn;
+            if (p > 0) {
+                JL_CUDA(cudaMemcpyAsync(h->kc + off, cl.k, (size_t)p * row_b, cudaMemcpyHostToDevice, e->st));
+                JL_CUDA(cudaMemcpyAsync(h->vc + off, cl.v, (size_t)p * row_b, cudaMemcpyHostToDevice, e->st));
+            }
+        }
+    }
+    e->slot_rows[sl] = rows_after;
+    *out = sl;
+    return JL_OK;
+}
+
 // One batched step through the drop-in: logits (host, [B, V]) and/or tokens.
 int dropin_step(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* positions, const float* xin,
                 int B, float* logits, int* out_tok, float* dbg_host = nullptr) {
@@ -938,55 +1107,13 @@ int dropin_step(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* po
     jl_dec* h = e->h;
     if (B > h->max_batch) return JL_ERR_CAPACITY;
     const int L = c->L, kn = h->kn;
-    const size_t row_b = (size_t)kn * 4, lay_b = (size_t)h->maxT * row_b;
+    const size_t row_b = (size_t)kn * 4;
     e->calls++;
     std::vector<int> slot(B);
     for (int b = 0; b < B; b++) {
-        if (positions[b] < 0 || positions[b] >= h->maxT) return JL_ERR_INVALID;
-        const float* key = kv[(size_t)b * L].k;
-        if (!key) return JL_ERR_INVALID;
-        auto it = e->seq_slot.find(key);
-        int sl;
-        if (it != e->seq_slot.end()) {
-            sl = it->second;
-        } else {  // a free slot, else the least recently used one not in this call
-            sl = -1;
-            for (int i = 0; i < h->slots; i++)
-                if (!e->slot_key[i]) {
-                    sl = i;
-                    break;
-                }
-            if (sl < 0) {
-                long long best = LLONG_MAX;
-                for (int i = 0; i < h->slots; i++)
-                    if (e->slot_used[i] < e->calls && e->slot_used[i] < best) {
-                        best = e->slot_used[i];
-                        sl = i;
-                    }
-                if (sl < 0) return JL_ERR_CAPACITY;
-                e->seq_slot.erase(e->slot_key[sl]);
-            }
-            e->seq_slot[key] = sl;
-            e->slot_key[sl] = key;
-            e->slot_rows[sl] = -1;
-        }
-        e->slot_used[sl] = e->calls;
-        slot[b] = sl;
-        const int p = positions[b];
-        if (e->slot_rows[sl] != p) {  // bring the host rows [0, p) of every layer over
-            for (int l = 0; l < L; l++) {
-                const KVCache& cl = kv[(size_t)b * L + l];
-                if (!cl.k || !cl.v) return JL_ERR_INVALID;
-                const size_t off = ((size_t)sl * L + l) * h->maxT * kn;
-                if (p > 0) {
-                    JL_CUDA(cudaMemcpyAsync(h->kc + off, cl.k, (size_t)p * row_b, cudaMemcpyHostToDevice, e->st));
-                    JL_CUDA(cudaMemcpyAsync(h->vc + off, cl.v, (size_t)p * row_b, cudaMemcpyHostToDevice, e->st));
-                }
-            }
-        }
-        e->slot_rows[sl] = p + 1;
+        rc = acquire_slot(e, kv + (size_t)b * L, L, positions[b], positions[b] + 1, &slot[b]);
+        if (rc) return rc;
     }
-    (void)lay_b;
     JL_CUDA(cudaMemcpyAsync(e->slots_d, slot.data(), (size_t)B * 4, cudaMemcpyHostToDevice, e->st));
     JL_CUDA(cudaMemcpyAsync(e->pos_d, positions, (size_t)B * 4, cudaMemcpyHostToDevice, e->st));
     JL_CUDA(cudaMemcpyAsync(e->x_d, xin, (size_t)B * c->d * 4, cudaMemcpyHostToDevice, e->st));
@@ -1078,22 +1205,60 @@ extern "C" void embed_lookup(const KernelW* W, const KernelCfg* c, int token, fl
     if (rc) nan_fill(out, (size_t)c->d);
 }
 
+// prefill_layers (decode_kernel.c:1606-1615) runs one B = 1 decode step per
+// position; here the positions run as batches of one sequence (jl_dec_prefill:
+// K/V rows appended before the attention, each token's own combine order),
+// which gives every position the bits of the one-position step.
+static int dropin_prefill(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* tokens, int T,
+                          float* logits) {
+    if (!c || !W || !kv || !tokens || T < 0) return JL_ERR_INVALID;
+    if (T == 0) return JL_OK;
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= c->V) return JL_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_dec_mu);
+    int rc = JL_OK;
+    dec_entry* e = dec_for(c, W, &rc);
+    if (!e) return rc;
+    jl_dec* h = e->h;
+    if (T > h->maxT) return JL_ERR_INVALID;
+    const int L = c->L, kn = h->kn;
+    e->calls++;
+    int sl = 0;
+    rc = acquire_slot(e, kv, L, 0, T, &sl);
+    if (rc) return rc;
+    int* tok_d = nullptr;
+    float* lg_d = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&tok_d), (size_t)T * 4, e->st) != cudaSuccess ||
+        cudaMallocAsync(reinterpret_cast<void**>(&lg_d), (size_t)c->V * 4, e->st) != cudaSuccess) {
+        cudaGetLastError();
+        if (tok_d) cudaFreeAsync(tok_d, e->st);
+        return JL_ERR_OOM;
+    }
+    rc = cudaMemcpyAsync(tok_d, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, e->st) == cudaSuccess ? JL_OK
+                                                                                                  : JL_ERR_CUDA;
+    if (!rc) rc = jl_dec_prefill(h, sl, tok_d, T, 0, logits ? lg_d : nullptr, nullptr, e->st);
+    if (!rc && logits &&
+        cudaMemcpyAsync(logits, lg_d, (size_t)c->V * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+        rc = JL_ERR_CUDA;
+    // the rows [0, T) of every layer back into the caller's caches
+    for (int l = 0; l < L && !rc; l++) {
+        const size_t off = ((size_t)sl * L + l) * h->maxT * kn;
+        if (cudaMemcpyAsync(kv[l].k, h->kc + off, (size_t)T * kn * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess ||
+            cudaMemcpyAsync(kv[l].v, h->vc + off, (size_t)T * kn * 4, cudaMemcpyDeviceToHost, e->st) != cudaSuccess)
+            rc = JL_ERR_CUDA;
+    }
+    cudaFreeAsync(tok_d, e->st);
+    cudaFreeAsync(lg_d, e->st);
+    if (cudaStreamSynchronize(e->st) != cudaSuccess && !rc) rc = JL_ERR_CUDA;
+    if (!rc) rc = jl_dec_check(h, e->st);
+    if (rc) e->slot_rows[sl] = -1;
+    return rc;
+}
+
 extern "C" void prefill_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* tokens, int T,
                                float* logits) {
-    // decode_kernel.c:1606-1615: one B = 1 step per position, logits at the last
-    t_dec_status = JL_OK;
-    if (!c || !W || !tokens || T < 0) {
-        t_dec_status = JL_ERR_INVALID;
-        return;
-    }
-    std::vector<float> x((size_t)c->d);
-    for (int t = 0; t < T && t_dec_status == JL_OK; t++) {
-        embed_lookup(W, c, tokens[t], x.data());
-        if (t_dec_status) break;
-        const int p[1] = {t};
-        t_dec_status = dropin_step(c, W, kv, p, x.data(), 1, t == T - 1 ? logits : nullptr, nullptr);
-    }
-    if (t_dec_status && logits) nan_fill(logits, (size_t)c->V);
+    t_dec_status = dropin_prefill(c, W, kv, tokens, T, logits);
+    if (t_dec_status && logits && c) nan_fill(logits, (size_t)c->V);
 }
 
 extern "C" void debug_decode_layers(const KernelCfg* c, const KernelW* W, KVCache* kv, int pos, const float* xin,

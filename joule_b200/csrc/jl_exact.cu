@@ -278,8 +278,12 @@ __global__ void __launch_bounds__(kXWarps * 32) k_down_exact(const uint8_t* __re
 // Combine (decode_kernel.c:1490-1507): out[b] = 0 + y of b's experts in union
 // order (experts b did not choose contribute +0 in the reference, which
 // leaves every nonzero partial sum unchanged). Also copies top/tw out.
+// With tokorder = 1 a token adds its slots in its own top-k order (b*k + j),
+// the union order it has when it is routed alone (B = 1): a batch of
+// positions of one sequence then gives each position the bits of a one-token
+// call (prefill_layers, decode_kernel.c:1606-1615, runs one position per call).
 __global__ void k_combine(int B, int k, int d, jl_ws ws, float* __restrict__ out,
-                          int* __restrict__ top, float* __restrict__ tw) {
+                          int* __restrict__ top, float* __restrict__ tw, int tokorder) {
     long long* tr = (blockIdx.x == 0 && blockIdx.y == 0) ? ws.trace : nullptr;
     trace_point(tr, kTraceCombine, 0);
     griddep_wait();
@@ -290,7 +294,7 @@ __global__ void k_combine(int B, int k, int d, jl_ws ws, float* __restrict__ out
     if (c < d) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < k; j++) {
-            const int slot = ws.comb[b * k + j];
+            const int slot = tokorder ? b * k + j : ws.comb[b * k + j];
             const float4 v = *reinterpret_cast<const float4*>(ws.y + (size_t)slot * d + c);
             acc.x = __fadd_rn(acc.x, v.x);
             acc.y = __fadd_rn(acc.y, v.y);
@@ -354,5 +358,5 @@ int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, c
     using namespace jl;
     const int tpb = 128;
     dim3 grid((h->d / 4 + tpb - 1) / tpb, B);
-    return launch(k_combine, grid, dim3(tpb), 0, s, B, h->k, h->d, h->ws, out, top, tw);
+    return launch(k_combine, grid, dim3(tpb), 0, s, B, h->k, h->d, h->ws, out, top, tw, h->comb_token_order);
 }

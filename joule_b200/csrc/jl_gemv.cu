@@ -150,12 +150,16 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_gateup_gemv(const uint8_t* __
     extern __shared__ __align__(16) float x_s[];  // [B][d]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = L.d, m = L.m, ngd = L.ngd, MT = m / 64;
+    long long* tr = blockIdx.x == 0 ? ws.trace : nullptr;
+    trace_point(tr, kTraceGateup, 0);
     griddep_wait();
     griddep_launch_dependents();
+    trace_point(tr, kTraceGateup, 1);
     const int U = *ws.U;
     for (int i = threadIdx.x; i < B * d / 4; i += blockDim.x)
         reinterpret_cast<float4*>(x_s)[i] = reinterpret_cast<const float4*>(x)[i];
     __syncthreads();
+    trace_point(tr, kTraceGateup, 2);
     const long long Q = (long long)U * MT * ngd;
     const int NW = (int)min((long long)gridDim.x * kGvWarps, Q);
     const int wg = blockIdx.x * kGvWarps + warp;
@@ -204,6 +208,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_gateup_gemv(const uint8_t* __
             }
         }
     }
+    if (warp == 0) trace_point(tr, kTraceGateup, 3);
 }
 
 // ---------------------------------------------------------------------------
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_gateup_gemv(const uint8_t* __
 // Each block stages the act rows of the union experts its warps touch.
 template <int NT>
 __global__ void __launch_bounds__(kGvWarps * 32) k_down_gemv(const uint8_t* __restrict__ store_l, jl_layout L,
-                                                             jl_ws ws) {
+                                                             jl_ws ws, int span) {
     extern __shared__ __align__(16) float a_s[];  // [units this block touches (<= 4)][NT][m]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = L.d, m = L.m, ngm = L.ngm, MT = d / 128;
@@ -227,16 +232,23 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_down_gemv(const uint8_t* __re
         const int e = ws.sel[unit / MT], mt = unit % MT;
         return store_l + (size_t)e * L.rec_bytes + L.tile_off(2, 4 * mt, g);
     };
+    long long* tr = blockIdx.x == 0 ? ws.trace : nullptr;
+    trace_point(tr, kTraceDown, 0);
     rec4 cur, nxt;
     if (active) load_rec4(addr(q0), lane, cur);  // weights before the wait: they do not depend on gate/up
     griddep_wait();
     griddep_launch_dependents();
+    trace_point(tr, kTraceDown, 1);
     // the block's experts: union positions from the first warp's to the last warp's
     const int wb0 = blockIdx.x * kGvWarps;
     const int wb1 = min(wb0 + kGvWarps, NW) - 1;
     if (wb0 >= NW) return;
     const long long bq0 = (long long)wb0 * Q / NW, bq1 = (long long)(wb1 + 1) * Q / NW - 1;
     const int u_lo = (int)(bq0 / ngm) / MT, u_hi = (int)(bq1 / ngm) / MT;
+    if (u_hi - u_lo + 1 > span) {  // more experts than the staging area holds (host bound violated)
+        if (threadIdx.x == 0) atomicOr(ws.err, kErrCapacity);
+        return;
+    }
     for (int uu = u_lo; uu <= u_hi; uu++) {
         const int s0 = ws.uh[uu], nt = min(NT, ws.uh[uu + 1] - s0);
         float* dst = a_s + (size_t)(uu - u_lo) * NT * m;
@@ -286,6 +298,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_down_gemv(const uint8_t* __re
             }
         }
     }
+    if (warp == 0) trace_point(tr, kTraceDown, 3);
 }
 
 }  // namespace jl
@@ -336,14 +349,19 @@ int jl_launch_down_gemv(const jl_moe* h, const uint8_t* store_l, int B, cudaStre
     int rc = gemv_attrs();
     if (rc) return rc;
     const int nt = B == 1 ? 1 : B == 2 ? 2 : 4;
-    // a block's warps span at most this many union experts
-    const int ngm = h->m / 64, MT = h->d / 128;
-    const int steps_per_expert = ngm * MT;
-    const int span = std::min(h->E, kGvWarps * 64 / std::max(1, steps_per_expert) + 2);
-    const size_t smem = (size_t)std::min(span, std::min(h->E, B * h->k)) * nt * h->m * sizeof(float);
+    // Experts one block's warps can touch: with U <= Umax union experts of spe
+    // K-steps each and NW = min(grid warps, Q) ranges, a warp holds at most
+    // spw = ceil(Qmax / grid warps) steps (1 when Q < grid warps), a block
+    // 8 * spw contiguous steps, which meet at most (8 spw - 1) / spe + 2 experts.
+    const long long spe = (long long)(h->m / 64) * (h->d / 128);
+    const int Umax = std::min(h->E, B * h->k);
+    const long long Qmax = Umax * spe, NWg = (long long)h->sm_count * kGvWarps;
+    const long long spw = Qmax <= NWg ? 1 : (Qmax + NWg - 1) / NWg;
+    const int span = (int)std::min<long long>(Umax, (kGvWarps * spw - 1) / spe + 2);
+    const size_t smem = (size_t)span * nt * h->m * sizeof(float);
     if (smem > 200 * 1024) return JL_ERR_INVALID;
     const dim3 grid(h->sm_count), block(kGvWarps * 32);
-    if (nt == 1) return launch(k_down_gemv<1>, grid, block, smem, s, store_l, h->lay, h->ws);
-    if (nt == 2) return launch(k_down_gemv<2>, grid, block, smem, s, store_l, h->lay, h->ws);
-    return launch(k_down_gemv<4>, grid, block, smem, s, store_l, h->lay, h->ws);
+    if (nt == 1) return launch(k_down_gemv<1>, grid, block, smem, s, store_l, h->lay, h->ws, span);
+    if (nt == 2) return launch(k_down_gemv<2>, grid, block, smem, s, store_l, h->lay, h->ws, span);
+    return launch(k_down_gemv<4>, grid, block, smem, s, store_l, h->lay, h->ws, span);
 }

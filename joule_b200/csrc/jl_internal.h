@@ -87,6 +87,7 @@ struct jl_moe {
     size_t ws_bytes;
     size_t store_bytes;
     int last_B;
+    int comb_token_order;     // combine each token's slots in its own top-k order (batched prefill)
     long long* trace_buf;     // trace buffer: kept until destroy (captured graphs hold it)
     cudaEvent_t phase_ev[5];  // optional phase timing events
     int n_phase_ev;

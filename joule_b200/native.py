@@ -111,6 +111,7 @@ SIGNATURES = {
     "jl_dec_embed": ([_P, _P, _I, _P, _P], _I),
     "jl_dec_step": ([_P, _P, _P, _P, _I, _P, _P, _P], _I),
     "jl_dec_check": ([_P, _P], _I),
+    "jl_dec_prefill": ([_P, _I, _P, _I, _I, _P, _P, _P], _I),
     "decode_layers_batch": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _P, _P, _I, _P], None),
     "decode_layers_batch_argmax": ([ctypes.POINTER(KernelCfg), ctypes.POINTER(KernelW), _P, _P, _P, _I, _P],
                                    None),

@@ -191,3 +191,32 @@ def test_device_api_greedy_qwen3s():
         pos = [p + 1 for p in pos]
     lib.jl_dec_destroy(h)
     assert np.array_equal(toks, g["tokens"])
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_batched_prefill_bit_identical_to_position_steps(name):
+    """jl_dec_prefill with 3 positions per pass (the last prompt: passes of 3,
+    3 and the rest) gives the reference prefill_layers' last-token logits bit
+    for bit, and its K/V rows let the next decode step match too."""
+    from joule_b200.native import check, get_dll
+    g, model, prompts = _model(name)
+    s = model.shape
+    lib = get_dll()
+    cfg, W, tables = _structs(model)
+    h = ctypes.c_void_p()
+    check(lib.jl_dec_create(ctypes.byref(cfg), ctypes.byref(W), 3, 3, 0, ctypes.byref(h)), "jl_dec_create")
+    moe = ctypes.c_void_p()
+    check(lib.jl_dec_moe(h, ctypes.byref(moe)), "jl_dec_moe")
+    check(lib.jl_moe_set_path(moe, 1), "jl_moe_set_path")  # exact
+    stream = torch.cuda.current_stream().cuda_stream
+    p = torch.tensor(prompts[-1], dtype=torch.int32, device="cuda")
+    logits = torch.empty(s.V, device="cuda")
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    check(lib.jl_dec_prefill(h, 1, p.data_ptr(), p.numel(), 0, logits.data_ptr(), tok.data_ptr(), stream),
+          "jl_dec_prefill")
+    torch.cuda.synchronize()
+    check(lib.jl_dec_check(h, stream), "jl_dec_check")
+    lib.jl_dec_destroy(h)
+    ref = g["prefill_logits"]
+    assert np.array_equal(logits.cpu().numpy(), ref)
+    assert int(tok.item()) == int(np.argmax(ref))
