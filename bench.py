@@ -42,6 +42,14 @@ DTYPE_TC = ("fp16 x fp16 -> fp32: Q4 weights dequantised to fp16 ((n-8)*s rounde
 DTYPE_EXACT = "f32: Q4 weights, fp32 arithmetic in the reference's order"
 
 
+_T0 = time.time()
+
+
+def log(msg: str) -> None:
+    """Progress on stderr (the JSON line alone goes to stdout)."""
+    print(f"[bench {time.time() - _T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def rec_bytes(d, m):
     return 3 * (m * d // 2 + m * d // 32)
 
@@ -682,6 +690,7 @@ def microbench(moe, a, hbm, peak_kind):
     tensor_peak = tensor_peak_tflops()
     res = {}
     for T in Ts:
+        log(f"microbench T={T}")
         U = routing_unions(moe, xs, T)
         total_ms, _ = time_batch(moe, xs, outs, T, max(3, a.steps // 2), 3, 1, phases=False)
         t_step = total_ms / max(3, a.steps // 2) / 1e3
@@ -717,8 +726,10 @@ def full_decode(a, hbm):
     steps, warm = a.steps, a.warmup
     cfg = qwen3_cfg(maxT=ctx + warm + steps + 64)
     t0 = time.time()
+    log("decoder build")
     dec = Decoder.random(cfg, Bmax, Bmax)
     build_s = time.time() - t0
+    log(f"decoder built ({build_s:.1f}s); prefill {ctx} positions x {Bmax} sequences")
     dev = torch.device("cuda", torch.cuda.current_device())
     V, d, L = cfg.V, cfg.d, cfg.L
     prompt = torch.randint(0, V, (Bmax, ctx), generator=torch.Generator().manual_seed(0),
@@ -738,6 +749,7 @@ def full_decode(a, hbm):
     clocks = None
     stream = torch.cuda.Stream()
     for B in [b for b in Bs if b != a.batch] + ([a.batch] if a.batch in Bs else []):
+        log(f"full decode B={B}")
         pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
         tok = tok0[:B].clone()
         xb = torch.empty(B, d, device=dev)
@@ -814,6 +826,7 @@ def run_ours(a):
     t = time.time()
     host = build_store(moe, host_layers)
     setup_s = time.time() - t
+    log(f"store built ({setup_s:.1f}s)")
     gen = torch.Generator(device="cuda").manual_seed(100 + rank)
     Bs = max(sweep)
     xs = torch.randn(L, Bs, d, generator=gen, device="cuda")
@@ -825,6 +838,7 @@ def run_ours(a):
     # the headline batch runs last, with the clocks sampled over >= 1 s of
     # warm-up replays and then its timed region
     for B in [b for b in sweep if b != a.batch] + [a.batch]:
+        log(f"moe layer B={B}")
         U = routing_unions(moe, xs, B)
         if B == a.batch:
             with Clocks(local) as clk:
@@ -878,11 +892,13 @@ def run_ours(a):
     line["clocks"] = clocks
     line["gpu_launches"] = launches_per_step(a.batch) * a.steps
     if a.e2e:
+        log("e2e drop-in")
         e2e, keep = e2e_dropin(host, a.batch, max(2, a.steps // 4), 1)
         line["e2e"] = e2e
     if a.cpu:
         cb = {}
         for B in sorted({1, a.batch}):
+            log(f"cpu moe sample B={B}")
             c = run_isolated("cpu_moe_sample", B=B)
             if c is not None and "value" in c:
                 cb[str(B)] = c
@@ -892,6 +908,7 @@ def run_ours(a):
         line["cpu_baseline"] = cb.get(str(a.batch))
         line["cpu_baseline_per_batch"] = cb
     if a.micro:
+        log("microbench")
         line["microbench"] = microbench(moe, a, hbm, peak_kind)
     if a.decode_sweep:
         moe.close()
@@ -941,6 +958,7 @@ def decode_headline(a, line, fd):
     if a.cpu:
         cb = {}
         for B in sorted({1, a.batch}):
+            log(f"cpu decode sample B={B}")
             c = run_isolated("cpu_decode_sample", timeout_s=900, B=B, ctx=a.ctx)
             if c is not None and "value" in c:
                 cb[str(B)] = c

@@ -174,6 +174,20 @@ int jl_moe_destroy(jl_moe* h);
 #define JL_CREATE_ROUTER_ONLY 1
 int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags, jl_moe** out);
 
+/* jl_moe_create for stores larger than HBM: all L layers' repacked records
+ * live in pinned host memory and only `resident_layers` of them in HBM at a
+ * time. A forward of a layer that is not resident first copies it in
+ * (cudaMemcpyAsync on the handle's side stream, into the least recently used
+ * slot once that slot's last reader has finished; the forward's stream waits
+ * for the copy), and every forward prefetches the next layer into another
+ * slot, so in-order decode overlaps the copy of layer l+1 with the kernels
+ * of layer l. Results are identical to a resident store. Staged handles
+ * cannot be captured into CUDA graphs (their copies run on a stream of their
+ * own) and cannot serve jl_ep_create. Replaces the reference's on-demand
+ * expert loading from its memory-mapped store (decoder3.py:329-367,
+ * q4_store.py:169-200). */
+int jl_moe_create_staged(const KernelCfg* cfg, int max_tokens, int resident_layers, jl_moe** out);
+
 /* Upload layer l: router rows gate_w [E, d] bf16 and, for each part p in
  * (gate, up, down) and expert e, the Q4 record pk[p*E+e] / sc[p*E+e] in the
  * reference layout (the pointers decoder3.py:355-361 builds). Pointers may

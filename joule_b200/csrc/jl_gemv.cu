@@ -32,12 +32,17 @@ namespace jl {
 constexpr int kGvWarps = 8;     // warps per block
 constexpr int kGvMaxTok = 4;    // B <= 4
 constexpr int kGvPiece = 4 * kGvMaxTok * 32;  // floats per stored piece: [4 records][tokens][32 lanes]
+constexpr int kMaxUnion = 256;  // union experts (E <= 256)
+
+// B*k: the slots of the batch (uh[U])
+__device__ __forceinline__ int uh_s_total(const jl_ws& ws, int U) { return ws.uh[U]; }
 
 // Owner warp of K-step q when Q steps are cut into NW contiguous ranges
 // [w*Q/NW, (w+1)*Q/NW) (NW <= Q, so every range is non-empty).
-__device__ __forceinline__ int owner(long long q, long long Q, int NW) {
-    return (int)(((q + 1) * NW - 1) / Q);
+__device__ __forceinline__ int owner(int q, int Q, int NW) {
+    return (int)(((long long)(q + 1) * NW - 1) / Q);
 }
+__device__ __forceinline__ int range_start(int w, int Q, int NW) { return (int)((long long)w * Q / NW); }
 
 struct rec4 {
     uint4 a[4][2];   // record r: bytes 0-15 and 16-31 of this lane's row group
@@ -129,13 +134,25 @@ __device__ __forceinline__ bool piece_done(float (&acc)[4][NT], int nt, int unit
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[i][t] = 0.0f;
-    for (int q = 0; q < np; q++) {
-        const float* pp = parts + ((size_t)unit * 64 + q) * kGvPiece;
+    // pieces in order; loads of 8 pieces are in flight before their adds
+    for (int q0 = 0; q0 < np; q0 += 8) {
+        float v[8][4][NT];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int j = 0; j < 8; j++) {
+            const float* pp = parts + ((size_t)unit * 64 + q0 + j) * kGvPiece;
 #pragma unroll
-            for (int t = 0; t < NT; t++)
-                if (t < nt) acc[i][t] = __fadd_rn(acc[i][t], __ldcg(pp + (i * kGvMaxTok + t) * 32 + lane));
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int t = 0; t < NT; t++)
+                    v[j][i][t] = (q0 + j < np && t < nt) ? __ldcg(pp + (i * kGvMaxTok + t) * 32 + lane) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (q0 + j < np)
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int t = 0; t < NT; t++) acc[i][t] = __fadd_rn(acc[i][t], v[j][i][t]);
     }
     if (lane == 0) counters[unit] = 0;  // every piece has arrived: ready for the next launch
     return true;
@@ -148,6 +165,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_gateup_gemv(const uint8_t* __
                                                                int k, const float* __restrict__ x, int B,
                                                                jl_ws ws) {
     extern __shared__ __align__(16) float x_s[];  // [B][d]
+    __shared__ int sel_s[kMaxUnion], uh_s[kMaxUnion + 1], tok_s[kGvMaxTok * 16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = L.d, m = L.m, ngd = L.ngd, MT = m / 64;
     long long* tr = blockIdx.x == 0 ? ws.trace : nullptr;
@@ -156,52 +174,55 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_gateup_gemv(const uint8_t* __
     griddep_launch_dependents();
     trace_point(tr, kTraceGateup, 1);
     const int U = *ws.U;
+    const int Q = U * MT * ngd;
+    const int NW = min((int)gridDim.x * kGvWarps, Q);
+    const int wg = blockIdx.x * kGvWarps + warp;
+    // this warp's first K-step: its weights go out before anything else
+    const int q0 = wg < NW ? range_start(wg, Q, NW) : 0, q1 = wg < NW ? range_start(wg + 1, Q, NW) : 0;
+    auto addr = [&](int q, const int* sel) {
+        const int unit = q / ngd, g = q - unit * ngd;
+        const int u = unit / MT, mt = unit - u * MT;
+        return store_l + (size_t)sel[u] * L.rec_bytes + L.tile_off(0, 2 * mt, g);
+    };
+    rec4 cur, nxt;
+    if (wg < NW) load_rec4(addr(q0, ws.sel), lane, cur);
+    for (int i = threadIdx.x; i < U; i += blockDim.x) sel_s[i] = ws.sel[i];
+    for (int i = threadIdx.x; i <= U; i += blockDim.x) uh_s[i] = ws.uh[i];
+    for (int i = threadIdx.x; i < B * k; i += blockDim.x) tok_s[i] = ws.uidx[i];
     for (int i = threadIdx.x; i < B * d / 4; i += blockDim.x)
         reinterpret_cast<float4*>(x_s)[i] = reinterpret_cast<const float4*>(x)[i];
     __syncthreads();
     trace_point(tr, kTraceGateup, 2);
-    const long long Q = (long long)U * MT * ngd;
-    const int NW = (int)min((long long)gridDim.x * kGvWarps, Q);
-    const int wg = blockIdx.x * kGvWarps + warp;
     if (wg >= NW) return;
-    const long long q0 = (long long)wg * Q / NW, q1 = (long long)(wg + 1) * Q / NW;
-    auto addr = [&](long long q) {
-        const int unit = (int)(q / ngd), g = (int)(q % ngd);
-        const int e = ws.sel[unit / MT], mt = unit % MT;
-        return store_l + (size_t)e * L.rec_bytes + L.tile_off(0, 2 * mt, g);
-    };
-    rec4 cur, nxt;
-    load_rec4(addr(q0), lane, cur);
     float acc[4][NT];
     int unit = -1, nt = 0, s0 = 0;
     const float* xs[NT];
-    for (long long q = q0; q < q1; q++) {
-        const int qu = (int)(q / ngd), g = (int)(q % ngd);
+    for (int q = q0; q < q1; q++) {
+        const int qu = q / ngd, g = q - qu * ngd;
         if (qu != unit) {
             unit = qu;
             const int u = unit / MT;
-            s0 = ws.uh[u];
-            nt = min(NT, ws.uh[u + 1] - s0);
+            s0 = uh_s[u];
+            nt = min(NT, uh_s[u + 1] - s0);
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 acc[0][t] = acc[1][t] = acc[2][t] = acc[3][t] = 0.0f;
-                xs[t] = x_s + (size_t)(t < nt ? ws.uidx[s0 + t] / k : 0) * d;
+                xs[t] = x_s + (size_t)(t < nt ? tok_s[s0 + t] / k : 0) * d;
             }
         }
-        if (q + 1 < q1) load_rec4(addr(q + 1), lane, nxt);
+        if (q + 1 < q1) load_rec4(addr(q + 1, sel_s), lane, nxt);
         const float* xg[NT];
 #pragma unroll
         for (int t = 0; t < NT; t++) xg[t] = xs[t] + g * 64;
         step_dot<NT>(cur, xg, nt, acc);
         cur = nxt;
-        const bool last = (q + 1 == q1) || ((q + 1) % ngd == 0);
-        if (last) {
-            const long long fq = (long long)unit * ngd;
+        if (q + 1 == q1 || g == ngd - 1) {
+            const int fq = unit * ngd;
             const int pw0 = owner(fq, Q, NW), pw1 = owner(fq + ngd - 1, Q, NW);
             if (piece_done<NT>(acc, nt, unit, wg - pw0, pw1 - pw0 + 1, ws.gv_parts, ws.gv_count)) {
                 const int mt = unit % MT;
                 for (int t = 0; t < nt; t++) {
-                    float* a = ws.act + (size_t)ws.uidx[s0 + t] * m + mt * 64 + lane;
+                    float* a = ws.act + (size_t)tok_s[s0 + t] * m + mt * 64 + lane;
                     a[0] = silu_mul(acc[0][t], acc[2][t]);
                     a[32] = silu_mul(acc[1][t], acc[3][t]);
                 }
@@ -218,44 +239,56 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_gateup_gemv(const uint8_t* __
 template <int NT>
 __global__ void __launch_bounds__(kGvWarps * 32) k_down_gemv(const uint8_t* __restrict__ store_l, jl_layout L,
                                                              jl_ws ws, int span) {
-    extern __shared__ __align__(16) float a_s[];  // [units this block touches (<= 4)][NT][m]
+    extern __shared__ __align__(16) float a_s[];  // [span experts][NT][m]
+    __shared__ int sel_s[kMaxUnion], uh_s[kMaxUnion + 1], slot_s[kGvMaxTok * 16];
+    __shared__ float w_s[kGvMaxTok * 16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = L.d, m = L.m, ngm = L.ngm, MT = d / 128;
-    const int U = *ws.U;  // the router's output: complete before gate/up released this grid
-    const long long Q = (long long)U * MT * ngm;
-    const int NW = (int)min((long long)gridDim.x * kGvWarps, Q);
+    // The routing is the router's output, complete before gate/up released
+    // this grid: read it (and this warp's first weights) before the wait.
+    const int U = *ws.U;
+    const int Q = U * MT * ngm;
+    const int NW = min((int)gridDim.x * kGvWarps, Q);
     const int wg = blockIdx.x * kGvWarps + warp;
     const bool active = wg < NW;
-    const long long q0 = active ? (long long)wg * Q / NW : 0, q1 = active ? (long long)(wg + 1) * Q / NW : 0;
-    auto addr = [&](long long q) {
-        const int unit = (int)(q / ngm), g = (int)(q % ngm);
-        const int e = ws.sel[unit / MT], mt = unit % MT;
-        return store_l + (size_t)e * L.rec_bytes + L.tile_off(2, 4 * mt, g);
+    const int q0 = active ? range_start(wg, Q, NW) : 0, q1 = active ? range_start(wg + 1, Q, NW) : 0;
+    auto addr = [&](int q, const int* sel) {
+        const int unit = q / ngm, g = q - unit * ngm;
+        const int u = unit / MT, mt = unit - u * MT;
+        return store_l + (size_t)sel[u] * L.rec_bytes + L.tile_off(2, 4 * mt, g);
     };
     long long* tr = blockIdx.x == 0 ? ws.trace : nullptr;
     trace_point(tr, kTraceDown, 0);
     rec4 cur, nxt;
-    if (active) load_rec4(addr(q0), lane, cur);  // weights before the wait: they do not depend on gate/up
+    if (active) load_rec4(addr(q0, ws.sel), lane, cur);
+    for (int i = threadIdx.x; i < U; i += blockDim.x) sel_s[i] = ws.sel[i];
+    for (int i = threadIdx.x; i <= U; i += blockDim.x) uh_s[i] = ws.uh[i];
+    const int S = uh_s_total(ws, U);
+    for (int i = threadIdx.x; i < S; i += blockDim.x) {
+        slot_s[i] = ws.uidx[i];
+        w_s[i] = ws.uw[i];
+    }
     griddep_wait();
     griddep_launch_dependents();
     trace_point(tr, kTraceDown, 1);
-    // the block's experts: union positions from the first warp's to the last warp's
+    // the block's experts: union positions from its first warp's to its last warp's
     const int wb0 = blockIdx.x * kGvWarps;
-    const int wb1 = min(wb0 + kGvWarps, NW) - 1;
     if (wb0 >= NW) return;
-    const long long bq0 = (long long)wb0 * Q / NW, bq1 = (long long)(wb1 + 1) * Q / NW - 1;
-    const int u_lo = (int)(bq0 / ngm) / MT, u_hi = (int)(bq1 / ngm) / MT;
+    const int wb1 = min(wb0 + kGvWarps, NW) - 1;
+    const int bq0 = range_start(wb0, Q, NW), bq1 = range_start(wb1 + 1, Q, NW) - 1;
+    const int u_lo = (bq0 / ngm) / MT, u_hi = (bq1 / ngm) / MT;
     if (u_hi - u_lo + 1 > span) {  // more experts than the staging area holds (host bound violated)
         if (threadIdx.x == 0) atomicOr(ws.err, kErrCapacity);
         return;
     }
+    __syncthreads();
     for (int uu = u_lo; uu <= u_hi; uu++) {
-        const int s0 = ws.uh[uu], nt = min(NT, ws.uh[uu + 1] - s0);
+        const int s0 = uh_s[uu], nt = min(NT, uh_s[uu + 1] - s0);
         float* dst = a_s + (size_t)(uu - u_lo) * NT * m;
         for (int i = threadIdx.x; i < nt * m / 4; i += blockDim.x) {
             const int t = i / (m / 4), c = i % (m / 4);
             reinterpret_cast<float4*>(dst + (size_t)t * m)[c] =
-                reinterpret_cast<const float4*>(ws.act + (size_t)ws.uidx[s0 + t] * m)[c];
+                reinterpret_cast<const float4*>(ws.act + (size_t)slot_s[s0 + t] * m)[c];
         }
     }
     __syncthreads();
@@ -263,34 +296,33 @@ __global__ void __launch_bounds__(kGvWarps * 32) k_down_gemv(const uint8_t* __re
     float acc[4][NT];
     int unit = -1, nt = 0, s0 = 0;
     const float* as[NT];
-    for (long long q = q0; q < q1; q++) {
-        const int qu = (int)(q / ngm), g = (int)(q % ngm);
+    for (int q = q0; q < q1; q++) {
+        const int qu = q / ngm, g = q - qu * ngm;
         if (qu != unit) {
             unit = qu;
             const int u = unit / MT;
-            s0 = ws.uh[u];
-            nt = min(NT, ws.uh[u + 1] - s0);
+            s0 = uh_s[u];
+            nt = min(NT, uh_s[u + 1] - s0);
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 acc[0][t] = acc[1][t] = acc[2][t] = acc[3][t] = 0.0f;
                 as[t] = a_s + ((size_t)(u - u_lo) * NT + (t < nt ? t : 0)) * m;
             }
         }
-        if (q + 1 < q1) load_rec4(addr(q + 1), lane, nxt);
+        if (q + 1 < q1) load_rec4(addr(q + 1, sel_s), lane, nxt);
         const float* ag[NT];
 #pragma unroll
         for (int t = 0; t < NT; t++) ag[t] = as[t] + g * 64;
         step_dot<NT>(cur, ag, nt, acc);
         cur = nxt;
-        const bool last = (q + 1 == q1) || ((q + 1) % ngm == 0);
-        if (last) {
-            const long long fq = (long long)unit * ngm;
+        if (q + 1 == q1 || g == ngm - 1) {
+            const int fq = unit * ngm;
             const int pw0 = owner(fq, Q, NW), pw1 = owner(fq + ngm - 1, Q, NW);
             if (piece_done<NT>(acc, nt, unit, wg - pw0, pw1 - pw0 + 1, ws.gv_parts_dn, ws.gv_count_dn)) {
                 const int mt = unit % MT;
                 for (int t = 0; t < nt; t++) {
-                    const int pos = s0 + t, slot = ws.uidx[pos];
-                    const float w = ws.uw[pos];
+                    const int slot = slot_s[s0 + t];
+                    const float w = w_s[s0 + t];
                     float* y = ws.y + (size_t)slot * d + mt * 128 + lane;
 #pragma unroll
                     for (int i = 0; i < 4; i++) y[32 * i] = __fadd_rn(0.0f, __fmul_rn(w, acc[i][t]));

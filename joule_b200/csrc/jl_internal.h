@@ -96,7 +96,27 @@ struct jl_moe {
     size_t pinned_bytes;
     uint8_t* dev_stage;       // device staging: one expert's reference records, or one layer's router rows
     size_t dev_stage_bytes;
+    // staged store (jl_moe_create_staged): all L layers in pinned host memory,
+    // `resident` of them in HBM slots, copied in on a side stream
+    int staged;
+    int resident;
+    uint8_t* host_store;      // [L, E] records, pinned host memory
+    uint8_t* dev_rec;         // one repacked expert record on its way to host_store
+    int* slot_layer;          // [resident] layer held by each slot (-1: none)
+    int* layer_slot;          // [L] slot holding each layer (-1: not resident)
+    long long* slot_used;     // [resident] last use (least recently used slot is refilled)
+    long long use_clock;
+    cudaEvent_t* ev_ready;    // [resident] copy into the slot finished
+    cudaEvent_t* ev_free;     // [resident] last kernel reading the slot finished
+    cudaStream_t side;        // the copy stream
 };
+
+// The device records of layer l for a forward on stream s: for a staged
+// store, the layer's slot (its copy enqueued on the side stream first when
+// it is not resident; s then waits for it). jl_moe_layer_done records the
+// slot's release after the forward's kernels and prefetches the next layer.
+int jl_moe_layer_store(jl_moe* h, int l, cudaStream_t s, const uint8_t** out);
+int jl_moe_layer_done(jl_moe* h, int l, cudaStream_t s);
 
 // ---- launchers (return JL_OK or JL_ERR_*) --------------------------------
 

@@ -1,5 +1,6 @@
 // Handle, store upload and the layer forward of the C ABI (joule_moe.h).
 #include <algorithm>
+#include <climits>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -148,7 +149,18 @@ extern "C" int jl_moe_create(const KernelCfg* cfg, int max_tokens, jl_moe** out)
     return jl_moe_create_ex(cfg, max_tokens, 0, out);
 }
 
+static int create_impl(const KernelCfg* cfg, int max_tokens, int flags, int resident, jl_moe** out);
+
 extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags, jl_moe** out) {
+    return create_impl(cfg, max_tokens, flags, 0, out);
+}
+
+extern "C" int jl_moe_create_staged(const KernelCfg* cfg, int max_tokens, int resident_layers, jl_moe** out) {
+    if (!cfg || resident_layers < 1 || resident_layers > cfg->L) return JL_ERR_INVALID;
+    return create_impl(cfg, max_tokens, 0, resident_layers, out);
+}
+
+static int create_impl(const KernelCfg* cfg, int max_tokens, int flags, int resident, jl_moe** out) {
     if (!out || (flags & ~JL_CREATE_ROUTER_ONLY)) return JL_ERR_INVALID;
     *out = nullptr;
     int rc = check_shape(cfg);
@@ -178,7 +190,9 @@ extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags,
     h->lay.dn_off = (size_t)(h->m / 64) * h->lay.ngd * 4 * 1088;
     h->lay.rec_bytes = h->lay.dn_off + (size_t)(h->d / 128) * h->lay.ngm * 4 * 1088;
     h->router_only = (flags & JL_CREATE_ROUTER_ONLY) ? 1 : 0;
-    h->store_bytes = h->router_only ? 0 : (size_t)h->L * h->E * h->lay.rec_bytes;
+    h->staged = resident > 0 ? 1 : 0;
+    h->resident = resident;
+    h->store_bytes = h->router_only ? 0 : (size_t)(h->staged ? resident : h->L) * h->E * h->lay.rec_bytes;
     const ws_plan wp = plan_ws(max_tokens, h->E, h->k, h->d, h->m);
     h->ws_bytes = wp.total;
     h->dev_stage_bytes = std::max(h->lay.rec_bytes, (size_t)h->E * h->d * 2);
@@ -230,6 +244,31 @@ extern "C" int jl_moe_create_ex(const KernelCfg* cfg, int max_tokens, int flags,
     // epilogue write only a tile's real rows, and the pad rows may feed only
     // accumulator columns that the epilogues drop, so a pad that ever reached a
     // result would show up as NaN in it.
+    if (h->staged) {
+        const size_t host_bytes = (size_t)h->L * h->E * h->lay.rec_bytes;
+        h->slot_layer = (int*)malloc(sizeof(int) * resident);
+        h->layer_slot = (int*)malloc(sizeof(int) * h->L);
+        h->slot_used = (long long*)calloc(resident, sizeof(long long));
+        h->ev_ready = (cudaEvent_t*)calloc(resident, sizeof(cudaEvent_t));
+        h->ev_free = (cudaEvent_t*)calloc(resident, sizeof(cudaEvent_t));
+        bool ok = h->slot_layer && h->layer_slot && h->slot_used && h->ev_ready && h->ev_free &&
+                  cudaHostAlloc(&h->host_store, host_bytes, cudaHostAllocDefault) == cudaSuccess &&
+                  cudaMalloc(&h->dev_rec, h->lay.rec_bytes) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&h->side, cudaStreamNonBlocking) == cudaSuccess;
+        for (int i = 0; ok && i < resident; i++) {
+            ok = cudaEventCreateWithFlags(&h->ev_ready[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&h->ev_free[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventRecord(h->ev_free[i], h->side) == cudaSuccess &&
+                 cudaEventRecord(h->ev_ready[i], h->side) == cudaSuccess;
+            if (ok) h->slot_layer[i] = -1;
+        }
+        if (!ok) {
+            cudaGetLastError();
+            jl_moe_destroy(h);
+            return JL_ERR_OOM;
+        }
+        for (int l = 0; l < h->L; l++) h->layer_slot[l] = -1;
+    }
     if (cudaMemset(h->ws_base, 0, h->ws_bytes) != cudaSuccess ||
         (h->ws.xc && cudaMemset(h->ws.xc, 0xFF, (wp.xc_plane + wp.ac_plane) * 2 * sizeof(__half)) != cudaSuccess) ||
         cudaMemset(h->gate_w, 0, gw) != cudaSuccess) {
@@ -248,6 +287,21 @@ extern "C" int jl_moe_destroy(jl_moe* h) {
     if (h->ws_base) cudaFree(h->ws_base);
     if (h->dev_stage) cudaFree(h->dev_stage);
     if (h->pinned) cudaFreeHost(h->pinned);
+    if (h->staged) {
+        if (h->side) cudaStreamSynchronize(h->side);
+        for (int i = 0; i < h->resident; i++) {
+            if (h->ev_ready && h->ev_ready[i]) cudaEventDestroy(h->ev_ready[i]);
+            if (h->ev_free && h->ev_free[i]) cudaEventDestroy(h->ev_free[i]);
+        }
+        if (h->side) cudaStreamDestroy(h->side);
+        if (h->host_store) cudaFreeHost(h->host_store);
+        if (h->dev_rec) cudaFree(h->dev_rec);
+        free(h->slot_layer);
+        free(h->layer_slot);
+        free(h->slot_used);
+        free(h->ev_ready);
+        free(h->ev_free);
+    }
     free(h->uploaded);
     delete h;
     return JL_OK;
@@ -291,7 +345,86 @@ extern "C" int jl_moe_set_phase_events(jl_moe* h, void* const* events, int n) {
 extern "C" long long jl_moe_device_bytes(const jl_moe* h) {
     if (!h) return 0;
     return (long long)(h->store_bytes + h->ws_bytes + (size_t)h->L * h->E * router_expert_halves(h->d) * 2 +
-                       h->dev_stage_bytes);
+                       h->dev_stage_bytes + (h->staged ? h->lay.rec_bytes : 0));
+}
+
+// Where expert e of layer l is written on upload: its place in the device
+// store, or (staged store) the one-record device buffer that is then copied
+// to the layer's place in the pinned host store.
+static uint8_t* upload_rec(jl_moe* h, int l, int e) {
+    if (h->staged) return h->dev_rec;
+    return h->store + ((size_t)l * h->E + e) * h->lay.rec_bytes;
+}
+
+static int upload_rec_done(jl_moe* h, int l, int e, cudaStream_t s) {
+    if (!h->staged) return JL_OK;
+    JL_CUDA(cudaMemcpyAsync(h->host_store + ((size_t)l * h->E + e) * h->lay.rec_bytes, h->dev_rec,
+                            h->lay.rec_bytes, cudaMemcpyDeviceToHost, s));
+    return JL_OK;
+}
+
+static void staged_invalidate(jl_moe* h, int l) {
+    if (!h->staged) return;
+    const int sl = h->layer_slot[l];
+    if (sl >= 0) h->slot_layer[sl] = -1;
+    h->layer_slot[l] = -1;
+}
+
+// Enqueue layer l's copy into the least recently used slot that is not
+// `keep` (side stream, after the slot's last reader). Returns the slot.
+static int staged_fill(jl_moe* h, int l, int keep, int* slot_out) {
+    int sl = -1;
+    long long best = LLONG_MAX;
+    for (int i = 0; i < h->resident; i++)
+        if (i != keep && h->slot_used[i] < best) {
+            best = h->slot_used[i];
+            sl = i;
+        }
+    if (sl < 0) return JL_ERR_INVALID;
+    if (h->slot_layer[sl] >= 0) h->layer_slot[h->slot_layer[sl]] = -1;
+    const size_t lb = (size_t)h->E * h->lay.rec_bytes;
+    JL_CUDA(cudaStreamWaitEvent(h->side, h->ev_free[sl], 0));
+    JL_CUDA(cudaMemcpyAsync(h->store + (size_t)sl * lb, h->host_store + (size_t)l * lb, lb, cudaMemcpyHostToDevice,
+                            h->side));
+    JL_CUDA(cudaEventRecord(h->ev_ready[sl], h->side));
+    h->slot_layer[sl] = l;
+    h->layer_slot[l] = sl;
+    h->slot_used[sl] = ++h->use_clock;
+    *slot_out = sl;
+    return JL_OK;
+}
+
+int jl_moe_layer_store(jl_moe* h, int l, cudaStream_t s, const uint8_t** out) {
+    if (!h->staged) {
+        *out = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+        return JL_OK;
+    }
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    JL_CUDA(cudaStreamIsCapturing(s, &cap));
+    if (cap != cudaStreamCaptureStatusNone) return JL_ERR_INVALID;  // copies run on the side stream
+    int sl = h->layer_slot[l];
+    if (sl < 0) {
+        const int rc = staged_fill(h, l, -1, &sl);
+        if (rc) return rc;
+    }
+    h->slot_used[sl] = ++h->use_clock;
+    JL_CUDA(cudaStreamWaitEvent(s, h->ev_ready[sl], 0));
+    *out = h->store + (size_t)sl * h->E * h->lay.rec_bytes;
+    return JL_OK;
+}
+
+int jl_moe_layer_done(jl_moe* h, int l, cudaStream_t s) {
+    if (!h->staged) return JL_OK;
+    const int sl = h->layer_slot[l];
+    if (sl < 0) return JL_ERR_INVALID;
+    JL_CUDA(cudaEventRecord(h->ev_free[sl], s));
+    // prefetch the next layer (decode runs the layers in order) into another slot
+    const int nl = (l + 1) % h->L;
+    if (h->resident > 1 && h->layer_slot[nl] < 0 && h->uploaded[nl]) {
+        int dummy = 0;
+        return staged_fill(h, nl, sl, &dummy);
+    }
+    return JL_OK;
 }
 
 static int part_rows(const jl_moe* h, int p) { return p < 2 ? h->m : h->d; }
@@ -308,9 +441,9 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
     int rc0 = jl_launch_repack_router((const uint16_t*)h->dev_stage, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d),
                                       h->E, h->d, s);
     if (rc0) return rc0;
-    uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    staged_invalidate(h, l);
     for (int e = 0; e < h->E; e++) {
-        uint8_t* rec = store_l + (size_t)e * h->lay.rec_bytes;
+        uint8_t* rec = upload_rec(h, l, e);
         for (int p = 0; p < 3; p++) {
             const unsigned char* src_pk = pk[p * h->E + e];
             const unsigned short* src_sc = sc[p * h->E + e];
@@ -324,6 +457,8 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
             int rc = jl_launch_repack_part(st_pk, st_sc, p, h->lay, rec, s);
             if (rc) return rc;
         }
+        const int rc = upload_rec_done(h, l, e, s);
+        if (rc) return rc;
     }
     JL_CUDA(cudaStreamSynchronize(s));
     h->uploaded[l] = 1;
@@ -339,11 +474,11 @@ extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gat
     int rc0 = jl_launch_repack_router(gate_w, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d), h->E,
                                       h->d, s);
     if (rc0) return rc0;
-    uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    staged_invalidate(h, l);
     const float* src[3] = {w_gate, w_up, w_down};
     const size_t numel = (size_t)h->m * h->d;
     for (int e = 0; e < h->E; e++) {
-        uint8_t* rec = store_l + (size_t)e * h->lay.rec_bytes;
+        uint8_t* rec = upload_rec(h, l, e);
         for (int p = 0; p < 3; p++) {
             uint8_t* st_pk = h->dev_stage;
             uint16_t* st_sc = (uint16_t*)(h->dev_stage + numel / 2);
@@ -352,6 +487,8 @@ extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gat
             rc = jl_launch_repack_part(st_pk, st_sc, p, h->lay, rec, s);
             if (rc) return rc;
         }
+        const int rc = upload_rec_done(h, l, e, s);
+        if (rc) return rc;
     }
     JL_CUDA(cudaStreamSynchronize(s));
     h->uploaded[l] = 1;
@@ -370,7 +507,11 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
         return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
     const unsigned short* gw = h->gate_w + (size_t)l * h->E * router_expert_halves(h->d);
-    const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    const uint8_t* store_l = nullptr;
+    if (!h->router_only) {
+        const int rs = jl_moe_layer_store(h, l, s, &store_l);
+        if (rs) return rs;
+    }
     // Inside stream capture an event record must be an external node to be
     // timed when the graph replays; outside capture it is a plain record.
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -403,6 +544,7 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
     }
     if (!rc && (mask & 4)) rc = jl_launch_combine(h, B, out, top, tw, s);
     if (!rc) rc = mark(3);
+    if (!rc && !h->router_only) rc = jl_moe_layer_done(h, l, s);
     if (rc) return rc;
     h->last_B = B;
     return JL_OK;
@@ -459,7 +601,9 @@ extern "C" int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, co
     if (!h->uploaded[l]) return JL_ERR_NOT_READY;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
-    const uint8_t* store_l = h->store + (size_t)l * h->E * h->lay.rec_bytes;
+    const uint8_t* store_l = nullptr;
+    const int rs = jl_moe_layer_store(h, l, s, &store_l);
+    if (rs) return rs;
     const size_t S = (size_t)B * h->k;
     JL_CUDA(cudaMemcpyAsync(h->ws.top, top, S * 4, cudaMemcpyDeviceToDevice, s));
     JL_CUDA(cudaMemcpyAsync(h->ws.tw, tw, S * 4, cudaMemcpyDeviceToDevice, s));
@@ -469,6 +613,7 @@ extern "C" int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, co
     if (!rc) rc = tc ? jl_launch_gateup_tc(h, store_l, x, B, s) : jl_launch_gateup_exact(h, store_l, x, B, s);
     if (!rc) rc = tc ? jl_launch_down_tc(h, store_l, B, s) : jl_launch_down_exact(h, store_l, B, s);
     if (!rc) rc = jl_launch_combine(h, B, out, nullptr, nullptr, s);
+    if (!rc) rc = jl_moe_layer_done(h, l, s);
     if (rc) return rc;
     h->last_B = B;
     return JL_OK;

@@ -56,15 +56,22 @@ def _stream(stream) -> int | None:
 class MoELayers:
     """All MoE layers of one model on the current CUDA device."""
 
-    def __init__(self, cfg: KernelCfg, max_tokens: int = 64, flags: int = 0):
+    def __init__(self, cfg: KernelCfg, max_tokens: int = 64, flags: int = 0,
+                 resident_layers: int | None = None):
         """flags = CREATE_ROUTER_ONLY: router weights and workspace only (no
-        expert store): upload_router + route."""
+        expert store): upload_router + route. resident_layers: a store larger
+        than HBM (jl_moe_create_staged): all layers in pinned host memory,
+        this many in HBM, copied in on a side stream as the layers run."""
         self._L = get_dll()
         self.cfg = cfg
         self.max_tokens = max_tokens
         h = ctypes.c_void_p()
-        check(self._L.jl_moe_create_ex(ctypes.byref(cfg), max_tokens, flags, ctypes.byref(h)),
-              "jl_moe_create_ex")
+        if resident_layers is not None:
+            check(self._L.jl_moe_create_staged(ctypes.byref(cfg), max_tokens, resident_layers,
+                                               ctypes.byref(h)), "jl_moe_create_staged")
+        else:
+            check(self._L.jl_moe_create_ex(ctypes.byref(cfg), max_tokens, flags, ctypes.byref(h)),
+                  "jl_moe_create_ex")
         self.h = h
 
     # -- lifetime -----------------------------------------------------------

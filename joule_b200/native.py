@@ -75,6 +75,7 @@ SIGNATURES = {
     "jl_moe_create": ([ctypes.POINTER(KernelCfg), _I, ctypes.POINTER(_P)], _I),
     "jl_moe_destroy": ([_P], _I),
     "jl_moe_create_ex": ([ctypes.POINTER(KernelCfg), _I, _I, ctypes.POINTER(_P)], _I),
+    "jl_moe_create_staged": ([ctypes.POINTER(KernelCfg), _I, _I, ctypes.POINTER(_P)], _I),
     "jl_moe_upload_router": ([_P, _I, _P, _I, _P], _I),
     "jl_moe_route": ([_P, _I, _P, _I, _P, _P, _P, _P], _I),
     "jl_moe_forward_routed": ([_P, _I, _P, _I, _P, _P, _P, _P], _I),
