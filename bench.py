@@ -40,6 +40,7 @@ TOL = 1e-3  # max row-relative error of expert outputs (north star)
 DTYPE_TC = ("fp16 x fp16 -> fp32: Q4 weights dequantised to fp16 ((n-8)*s rounded), activations "
             "as fp16 hi + lo pairs, fp32 accumulate")
 DTYPE_EXACT = "f32: Q4 weights, fp32 arithmetic in the reference's order"
+DTYPE_GEMV = "f32: Q4 weights dequantised exactly, fp32 accumulate (another summation order)"
 
 
 _T0 = time.time()
@@ -471,8 +472,10 @@ def run_ep(a, ws, rank, local):
     from joule_b200.moe import PATH_EXACT, MoELayers, make_cfg
     d, E, k, m, L = SHAPE["d"], SHAPE["E"], SHAPE["k"], SHAPE["m"], SHAPE["L"]
     B = a.batch
+    Bs = a.global_batch // ws if a.global_batch else 0  # strong scaling: fixed global batch
+    Bcap = max(B, Bs)
     cfg = make_cfg(L, d, E, k, m, SHAPE["norm"])
-    be = CudaEPBackend(cfg, B, rank, ws)
+    be = CudaEPBackend(cfg, Bcap, rank, ws)
     El = E // ws
     sl = slice(rank * El, (rank + 1) * El)
     dev = torch.device("cuda", local)
@@ -492,7 +495,7 @@ def run_ep(a, ws, rank, local):
     setup_s = time.time() - t
     if a.ep == "p2p":
         from joule_b200.ep import P2PExpertParallelMoE
-        ep = P2PExpertParallelMoE(be, B)
+        ep = P2PExpertParallelMoE(be, Bcap)
     else:
         ep = ExpertParallelMoE(be, E)
     gx = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -609,6 +612,31 @@ def run_ep(a, ws, rank, local):
                     mean_local_union=float(np.mean(Ul)),
                     nvlink_bytes_per_layer_per_rank=nv,
                     nvlink_gbs=nv / (us_layer * 1e-6) / 1e9, nvlink_peak_gbs=770.0)
+    # strong scaling: the global batch a.global_batch (256
+    # sequences) split over the ranks, same layers
+    strong = None
+    if Bs >= 1:
+        xs_s = torch.randn(L, Bs, d, generator=gx, device=dev)
+        for _ in range(2):
+            for l in range(L):
+                ep.forward(l, xs_s[l])
+        barrier(ws)
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(a.steps):
+            for l in range(L):
+                ep.forward(l, xs_s[l])
+        s1.record()
+        s1.synchronize()
+        barrier(ws)
+        ms_s = max_over_ranks(ws, s0.elapsed_time(s1))
+        be.check()
+        strong = dict(global_batch=Bs * ws, batch_per_gpu=Bs, tok_s=Bs * ws * a.steps / (ms_s / 1e3),
+                      ms_per_step=ms_s / a.steps, us_per_layer=ms_s / a.steps * 1e3 / L,
+                      note="one GPU's point: moe_layer per_batch at B = global_batch in the N = 1 line")
+        del xs_s
     # end to end: host x in, host out back, per layer
     xh = torch.randn(L, B, d, generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
     oh = torch.empty(B, d).pin_memory()
@@ -651,6 +679,7 @@ def run_ep(a, ws, rank, local):
                     us_per_layer=us_layer,
                     parity=parity,
                     rows_received_per_layer=[round(float(r.item()), 1) for r in rows_all],
+                    strong_scaling=strong,
                     ep_breakdown=breakdown,
                     clocks=clk.summary(),
                     gpu_launches=L * a.steps * per_layer_launches,
@@ -865,14 +894,15 @@ def run_ours(a):
     line = dict(metric=METRIC, value=head["tok_s"], unit="tok/s", n_gpus=ws, steps=a.steps,
                 warmup=a.warmup, ms_per_step=head["ms_per_step"], higher_is_better=True,
                 scaling="weak", vs_baseline=None,
-                dtype=DTYPE_EXACT if path_of(a.batch) == "exact" else DTYPE_TC,
+                dtype=dtype_of(a.batch),
                 data="synthetic: seeded N(0,0.02) weights quantised to the reference Q4 format, "
                      "x ~ N(0,1)",
                 config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
                             batch=a.batch, layers=L, d=d, E=E, topk=k, intermediate=m,
                             norm_topk_prob=1,
-                            path=("exact (CUDA-core FP32 in the reference's order, bit-identical)"
-                                  if path_of(a.batch) == "exact" else
+                            path=("gemv (stream-K warp-per-row GEMVs, fp32 in another order; "
+                                  "<= 1e-3 row-relative)"
+                                  if path_of(a.batch) == "gemv" else
                                   "tensor-core (tcgen05 grouped GEMM, fp16 weights x fp16 hi+lo "
                                   "activations, fp32 accumulate; <= 1e-3 row-relative)"),
                             l2="not flushed: each step streams >= 1 GB of distinct expert weights "
@@ -880,10 +910,10 @@ def run_ours(a):
                             parallelism="single GPU",
                             store_setup_s=round(setup_s, 1)),
                 per_batch=per_b)
-    kern = "k_gateup_exact" if path_of(a.batch) == "exact" else "k_expert_tc<false>"
+    kern = gateup_kernel(a.batch)
     line["roofline"] = dict(bound="hbm",
                             kernel=f"{kern} (gate + up rows of the union experts, SwiGLU fused; "
-                                   f"phase time includes {'nothing else' if kern == 'k_gateup_exact' else 'the token permute'})",
+                                   f"phase time includes {'nothing else' if kern == 'k_gateup_gemv' else 'the token permute'})",
                             achieved=head["gateup_gbs"], peak=hbm, unit="GB/s",
                             frac=head["gateup_gbs"] / hbm, peak_kind=peak_kind,
                             traffic=traffic_from_profiles(kern, a.batch),
@@ -938,7 +968,7 @@ def decode_headline(a, line, fd):
                warmup=a.warmup, ms_per_step=head["ms_per_step"], higher_is_better=True, scaling="weak",
                vs_baseline=None,
                dtype=("f32 (attention, norms, projections, lm_head in the reference's fp32 order); MoE: "
-                      + (DTYPE_EXACT if path_of(a.batch) == "exact" else DTYPE_TC)),
+                      + dtype_of(a.batch)),
                data="synthetic: seeded random-init weights (bf16 dense N(0,0.02), fp32 lm_head, Q4 experts "
                     "quantised from N(0,0.02)), 512-token contexts of uniform-random ids",
                config=dict(workload=f"Qwen3-30B-A3B decode step, batch B={a.batch} at context {a.ctx}",
@@ -971,14 +1001,22 @@ def decode_headline(a, line, fd):
 
 def path_of(B):
     """The path jl_moe_forward takes (JL_PATH_AUTO) at batch B for this shape."""
-    return "exact" if B <= 3 else "tensor-core"
+    return "gemv" if B <= 4 else "tensor-core"
+
+
+def dtype_of(B):
+    return DTYPE_GEMV if path_of(B) == "gemv" else DTYPE_TC
+
+
+def gateup_kernel(B):
+    return "k_gateup_gemv" if path_of(B) == "gemv" else "k_expert_tc<false>"
 
 
 def launches_per_step(B):
     # per layer: the cluster router (routing, and the dispatch for B <= 32),
     # k_dispatch_fast for B > 32, then
-    #   exact: gate/up, down, combine; tensor-core: permute, gate/up, down, combine
-    return SHAPE["L"] * (1 + (1 if B > 32 else 0) + (3 if path_of(B) == "exact" else 4))
+    #   gemv: gate/up, down, combine; tensor-core: permute, gate/up, down, combine
+    return SHAPE["L"] * (1 + (1 if B > 32 else 0) + (3 if path_of(B) == "gemv" else 4))
 
 
 def traffic_from_profiles(kernel, B):
@@ -1071,7 +1109,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--sweep", default="1,8,32,64")
+    ap.add_argument("--sweep", default="1,8,32,64,256")
+    ap.add_argument("--global-batch", type=int, default=256,
+                    help="N > 1: also time this global batch split over the ranks (strong scaling; 0: off)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--layers", type=int, default=48, help="MoE layers per step (48 = the model)")

@@ -36,7 +36,7 @@
 
 namespace jl {
 
-constexpr int kMvRows = 32;           // rows per matvec block (x 8 lanes = 256 threads)
+constexpr int kMvRows = 16;           // rows per matvec block (x 8 lanes = 128 threads)
 constexpr int kMvTok = 8;             // tokens per pass of a matvec block
 constexpr int kAttnThreads = 128;     // attention block (head dim <= 128)
 constexpr int kNormThreads = 256;
@@ -77,26 +77,64 @@ __device__ __forceinline__ float chain_sum(const float* v, int n) {
 __global__ void __launch_bounds__(kNormThreads) k_rms(float* __restrict__ h, const float* __restrict__ add,
                                                       const uint16_t* __restrict__ w, float eps, int d,
                                                       float* __restrict__ t) {
-    extern __shared__ __align__(16) float sq[];  // [d]
+    extern __shared__ __align__(16) float sm[];  // v [d], squares [d]
+    float* v_s = sm;
+    float* sq = sm + d;
     __shared__ float inv_s;
     griddep_wait();
     griddep_launch_dependents();
-    const int b = blockIdx.x;
-    float* hb = h + (size_t)b * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        float v = hb[i];
-        if (add) {
-            v = __fadd_rn(v, add[(size_t)b * d + i]);
-            hb[i] = v;
+    const int b = blockIdx.x, n4 = d / 4;
+    float4* h4 = reinterpret_cast<float4*>(h + (size_t)b * d);
+    const float4* a4 = add ? reinterpret_cast<const float4*>(add + (size_t)b * d) : nullptr;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * blockDim.x) {  // four float4 loads in flight
+        float4 hv[4], av[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i < n4) {
+                hv[j] = h4[i];
+                if (a4) av[j] = a4[i];
+            }
         }
-        sq[i] = __fmul_rn(v, v);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i >= n4) continue;
+            float4 v = hv[j];
+            if (a4) {
+                v = make_float4(__fadd_rn(v.x, av[j].x), __fadd_rn(v.y, av[j].y), __fadd_rn(v.z, av[j].z),
+                                __fadd_rn(v.w, av[j].w));
+                h4[i] = v;
+            }
+            reinterpret_cast<float4*>(v_s)[i] = v;
+            reinterpret_cast<float4*>(sq)[i] =
+                make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w));
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) inv_s = rms_inv(chain_sum(sq, d), d, eps);
     __syncthreads();
     const float inv = inv_s;
-    for (int i = threadIdx.x; i < d; i += blockDim.x)
-        t[(size_t)b * d + i] = __fmul_rn(__fmul_rn(hb[i], inv), bf16_to_f32(w[i]));
+    const uint2* w4 = reinterpret_cast<const uint2*>(w);  // 4 bf16 per load
+    float4* t4 = reinterpret_cast<float4*>(t + (size_t)b * d);
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * blockDim.x) {
+        uint2 wv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i < n4) wv[j] = __ldg(w4 + i);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i >= n4) continue;
+            const float4 v = reinterpret_cast<const float4*>(v_s)[i];
+            t4[i] = make_float4(__fmul_rn(__fmul_rn(v.x, inv), bf16_to_f32(wv[j].x & 0xFFFFu)),
+                                __fmul_rn(__fmul_rn(v.y, inv), bf16_to_f32(wv[j].x >> 16)),
+                                __fmul_rn(__fmul_rn(v.z, inv), bf16_to_f32(wv[j].y & 0xFFFFu)),
+                                __fmul_rn(__fmul_rn(v.w, inv), bf16_to_f32(wv[j].y >> 16)));
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -139,44 +177,68 @@ __device__ __forceinline__ void fma_chunk(const uint4 w, const float* xp, float&
 
 __host__ __device__ inline int mv_xstride(int K) { return K / 8 + 4; }
 
+// Block (token group blockIdx.x, row blocks blockIdx.y) stages the NT token
+// rows of its group once, then runs RT consecutive tiles of kMvRows rows
+// against them. The token group varies fastest in the grid, so the blocks
+// that read the same weight rows run at about the same time and all but the
+// first find them in L2.
 template <typename WT, int NT>
 __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, const float* __restrict__ x,
                                                     int N, int K, int B, const float* __restrict__ bias,
-                                                    float* __restrict__ out) {
+                                                    float* __restrict__ out, int RT) {
     constexpr int U = mv_traits<WT>::U;
     constexpr int P = 8;  // chunks per load group; the next group is in flight while one is used
     extern __shared__ __align__(16) float x_s[];  // [NT][8][K/8 + 4]
     const int tid = threadIdx.x, j = tid & 7;
-    const int n = blockIdx.x * kMvRows + (tid >> 3);
-    const bool live = n < N;
     const int nc = K / (8 * U), xs = mv_xstride(K);
-    const uint4* wp = reinterpret_cast<const uint4*>(W) + (size_t)(live ? n : 0) * 8 + j;
     const size_t cstride = (size_t)N * 8;  // uint4 per chunk
-    auto load_group = [&](int c0, uint4 (&w)[P]) {
+    const int tile0 = blockIdx.y * RT;
+    auto row_of = [=](int rt) { return (tile0 + rt) * kMvRows + (tid >> 3); };
+    auto load_group = [=](int n, int c0, uint4 (&w)[P]) {
+        const bool live = n < N;
+        const uint4* wp = reinterpret_cast<const uint4*>(W) + (size_t)(live ? n : 0) * 8 + j;
 #pragma unroll
         for (int i = 0; i < P; i++)
             w[i] = (live && c0 + i < nc) ? __ldg(wp + (size_t)(c0 + i) * cstride) : make_uint4(0, 0, 0, 0);
     };
-    uint4 first[P];
-    load_group(0, first);  // weights do not depend on the previous kernel: fetch before the wait
+    uint4 cur[P], nxt[P];
+    load_group(row_of(0), 0, cur);  // weights do not depend on the previous kernel: fetch before the wait
     griddep_wait();
     griddep_launch_dependents();
-    for (int b0 = 0; b0 < B; b0 += NT) {
-        const int nt = min(NT, B - b0);
-        __syncthreads();
-        for (int i = tid; i < nt * K; i += blockDim.x) {
-            const int t = i / K, c = i % K;
-            x_s[(t * 8 + (c & 7)) * xs + (c >> 3)] = x[(size_t)(b0 + t) * K + c];
+    const int b0 = blockIdx.x * NT, nt = min(NT, B - b0);
+    {  // the group's token rows into lane-major rows; float4 loads, four in flight per thread
+        const int n4 = nt * K / 4, k4 = K / 4;
+        for (int i0 = tid; i0 < n4; i0 += 4 * blockDim.x) {
+            float4 r[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                const int i = i0 + jj * blockDim.x;
+                if (i < n4) r[jj] = reinterpret_cast<const float4*>(x + (size_t)b0 * K)[i];
+            }
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                const int i = i0 + jj * blockDim.x;
+                if (i >= n4) continue;
+                const int t = i / k4, c = (i - t * k4) * 4;  // c % 8 is 0 or 4
+                float* dst = x_s + (size_t)(t * 8 + (c & 7)) * xs + (c >> 3);
+                dst[0] = r[jj].x;
+                dst[xs] = r[jj].y;
+                dst[2 * xs] = r[jj].z;
+                dst[3 * xs] = r[jj].w;
+            }
         }
-        __syncthreads();
+    }
+    __syncthreads();
+    for (int rt = 0; rt < RT; rt++) {
+        const int n = row_of(rt);
+        if ((tile0 + rt) * kMvRows >= N) break;  // whole block: past the last row tile
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = 0.0f;
-        uint4 cur[P], nxt[P];
-#pragma unroll
-        for (int i = 0; i < P; i++) cur[i] = first[i];
         for (int c0 = 0; c0 < nc; c0 += P) {
-            if (c0 + P < nc) load_group(c0 + P, nxt);
+            // the next group of this tile, or the first group of the next tile
+            if (c0 + P < nc) load_group(n, c0 + P, nxt);
+            else if (rt + 1 < RT) load_group(row_of(rt + 1), 0, nxt);
 #pragma unroll
             for (int i = 0; i < P; i++) {
                 if (c0 + i < nc) {
@@ -188,14 +250,13 @@ __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, co
 #pragma unroll
             for (int i = 0; i < P; i++) cur[i] = nxt[i];
         }
-        if (b0 + NT < B) load_group(0, first);
 #pragma unroll
         for (int t = 0; t < NT; t++) {
             float a = acc[t];
             a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
             a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
             a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-            if (live && j == 0 && t < nt) {
+            if (n < N && j == 0 && t < nt) {
                 if (bias) a = __fadd_rn(a, bias[n]);
                 out[(size_t)(b0 + t) * N + n] = a;
             }
@@ -246,20 +307,54 @@ struct attn_args {
     int* err;
 };
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Squares of v[0..n) into sq (n % 4 == 0, 16-byte aligned), loads batched.
+__device__ __forceinline__ void squares(const float* __restrict__ v, int n, float* sq) {
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    float4* s4 = reinterpret_cast<float4*>(sq);
+    for (int i0 = threadIdx.x; i0 < n / 4; i0 += 4 * blockDim.x) {
+        float4 r[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i < n / 4) r[j] = v4[i];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i < n / 4)
+                s4[i] = make_float4(__fmul_rn(r[j].x, r[j].x), __fmul_rn(r[j].y, r[j].y), __fmul_rn(r[j].z, r[j].z),
+                                    __fmul_rn(r[j].w, r[j].w));
+        }
+    }
+}
+
+constexpr int kAttnTile = 64;  // positions per K / V tile (two tiles in flight)
+
 __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
     extern __shared__ __align__(16) float sm[];
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, gsz = a.H / a.KH, g = h / gsz;
-    const int kTile = kAttnThreads;
-    // shared layout: q, k, v [hd]; sq [max(qn, kn)] (squares for the norms);
-    // ks [kTile][hd + 1]; sc [maxT]
+    // shared layout: q, k, v [128]; sq [2][sqn] (squares for the norms);
+    // two tiles, each [kAttnTile][hd + 1] (K, padded) or [kAttnTile][hd] (V); sc [maxT]
     float* q_s = sm;
     float* k_s = q_s + 128;
     float* v_s = k_s + 128;
     const int sqn = a.sqn;
-    float* sq = v_s + 128;                       // [2][sqn] (q and k squares)
-    float* ks = sq + 2 * sqn;                    // [kTile][hd + 1]
-    float* sc = ks + kTile * (hd + 1);           // [maxT]
+    float* sq = v_s + 128;
+    const int KP = hd + 4;  // K tile row stride: 16-byte rows for the async copies
+    const int tile_f = kAttnTile * KP;
+    float* tb0 = sq + 2 * sqn;  // tile j is at tb0 + (j & 1) * tile_f
+    float* sc = tb0 + 2 * tile_f;  // [maxT]
     __shared__ float red[kAttnThreads / 32];
     __shared__ float inv_q, inv_k, smax_s, sum_s;
     griddep_wait();
@@ -278,8 +373,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
     }
     // QK-norm
     if (a.qk_type == 2) {  // whole vectors q [qn], k [kn] (decode_kernel.c:1162-1174)
-        for (int i = tid; i < qn; i += blockDim.x) sq[i] = __fmul_rn(row[i], row[i]);
-        for (int i = tid; i < kn; i += blockDim.x) sq[sqn + i] = __fmul_rn(row[qn + i], row[qn + i]);
+        squares(row, qn, sq);
+        squares(row + qn, kn, sq + sqn);
         __syncthreads();
         if (tid == 0) inv_q = rms_inv(chain_sum(sq, qn), qn, a.eps);
         if (tid == 32) inv_k = rms_inv(chain_sum(sq + sqn, kn), kn, a.eps);
@@ -334,30 +429,60 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
         K[(size_t)pos * kn + g * hd + tid] = k_s[tid];
         V[(size_t)pos * kn + g * hd + tid] = v_s[tid];
     }
-    // scores (decode_kernel.c:1212-1218), tiles of kTile positions
     const int T = pos + 1;
+    const int ntiles = (T + kAttnTile - 1) / kAttnTile;
+    // K tiles: rows t0..t0+63 of this KV head in rows of hd + 4 floats (the
+    // per-position chains, thread = position, then meet at most 4-way bank
+    // conflicts, hidden behind their dependent adds); 16-byte cp.async, two
+    // tiles in flight. The row at `own` is not copied (a block of the group
+    // may be writing it): it comes from k_s.
+    auto issue_k = [&](int t0, float* buf) {
+        const int nt = min(kAttnTile, T - t0), c4 = hd / 4;
+        for (int i = tid; i < nt * c4; i += blockDim.x) {
+            const int r = i / c4, c = (i - r * c4) * 4, t = t0 + r;
+            if (t != own) cp_async16(buf + r * KP + c, K + (size_t)t * kn + g * hd + c);
+        }
+        cp_async_commit();
+    };
+    // scores (decode_kernel.c:1212-1218)
     const float scale = sqrtf_fast((float)hd);
     float mx = -1e30f;
-    for (int t0 = 0; t0 < T; t0 += kTile) {
-        const int nt = min(kTile, T - t0);
-        __syncthreads();
-        for (int i = tid; i < nt * hd; i += blockDim.x) {
-            const int r = i / hd, c = i % hd, t = t0 + r;
-            ks[r * (hd + 1) + c] = (t == own) ? k_s[c] : K[(size_t)t * kn + g * hd + c];
+    issue_k(0, tb0);
+    for (int j = 0; j < ntiles; j++) {
+        const int t0 = j * kAttnTile, nt = min(kAttnTile, T - t0);
+        float* buf = tb0 + (j & 1) * tile_f;
+        if (j + 1 < ntiles) {
+            issue_k(t0 + kAttnTile, tb0 + ((j + 1) & 1) * tile_f);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
+        if (own >= t0 && own < t0 + nt && tid < hd) buf[(own - t0) * KP + tid] = k_s[tid];
         __syncthreads();
         if (tid < nt) {
-            const float* kr = ks + tid * (hd + 1);
+            const float* kr = buf + tid * KP;
             float s = 0.0f;
+#pragma unroll 8
             for (int i = 0; i < hd; i++) s = __fadd_rn(s, __fmul_rn(q_s[i], kr[i]));
             const float v = __fdiv_rn(s, scale);
             sc[t0 + tid] = v;
             if (v > mx) mx = v;
         }
+        __syncthreads();  // the buffer is refilled two tiles later
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((tid & 31) == 0) red[tid >> 5] = mx;
+    // V tiles: [kAttnTile][hd] rows, 16-byte cp.async; the first goes out now
+    auto issue_v = [&](int t0, float* buf) {
+        const int nt = min(kAttnTile, T - t0), c4 = hd / 4;
+        for (int i = tid; i < nt * c4; i += blockDim.x) {
+            const int r = i / c4, c = (i - r * c4) * 4, t = t0 + r;
+            if (t != own) cp_async16(buf + r * hd + c, V + (size_t)t * kn + g * hd + c);
+        }
+        cp_async_commit();
+    };
+    issue_v(0, tb0);
     __syncthreads();
     if (tid == 0) {
         float m = red[0];
@@ -381,27 +506,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
     __syncthreads();
     const float sum = sum_s;
     for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
-    __syncthreads();
-    if (tid < hd) {  // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229)
-        const float* vp = V + g * hd + tid;
-        float o = 0.0f;
-        int t = 0;
-        for (; t + 4 <= T; t += 4) {
-            const float v0 = (t == own) ? v_s[tid] : vp[(size_t)t * kn];
-            const float v1 = (t + 1 == own) ? v_s[tid] : vp[(size_t)(t + 1) * kn];
-            const float v2 = (t + 2 == own) ? v_s[tid] : vp[(size_t)(t + 2) * kn];
-            const float v3 = (t + 3 == own) ? v_s[tid] : vp[(size_t)(t + 3) * kn];
-            o = __fadd_rn(o, __fmul_rn(sc[t], v0));
-            o = __fadd_rn(o, __fmul_rn(sc[t + 1], v1));
-            o = __fadd_rn(o, __fmul_rn(sc[t + 2], v2));
-            o = __fadd_rn(o, __fmul_rn(sc[t + 3], v3));
+    // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229)
+    float o = 0.0f;
+    for (int j = 0; j < ntiles; j++) {
+        const int t0 = j * kAttnTile, nt = min(kAttnTile, T - t0);
+        float* buf = tb0 + (j & 1) * tile_f;
+        if (j + 1 < ntiles) {
+            issue_v(t0 + kAttnTile, tb0 + ((j + 1) & 1) * tile_f);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
-        for (; t < T; t++) {
-            const float v0 = (t == own) ? v_s[tid] : vp[(size_t)t * kn];
-            o = __fadd_rn(o, __fmul_rn(sc[t], v0));
+        if (own >= t0 && own < t0 + nt && tid < hd) buf[(own - t0) * hd + tid] = v_s[tid];
+        __syncthreads();
+        if (tid < hd) {
+            const float* vr = buf + tid;
+#pragma unroll 8
+            for (int r = 0; r < nt; r++) o = __fadd_rn(o, __fmul_rn(sc[t0 + r], vr[r * hd]));
         }
-        a.att[(size_t)b * qn + h * hd + tid] = o;
+        __syncthreads();
     }
+    if (tid < hd) a.att[(size_t)b * qn + h * hd + tid] = o;
 }
 
 // K/V append for a batch of positions of one or more sequences (batched
@@ -427,7 +552,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_kv_append(attn_args a) {
     const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
     if (tid < hd) k_s[tid] = row[qn + g * hd + tid];
     if (a.qk_type == 2) {
-        for (int i = tid; i < kn; i += blockDim.x) sq[i] = __fmul_rn(row[qn + i], row[qn + i]);
+        squares(row + qn, kn, sq);
         __syncthreads();
         if (tid == 0) inv_k = rms_inv(chain_sum(sq, kn), kn, a.eps);
         __syncthreads();
@@ -469,51 +594,80 @@ int attn_sqn(int qk_type, int H, int KH, int hd) {
 }
 
 size_t attn_smem(int sqn, int hd, int maxT) {
-    return (size_t)(3 * 128 + 2 * sqn + kAttnThreads * (hd + 1) + maxT) * sizeof(float);
+    const int tile = kAttnTile * (hd + 4);
+    return (size_t)(3 * 128 + 2 * sqn + 2 * tile + maxT) * sizeof(float);
 }
 
 // ---------------------------------------------------------------------------
 // argmax over each logits row, lowest index on ties (the first maximum of an
 // ascending scan with strict '>', as the greedy pick over the reference's
-// logits).
-__global__ void k_argmax(const float* __restrict__ logits, int V, int* __restrict__ tok) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
+// logits). Two launches: blocks (part, b) reduce slices of the row to a
+// (value, index) pair (four float4 loads in flight per thread), then one
+// warp per row reduces the pairs.
+constexpr int kArgParts = 32;
+
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_argmax_part(const float* __restrict__ logits, int V, float* pv, int* pi) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
     griddep_wait();
     griddep_launch_dependents();
-    const int b = blockIdx.x, tid = threadIdx.x;
+    const int part = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int per = (V + kArgParts - 1) / kArgParts;
+    const int lo = part * per, hi = min(V, lo + per);
     const float* r = logits + (size_t)b * V;
-    float best = -__int_as_float(0x7f800000);
-    int idx = INT_MAX;
-    for (int v = tid; v < V; v += blockDim.x) {
-        const float x = r[v];
-        if (x > best) {  // ascending per thread: the first maximum stays
-            best = x;
-            idx = v;
+    float bv = -__int_as_float(0x7f800000);
+    int bi = INT_MAX;
+    for (int i0 = lo + tid; i0 < hi; i0 += 4 * blockDim.x) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            v[j] = i < hi ? r[i] : bv;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = i0 + j * blockDim.x;
+            if (i < hi) better(bv, bi, v[j], i);
         }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ob > best || (ob == best && oi < idx)) {
-            best = ob;
-            idx = oi;
-        }
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        better(bv, bi, ov, oi);
     }
     if ((tid & 31) == 0) {
-        bv[tid >> 5] = best;
-        bi[tid >> 5] = idx;
+        sv[tid >> 5] = bv;
+        si[tid >> 5] = bi;
     }
     __syncthreads();
     if (tid == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
-            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
-                best = bv[w];
-                idx = bi[w];
-            }
-        tok[b] = idx == INT_MAX ? 0 : idx;
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) better(bv, bi, sv[w], si[w]);
+        pv[b * kArgParts + part] = bv;
+        pi[b * kArgParts + part] = bi;
     }
+}
+
+__global__ void k_argmax_fin(const float* __restrict__ pv, const int* __restrict__ pi, int* __restrict__ tok) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int b = blockIdx.x, lane = threadIdx.x;
+    float bv = pv[b * kArgParts + lane];
+    int bi = pi[b * kArgParts + lane];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        better(bv, bi, ov, oi);
+    }
+    if (lane == 0) tok[b] = bi == INT_MAX ? 0 : bi;
 }
 
 // embed_lookup (decode_kernel.c:1597-1600): x[b] = bf16 embed[tok[b]] as fp32.
@@ -565,6 +719,8 @@ struct jl_dec {
     float* att;        // [max_batch, qn]
     float* logits;     // [max_batch, V]
     int* tok;          // [max_batch]
+    float* arg_v;      // [max_batch][kArgParts] argmax partials
+    int* arg_i;
     int* pre_pos;      // [max_batch] positions of a prefill chunk
     int* pre_slot;     // [max_batch] its slot, repeated
     int* err;          // [1]
@@ -592,18 +748,22 @@ int dec_attrs() {
     });
 }
 
+// Row tiles per block: one for a single token group (the most blocks), more
+// when the token rows are staged per block for several groups.
 template <typename WT>
 int launch_mv(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, cudaStream_t s) {
     using namespace jl;
     const int nt = B >= 8 ? 8 : B >= 4 ? 4 : B >= 2 ? 2 : 1;
     const size_t smem = (size_t)nt * 8 * mv_xstride(K) * sizeof(float);
     if (smem > 200 * 1024) return JL_ERR_INVALID;
-    const dim3 grid((N + kMvRows - 1) / kMvRows), block(kMvRows * 8);
+    const int groups = (B + nt - 1) / nt, tiles = (N + kMvRows - 1) / kMvRows;
+    const int RT = groups == 1 ? 1 : 4;
+    const dim3 grid(groups, (tiles + RT - 1) / RT), block(kMvRows * 8);
     switch (nt) {
-        case 8: return launch(k_mv<WT, 8>, grid, block, smem, s, W, x, N, K, B, bias, out);
-        case 4: return launch(k_mv<WT, 4>, grid, block, smem, s, W, x, N, K, B, bias, out);
-        case 2: return launch(k_mv<WT, 2>, grid, block, smem, s, W, x, N, K, B, bias, out);
-        default: return launch(k_mv<WT, 1>, grid, block, smem, s, W, x, N, K, B, bias, out);
+        case 8: return launch(k_mv<WT, 8>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
+        case 4: return launch(k_mv<WT, 4>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
+        case 2: return launch(k_mv<WT, 2>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
+        default: return launch(k_mv<WT, 1>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
     }
 }
 
@@ -640,7 +800,7 @@ extern "C" int jl_dec_destroy(jl_dec* h) {
     if (h->moe) jl_moe_destroy(h->moe);
     void* ptrs[] = {h->embed, h->norm1, h->norm2, h->fnorm, h->qnw, h->knw, h->wqkv, h->wo, h->bqkv, h->lm,
                     h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->logits,
-                    h->tok, h->pre_pos, h->pre_slot, h->err, h->stage};
+                    h->tok, h->arg_v, h->arg_i, h->pre_pos, h->pre_slot, h->err, h->stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete h;
@@ -701,6 +861,8 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
         {(void**)&h->att, (size_t)max_batch * h->qn * 4},
         {(void**)&h->logits, (size_t)max_batch * V * 4},
         {(void**)&h->tok, (size_t)max_batch * 4},
+        {(void**)&h->arg_v, (size_t)max_batch * kArgParts * 4},
+        {(void**)&h->arg_i, (size_t)max_batch * kArgParts * 4},
         {(void**)&h->pre_pos, (size_t)max_batch * 4},
         {(void**)&h->pre_slot, (size_t)max_batch * 4},
         {(void**)&h->err, 16},
@@ -832,7 +994,7 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
         return e == cudaSuccess ? JL_OK : jl_note_cuda(e);
     };
     JL_CUDA(cudaMemcpyAsync(h->h, x, (size_t)B * d * 4, cudaMemcpyDeviceToDevice, s));
-    const size_t nsm = (size_t)d * sizeof(float);
+    const size_t nsm = (size_t)2 * d * sizeof(float);
     attn_args aa;
     aa.qkv = h->qkv, aa.att = h->att, aa.positions = positions, aa.slots = slots, aa.kc = h->kc, aa.vc = h->vc;
     aa.cosb = h->cosb, aa.sinb = h->sinb, aa.L = h->L, aa.H = h->H, aa.KH = h->KH, aa.hd = h->hd, aa.maxT = h->maxT;
@@ -886,7 +1048,11 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
         const int nb = prefill ? 1 : B;
         const float* tx = prefill ? h->t + (size_t)(B - 1) * d : h->t;
         rc = launch_mv<float>(h->lm, tx, h->V, d, nb, nullptr, h->logits, s);
-        if (!rc && tok) rc = launch(k_argmax, dim3(nb), dim3(1024), 0, s, (const float*)h->logits, h->V, tok);
+        if (!rc && tok)
+            rc = launch(k_argmax_part, dim3(kArgParts, nb), dim3(256), 0, s, (const float*)h->logits, h->V,
+                        h->arg_v, h->arg_i);
+        if (!rc && tok) rc = launch(k_argmax_fin, dim3(nb), dim3(32), 0, s, (const float*)h->arg_v,
+                                    (const int*)h->arg_i, tok);
         if (!rc && logits)
             rc = cudaMemcpyAsync(logits, h->logits, (size_t)nb * h->V * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess
                      ? JL_OK

@@ -59,11 +59,6 @@ struct jl_ws {
     __half* xc;        // token tiles: per tile [d/8][2N rows: hi, lo][8] fp16 (UMMA core layout)
     __half* ac;        // SwiGLU activations of the tiles, same layout over m
     size_t xc_plane, ac_plane;  // halves per plane
-    // small-batch GEMV path (jl_gemv.cu): per-M-tile partial sums and arrival counters
-    float* gv_parts;     // gate/up pieces [U x m/64 tiles][64][4 x 4 x 32]
-    float* gv_parts_dn;  // down pieces [U x d/128 tiles][64][4 x 4 x 32]
-    int* gv_count;       // [U x m/64] gate/up arrivals (0 between launches)
-    int* gv_count_dn;    // [U x d/128] down arrivals
 };
 
 // Trace buffer layout: per kernel kind a row of 16 slots of %globaltimer
@@ -172,8 +167,7 @@ int jl_launch_gateup_exact(const jl_moe* h, const uint8_t* store_l, const float*
 int jl_launch_down_exact(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
 int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, cudaStream_t s);
 
-// jl_gemv.cu: small-batch (B <= 4) expert FFN, stream-K GEMVs over all warps.
-size_t jl_gemv_ws_floats(int E, int k, int d, int m, size_t* dn_off, size_t* count_off);
+// jl_gemv.cu: small-batch (B <= 4) expert FFN, warp-per-row GEMVs over all SMs.
 bool jl_gemv_ok(const jl_moe* h, int B);
 int jl_launch_gateup_gemv(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s);
 int jl_launch_down_gemv(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);

@@ -33,19 +33,16 @@ int check_shape(const KernelCfg* c) {
 }
 
 struct ws_plan {
-    size_t off[17];
+    size_t off[16];
     size_t total;
     size_t xc_plane, ac_plane;
-    size_t gv_dn, gv_cnt;  // float offsets of the GEMV path's down pieces and counters
 };
 
 ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
     const size_t S = (size_t)Bmax * k;
     size_t xc_plane = 0, ac_plane = 0;
     const size_t tc_bytes = jl_tc_ws_bytes(Bmax, E, k, d, m, &xc_plane, &ac_plane);
-    size_t gv_dn = 0, gv_cnt = 0;
-    const size_t gv_floats = jl_gemv_ws_floats(E, k, d, m, &gv_dn, &gv_cnt);
-    const size_t sizes[17] = {
+    const size_t sizes[16] = {
         (size_t)Bmax * E * 4,  // logits
         S * 4,                 // top
         S * 4,                 // tw
@@ -62,15 +59,12 @@ ws_plan plan_ws(int Bmax, int E, int k, int d, int m) {
         16,                    // err
         16,                    // (unused)
         tc_bytes,              // tensor-core path: xc, ac, tile table, tile count
-        gv_floats * 4,         // GEMV path: pieces and counters
     };
     ws_plan p;
     p.xc_plane = xc_plane;
     p.ac_plane = ac_plane;
     size_t o = 0;
-    p.gv_dn = gv_dn;
-    p.gv_cnt = gv_cnt;
-    for (int i = 0; i < 17; i++) {
+    for (int i = 0; i < 16; i++) {
         p.off[i] = o;
         o = align_up(o + sizes[i], 256);
     }
@@ -231,14 +225,6 @@ static int create_impl(const KernelCfg* cfg, int max_tokens, int flags, int resi
         t += wp.ac_plane * 2 * sizeof(__half);
         h->ws.tc_ntiles = (int*)t;
         h->ws.tc_tile = (int*)(t + 16);
-    }
-    {
-        float* g = (float*)(b + wp.off[16]);
-        h->ws.gv_parts = g;
-        h->ws.gv_parts_dn = g + wp.gv_dn;
-        h->ws.gv_count = (int*)(g + wp.gv_cnt);
-        const int Ug = std::min(h->E, 4 * h->k);
-        h->ws.gv_count_dn = h->ws.gv_count + (size_t)Ug * (h->m / 64);
     }
     // The tensor-core token tiles start as fp16 NaN: the permute and the gate/up
     // epilogue write only a tile's real rows, and the pad rows may feed only
@@ -645,12 +631,7 @@ extern "C" int jl_moe_check(jl_moe* h, void* stream) {
     int err = 0;
     JL_CUDA(cudaMemcpyAsync(&err, h->ws.err, sizeof(int), cudaMemcpyDeviceToHost, s));
     JL_CUDA(cudaStreamSynchronize(s));
-    if (err) {
-        JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
-        // a launch that failed part-way may have left GEMV arrival counters behind
-        const int Ug = std::min(h->E, 4 * h->k);
-        JL_CUDA(cudaMemsetAsync(h->ws.gv_count, 0, (size_t)Ug * (h->m / 64 + h->d / 128) * sizeof(int), s));
-    }
+    if (err) JL_CUDA(cudaMemsetAsync(h->ws.err, 0, sizeof(int), s));
     JL_CUDA(cudaStreamSynchronize(s));
     if (err & jl::kErrTimeout) return JL_ERR_TIMEOUT;
     if (err) return JL_ERR_DEVICE;
