@@ -33,6 +33,7 @@
 
 #include "jl_common.cuh"
 #include "jl_internal.h"
+#include "jl_mv.cuh"
 
 namespace jl {
 
@@ -144,38 +145,6 @@ __global__ void __launch_bounds__(kNormThreads) k_rms(float* __restrict__ h, con
 // rows staged lane-major in shared memory (x_s[t][j][i] = x[b0+t][j + 8i], rows
 // padded by 4 floats so the 8 lanes' float4 reads hit distinct banks). The
 // block's weight rows are re-read from L2 on later passes.
-template <typename WT>
-struct mv_traits;
-template <>
-struct mv_traits<uint16_t> {
-    static constexpr int U = 8;  // values per 16-byte chunk
-};
-template <>
-struct mv_traits<float> {
-    static constexpr int U = 4;
-};
-
-__device__ __forceinline__ void fma_chunk(const uint4 w, const float* xp, float& acc, uint16_t) {
-    const float4 x0 = *reinterpret_cast<const float4*>(xp);
-    const float4 x1 = *reinterpret_cast<const float4*>(xp + 4);
-    acc = __fmaf_rn(__uint_as_float(w.x << 16), x0.x, acc);
-    acc = __fmaf_rn(__uint_as_float(w.x & 0xFFFF0000u), x0.y, acc);
-    acc = __fmaf_rn(__uint_as_float(w.y << 16), x0.z, acc);
-    acc = __fmaf_rn(__uint_as_float(w.y & 0xFFFF0000u), x0.w, acc);
-    acc = __fmaf_rn(__uint_as_float(w.z << 16), x1.x, acc);
-    acc = __fmaf_rn(__uint_as_float(w.z & 0xFFFF0000u), x1.y, acc);
-    acc = __fmaf_rn(__uint_as_float(w.w << 16), x1.z, acc);
-    acc = __fmaf_rn(__uint_as_float(w.w & 0xFFFF0000u), x1.w, acc);
-}
-__device__ __forceinline__ void fma_chunk(const uint4 w, const float* xp, float& acc, float) {
-    const float4 x0 = *reinterpret_cast<const float4*>(xp);
-    acc = __fmaf_rn(__uint_as_float(w.x), x0.x, acc);
-    acc = __fmaf_rn(__uint_as_float(w.y), x0.y, acc);
-    acc = __fmaf_rn(__uint_as_float(w.z), x0.z, acc);
-    acc = __fmaf_rn(__uint_as_float(w.w), x0.w, acc);
-}
-
-__host__ __device__ inline int mv_xstride(int K) { return K / 8 + 4; }
 
 // Block (token group blockIdx.x, row blocks blockIdx.y) stages the NT token
 // rows of its group once, then runs RT consecutive tiles of kMvRows rows
@@ -264,21 +233,6 @@ __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, co
     }
 }
 
-// W [N, K] (row-major, device) -> the chunked lane-major layout.
-template <typename WT>
-__global__ void k_repack_mv(const WT* __restrict__ src, WT* __restrict__ dst, int N, int K) {
-    constexpr int U = mv_traits<WT>::U;
-    const size_t total = (size_t)N * K;
-    for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
-        // o = ((c * N + n) * 8 + j) * U + u
-        const int u = (int)(o % U);
-        const int j = (int)((o / U) % 8);
-        const size_t cn = o / (8 * U);
-        const int n = (int)(cn % N);
-        const int c = (int)(cn / N);
-        dst[o] = src[(size_t)n * K + j + 8 * (U * c + u)];
-    }
-}
 
 // ---------------------------------------------------------------------------
 // Attention of one (head h, sequence b) (decode_kernel.c:1150-1231): QK-norm,

@@ -373,7 +373,7 @@ struct jl_ep {
 extern "C" int jl_ep_create(jl_moe* local, int rank, int world, int max_tokens, int topk, jl_ep** out) {
     using namespace jl;
     if (!out || !local || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world || max_tokens < 1 ||
-        topk < 1 || local->k != 1 || local->router_only || local->staged)
+        topk < 1 || local->k != 1 || local->router_only || local->staged || local->bf16)
         return JL_ERR_INVALID;
     *out = nullptr;
     const int cap = max_tokens * topk;

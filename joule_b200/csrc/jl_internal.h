@@ -71,6 +71,7 @@ struct jl_moe {
     int sm_count;  // streaming multiprocessors of the device (persistent grids)
     int router_only;  // JL_CREATE_ROUTER_ONLY: router weights and workspace, no expert store
     int L, d, E, k, m, norm;
+    int bf16;                 // bf16 expert tier (KernelCfg.expert_bf16): bf16 matrices, no Q4
     int max_tokens;
     int path;
     jl_layout lay;
@@ -121,7 +122,7 @@ int jl_moe_layer_done(jl_moe* h, int l, cudaStream_t s);
 // callers from several host threads are serialised. key < 32.
 enum {
     kOnceExact = 0, kOnceRouter, kOnceRouterFast, kOnceDispatch, kOnceGemm, kOnceTc, kOnceGemv,
-    kOnceDecode, kOnceEp
+    kOnceDecode, kOnceEp, kOnceBf16
 };
 int jl_device_once(int key, int (*setup)());
 
@@ -171,6 +172,10 @@ int jl_launch_combine(const jl_moe* h, int B, float* out, int* top, float* tw, c
 bool jl_gemv_ok(const jl_moe* h, int B);
 int jl_launch_gateup_gemv(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s);
 int jl_launch_down_gemv(const jl_moe* h, const uint8_t* store_l, int B, cudaStream_t s);
+
+// jl_bf16.cu: the bf16 expert tier (gate/up + SwiGLU, down; the combine follows).
+int jl_launch_bf16_ffn(const jl_moe* h, const uint8_t* store_l, const float* x, int B, cudaStream_t s);
+int jl_repack_bf16_part(const uint16_t* src, int p, const jl_moe* h, uint8_t* rec, cudaStream_t s);
 
 // jl_tc.cu: tensor-core expert FFN (permute -> gate/up+SwiGLU -> down).
 // The tile table is built at the end of the dispatch step (jl_tiles.cuh).

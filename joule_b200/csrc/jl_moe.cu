@@ -28,7 +28,7 @@ int check_shape(const KernelCfg* c) {
     // whole Q4 groups; gate/up M-tiles of 64 rows, down M-tiles of 128 rows
     if (c->d % 128 || c->intermediate % 64) return JL_ERR_INVALID;
     if (c->E > 256 || c->topk > 16 || c->topk > c->E) return JL_ERR_INVALID;
-    if (c->expert_i8 || c->expert_bf16) return JL_ERR_INVALID;       // Q4 store only
+    if (c->expert_i8) return JL_ERR_INVALID;  // Q4 store or the bf16 tier
     return JL_OK;
 }
 
@@ -183,6 +183,8 @@ static int create_impl(const KernelCfg* cfg, int max_tokens, int flags, int resi
     h->lay.ngm = h->m / 64;
     h->lay.dn_off = (size_t)(h->m / 64) * h->lay.ngd * 4 * 1088;
     h->lay.rec_bytes = h->lay.dn_off + (size_t)(h->d / 128) * h->lay.ngm * 4 * 1088;
+    h->bf16 = cfg->expert_bf16 ? 1 : 0;
+    if (h->bf16) h->lay.rec_bytes = (size_t)3 * h->m * h->d * 2;  // gate', up', down' (bf16, chunked)
     h->router_only = (flags & JL_CREATE_ROUTER_ONLY) ? 1 : 0;
     h->staged = resident > 0 ? 1 : 0;
     h->resident = resident;
@@ -430,6 +432,19 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
     staged_invalidate(h, l);
     for (int e = 0; e < h->E; e++) {
         uint8_t* rec = upload_rec(h, l, e);
+        if (h->bf16) {  // pk[p*E + e]: the bf16 matrix itself (decode_kernel.c:1280-1284); no scales
+            for (int p = 0; p < 3; p++) {
+                const unsigned char* src = pk[p * h->E + e];
+                if (!src) return JL_ERR_INVALID;
+                const size_t bytes = (size_t)part_rows(h, p) * part_cols(h, p) * 2;
+                JL_CUDA(cudaMemcpyAsync(h->dev_stage, src, bytes, kind, s));
+                const int rc = jl_repack_bf16_part(reinterpret_cast<const uint16_t*>(h->dev_stage), p, h, rec, s);
+                if (rc) return rc;
+            }
+            const int rc = upload_rec_done(h, l, e, s);
+            if (rc) return rc;
+            continue;
+        }
         for (int p = 0; p < 3; p++) {
             const unsigned char* src_pk = pk[p * h->E + e];
             const unsigned short* src_sc = sc[p * h->E + e];
@@ -454,7 +469,7 @@ extern "C" int jl_moe_upload_layer(jl_moe* h, int l, const unsigned short* gate_
 extern "C" int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
                                      const float* w_gate, const float* w_up, const float* w_down,
                                      void* stream) {
-    if (!h || l < 0 || l >= h->L || !gate_w || !w_gate || !w_up || !w_down || h->router_only)
+    if (!h || l < 0 || l >= h->L || !gate_w || !w_gate || !w_up || !w_down || h->router_only || h->bf16)
         return JL_ERR_INVALID;
     cudaStream_t s = (cudaStream_t)stream;
     int rc0 = jl_launch_repack_router(gate_w, h->gate_w + (size_t)l * h->E * router_expert_halves(h->d), h->E,
@@ -511,11 +526,15 @@ extern "C" int jl_moe_forward_phases(jl_moe* h, int l, const float* x, int B, fl
     };
     int rc = mark(0);
     const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
-    const bool gemv = (h->path == JL_PATH_GEMV || (h->path == JL_PATH_AUTO && B <= kGemvMaxB)) && jl_gemv_ok(h, B);
-    const bool tc = !gemv && (h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok));
+    const bool gemv = !h->bf16 && (h->path == JL_PATH_GEMV || (h->path == JL_PATH_AUTO && B <= kGemvMaxB)) &&
+                      jl_gemv_ok(h, B);
+    const bool tc = !h->bf16 && !gemv && (h->path == JL_PATH_TC || (h->path == JL_PATH_AUTO && B > kExactMaxB && tc_ok));
     if (!rc && (mask & 1)) rc = jl_launch_route(h, gw, x, B, tc, s);
     if (!rc) rc = mark(1);
-    if (gemv) {
+    if (h->bf16) {  // the bf16 tier: one exact path (its kernels cover gate/up and down)
+        if (!rc && (mask & 6)) rc = jl_launch_bf16_ffn(h, store_l, x, B, s);
+        if (!rc) rc = mark(2);
+    } else if (gemv) {
         if (!rc && (mask & 2)) rc = jl_launch_gateup_gemv(h, store_l, x, B, s);
         if (!rc) rc = mark(2);
         if (!rc && (mask & 4)) rc = jl_launch_down_gemv(h, store_l, B, s);
@@ -596,8 +615,12 @@ extern "C" int jl_moe_forward_routed(jl_moe* h, int l, const float* x, int B, co
     const bool tc_ok = h->d % 512 == 0 && h->m % 256 == 0;
     const bool tc = h->path == JL_PATH_TC || ((h->path == JL_PATH_AUTO || h->path == JL_PATH_GEMV) && B > kExactMaxB && tc_ok);
     int rc = jl_launch_dispatch(h, B, s);
-    if (!rc) rc = tc ? jl_launch_gateup_tc(h, store_l, x, B, s) : jl_launch_gateup_exact(h, store_l, x, B, s);
-    if (!rc) rc = tc ? jl_launch_down_tc(h, store_l, B, s) : jl_launch_down_exact(h, store_l, B, s);
+    if (h->bf16) {
+        if (!rc) rc = jl_launch_bf16_ffn(h, store_l, x, B, s);
+    } else {
+        if (!rc) rc = tc ? jl_launch_gateup_tc(h, store_l, x, B, s) : jl_launch_gateup_exact(h, store_l, x, B, s);
+        if (!rc) rc = tc ? jl_launch_down_tc(h, store_l, B, s) : jl_launch_down_exact(h, store_l, B, s);
+    }
     if (!rc) rc = jl_launch_combine(h, B, out, nullptr, nullptr, s);
     if (!rc) rc = jl_moe_layer_done(h, l, s);
     if (rc) return rc;
