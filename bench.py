@@ -828,8 +828,9 @@ def full_decode(a, hbm):
                        "fp32 lm_head, Q4 experts), 48 layers, GQA 32/4 x 128, per-head QK-norm, RoPE theta "
                        "1e6, eps 1e-6, vocab 151936; context 512 uniform-random ids (seed 0) then greedy decode",
                 context=ctx, build_s=round(build_s, 1), prefill_s=round(prefill_s, 1),
-                path="norms, attention, projections and lm_head in the reference's fp32 order on CUDA cores; "
-                     "MoE layers JL_PATH_AUTO (exact for B <= 3, tensor cores above)",
+                path="norms, attention, projections and lm_head in the reference's fp32 order on CUDA cores "
+                     "(register-tiled matvecs from B = 16); MoE layers JL_PATH_AUTO (GEMV path for B <= 4, "
+                     "tensor cores above)",
                 per_batch=res)
 
 
@@ -900,7 +901,7 @@ def run_ours(a):
                 config=dict(workload=f"Qwen3-30B-A3B-shape MoE FFN x48 layers, decode batch B={a.batch}",
                             batch=a.batch, layers=L, d=d, E=E, topk=k, intermediate=m,
                             norm_topk_prob=1,
-                            path=("gemv (stream-K warp-per-row GEMVs, fp32 in another order; "
+                            path=("gemv (warp-per-row GEMVs over every SM, fp32 in another order; "
                                   "<= 1e-3 row-relative)"
                                   if path_of(a.batch) == "gemv" else
                                   "tensor-core (tcgen05 grouped GEMM, fp16 weights x fp16 hi+lo "
@@ -978,7 +979,7 @@ def decode_headline(a, line, fd):
                               "experts of 48 layers vs 126 MB L2",
                            parallelism="single GPU"),
                e2e=head["e2e"], clocks=fd.get("clocks"),
-               gpu_launches=(L * (5 + moe_launches) + 4) * a.steps,
+               gpu_launches=(L * (6 + moe_launches) + 5) * a.steps,
                full_decode=fd)
     for k in ("roofline", "microbench"):
         if k in line:

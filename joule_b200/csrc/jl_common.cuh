@@ -253,6 +253,15 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
         : "memory");
 }
 
+// Per-thread asynchronous global -> shared copies (16 bytes, both addresses
+// 16-byte aligned), completed by commit / wait groups.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // Phase stamp for the optional trace buffer (thread 0 of the calling block).
 __device__ __forceinline__ void trace_point(long long* trace, int kind, int slot) {
     if (trace != nullptr && threadIdx.x == 0) trace[kind * 16 + slot] = (long long)globaltimer_ns();

@@ -8,7 +8,8 @@
 // on its exact path.
 //
 // Per layer: k_rms (h += previous residual, norm1) -> k_mv (QKV, + bias) ->
-// k_attn (QK-norm, RoPE, KV append, softmax attention) -> k_mv (o_proj) ->
+// k_attn_qk (QK-norm, RoPE, KV append, scores) -> k_attn_pv (softmax, values)
+// -> k_mv (o_proj) ->
 // k_rms (h += o, norm2) -> the MoE layer (jl_moe_forward) -> next layer.
 // Then k_rms (final norm) -> k_mv (fp32 lm_head) -> k_argmax.
 //
@@ -235,13 +236,25 @@ __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, co
 
 
 // ---------------------------------------------------------------------------
-// Attention of one (head h, sequence b) (decode_kernel.c:1150-1231): QK-norm,
-// RoPE, the KV append, scores q.k_t for t <= pos (each a sequential sum over
-// the head dimension), scaled by 1/sqrtf_fast(hd), softmax with expf_fast and
-// a sequential sum over t, and att[i] = sum over t of (p_t * v_t[i]) in t
-// order. The block of the first q head of each KV group writes the group's K
-// and V rows at pos; the other blocks of the group use the row they computed
-// themselves for t = pos, so no block reads a row another block is writing.
+// Attention (decode_kernel.c:1150-1231) in two launches.
+//
+// k_attn_qk, block (KV head g, sequence b, position split p): QK-norm and RoPE
+// of the group's q heads and of k, the KV append (split 0), then the scores
+// q.k_t / sqrtf_fast(hd) of the group's heads for the split's positions, each
+// a sequential sum over the head dimension (two chains per thread), into a
+// [B][H][maxT] score buffer. The block that holds
+// position pos uses the k row it computed itself, so no block reads a row
+// another block is writing.
+//
+// k_attn_pv, block (heads h0..h0+hpb of one KV group, sequence b, dimension
+// slice z): per head (one warp each) max over t, p_t = expf_fast(s_t - max),
+// their sum in t order by one lane, p_t /= sum; then att[i] = 0 + p_0 v_0[i]
+// + p_1 v_1[i] + ... in t order for the slice's dimensions of every head, V
+// tiles by 16-byte cp.async, read once for the block's heads (hpb = the group
+// size at large batches; one head per block at small ones, for more blocks).
+//
+// Parallelism is across (group, sequence, positions) and (head, sequence,
+// dimensions); every sum the reference forms sequentially stays one chain.
 struct attn_args {
     const float* qkv;        // [B][qn + 2 kn] (bias added)
     float* att;              // [B][qn]
@@ -256,20 +269,10 @@ struct attn_args {
     int l, L, H, KH, hd, maxT, qk_type;
     int nslots;              // KV cache slots held
     int from_cache;          // 1: this position's K/V rows are already in the cache (k_kv_append ran)
-    int sqn;                 // floats per squares buffer: max(qn, kn) for whole-vector norms, else hd
+    int sqn;                 // floats per squares buffer of k_kv_append: max(qn, kn) for whole-vector norms, else hd
     float eps;
     int* err;
 };
-
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Squares of v[0..n) into sq (n % 4 == 0, 16-byte aligned), loads batched.
 __device__ __forceinline__ void squares(const float* __restrict__ v, int n, float* sq) {
@@ -292,25 +295,40 @@ __device__ __forceinline__ void squares(const float* __restrict__ v, int n, floa
     }
 }
 
-constexpr int kAttnTile = 64;  // positions per K / V tile (two tiles in flight)
+constexpr int kQkThreads = 256;
+constexpr int kQkTile = 64;   // positions per K tile (two tiles in flight)
+constexpr int kPvThreads = 256;
+constexpr int kPvTile = 32;   // positions per V tile (two tiles in flight)
+constexpr int kPvItems = 4;   // (head, dimension pair) items per thread at most (NI of k_attn_pv)
 
-__global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
+// Shared-memory layout of k_attn_qk (floats): q [gsz][hd + 4], k [hd],
+// v [hd], squares, inverse norms [gsz + 1] (padded to 4), two K tiles
+// [kQkTile][hd + 4].
+struct qk_layout {
+    int qs, sq, inv, tiles, total;
+    __host__ __device__ qk_layout(int qk_type, int H, int KH, int hd) {
+        const int gsz = H / KH, qrow = hd + 4;
+        qs = qrow;
+        sq = gsz * qrow + 2 * hd;
+        const int nsq = qk_type == 2 ? (H * hd + 3) / 4 * 4 + (KH * hd + 3) / 4 * 4 : (gsz + 1) * hd;
+        inv = sq + (nsq + 3) / 4 * 4;
+        tiles = inv + (gsz + 4) / 4 * 4;
+        total = tiles + 2 * kQkTile * qrow;
+    }
+};
+
+__global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __restrict__ scores, int tp) {
     extern __shared__ __align__(16) float sm[];
-    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-    const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, gsz = a.H / a.KH, g = h / gsz;
-    // shared layout: q, k, v [128]; sq [2][sqn] (squares for the norms);
-    // two tiles, each [kAttnTile][hd + 1] (K, padded) or [kAttnTile][hd] (V); sc [maxT]
-    float* q_s = sm;
-    float* k_s = q_s + 128;
-    float* v_s = k_s + 128;
-    const int sqn = a.sqn;
-    float* sq = v_s + 128;
-    const int KP = hd + 4;  // K tile row stride: 16-byte rows for the async copies
-    const int tile_f = kAttnTile * KP;
-    float* tb0 = sq + 2 * sqn;  // tile j is at tb0 + (j & 1) * tile_f
-    float* sc = tb0 + 2 * tile_f;  // [maxT]
-    __shared__ float red[kAttnThreads / 32];
-    __shared__ float inv_q, inv_k, smax_s, sum_s;
+    const int g = blockIdx.x, b = blockIdx.y, split = blockIdx.z, tid = threadIdx.x;
+    const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, gsz = a.H / a.KH, h0 = g * gsz;
+    const qk_layout lay(a.qk_type, a.H, a.KH, hd);
+    const int QS = lay.qs, KP = hd + 4;
+    float* q_s = sm;                 // [gsz][QS]
+    float* k_s = sm + gsz * QS;      // [hd]
+    float* v_s = k_s + hd;           // [hd]
+    float* sq = sm + lay.sq;
+    float* inv = sm + lay.inv;
+    float* tb0 = sm + lay.tiles;     // tile j at tb0 + (j & 1) * kQkTile * KP
     griddep_wait();
     griddep_launch_dependents();
     const int pos = a.positions[b];
@@ -319,174 +337,241 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(attn_args a) {
         if (tid == 0) atomicOr(a.err, kErrPosition);
         return;
     }
+    const int T = pos + 1, t_lo = split * tp, t_hi = min(T, t_lo + tp);
+    if (t_lo >= T) return;  // split 0 always has positions (and appends the rows)
     const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
-    if (tid < hd) {
-        q_s[tid] = row[h * hd + tid];
-        k_s[tid] = row[qn + g * hd + tid];
-        v_s[tid] = row[qn + kn + g * hd + tid];
+    for (int i = tid; i < gsz * hd; i += blockDim.x) q_s[(i / hd) * QS + i % hd] = row[h0 * hd + i];
+    for (int i = tid; i < hd; i += blockDim.x) {
+        k_s[i] = row[qn + g * hd + i];
+        v_s[i] = row[qn + kn + g * hd + i];
     }
     // QK-norm
     if (a.qk_type == 2) {  // whole vectors q [qn], k [kn] (decode_kernel.c:1162-1174)
+        const int qn4 = (qn + 3) / 4 * 4;
         squares(row, qn, sq);
-        squares(row + qn, kn, sq + sqn);
+        squares(row + qn, kn, sq + qn4);
         __syncthreads();
-        if (tid == 0) inv_q = rms_inv(chain_sum(sq, qn), qn, a.eps);
-        if (tid == 32) inv_k = rms_inv(chain_sum(sq + sqn, kn), kn, a.eps);
+        if (tid == 0) inv[0] = rms_inv(chain_sum(sq, qn), qn, a.eps);
+        if (tid == 32) inv[1] = rms_inv(chain_sum(sq + qn4, kn), kn, a.eps);
         __syncthreads();
-        if (tid < hd) {
-            q_s[tid] = __fmul_rn(__fmul_rn(q_s[tid], inv_q), bf16_to_f32(a.qnw[h * hd + tid]));
-            k_s[tid] = __fmul_rn(__fmul_rn(k_s[tid], inv_k), bf16_to_f32(a.knw[g * hd + tid]));
+        for (int i = tid; i < gsz * hd; i += blockDim.x) {
+            float* q = q_s + (i / hd) * QS + i % hd;
+            *q = __fmul_rn(__fmul_rn(*q, inv[0]), bf16_to_f32(a.qnw[h0 * hd + i]));
         }
+        for (int i = tid; i < hd; i += blockDim.x)
+            k_s[i] = __fmul_rn(__fmul_rn(k_s[i], inv[1]), bf16_to_f32(a.knw[g * hd + i]));
     } else if (a.qk_type == 1) {  // per head, weights [hd] (decode_kernel.c:1180-1193)
         __syncthreads();
-        if (tid < hd) {
-            sq[tid] = __fmul_rn(q_s[tid], q_s[tid]);
-            sq[sqn + tid] = __fmul_rn(k_s[tid], k_s[tid]);
+        for (int i = tid; i < (gsz + 1) * hd; i += blockDim.x) {
+            const int hh = i / hd, c = i - hh * hd;
+            const float v = hh < gsz ? q_s[hh * QS + c] : k_s[c];
+            sq[i] = __fmul_rn(v, v);
         }
         __syncthreads();
-        if (tid == 0) inv_q = rms_inv(chain_sum(sq, hd), hd, a.eps);
-        if (tid == 32) inv_k = rms_inv(chain_sum(sq + sqn, hd), hd, a.eps);
+        if (tid <= gsz) inv[tid] = rms_inv(chain_sum(sq + tid * hd, hd), hd, a.eps);
         __syncthreads();
-        if (tid < hd) {
-            q_s[tid] = __fmul_rn(__fmul_rn(q_s[tid], inv_q), bf16_to_f32(a.qnw[tid]));
-            k_s[tid] = __fmul_rn(__fmul_rn(k_s[tid], inv_k), bf16_to_f32(a.knw[tid]));
+        for (int i = tid; i < gsz * hd; i += blockDim.x) {
+            float* q = q_s + (i / hd) * QS + i % hd;
+            *q = __fmul_rn(__fmul_rn(*q, inv[i / hd]), bf16_to_f32(a.qnw[i % hd]));
         }
+        for (int i = tid; i < hd; i += blockDim.x)
+            k_s[i] = __fmul_rn(__fmul_rn(k_s[i], inv[gsz]), bf16_to_f32(a.knw[i]));
     }
     __syncthreads();
-    // RoPE, rotate-half (decode_kernel.c:259-266, 1195-1199)
+    // RoPE, rotate-half (decode_kernel.c:259-266, 1195-1199); each item owns its pair
     const int half = hd / 2;
-    float qa = 0.f, qb = 0.f, ka = 0.f, kb = 0.f;
-    if (tid < half) {
-        const float cs = a.cosb[(size_t)pos * hd + tid], sn = a.sinb[(size_t)pos * hd + tid];
-        const float x0 = q_s[tid], x1 = q_s[tid + half];
-        qa = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-        qb = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-        const float y0 = k_s[tid], y1 = k_s[tid + half];
-        ka = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
-        kb = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
-    }
-    __syncthreads();
-    if (tid < half) {
-        q_s[tid] = qa;
-        q_s[tid + half] = qb;
-        k_s[tid] = ka;
-        k_s[tid + half] = kb;
+    for (int it = tid; it < (gsz + 1) * half; it += blockDim.x) {
+        const int hh = it / half, i = it - hh * half;
+        float* v = hh < gsz ? q_s + hh * QS : k_s;
+        const float cs = a.cosb[(size_t)pos * hd + i], sn = a.sinb[(size_t)pos * hd + i];
+        const float x0 = v[i], x1 = v[i + half];
+        v[i] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        v[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
     }
     __syncthreads();
     const size_t cache_off = ((size_t)slot * a.L + a.l) * a.maxT * kn;
-    float* K = a.kc + cache_off;
-    float* V = a.vc + cache_off;
-    // The position whose K/V rows this block holds in registers (-1: every row
-    // comes from the cache, where k_kv_append put this step's rows).
-    const int own = a.from_cache ? -1 : pos;
-    if (!a.from_cache && h % gsz == 0 && tid < hd) {  // KV append (decode_kernel.c:1200-1205)
-        K[(size_t)pos * kn + g * hd + tid] = k_s[tid];
-        V[(size_t)pos * kn + g * hd + tid] = v_s[tid];
-    }
-    const int T = pos + 1;
-    const int ntiles = (T + kAttnTile - 1) / kAttnTile;
-    // K tiles: rows t0..t0+63 of this KV head in rows of hd + 4 floats (the
-    // per-position chains, thread = position, then meet at most 4-way bank
-    // conflicts, hidden behind their dependent adds); 16-byte cp.async, two
-    // tiles in flight. The row at `own` is not copied (a block of the group
-    // may be writing it): it comes from k_s.
-    auto issue_k = [&](int t0, float* buf) {
-        const int nt = min(kAttnTile, T - t0), c4 = hd / 4;
-        for (int i = tid; i < nt * c4; i += blockDim.x) {
-            const int r = i / c4, c = (i - r * c4) * 4, t = t0 + r;
-            if (t != own) cp_async16(buf + r * KP + c, K + (size_t)t * kn + g * hd + c);
+    const float* K = a.kc + cache_off;
+    const int own = a.from_cache ? -1 : pos;  // the row this block takes from k_s
+    if (!a.from_cache && split == 0) {        // KV append (decode_kernel.c:1200-1205)
+        for (int i = tid; i < hd; i += blockDim.x) {
+            a.kc[cache_off + (size_t)pos * kn + g * hd + i] = k_s[i];
+            a.vc[cache_off + (size_t)pos * kn + g * hd + i] = v_s[i];
         }
+    }
+    // tile copies: thread (row r0 + i * rstep, column c) with c fixed per thread
+    const int c4 = hd / 4, rstep = kQkThreads / c4, kr0 = tid / c4, kc = (tid - kr0 * c4) * 4;
+    auto issue_k = [&](int t0, float* buf) {
+        const int nt = min(kQkTile, t_hi - t0);
+        if (kr0 < rstep)
+            for (int r = kr0; r < nt; r += rstep)
+                if (t0 + r != own) cp_async16(buf + r * KP + kc, K + (size_t)(t0 + r) * kn + g * hd + kc);
         cp_async_commit();
     };
-    // scores (decode_kernel.c:1212-1218)
+    // scores (decode_kernel.c:1212-1218): chains (position, head) in pairs
     const float scale = sqrtf_fast((float)hd);
-    float mx = -1e30f;
-    issue_k(0, tb0);
-    for (int j = 0; j < ntiles; j++) {
-        const int t0 = j * kAttnTile, nt = min(kAttnTile, T - t0);
-        float* buf = tb0 + (j & 1) * tile_f;
-        if (j + 1 < ntiles) {
-            issue_k(t0 + kAttnTile, tb0 + ((j + 1) & 1) * tile_f);
+    float* out = scores + ((size_t)b * a.H + h0) * a.maxT;
+    const int ntiles = (t_hi - t_lo + kQkTile - 1) / kQkTile;
+    const int npairs = kQkTile * gsz / 2 + (kQkTile * gsz) % 2;
+    issue_k(t_lo, tb0);
+    for (int jt = 0; jt < ntiles; jt++) {
+        const int t0 = t_lo + jt * kQkTile, nt = min(kQkTile, t_hi - t0);
+        float* buf = tb0 + (jt & 1) * kQkTile * KP;
+        if (jt + 1 < ntiles) {
+            issue_k(t0 + kQkTile, tb0 + ((jt + 1) & 1) * kQkTile * KP);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
-        if (own >= t0 && own < t0 + nt && tid < hd) buf[(own - t0) * KP + tid] = k_s[tid];
+        if (own >= t0 && own < t0 + nt)
+            for (int i = tid; i < hd; i += blockDim.x) buf[(own - t0) * KP + i] = k_s[i];
         __syncthreads();
-        if (tid < nt) {
-            const float* kr = buf + tid * KP;
-            float s = 0.0f;
-#pragma unroll 8
-            for (int i = 0; i < hd; i++) s = __fadd_rn(s, __fmul_rn(q_s[i], kr[i]));
-            const float v = __fdiv_rn(s, scale);
-            sc[t0 + tid] = v;
-            if (v > mx) mx = v;
+        for (int pi = tid; pi < npairs; pi += blockDim.x) {
+            const int ca = 2 * pi, cb = min(2 * pi + 1, kQkTile * gsz - 1);
+            const int ta = ca / gsz, ha = ca - ta * gsz, tb = cb / gsz, hb = cb - tb * gsz;
+            if (ta >= nt) continue;
+            const int tbc = tb < nt ? tb : ta;
+            const float* qa = q_s + ha * QS;
+            const float* qb = q_s + hb * QS;
+            const float* ka = buf + ta * KP;
+            const float* kb = buf + tbc * KP;
+            float s0 = 0.0f, s1 = 0.0f;  // two chains, each a product then a sum per element
+            if (ka == kb) {              // two heads of one position (even group sizes): one k row
+#pragma unroll 4
+                for (int i = 0; i < hd; i += 4) {
+                    const float4 x = *reinterpret_cast<const float4*>(qa + i);
+                    const float4 y = *reinterpret_cast<const float4*>(qb + i);
+                    const float4 u = *reinterpret_cast<const float4*>(ka + i);
+                    s0 = __fadd_rn(s0, __fmul_rn(x.x, u.x));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.x, u.x));
+                    s0 = __fadd_rn(s0, __fmul_rn(x.y, u.y));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.y, u.y));
+                    s0 = __fadd_rn(s0, __fmul_rn(x.z, u.z));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.z, u.z));
+                    s0 = __fadd_rn(s0, __fmul_rn(x.w, u.w));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.w, u.w));
+                }
+            } else {
+#pragma unroll 4
+                for (int i = 0; i < hd; i += 4) {
+                    const float4 x = *reinterpret_cast<const float4*>(qa + i);
+                    const float4 y = *reinterpret_cast<const float4*>(qb + i);
+                    const float4 u = *reinterpret_cast<const float4*>(ka + i);
+                    const float4 w = *reinterpret_cast<const float4*>(kb + i);
+                    s0 = __fadd_rn(s0, __fmul_rn(x.x, u.x));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.x, w.x));
+                    s0 = __fadd_rn(s0, __fmul_rn(x.y, u.y));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.y, w.y));
+                    s0 = __fadd_rn(s0, __fmul_rn(x.z, u.z));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.z, w.z));
+                    s0 = __fadd_rn(s0, __fmul_rn(x.w, u.w));
+                    s1 = __fadd_rn(s1, __fmul_rn(y.w, w.w));
+                }
+            }
+            out[(size_t)ha * a.maxT + t0 + ta] = __fdiv_rn(s0, scale);
+            if (tb < nt && cb != ca) out[(size_t)hb * a.maxT + t0 + tb] = __fdiv_rn(s1, scale);
         }
         __syncthreads();  // the buffer is refilled two tiles later
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
-    // V tiles: [kAttnTile][hd] rows, 16-byte cp.async; the first goes out now
+}
+
+template <int NI>
+__global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float* __restrict__ scores, int hpb,
+                                                         int dw) {
+    extern __shared__ __align__(16) float sm[];
+    const int hb = blockIdx.x, b = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, h0 = hb * hpb, g = h0 / (a.H / a.KH);
+    const int maxT4 = (a.maxT + 3) / 4 * 4;
+    float* p_s = sm;                 // [hpb][maxT4]
+    float* vt0 = sm + hpb * maxT4;   // two V tiles [kPvTile][dw]
+    __shared__ float red[kPvThreads / 32];
+    __shared__ float stat[kPvThreads / 32];
+    griddep_wait();
+    griddep_launch_dependents();
+    const int pos = a.positions[b];
+    const int slot = a.slots[b];
+    if (pos < 0 || pos >= a.maxT || slot < 0 || slot >= a.nslots) return;  // k_attn_qk flagged it
+    const int T = pos + 1, T4 = (T + 3) / 4 * 4;
+    const float* V = a.vc + ((size_t)slot * a.L + a.l) * a.maxT * kn + g * hd + z * dw;
+    const int c4 = dw / 4, rstep = kPvThreads / c4, vr0 = tid / c4, vc = (tid - vr0 * c4) * 4;
     auto issue_v = [&](int t0, float* buf) {
-        const int nt = min(kAttnTile, T - t0), c4 = hd / 4;
-        for (int i = tid; i < nt * c4; i += blockDim.x) {
-            const int r = i / c4, c = (i - r * c4) * 4, t = t0 + r;
-            if (t != own) cp_async16(buf + r * hd + c, V + (size_t)t * kn + g * hd + c);
-        }
+        const int nt = min(kPvTile, T - t0);
+        if (vr0 < rstep)
+            for (int r = vr0; r < nt; r += rstep) cp_async16(buf + r * dw + vc, V + (size_t)(t0 + r) * kn + vc);
         cp_async_commit();
     };
-    issue_v(0, tb0);
-    __syncthreads();
-    if (tid == 0) {
-        float m = red[0];
-        for (int w = 1; w < kAttnThreads / 32; w++) m = fmaxf(m, red[w]);
-        smax_s = m;
+    issue_v(0, vt0);  // the values do not depend on the softmax: first tile now
+    // softmax: head hh by the wph warps [hh * wph, (hh + 1) * wph) (hpb <= 8)
+    const int wph = kPvThreads / 32 / hpb, hh = warp / wph, sub = (warp - hh * wph) * 32 + lane, nsub = wph * 32;
+    float* p = p_s + hh * maxT4;
+    const float* src = scores + ((size_t)b * a.H + h0 + hh) * a.maxT;
+    float mx = -1e30f;
+    for (int t = sub; t < T4; t += nsub) {
+        const float v = t < T ? src[t] : 0.0f;  // pads are +0 for the sum
+        p[t] = v;
+        if (t < T && v > mx) mx = v;
     }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
     __syncthreads();
-    const float smax = smax_s;
-    for (int t = tid; t < T; t += blockDim.x) sc[t] = expf_fast(__fsub_rn(sc[t], smax));
+    mx = red[hh * wph];
+    for (int w = 1; w < wph; w++) mx = fmaxf(mx, red[hh * wph + w]);
+    for (int t = sub; t < T; t += nsub) p[t] = expf_fast(__fsub_rn(p[t], mx));
     __syncthreads();
-    if (tid == 0) {  // sequential sum over t (decode_kernel.c:1220)
-        float s = 0.0f;
-        int t = 0;
-        for (; t + 4 <= T; t += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(sc + t);
-            s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
-        }
-        for (; t < T; t++) s = __fadd_rn(s, sc[t]);
-        sum_s = s;
+    if (sub == 0) stat[hh] = chain_sum(p, T4);  // sequential over t (decode_kernel.c:1220)
+    __syncthreads();
+    const float sum = stat[hh];
+    for (int t = sub; t < T; t += nsub) p[t] = __fdiv_rn(p[t], sum);
+    // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229): items (head, pair of
+    // dimensions), NI per thread, their chains interleaved
+    const int np = dw / 2, items = hpb * np;
+    int ih[NI], ii[NI];
+    float ox[NI], oy[NI];
+#pragma unroll
+    for (int k = 0; k < NI; k++) {
+        const int it = min(tid + k * kPvThreads, items - 1);
+        ih[k] = it / np;
+        ii[k] = it - ih[k] * np;
+        ox[k] = oy[k] = 0.0f;
     }
-    __syncthreads();
-    const float sum = sum_s;
-    for (int t = tid; t < T; t += blockDim.x) sc[t] = __fdiv_rn(sc[t], sum);
-    // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229)
-    float o = 0.0f;
+    const bool live = tid < items;  // the last item's thread set is complete (items <= NI * threads)
+    const int ntiles = (T + kPvTile - 1) / kPvTile;
     for (int j = 0; j < ntiles; j++) {
-        const int t0 = j * kAttnTile, nt = min(kAttnTile, T - t0);
-        float* buf = tb0 + (j & 1) * tile_f;
+        const int t0 = j * kPvTile, nt = min(kPvTile, T - t0);
+        float* buf = vt0 + (j & 1) * kPvTile * dw;
         if (j + 1 < ntiles) {
-            issue_v(t0 + kAttnTile, tb0 + ((j + 1) & 1) * tile_f);
+            issue_v(t0 + kPvTile, vt0 + ((j + 1) & 1) * kPvTile * dw);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
-        if (own >= t0 && own < t0 + nt && tid < hd) buf[(own - t0) * hd + tid] = v_s[tid];
         __syncthreads();
-        if (tid < hd) {
-            const float* vr = buf + tid;
-#pragma unroll 8
-            for (int r = 0; r < nt; r++) o = __fadd_rn(o, __fmul_rn(sc[t0 + r], vr[r * hd]));
+        if (live) {
+#pragma unroll 4
+            for (int r = 0; r < nt; r++) {
+#pragma unroll
+                for (int k = 0; k < NI; k++) {
+                    const float pp = p_s[ih[k] * maxT4 + t0 + r];
+                    const float2 v = *reinterpret_cast<const float2*>(buf + r * dw + 2 * ii[k]);
+                    ox[k] = __fadd_rn(ox[k], __fmul_rn(pp, v.x));
+                    oy[k] = __fadd_rn(oy[k], __fmul_rn(pp, v.y));
+                }
+            }
         }
         __syncthreads();
     }
-    if (tid < hd) a.att[(size_t)b * qn + h * hd + tid] = o;
+#pragma unroll
+    for (int k = 0; k < NI; k++)
+        if (tid + k * kPvThreads < items)
+            *reinterpret_cast<float2*>(a.att + (size_t)b * qn + (h0 + ih[k]) * hd + z * dw + 2 * ii[k]) =
+                make_float2(ox[k], oy[k]);
 }
 
 // K/V append for a batch of positions of one or more sequences (batched
 // prefill, where one launch's positions of a sequence attend to each other):
 // per (KV head g, row b) the K row gets its QK-norm and RoPE exactly as in
-// k_attn, and both rows go into the cache at positions[b]. k_attn then runs
+// k_attn_qk, and both rows go into the cache at positions[b]. k_attn_qk then runs
 // with from_cache = 1.
 __global__ void __launch_bounds__(kAttnThreads) k_kv_append(attn_args a) {
     extern __shared__ __align__(16) float sm[];
@@ -547,10 +632,6 @@ int attn_sqn(int qk_type, int H, int KH, int hd) {
     return (n + 3) / 4 * 4;
 }
 
-size_t attn_smem(int sqn, int hd, int maxT) {
-    const int tile = kAttnTile * (hd + 4);
-    return (size_t)(3 * 128 + 2 * sqn + 2 * tile + maxT) * sizeof(float);
-}
 
 // ---------------------------------------------------------------------------
 // argmax over each logits row, lowest index on ties (the first maximum of an
@@ -671,6 +752,7 @@ struct jl_dec {
     float* h2;         // [max_batch, d]
     float* qkv;        // [max_batch, nqkv]
     float* att;        // [max_batch, qn]
+    float* scores;     // [max_batch, H, maxT] attention scores
     float* logits;     // [max_batch, V]
     int* tok;          // [max_batch]
     float* arg_v;      // [max_batch][kArgParts] argmax partials
@@ -696,7 +778,10 @@ int dec_attrs() {
         JL_CUDA(cudaFuncSetAttribute(k_mv<float, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         JL_CUDA(cudaFuncSetAttribute(k_mv<float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         JL_CUDA(cudaFuncSetAttribute(k_mv<float, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-        JL_CUDA(cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_qk, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_pv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_pv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_pv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         JL_CUDA(cudaFuncSetAttribute(k_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         return JL_OK;
     });
@@ -705,8 +790,10 @@ int dec_attrs() {
 // Row tiles per block: one for a single token group (the most blocks), more
 // when the token rows are staged per block for several groups.
 template <typename WT>
-int launch_mv(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, cudaStream_t s) {
+int launch_mv(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
+              cudaStream_t s) {
     using namespace jl;
+    if (jl_mm_ok(N, K, B)) return jl_launch_mm<WT>(W, x, N, K, B, bias, out, sm_count, s);
     const int nt = B >= 8 ? 8 : B >= 4 ? 4 : B >= 2 ? 2 : 1;
     const size_t smem = (size_t)nt * 8 * mv_xstride(K) * sizeof(float);
     if (smem > 200 * 1024) return JL_ERR_INVALID;
@@ -753,7 +840,7 @@ extern "C" int jl_dec_destroy(jl_dec* h) {
     if (!h) return JL_OK;
     if (h->moe) jl_moe_destroy(h->moe);
     void* ptrs[] = {h->embed, h->norm1, h->norm2, h->fnorm, h->qnw, h->knw, h->wqkv, h->wo, h->bqkv, h->lm,
-                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->logits,
+                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->scores, h->logits,
                     h->tok, h->arg_v, h->arg_i, h->pre_pos, h->pre_slot, h->err, h->stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -813,6 +900,7 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
         {(void**)&h->h2, (size_t)max_batch * d * 4},
         {(void**)&h->qkv, (size_t)max_batch * h->nqkv * 4},
         {(void**)&h->att, (size_t)max_batch * h->qn * 4},
+        {(void**)&h->scores, (size_t)max_batch * h->H * h->maxT * 4},
         {(void**)&h->logits, (size_t)max_batch * V * 4},
         {(void**)&h->tok, (size_t)max_batch * 4},
         {(void**)&h->arg_v, (size_t)max_batch * kArgParts * 4},
@@ -939,7 +1027,7 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     if (dbg && B != 1) return JL_ERR_INVALID;
     int rc = dec_attrs();
     if (rc) return rc;
-    const int d = h->d;
+    const int d = h->d, sms = h->moe->sm_count;
     const size_t rowlen = (size_t)std::max(h->E, d);
     auto snap = [&](int l, int r, const float* src, int n) -> int {
         if (!dbg) return JL_OK;
@@ -955,8 +1043,33 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err;
     aa.sqn = attn_sqn(h->qk_type, h->H, h->KH, h->hd);
     aa.nslots = h->slots;
-    const size_t asm_ = attn_smem(aa.sqn, h->hd, h->maxT);
-    if (asm_ > 200 * 1024) return JL_ERR_INVALID;
+    // attention work split: score blocks (group, sequence, position split) and
+    // value blocks (head, sequence, dimension slice), about two blocks per SM
+    const qk_layout qkl(h->qk_type, h->H, h->KH, h->hd);
+    const size_t qk_smem = (size_t)qkl.total * sizeof(float);
+    int splits = std::max(1, std::min((2 * sms + h->KH * B - 1) / (h->KH * B), (h->maxT + kQkTile - 1) / kQkTile));
+    const int tp = ((h->maxT + splits - 1) / splits + kQkTile - 1) / kQkTile * kQkTile;
+    splits = (h->maxT + tp - 1) / tp;
+    // value blocks: whole KV groups when that still gives >= one block per SM
+    // (V read once per group), else single heads; slices of the head
+    // dimension (multiples of 4 floats) up to 4 per head
+    const int gsz = h->H / h->KH, maxT4 = (h->maxT + 3) / 4 * 4;
+    auto pick_slices = [&](int units, int target) {
+        int ds = 1;
+        while (ds < 4 && units * ds < target && h->hd % (8 * ds) == 0) ds *= 2;
+        return ds;
+    };
+    int hpb = gsz, dslices = pick_slices(h->KH * B, sms);
+    auto pv_bytes = [&](int hp, int ds) { return ((size_t)hp * maxT4 + 2 * kPvTile * (h->hd / ds)) * sizeof(float); };
+    if (gsz > 8 || 8 % gsz || h->KH * B * dslices < sms || hpb * (h->hd / dslices) / 2 > kPvItems * kPvThreads ||
+        pv_bytes(hpb, dslices) > 200 * 1024) {
+        hpb = 1;
+        dslices = pick_slices(h->H * B, 2 * sms);
+    }
+    const int pv_items = (hpb * (h->hd / dslices) / 2 + kPvThreads - 1) / kPvThreads;
+    const int dw = h->hd / dslices;
+    const size_t pv_smem = pv_bytes(hpb, dslices);
+    if (qk_smem > 200 * 1024 || pv_smem > 200 * 1024) return JL_ERR_INVALID;
     for (int l = 0; l < h->L; l++) {
         // norm1 (adding the previous layer's MoE output to the residual)
         rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)(l ? h->h2 : nullptr),
@@ -965,7 +1078,7 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
         if (!rc) rc = snap(l, 0, h->t, d);
         if (!rc)
             rc = launch_mv<uint16_t>(h->wqkv + (size_t)l * h->nqkv * d, h->t, h->nqkv, d, B,
-                                     h->bias ? h->bqkv + (size_t)l * h->nqkv : nullptr, h->qkv, s);
+                                     h->bias ? h->bqkv + (size_t)l * h->nqkv : nullptr, h->qkv, sms, s);
         if (!rc) {
             aa.l = l;
             const size_t qs = h->qk_type == 2 ? (size_t)h->qn : h->hd, ks = h->qk_type == 2 ? (size_t)h->kn : h->hd;
@@ -975,9 +1088,14 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
             if (prefill)
                 rc = launch(k_kv_append, dim3(h->KH, B), dim3(kAttnThreads), (size_t)(128 + aa.sqn) * sizeof(float),
                             s, aa);
-            if (!rc) rc = launch(k_attn, dim3(h->H, B), dim3(kAttnThreads), asm_, s, aa);
+            if (!rc) rc = launch(k_attn_qk, dim3(h->KH, B, splits), dim3(kQkThreads), qk_smem, s, aa, h->scores, tp);
+            if (!rc) {
+                auto kern = pv_items <= 1 ? k_attn_pv<1> : pv_items <= 2 ? k_attn_pv<2> : k_attn_pv<4>;
+                rc = launch(kern, dim3(h->H / hpb, B, dslices), dim3(kPvThreads), pv_smem, s, aa,
+                            (const float*)h->scores, hpb, dw);
+            }
         }
-        if (!rc) rc = launch_mv<uint16_t>(h->wo + (size_t)l * d * h->qn, h->att, d, h->qn, B, nullptr, h->h2, s);
+        if (!rc) rc = launch_mv<uint16_t>(h->wo + (size_t)l * d * h->qn, h->att, d, h->qn, B, nullptr, h->h2, sms, s);
         if (!rc) rc = snap(l, 1, h->h2, d);
         // norm2 (adding the attention output to the residual), then the MoE layer
         if (!rc)
@@ -1001,7 +1119,7 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     if (logits || tok) {
         const int nb = prefill ? 1 : B;
         const float* tx = prefill ? h->t + (size_t)(B - 1) * d : h->t;
-        rc = launch_mv<float>(h->lm, tx, h->V, d, nb, nullptr, h->logits, s);
+        rc = launch_mv<float>(h->lm, tx, h->V, d, nb, nullptr, h->logits, sms, s);
         if (!rc && tok)
             rc = launch(k_argmax_part, dim3(kArgParts, nb), dim3(256), 0, s, (const float*)h->logits, h->V,
                         h->arg_v, h->arg_i);
@@ -1251,7 +1369,7 @@ int dropin_step(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* po
         cudaFreeAsync(dbg_d, e->st);
     }
     if (!rc && logits)
-        rc = launch_mv<float>(h->lm, h->t, h->V, c->d, B, nullptr, h->logits, e->st);
+        rc = launch_mv<float>(h->lm, h->t, h->V, c->d, B, nullptr, h->logits, h->moe->sm_count, e->st);
     if (rc) return rc;
     // the new K/V row of every layer back into the caller's caches
     for (int b = 0; b < B; b++)

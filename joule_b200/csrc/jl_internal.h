@@ -122,9 +122,16 @@ int jl_moe_layer_done(jl_moe* h, int l, cudaStream_t s);
 // callers from several host threads are serialised. key < 32.
 enum {
     kOnceExact = 0, kOnceRouter, kOnceRouterFast, kOnceDispatch, kOnceGemm, kOnceTc, kOnceGemv,
-    kOnceDecode, kOnceEp, kOnceBf16
+    kOnceDecode, kOnceEp, kOnceBf16, kOnceMmBf16, kOnceMmF32, kOnceAttn
 };
 int jl_device_once(int key, int (*setup)());
+
+// Decode-step matvecs for B >= 16 tokens (jl_mm.cu): the reference's 8-lane
+// FMA order, register-tiled; W in the chunked lane-major layout (jl_mv.cuh).
+bool jl_mm_ok(int N, int K, int B);
+template <typename WT>
+int jl_launch_mm(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
+                 cudaStream_t s);
 
 // Fingerprint of the host weights a (cfg, W) pair points at: leading bytes of
 // the router rows and of the first and last expert records, the expert

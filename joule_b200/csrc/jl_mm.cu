@@ -1,0 +1,214 @@
+// Matvecs of the decode step for batches of 16 tokens and more (QKV, o_proj,
+// lm_head): out[b][n] = hsum8_j( chain over s of fma(W[n][8s + j], x[b][8s + j]) )
+// (+ bias[n]), the reference's 8-lane FMA order (decode_kernel.c:693-718,
+// 969-995) with the AVX tree at the end, bit for bit.
+//
+// At these batch sizes the work is FP32-FMA bound (the order forbids tensor
+// cores), so the kernel is register-tiled like an SGEMM: block = BN rows x BT
+// tokens; warp j is lane j of the reference's accumulator, and its thread
+// (rg, tg) holds RN x RT chains (rows rg*RN + r, tokens tg + 8q): per 8-column
+// step it reads RN weights (RN/4 16-byte shared loads) and RT token values
+// and issues RN*RT FMAs. Each block reads its weight rows once.
+//
+// Stages of 64 columns flow through a ring of 3 to 6 slots of 16-byte cp.async copies:
+// the weight rows (the chunked lane-major layout of jl_mv.cuh, so a block's
+// rows of one chunk are one contiguous run) and the token rows. Each stage's
+// weights are widened to fp32 into [step][lane][row] once, one stage ahead
+// of use; one barrier per stage. The 8 lanes' sums meet in shared memory and
+// the AVX tree adds them.
+#include <algorithm>
+
+#include "jl_common.cuh"
+#include "jl_internal.h"
+#include "jl_mv.cuh"
+
+namespace jl {
+
+constexpr int kMmThreads = 256;
+constexpr int kMmXStride = 68;  // floats per staged token row (64 + 4: 16-byte rows, spread banks)
+constexpr size_t kMmSmemCap = 110 * 1024;  // two blocks per SM
+
+template <typename WT, int RN, int RT>
+struct mm_shape {
+    static constexpr int BN = 4 * RN, BT = 8 * RT;
+    static constexpr int U = mv_traits<WT>::U;
+    static constexpr int CPS = 8 / U;                 // weight chunks per 64-column stage
+    static constexpr int WSS = BN + 4;                // fp32 weight row stride [step][lane][row]
+    static constexpr int X_F = BT * kMmXStride;       // floats per token stage
+    static constexpr int WR_B = CPS * BN * 8 * 16;    // raw weight bytes per stage
+    static constexpr int WS_F = 8 * 8 * WSS;          // floats per widened weight stage
+    // ring depth: as many 64-column stages as fit two blocks per SM (3 to 6)
+    static constexpr size_t stage_bytes = (size_t)X_F * 4 + WR_B;
+    static constexpr int NS_fit = (int)((kMmSmemCap - (size_t)2 * WS_F * 4) / stage_bytes);
+    static constexpr int NS = NS_fit < 3 ? 3 : NS_fit > 6 ? 6 : NS_fit;
+    static constexpr size_t ring_bytes = (size_t)NS * stage_bytes + (size_t)2 * WS_F * 4;
+    static constexpr size_t red_bytes = (size_t)8 * BT * (BN + 1) * 4;
+    static constexpr size_t smem = ring_bytes > red_bytes ? ring_bytes : red_bytes;
+};
+
+__device__ __forceinline__ void widen(uint4 v, float* dst, int stride, uint16_t) {  // 8 bf16 -> rows of dst
+    dst[0] = __uint_as_float(v.x << 16);
+    dst[stride] = __uint_as_float(v.x & 0xFFFF0000u);
+    dst[2 * stride] = __uint_as_float(v.y << 16);
+    dst[3 * stride] = __uint_as_float(v.y & 0xFFFF0000u);
+    dst[4 * stride] = __uint_as_float(v.z << 16);
+    dst[5 * stride] = __uint_as_float(v.z & 0xFFFF0000u);
+    dst[6 * stride] = __uint_as_float(v.w << 16);
+    dst[7 * stride] = __uint_as_float(v.w & 0xFFFF0000u);
+}
+__device__ __forceinline__ void widen(uint4 v, float* dst, int stride, float) {  // 4 fp32
+    dst[0] = __uint_as_float(v.x);
+    dst[stride] = __uint_as_float(v.y);
+    dst[2 * stride] = __uint_as_float(v.z);
+    dst[3 * stride] = __uint_as_float(v.w);
+}
+
+template <typename WT, int RN, int RT>
+__global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, const float* __restrict__ x, int N,
+                                                      int K, int B, const float* __restrict__ bias,
+                                                      float* __restrict__ out) {
+    using S = mm_shape<WT, RN, RT>;
+    constexpr int BN = S::BN, BT = S::BT, U = S::U, CPS = S::CPS, WSS = S::WSS, NS = S::NS;
+    extern __shared__ __align__(16) float sm[];
+    float* xr = sm;                                                      // [NS][BT][kMmXStride]
+    uint8_t* wr = reinterpret_cast<uint8_t*>(sm + NS * S::X_F);         // [NS][CPS][BN][8][U] raw
+    float* ws = reinterpret_cast<float*>(wr + NS * S::WR_B);            // [2][8 steps][8 lanes][WSS]
+    const int tid = threadIdx.x, j = tid >> 5, lane = tid & 31, rg = lane >> 3, tg = lane & 7;
+    const int n0 = blockIdx.x * BN, t0 = blockIdx.y * BT;
+    const int nst = K / 64;
+    const size_t cstride = (size_t)N * 8 * U;  // elements per chunk of W'
+
+    auto issue_w = [&](int st) {  // this stage's weight rows: CPS runs of BN * 128 bytes
+        uint8_t* dst = wr + (st % NS) * S::WR_B;
+        for (int p = tid; p < CPS * BN * 8; p += kMmThreads) {
+            const int cc = p / (BN * 8), r = (p >> 3) % BN;
+            if (n0 + r < N)
+                cp_async16(dst + p * 16, W + (size_t)(st * CPS + cc) * cstride + (size_t)(n0 * 8) * U + (size_t)p % (BN * 8) * U);
+        }
+    };
+    auto issue_x = [&](int st) {  // the token rows' 64 columns of this stage
+        float* dst = xr + (st % NS) * S::X_F;
+        for (int p = tid; p < BT * 16; p += kMmThreads) {
+            const int t = p >> 4, c = (p & 15) * 4;
+            if (t0 + t < B) cp_async16(dst + t * kMmXStride + c, x + (size_t)(t0 + t) * K + st * 64 + c);
+        }
+    };
+    auto widen_stage = [&](int st) {  // raw weights of stage st -> ws[st & 1][s][j][row]
+        const uint4* src = reinterpret_cast<const uint4*>(wr + (st % NS) * S::WR_B);
+        float* dst = ws + (st & 1) * S::WS_F;
+        for (int p = tid; p < CPS * BN * 8; p += kMmThreads) {
+            const int cc = p / (BN * 8), r = (p >> 3) % BN, jj = p & 7;
+            widen(src[p], dst + ((cc * U) * 8 + jj) * WSS + r, 8 * WSS, WT());
+        }
+    };
+
+    // weights do not depend on the previous kernel: their first NS - 1 stages
+    // go out before the wait. Groups: G0 = {w0..w(NS-2), x0}, Gi = {xi} up to
+    // G(NS-2); the loop's iteration st adds G(st+NS-1) = {w, x of stage st+NS-1}.
+    for (int st = 0; st < NS - 1 && st < nst; st++) issue_w(st);
+    griddep_wait();
+    griddep_launch_dependents();
+    for (int st = 0; st < NS - 1; st++) {
+        if (st < nst) issue_x(st);
+        cp_async_commit();
+    }
+    cp_async_wait<NS - 2>();  // G0
+    __syncthreads();
+    widen_stage(0);
+
+    float acc[RN][RT];
+#pragma unroll
+    for (int r = 0; r < RN; r++)
+#pragma unroll
+        for (int q = 0; q < RT; q++) acc[r][q] = 0.0f;
+
+    for (int st = 0; st < nst; st++) {
+        cp_async_wait<NS - 3>();  // this thread's copies up to stage st + 1 have landed
+        __syncthreads();          // everyone's have; stage st - 1 is consumed; ws[st & 1] is complete
+        if (st + NS - 1 < nst) {
+            issue_w(st + NS - 1);
+            issue_x(st + NS - 1);
+        }
+        cp_async_commit();
+        if (st + 1 < nst) widen_stage(st + 1);
+        const float* wsb = ws + (st & 1) * S::WS_F + j * WSS + rg * RN;
+        const float* xb = xr + (st % NS) * S::X_F + tg * kMmXStride + j;
+#pragma unroll
+        for (int s = 0; s < 8; s++) {
+            float w[RN], xv[RT];
+#pragma unroll
+            for (int r4 = 0; r4 < RN / 4; r4++) {
+                const float4 v = *reinterpret_cast<const float4*>(wsb + s * 8 * WSS + r4 * 4);
+                w[4 * r4] = v.x;
+                w[4 * r4 + 1] = v.y;
+                w[4 * r4 + 2] = v.z;
+                w[4 * r4 + 3] = v.w;
+            }
+#pragma unroll
+            for (int q = 0; q < RT; q++) xv[q] = xb[q * 8 * kMmXStride + s * 8];
+#pragma unroll
+            for (int r = 0; r < RN; r++)
+#pragma unroll
+                for (int q = 0; q < RT; q++) acc[r][q] = __fmaf_rn(w[r], xv[q], acc[r][q]);
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is free: it becomes the lanes' reduction area [j][token][row]
+    float* red = sm;
+#pragma unroll
+    for (int r = 0; r < RN; r++)
+#pragma unroll
+        for (int q = 0; q < RT; q++) red[(j * BT + tg + 8 * q) * (BN + 1) + rg * RN + r] = acc[r][q];
+    __syncthreads();
+    for (int o = tid; o < BN * BT; o += kMmThreads) {
+        const int r = o % BN, t = o / BN;
+        if (n0 + r >= N || t0 + t >= B) continue;
+        float l[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) l[jj] = red[(jj * BT + t) * (BN + 1) + r];
+        float v = hsum8(l);
+        if (bias) v = __fadd_rn(v, bias[n0 + r]);
+        out[(size_t)(t0 + t) * N + n0 + r] = v;
+    }
+}
+
+template <typename WT, int RN, int RT>
+int launch_mm_shape(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, cudaStream_t s) {
+    using S = mm_shape<WT, RN, RT>;
+    const dim3 grid((N + S::BN - 1) / S::BN, (B + S::BT - 1) / S::BT);
+    return launch(k_mm<WT, RN, RT>, grid, dim3(kMmThreads), S::smem, s, W, x, N, K, B, bias, out);
+}
+
+template <typename WT>
+int mm_attrs_for() {
+    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, 8, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)mm_shape<WT, 8, 8>::smem));
+    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, 8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)mm_shape<WT, 8, 4>::smem));
+    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)mm_shape<WT, 4, 4>::smem));
+    return JL_OK;
+}
+
+}  // namespace jl
+
+bool jl_mm_ok(int N, int K, int B) { return B >= 16 && K % 64 == 0 && N >= 1; }
+
+// Tile choice: 32 x 64 tiles when they give two blocks per SM, else 32 x 32,
+// else 16 x 32 (o_proj-sized N at B <= 64 still fills the SMs).
+template <typename WT>
+int jl_launch_mm(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
+                 cudaStream_t s) {
+    using namespace jl;
+    if (!jl_mm_ok(N, K, B)) return JL_ERR_INVALID;
+    const int rc = jl_device_once(sizeof(WT) == 2 ? kOnceMmBf16 : kOnceMmF32, [] { return mm_attrs_for<WT>(); });
+    if (rc) return rc;
+    const long rows32 = (N + 31) / 32;
+    if (rows32 * ((B + 63) / 64) >= 2L * sm_count) return launch_mm_shape<WT, 8, 8>(W, x, N, K, B, bias, out, s);
+    if (rows32 * ((B + 31) / 32) >= sm_count) return launch_mm_shape<WT, 8, 4>(W, x, N, K, B, bias, out, s);
+    return launch_mm_shape<WT, 4, 4>(W, x, N, K, B, bias, out, s);
+}
+
+template int jl_launch_mm<uint16_t>(const uint16_t*, const float*, int, int, int, const float*, float*, int,
+                                    cudaStream_t);
+template int jl_launch_mm<float>(const float*, const float*, int, int, int, const float*, float*, int, cudaStream_t);

@@ -190,7 +190,8 @@ __device__ __forceinline__ void cluster_logits(const uint16_t* g_s, const float*
 
 // ---------------------------------------------------------------------------
 // Routing of one token by one warp (decode_kernel.c:1425-1448) with the
-// top-k as k rounds of a warp argmax. Lane l holds experts l + 32 i.
+// top-k as k rounds of a warp argmax (two warp reductions a round). Lane l
+// holds experts l + 32 i.
 //  - smax: max over experts; p_e = expf_fast(s_e - smax), summed
 //    SEQUENTIALLY in expert order by lane 0 from `p_s` (32 * EPL floats of
 //    this warp's shared memory; zeros past E leave the sum unchanged)
@@ -249,31 +250,32 @@ __device__ __forceinline__ void route_token_warp_argmax(const float* logits_b, i
     sum = __shfl_sync(0xffffffffu, sum, 0);
 #pragma unroll
     for (int i = 0; i < EPL; i++) p[i] = __fdiv_rn(p[i], sum);
+    // Each round: key = float bits of p + 1 for unused experts (p >= 0, so keys
+    // order like p; 0 marks a picked expert), the lane's best key over its
+    // experts in ascending order (strict '>': the lowest index among equals;
+    // NaN never wins, as under the reference's '>'),
+    // the warp's largest key by one redux, then the lowest expert index among
+    // the lanes holding it by a second.
     unsigned used = 0;  // bit i: expert lane + 32 i already picked
     float ssum = 0.0f, mine = 0.0f;
     for (int r = 0; r < k; r++) {
-        float bv = -1.0f;
+        uint32_t bk = 0;
         int be = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < EPL; i++) {
             const int e = lane + 32 * i;
-            if (e < E && !((used >> i) & 1u) && (p[i] > bv || (p[i] == bv && e < be))) {
-                bv = p[i];
+            const uint32_t key = (e < E && !((used >> i) & 1u) && p[i] == p[i]) ? __float_as_uint(p[i]) + 1u : 0u;
+            if (key > bk) {
+                bk = key;
                 be = e;
             }
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-            if (ov > bv || (ov == bv && oe < be)) {
-                bv = ov;
-                be = oe;
-            }
-        }
-        if ((be & 31) == lane) used |= 1u << (be >> 5);
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+        const int we = (int)__reduce_min_sync(0xffffffffu, bk == wk ? (uint32_t)be : 0x7fffffffu);
+        const float bv = __uint_as_float(wk - 1u);
+        if ((we & 31) == lane) used |= 1u << (we >> 5);
         if (lane == r) mine = bv;
-        if (lane == 0) top_b[r] = be;
+        if (lane == 0) top_b[r] = we;
         ssum = __fadd_rn(ssum, bv);
     }
     if (lane < k) tw_b[lane] = norm ? __fdiv_rn(mine, ssum) : mine;

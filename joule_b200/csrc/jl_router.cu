@@ -335,96 +335,6 @@ constexpr int kClusterCTAs = 8;
 constexpr int kClusterThreads = 256;
 constexpr int kMaxTPC = 8;
 
-// Scratch layout of route_token_block (floats): p [E, padded to 4], warp
-// maxima [32], the picked ids [16] and their final weights [16], two stats.
-__host__ __device__ inline int route_block_red_off(int E) { return (E + 3) / 4 * 4; }
-__host__ __device__ inline int route_block_top_off(int E) { return route_block_red_off(E) + 32; }
-__host__ __device__ inline int route_block_tw_off(int E) { return route_block_top_off(E) + 16; }
-__host__ __device__ inline int route_block_stat_off(int E) { return route_block_tw_off(E) + 16; }
-
-// Softmax / top-k / renorm of ONE token by a whole CTA, one expert per thread
-// (E <= blockDim.x), with the reference's arithmetic (decode_kernel.c:1425-
-// 1448): max (order-free), p_e = expf_fast(s_e - max), the sum in expert order
-// by one thread, p_e /= sum; expert e's pick round is its rank under (p
-// descending, index ascending), the order of the reference's k strict-'>'
-// argmax passes; the optional renorm sums the k weights in pick order. The
-// ids and weights go to top_b / tw_b and stay in scratch (route_block_*_off).
-__device__ __forceinline__ void route_token_block(const float* logits_b, int E, int k, int norm, int* top_b,
-                                               float* tw_b, float* scratch) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* p_s = scratch;
-    float* red = scratch + route_block_red_off(E);
-    int* top1 = reinterpret_cast<int*>(scratch + route_block_top_off(E));
-    float* w_s = scratch + route_block_tw_off(E);
-    float* stat = scratch + route_block_stat_off(E);
-    const bool live = tid < E;
-    const float v = live ? logits_b[tid] : 0.0f;
-    float mx = (live && v > -1e30f) ? v : -1e30f;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    if (tid < route_block_red_off(E)) p_s[tid] = 0.0f;  // zero padding: +0 leaves the sum unchanged
-    __syncthreads();
-    if (tid == 0) {
-        float m = red[0];
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
-        stat[0] = m;
-    }
-    __syncthreads();
-    float p = live ? expf_fast(__fsub_rn(v, stat[0])) : 0.0f;
-    if (live) p_s[tid] = p;
-    __syncthreads();
-    if (tid == 0) {  // sequential sum in expert order
-        const float4* q4 = reinterpret_cast<const float4*>(p_s);
-        float sum = 0.0f;
-#pragma unroll 8
-        for (int c = 0; c < route_block_red_off(E) / 4; c++) {
-            const float4 q = q4[c];
-            sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, q.x), q.y), q.z), q.w);
-        }
-        stat[1] = sum;
-    }
-    __syncthreads();
-    p = __fdiv_rn(p, stat[1]);
-    __syncthreads();  // every read of the unnormalised p_s is done
-    if (live) p_s[tid] = p;
-    __syncthreads();
-    if (live) {
-        int rank = 0;
-        const float4* q4 = reinterpret_cast<const float4*>(p_s);
-        for (int c = 0; c < route_block_red_off(E) / 4; c++) {
-            const float4 q = q4[c];
-            const float qq[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const int j = 4 * c + t;
-                rank += (j < E) && ((qq[t] > p) || (qq[t] == p && j < tid));
-            }
-        }
-        if (rank < k) {
-            top1[rank] = tid;
-            w_s[rank] = p;
-            top_b[rank] = tid;
-        }
-    }
-    __syncthreads();
-    float w = 0.0f;
-    if (tid < k) {
-        w = w_s[tid];
-        if (norm) {
-            float ssum = 0.0f;
-            for (int i = 0; i < k; i++) ssum = __fadd_rn(ssum, w_s[i]);
-            w = __fdiv_rn(w, ssum);
-        }
-    }
-    __syncthreads();  // every thread has read the picked weights
-    if (tid < k) {
-        tw_b[tid] = w;
-        w_s[tid] = w;  // the final weight stays in scratch for the dispatch
-    }
-    __syncthreads();
-}
-
 __host__ __device__ inline int route_tpc(int B) {  // tokens per cluster: 1, 2, 4 or 8
     const int t = (B + 31) / 32;
     return t <= 1 ? 1 : t <= 2 ? 2 : t <= 4 ? 4 : kMaxTPC;
@@ -495,9 +405,7 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kClusterT
     if (rank != 0) return;
     trace_point(tr, kTraceRouter, 4);
     // leader: the staging area is free; routing scratch, then dispatch scratch
-    if (nb == 1) {  // one token: the whole CTA routes it (one expert per thread)
-        route_token_block(lg_s, E, k, norm, ws.top + b0 * k, ws.tw + b0 * k, reinterpret_cast<float*>(smem));
-    } else if ((int)(threadIdx.x >> 5) < nb) {  // one warp per token
+    if ((int)(threadIdx.x >> 5) < nb) {  // one warp per token
         const int w = threadIdx.x >> 5;
         route_token_lean(lg_s + (size_t)w * E, E, k, norm, ws.top + (b0 + w) * k, ws.tw + (b0 + w) * k,
                          reinterpret_cast<float*>(smem) + w * kMaxE);
@@ -519,16 +427,13 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(kClusterT
     trace_point(tr, kTraceRouter, 6);
     // every token's ids and weights, read through L2 (other clusters wrote them)
     const int S = B * k;
-    if (B == 1) {  // this CTA routed the only token: its ids and weights are in shared memory
-        const float* rs = reinterpret_cast<const float*>(smem);
-        const int* top1 = reinterpret_cast<const int*>(rs + route_block_top_off(E));
-        const float* tw1 = rs + route_block_tw_off(E);
+    if (B == 1) {  // this CTA routed the only token (its stores are visible after the barrier)
         trace_point(tr, kTraceRouter, 7);
         if (tid < k) {
-            ws.sel[tid] = top1[tid];
+            ws.sel[tid] = ws.top[tid];
             ws.uh[tid] = tid;
             ws.uidx[tid] = tid;
-            ws.uw[tid] = tw1[tid];
+            ws.uw[tid] = ws.tw[tid];
             ws.slot_pos[tid] = tid;
             ws.comb[tid] = tid;
         }

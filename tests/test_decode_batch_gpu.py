@@ -1,0 +1,98 @@
+"""Large-batch decode steps on the GPU against the C restatement of the
+reference's decode step (needs a GPU).
+
+At B >= 16 the step's matvecs (QKV, o_proj, lm_head) run on the register-tiled
+kernel (jl_mm.cu) and attention reads long, ragged contexts. One step of B
+sequences, each at its own position with a KV cache pre-filled with seeded
+values (the same rows in the oracle's caches and in the library's slots), must
+give the restatement's logits bit for bit (MoE on its exact path), and the
+K/V rows it appends must equal the restatement's. The restatement
+(oracle/joule_oracle.c: jo_decode_step) is pinned to the reference's compiled
+decode_layers_batch by tests/test_decode_oracle.py.
+
+Shapes: d = 512, 32 q / 4 kv heads of 64 (GQA 8, qn 2048), so the QKV matvec
+(2560 rows) and the o_proj (512 rows, K = 2048) take different tile shapes;
+V = 4096 or 16384 for the fp32 lm_head's tile shapes.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+class _DevArray:
+    """A device buffer as a torch tensor, without a copy."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2}
+
+
+def _shape(V: int):
+    from oracle.decode import DecodeShape
+    return DecodeShape("qwen3b", 2, 512, 32, 4, 64, 8, 2, 128, V, 160, 1, 0, 1, 1e-6, 1e6)
+
+
+@pytest.mark.parametrize("B,V", [(16, 4096), (40, 16384), (64, 4096), (64, 16384)])
+def test_batched_step_bit_identical_to_restatement(B, V):
+    from oracle.decode import RestatedDecoder, _Caches, embed, make_model
+    from test_decode_gpu import _structs
+    from joule_b200.native import check, get_dll
+    s = _shape(V)
+    model = make_model(s, seed=41)
+    rng = np.random.default_rng(7 + B)
+    positions = np.array([(5 + 37 * b) % (s.maxT - 2) for b in range(B)], np.int32)
+    tokens = rng.integers(0, s.V, B).astype(np.int32)
+    kn = s.KH * s.hd
+    caches = _Caches(s, B)
+    for b in range(B):
+        for l in range(s.L):
+            caches.k[b * s.L + l][: positions[b]] = rng.standard_normal((positions[b], kn), np.float32)
+            caches.v[b * s.L + l][: positions[b]] = rng.standard_normal((positions[b], kn), np.float32)
+    x = embed(model, tokens)
+
+    lib = get_dll()
+    cfg, W, tables = _structs(model)
+    h = ctypes.c_void_p()
+    check(lib.jl_dec_create(ctypes.byref(cfg), ctypes.byref(W), B, B, 0, ctypes.byref(h)), "jl_dec_create")
+    try:
+        moe = ctypes.c_void_p()
+        check(lib.jl_dec_moe(h, ctypes.byref(moe)), "jl_dec_moe")
+        check(lib.jl_moe_set_path(moe, 1), "jl_moe_set_path")  # exact
+        kp, vp = ctypes.c_void_p(), ctypes.c_void_p()
+        check(lib.jl_dec_kv(h, ctypes.byref(kp), ctypes.byref(vp)), "jl_dec_kv")
+        shape = (B, s.L, s.maxT, kn)
+        kc = torch.as_tensor(_DevArray(kp.value, shape), device="cuda")
+        vc = torch.as_tensor(_DevArray(vp.value, shape), device="cuda")
+        kc.copy_(torch.from_numpy(np.stack([np.stack(caches.k[b * s.L:(b + 1) * s.L]) for b in range(B)])))
+        vc.copy_(torch.from_numpy(np.stack([np.stack(caches.v[b * s.L:(b + 1) * s.L]) for b in range(B)])))
+        dev = torch.device("cuda")
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        pos = torch.from_numpy(positions).to(dev)
+        xd = torch.from_numpy(x).to(dev)
+        logits = torch.empty(B, s.V, device=dev)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
+        stream = torch.cuda.current_stream().cuda_stream
+        check(lib.jl_dec_step(h, slots.data_ptr(), pos.data_ptr(), xd.data_ptr(), B, logits.data_ptr(),
+                              tok.data_ptr(), stream), "jl_dec_step")
+        torch.cuda.synchronize()
+        check(lib.jl_dec_check(h, stream), "jl_dec_check")
+        got = logits.cpu().numpy()
+        k_rows = np.stack([kc[b, :, positions[b]].cpu().numpy() for b in range(B)])
+        v_rows = np.stack([vc[b, :, positions[b]].cpu().numpy() for b in range(B)])
+    finally:
+        lib.jl_dec_destroy(h)
+
+    ref_tok, ref = RestatedDecoder(model).step(caches, 0, x, positions)
+    ref_k = np.stack([np.stack([caches.k[b * s.L + l][positions[b]] for l in range(s.L)]) for b in range(B)])
+    ref_v = np.stack([np.stack([caches.v[b * s.L + l][positions[b]] for l in range(s.L)]) for b in range(B)])
+    assert np.array_equal(k_rows, ref_k)
+    assert np.array_equal(v_rows, ref_v)
+    bad = np.argwhere(got != ref)
+    assert bad.size == 0, f"{len(bad)} logits differ, first at {bad[:4].tolist()}"
+    assert np.array_equal(tok.cpu().numpy(), np.argmax(ref, axis=1).astype(np.int32))
