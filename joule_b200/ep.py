@@ -214,6 +214,9 @@ class P2PExpertParallelMoE:
         """torch.cuda.Event objects (enable_timing), up to 9; [] turns it off."""
         import ctypes
         from joule_b200.native import check
+        for e in events:
+            if not e.cuda_event:  # torch creates the CUDA event on its first record
+                e.record()
         arr = (ctypes.c_void_p * max(1, len(events)))(*[e.cuda_event for e in events])
         check(self._L.jl_ep_set_phase_events(self.ep, arr, len(events)), "jl_ep_set_phase_events")
 
