@@ -210,8 +210,9 @@ int jl_moe_quantize_layer(jl_moe* h, int l, const unsigned short* gate_w,
 #define JL_PATH_AUTO 0  /* GEMV for B <= 4, tensor-core beyond (d % 512 == 0, m % 256 == 0), else exact */
 #define JL_PATH_EXACT 1 /* CUDA-core FP32 in the reference's order (bit-identical outputs) */
 #define JL_PATH_TC 2    /* tcgen05 grouped GEMM (fp16 operands, fp32 acc) */
-#define JL_PATH_GEMV 3  /* B <= 4: warp-per-row GEMVs over every warp of the GPU, fp32 in another
-                           order (<= 1e-3 row-relative); larger B runs as JL_PATH_AUTO */
+#define JL_PATH_GEMV 3  /* B <= 4: dequantising GEMVs over every SM, exact fp16 (n - 8) weights x
+                           fp16 hi + lo activations on mma.sync, fp32 accumulate and scale
+                           (<= 1e-3 row-relative); larger B runs as JL_PATH_AUTO */
 int jl_moe_set_path(jl_moe* h, int path);
 
 /* One MoE FFN layer: out[B, d] = MoE(x[B, d]) for layer l (device fp32).

@@ -179,23 +179,36 @@ int launch_mm_shape(const WT* W, const float* x, int N, int K, int B, const floa
     return launch(k_mm<WT, RN, RT>, grid, dim3(kMmThreads), S::smem, s, W, x, N, K, B, bias, out);
 }
 
+template <typename WT, int RN, int RT>
+int mm_attr() {
+    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, RN, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)mm_shape<WT, RN, RT>::smem));
+    return JL_OK;
+}
+
 template <typename WT>
 int mm_attrs_for() {
-    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, 8, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)mm_shape<WT, 8, 8>::smem));
-    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, 8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)mm_shape<WT, 8, 4>::smem));
-    JL_CUDA(cudaFuncSetAttribute(k_mm<WT, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)mm_shape<WT, 4, 4>::smem));
-    return JL_OK;
+    int rc = mm_attr<WT, 8, 8>();
+    if (!rc) rc = mm_attr<WT, 8, 4>();
+    if (!rc) rc = mm_attr<WT, 8, 2>();
+    if (!rc) rc = mm_attr<WT, 4, 4>();
+    if (!rc) rc = mm_attr<WT, 4, 2>();
+    return rc;
 }
 
 }  // namespace jl
 
 bool jl_mm_ok(int N, int K, int B) { return B >= 16 && K % 64 == 0 && N >= 1; }
 
-// Tile choice: 32 x 64 tiles when they give two blocks per SM, else 32 x 32,
-// else 16 x 32 (o_proj-sized N at B <= 64 still fills the SMs).
+// Tile choice (BN x BT = 4 RN x 8 RT), from timings of every shape on the
+// decode step's matrices on a B200 (QKV 5120 x 2048, o_proj 2048 x 4096,
+// lm_head 151936 x 2048 at B = 16, 32, 64; microseconds, best shape first):
+//   QKV     B=16: 32x16 26.7, 16x16 26.8 | B=32: 16x32 37.7 | B=64: 16x32 59.5
+//   o_proj  B=16: 16x16 22.7 | B=32: 32x16 30.0 | B=64: 32x32 48.1
+//   lm_head B=16: 32x16 442 | B=32: 32x32 688 | B=64: 32x64 1146
+// Token tiles no wider than the batch; for large N the widest such tile; for
+// projection-sized N, 16-row tiles (more blocks) except at long K, where the
+// per-block work is large anyway.
 template <typename WT>
 int jl_launch_mm(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
                  cudaStream_t s) {
@@ -204,8 +217,16 @@ int jl_launch_mm(const WT* W, const float* x, int N, int K, int B, const float* 
     const int rc = jl_device_once(sizeof(WT) == 2 ? kOnceMmBf16 : kOnceMmF32, [] { return mm_attrs_for<WT>(); });
     if (rc) return rc;
     const long rows32 = (N + 31) / 32;
-    if (rows32 * ((B + 63) / 64) >= 2L * sm_count) return launch_mm_shape<WT, 8, 8>(W, x, N, K, B, bias, out, s);
-    if (rows32 * ((B + 31) / 32) >= sm_count) return launch_mm_shape<WT, 8, 4>(W, x, N, K, B, bias, out, s);
+    if (rows32 >= 8L * sm_count) {  // lm_head-sized
+        if (B <= 16) return launch_mm_shape<WT, 8, 2>(W, x, N, K, B, bias, out, s);
+        if (B <= 32) return launch_mm_shape<WT, 8, 4>(W, x, N, K, B, bias, out, s);
+        return launch_mm_shape<WT, 8, 8>(W, x, N, K, B, bias, out, s);
+    }
+    if (B <= 16) return launch_mm_shape<WT, 4, 2>(W, x, N, K, B, bias, out, s);
+    if (K >= 4096) {
+        if (B <= 32) return launch_mm_shape<WT, 8, 2>(W, x, N, K, B, bias, out, s);
+        return launch_mm_shape<WT, 8, 4>(W, x, N, K, B, bias, out, s);
+    }
     return launch_mm_shape<WT, 4, 4>(W, x, N, K, B, bias, out, s);
 }
 

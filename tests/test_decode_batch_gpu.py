@@ -10,9 +10,11 @@ K/V rows it appends must equal the restatement's. The restatement
 (oracle/joule_oracle.c: jo_decode_step) is pinned to the reference's compiled
 decode_layers_batch by tests/test_decode_oracle.py.
 
-Shapes: d = 512, 32 q / 4 kv heads of 64 (GQA 8, qn 2048), so the QKV matvec
-(2560 rows) and the o_proj (512 rows, K = 2048) take different tile shapes;
-V = 4096 or 16384 for the fp32 lm_head's tile shapes.
+Shapes: d = 512, heads of 64 with GQA 8: 32 q / 4 kv heads (qn 2048) or 64 /
+8 (qn 4096, so the o_proj's K is 4096); V = 4096 or 40960. Together with B
+they take the matvec kernel through its tile shapes: lm_head (fp32) 32 x 16,
+32 x 32, 32 x 64 (large V) and 16 x 32 (small V); projections (bf16) 16 x 16,
+16 x 32, 32 x 16 and 32 x 32.
 """
 from __future__ import annotations
 
@@ -33,17 +35,18 @@ class _DevArray:
                                          "version": 2}
 
 
-def _shape(V: int):
+def _shape(V: int, H: int, KH: int):
     from oracle.decode import DecodeShape
-    return DecodeShape("qwen3b", 2, 512, 32, 4, 64, 8, 2, 128, V, 160, 1, 0, 1, 1e-6, 1e6)
+    return DecodeShape("qwen3b", 2, 512, H, KH, 64, 8, 2, 128, V, 160, 1, 0, 1, 1e-6, 1e6)
 
 
-@pytest.mark.parametrize("B,V", [(16, 4096), (40, 16384), (64, 4096), (64, 16384)])
-def test_batched_step_bit_identical_to_restatement(B, V):
+@pytest.mark.parametrize("B,V,H,KH", [(16, 40960, 32, 4), (32, 40960, 64, 8), (40, 4096, 32, 4),
+                                      (64, 40960, 64, 8)])
+def test_batched_step_bit_identical_to_restatement(B, V, H, KH):
     from oracle.decode import RestatedDecoder, _Caches, embed, make_model
     from test_decode_gpu import _structs
     from joule_b200.native import check, get_dll
-    s = _shape(V)
+    s = _shape(V, H, KH)
     model = make_model(s, seed=41)
     rng = np.random.default_rng(7 + B)
     positions = np.array([(5 + 37 * b) % (s.maxT - 2) for b in range(B)], np.int32)
