@@ -253,6 +253,12 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
         : "memory");
 }
 
+// Prefetch [p, p + bytes) of this GPU's own memory into L2 (p 16-byte aligned,
+// bytes a multiple of 16); no data is returned and no completion is tracked.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Per-thread asynchronous global -> shared copies (16 bytes, both addresses
 // 16-byte aligned), completed by commit / wait groups.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {

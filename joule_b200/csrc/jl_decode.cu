@@ -78,7 +78,7 @@ __device__ __forceinline__ float chain_sum(const float* v, int n) {
 // with inv from the sum of squares in index order.
 __global__ void __launch_bounds__(kNormThreads) k_rms(float* __restrict__ h, const float* __restrict__ add,
                                                       const uint16_t* __restrict__ w, float eps, int d,
-                                                      float* __restrict__ t) {
+                                                      float* __restrict__ t, float* __restrict__ tT, int Bp) {
     extern __shared__ __align__(16) float sm[];  // v [d], squares [d]
     float* v_s = sm;
     float* sq = sm + d;
@@ -131,10 +131,17 @@ __global__ void __launch_bounds__(kNormThreads) k_rms(float* __restrict__ h, con
             const int i = i0 + j * blockDim.x;
             if (i >= n4) continue;
             const float4 v = reinterpret_cast<const float4*>(v_s)[i];
-            t4[i] = make_float4(__fmul_rn(__fmul_rn(v.x, inv), bf16_to_f32(wv[j].x & 0xFFFFu)),
+            const float4 o = make_float4(__fmul_rn(__fmul_rn(v.x, inv), bf16_to_f32(wv[j].x & 0xFFFFu)),
                                 __fmul_rn(__fmul_rn(v.y, inv), bf16_to_f32(wv[j].x >> 16)),
                                 __fmul_rn(__fmul_rn(v.z, inv), bf16_to_f32(wv[j].y & 0xFFFFu)),
                                 __fmul_rn(__fmul_rn(v.w, inv), bf16_to_f32(wv[j].y >> 16)));
+            t4[i] = o;
+            if (tT) {  // column-major copy [d][Bp] for the large-batch matvec
+                tT[(size_t)(4 * i) * Bp + b] = o.x;
+                tT[(size_t)(4 * i + 1) * Bp + b] = o.y;
+                tT[(size_t)(4 * i + 2) * Bp + b] = o.z;
+                tT[(size_t)(4 * i + 3) * Bp + b] = o.w;
+            }
         }
     }
 }
@@ -155,7 +162,7 @@ __global__ void __launch_bounds__(kNormThreads) k_rms(float* __restrict__ h, con
 template <typename WT, int NT>
 __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, const float* __restrict__ x,
                                                     int N, int K, int B, const float* __restrict__ bias,
-                                                    float* __restrict__ out, int RT) {
+                                                    float* __restrict__ out, int RT, int pf) {
     constexpr int U = mv_traits<WT>::U;
     constexpr int P = 8;  // chunks per load group; the next group is in flight while one is used
     extern __shared__ __align__(16) float x_s[];  // [NT][8][K/8 + 4]
@@ -173,6 +180,11 @@ __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, co
     };
     uint4 cur[P], nxt[P];
     load_group(row_of(0), 0, cur);  // weights do not depend on the previous kernel: fetch before the wait
+    if (pf && blockIdx.x == 0) {  // and the rest of this block's rows into L2 while the producer runs
+        const int r0 = tile0 * kMvRows, r1 = min(N, (tile0 + RT) * kMvRows);
+        for (int c = tid; c < nc && r1 > r0; c += blockDim.x)
+            prefetch_l2(W + ((size_t)c * N + r0) * 8 * U, (uint32_t)(r1 - r0) * 128u);
+    }
     griddep_wait();
     griddep_launch_dependents();
     const int b0 = blockIdx.x * NT, nt = min(NT, B - b0);
@@ -258,6 +270,8 @@ __global__ void __launch_bounds__(kMvRows * 8) k_mv(const WT* __restrict__ W, co
 struct attn_args {
     const float* qkv;        // [B][qn + 2 kn] (bias added)
     float* att;              // [B][qn]
+    float* attT;             // [qn][Bp] column-major copy for the large-batch matvec, or null
+    int Bp;
     const int* positions;    // [B]
     const int* slots;        // [B] KV cache slot of each sequence
     float* kc;               // [slots][L][maxT][kn]
@@ -296,14 +310,16 @@ __device__ __forceinline__ void squares(const float* __restrict__ v, int n, floa
 }
 
 constexpr int kQkThreads = 256;
-constexpr int kQkTile = 64;   // positions per K tile (two tiles in flight)
+constexpr int kQkTile = 64;   // positions per K tile
+constexpr int kQkRing = 3;    // K tiles in the ring (two in flight while one is used)
 constexpr int kPvThreads = 256;
-constexpr int kPvTile = 32;   // positions per V tile (two tiles in flight)
+constexpr int kPvTile = 16;   // positions per V tile
+constexpr int kPvRing = 8;    // V tiles in the ring (seven in flight while one is used)
 constexpr int kPvItems = 4;   // (head, dimension pair) items per thread at most (NI of k_attn_pv)
 
 // Shared-memory layout of k_attn_qk (floats): q [gsz][hd + 4], k [hd],
 // v [hd], squares, inverse norms [gsz + 1] (padded to 4), two K tiles
-// [kQkTile][hd + 4].
+// [kQkTile][hd + 4] x kQkRing.
 struct qk_layout {
     int qs, sq, inv, tiles, total;
     __host__ __device__ qk_layout(int qk_type, int H, int KH, int hd) {
@@ -313,7 +329,7 @@ struct qk_layout {
         const int nsq = qk_type == 2 ? (H * hd + 3) / 4 * 4 + (KH * hd + 3) / 4 * 4 : (gsz + 1) * hd;
         inv = sq + (nsq + 3) / 4 * 4;
         tiles = inv + (gsz + 4) / 4 * 4;
-        total = tiles + 2 * kQkTile * qrow;
+        total = tiles + kQkRing * kQkTile * qrow;
     }
 };
 
@@ -328,7 +344,7 @@ __global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __re
     float* v_s = k_s + hd;           // [hd]
     float* sq = sm + lay.sq;
     float* inv = sm + lay.inv;
-    float* tb0 = sm + lay.tiles;     // tile j at tb0 + (j & 1) * kQkTile * KP
+    float* tb0 = sm + lay.tiles;     // tile j at tb0 + (j % kQkRing) * kQkTile * KP
     griddep_wait();
     griddep_launch_dependents();
     const int pos = a.positions[b];
@@ -339,6 +355,29 @@ __global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __re
     }
     const int T = pos + 1, t_lo = split * tp, t_hi = min(T, t_lo + tp);
     if (t_lo >= T) return;  // split 0 always has positions (and appends the rows)
+    const size_t cache_off = ((size_t)slot * a.L + a.l) * a.maxT * kn;
+    const float* K = a.kc + cache_off;
+    const int own = a.from_cache ? -1 : pos;  // the row this block takes from k_s
+    // tile copies: thread (row r0 + i * rstep, column c) with c fixed per thread
+    const int c4 = hd / 4, rstep = kQkThreads / c4, kr0 = tid / c4, kc = (tid - kr0 * c4) * 4;
+    auto issue_k = [&](int t0, float* buf) {
+        const int nt = min(kQkTile, t_hi - t0);
+        if (kr0 < rstep)
+            for (int r = kr0; r < nt; r += rstep)
+                if (t0 + r != own) cp_async16(buf + r * KP + kc, K + (size_t)(t0 + r) * kn + g * hd + kc);
+        cp_async_commit();
+    };
+    // scores (decode_kernel.c:1212-1218): chains (position, head) in pairs
+    const float scale = sqrtf_fast((float)hd);
+    float* out = scores + ((size_t)b * a.H + h0) * a.maxT;
+    const int ntiles = (t_hi - t_lo + kQkTile - 1) / kQkTile;
+    const int npairs = kQkTile * gsz / 2 + (kQkTile * gsz) % 2;
+    // a ring of kQkRing tiles, kQkRing - 1 in flight: one commit group per tile (empty past the
+    // end). The first ones go out before the norms: they depend only on the position.
+    for (int jt = 0; jt < kQkRing - 1; jt++) {
+        if (jt < ntiles) issue_k(t_lo + jt * kQkTile, tb0 + jt * kQkTile * KP);
+        else cp_async_commit();
+    }
     const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
     for (int i = tid; i < gsz * hd; i += blockDim.x) q_s[(i / hd) * QS + i % hd] = row[h0 * hd + i];
     for (int i = tid; i < hd; i += blockDim.x) {
@@ -389,39 +428,19 @@ __global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __re
         v[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
     }
     __syncthreads();
-    const size_t cache_off = ((size_t)slot * a.L + a.l) * a.maxT * kn;
-    const float* K = a.kc + cache_off;
-    const int own = a.from_cache ? -1 : pos;  // the row this block takes from k_s
     if (!a.from_cache && split == 0) {        // KV append (decode_kernel.c:1200-1205)
         for (int i = tid; i < hd; i += blockDim.x) {
             a.kc[cache_off + (size_t)pos * kn + g * hd + i] = k_s[i];
             a.vc[cache_off + (size_t)pos * kn + g * hd + i] = v_s[i];
         }
     }
-    // tile copies: thread (row r0 + i * rstep, column c) with c fixed per thread
-    const int c4 = hd / 4, rstep = kQkThreads / c4, kr0 = tid / c4, kc = (tid - kr0 * c4) * 4;
-    auto issue_k = [&](int t0, float* buf) {
-        const int nt = min(kQkTile, t_hi - t0);
-        if (kr0 < rstep)
-            for (int r = kr0; r < nt; r += rstep)
-                if (t0 + r != own) cp_async16(buf + r * KP + kc, K + (size_t)(t0 + r) * kn + g * hd + kc);
-        cp_async_commit();
-    };
-    // scores (decode_kernel.c:1212-1218): chains (position, head) in pairs
-    const float scale = sqrtf_fast((float)hd);
-    float* out = scores + ((size_t)b * a.H + h0) * a.maxT;
-    const int ntiles = (t_hi - t_lo + kQkTile - 1) / kQkTile;
-    const int npairs = kQkTile * gsz / 2 + (kQkTile * gsz) % 2;
-    issue_k(t_lo, tb0);
     for (int jt = 0; jt < ntiles; jt++) {
         const int t0 = t_lo + jt * kQkTile, nt = min(kQkTile, t_hi - t0);
-        float* buf = tb0 + (jt & 1) * kQkTile * KP;
-        if (jt + 1 < ntiles) {
-            issue_k(t0 + kQkTile, tb0 + ((jt + 1) & 1) * kQkTile * KP);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        float* buf = tb0 + (jt % kQkRing) * kQkTile * KP;
+        const int jn = jt + kQkRing - 1;  // refills the slot tile jt - 1 used
+        if (jn < ntiles) issue_k(t_lo + jn * kQkTile, tb0 + (jn % kQkRing) * kQkTile * KP);
+        else cp_async_commit();
+        cp_async_wait<kQkRing - 1>();
         if (own >= t0 && own < t0 + nt)
             for (int i = tid; i < hd; i += blockDim.x) buf[(own - t0) * KP + i] = k_s[i];
         __syncthreads();
@@ -470,20 +489,20 @@ __global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __re
             out[(size_t)ha * a.maxT + t0 + ta] = __fdiv_rn(s0, scale);
             if (tb < nt && cb != ca) out[(size_t)hb * a.maxT + t0 + tb] = __fdiv_rn(s1, scale);
         }
-        __syncthreads();  // the buffer is refilled two tiles later
+        __syncthreads();  // the slot is refilled in the next iteration
     }
 }
 
 template <int NI>
 __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float* __restrict__ scores, int hpb,
-                                                         int dw) {
+                                                         int dw, int whole) {
     extern __shared__ __align__(16) float sm[];
     const int hb = blockIdx.x, b = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, h0 = hb * hpb, g = h0 / (a.H / a.KH);
     const int maxT4 = (a.maxT + 3) / 4 * 4;
     float* p_s = sm;                 // [hpb][maxT4]
-    float* vt0 = sm + hpb * maxT4;   // two V tiles [kPvTile][dw]
+    float* vt0 = sm + hpb * maxT4;   // whole: all rows [maxT][dw]; else a ring of kPvRing tiles [kPvTile][dw]
     __shared__ float red[kPvThreads / 32];
     __shared__ float stat[kPvThreads / 32];
     griddep_wait();
@@ -500,7 +519,19 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
             for (int r = vr0; r < nt; r += rstep) cp_async16(buf + r * dw + vc, V + (size_t)(t0 + r) * kn + vc);
         cp_async_commit();
     };
-    issue_v(0, vt0);  // the values do not depend on the softmax: first tile now
+    // the values do not depend on the softmax: all rows (whole) or the ring's
+    // first kPvRing - 1 tiles go out now
+    const int ntiles = (T + kPvTile - 1) / kPvTile;
+    if (whole) {
+        if (vr0 < rstep)
+            for (int r = vr0; r < T; r += rstep) cp_async16(vt0 + r * dw + vc, V + (size_t)r * kn + vc);
+        cp_async_commit();
+    } else {
+        for (int j = 0; j < kPvRing - 1; j++) {
+            if (j < ntiles) issue_v(j * kPvTile, vt0 + j * kPvTile * dw);
+            else cp_async_commit();
+        }
+    }
     // softmax: head hh by the wph warps [hh * wph, (hh + 1) * wph) (hpb <= 8)
     const int wph = kPvThreads / 32 / hpb, hh = warp / wph, sub = (warp - hh * wph) * 32 + lane, nsub = wph * 32;
     float* p = p_s + hh * maxT4;
@@ -536,16 +567,29 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
         ox[k] = oy[k] = 0.0f;
     }
     const bool live = tid < items;  // the last item's thread set is complete (items <= NI * threads)
-    const int ntiles = (T + kPvTile - 1) / kPvTile;
-    for (int j = 0; j < ntiles; j++) {
-        const int t0 = j * kPvTile, nt = min(kPvTile, T - t0);
-        float* buf = vt0 + (j & 1) * kPvTile * dw;
-        if (j + 1 < ntiles) {
-            issue_v(t0 + kPvTile, vt0 + ((j + 1) & 1) * kPvTile * dw);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
+    if (whole) {  // one wait, then the chains over every row without a barrier
+        cp_async_wait<0>();
+        __syncthreads();
+        if (live) {
+#pragma unroll 4
+            for (int r = 0; r < T; r++) {
+#pragma unroll
+                for (int k = 0; k < NI; k++) {
+                    const float pp = p_s[ih[k] * maxT4 + r];
+                    const float2 v = *reinterpret_cast<const float2*>(vt0 + r * dw + 2 * ii[k]);
+                    ox[k] = __fadd_rn(ox[k], __fmul_rn(pp, v.x));
+                    oy[k] = __fadd_rn(oy[k], __fmul_rn(pp, v.y));
+                }
+            }
         }
+    }
+    for (int j = 0; j < (whole ? 0 : ntiles); j++) {
+        const int t0 = j * kPvTile, nt = min(kPvTile, T - t0);
+        float* buf = vt0 + (j % kPvRing) * kPvTile * dw;
+        const int jn = j + kPvRing - 1;  // refills the slot tile j - 1 used
+        if (jn < ntiles) issue_v(jn * kPvTile, vt0 + (jn % kPvRing) * kPvTile * dw);
+        else cp_async_commit();
+        cp_async_wait<kPvRing - 1>();
         __syncthreads();
         if (live) {
 #pragma unroll 4
@@ -563,9 +607,14 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
     }
 #pragma unroll
     for (int k = 0; k < NI; k++)
-        if (tid + k * kPvThreads < items)
-            *reinterpret_cast<float2*>(a.att + (size_t)b * qn + (h0 + ih[k]) * hd + z * dw + 2 * ii[k]) =
-                make_float2(ox[k], oy[k]);
+        if (tid + k * kPvThreads < items) {
+            const int col = (h0 + ih[k]) * hd + z * dw + 2 * ii[k];
+            *reinterpret_cast<float2*>(a.att + (size_t)b * qn + col) = make_float2(ox[k], oy[k]);
+            if (a.attT) {
+                a.attT[(size_t)col * a.Bp + b] = ox[k];
+                a.attT[(size_t)(col + 1) * a.Bp + b] = oy[k];
+            }
+        }
 }
 
 // K/V append for a batch of positions of one or more sequences (batched
@@ -752,6 +801,9 @@ struct jl_dec {
     float* h2;         // [max_batch, d]
     float* qkv;        // [max_batch, nqkv]
     float* att;        // [max_batch, qn]
+    float* tT;         // [d, Bp] column-major copies of the norm output and of att (large batches)
+    float* attT;       // [qn, Bp]
+    int Bp;            // max_batch rounded up to 8
     float* scores;     // [max_batch, H, maxT] attention scores
     float* logits;     // [max_batch, V]
     int* tok;          // [max_batch]
@@ -789,22 +841,30 @@ int dec_attrs() {
 
 // Row tiles per block: one for a single token group (the most blocks), more
 // when the token rows are staged per block for several groups.
+// x: [B][K] row-major; xT: the same as a column-major [K][Bp] copy (the
+// register-tiled kernel at B >= 16 reads that one).
 template <typename WT>
-int launch_mv(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
-              cudaStream_t s) {
+int launch_mv(const WT* W, const float* x, const float* xT, int Bp, int N, int K, int B, const float* bias,
+              float* out, int sm_count, cudaStream_t s) {
     using namespace jl;
-    if (jl_mm_ok(N, K, B)) return jl_launch_mm<WT>(W, x, N, K, B, bias, out, sm_count, s);
+    if (jl_mm_ok(N, K, B)) {
+        if (!xT) return JL_ERR_INVALID;
+        return jl_launch_mm<WT>(W, xT, Bp, N, K, B, bias, out, sm_count, s);
+    }
     const int nt = B >= 8 ? 8 : B >= 4 ? 4 : B >= 2 ? 2 : 1;
     const size_t smem = (size_t)nt * 8 * mv_xstride(K) * sizeof(float);
     if (smem > 200 * 1024) return JL_ERR_INVALID;
     const int groups = (B + nt - 1) / nt, tiles = (N + kMvRows - 1) / kMvRows;
     const int RT = groups == 1 ? 1 : 4;
     const dim3 grid(groups, (tiles + RT - 1) / RT), block(kMvRows * 8);
+    // matrices that fit comfortably in L2 are prefetched there before the
+    // dependent-grid wait (the previous kernel is latency-bound at small B)
+    const int pf = (size_t)N * K * sizeof(WT) <= ((size_t)64 << 20);
     switch (nt) {
-        case 8: return launch(k_mv<WT, 8>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
-        case 4: return launch(k_mv<WT, 4>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
-        case 2: return launch(k_mv<WT, 2>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
-        default: return launch(k_mv<WT, 1>, grid, block, smem, s, W, x, N, K, B, bias, out, RT);
+        case 8: return launch(k_mv<WT, 8>, grid, block, smem, s, W, x, N, K, B, bias, out, RT, pf);
+        case 4: return launch(k_mv<WT, 4>, grid, block, smem, s, W, x, N, K, B, bias, out, RT, pf);
+        case 2: return launch(k_mv<WT, 2>, grid, block, smem, s, W, x, N, K, B, bias, out, RT, pf);
+        default: return launch(k_mv<WT, 1>, grid, block, smem, s, W, x, N, K, B, bias, out, RT, pf);
     }
 }
 
@@ -840,7 +900,7 @@ extern "C" int jl_dec_destroy(jl_dec* h) {
     if (!h) return JL_OK;
     if (h->moe) jl_moe_destroy(h->moe);
     void* ptrs[] = {h->embed, h->norm1, h->norm2, h->fnorm, h->qnw, h->knw, h->wqkv, h->wo, h->bqkv, h->lm,
-                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->scores, h->logits,
+                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->tT, h->attT, h->scores, h->logits,
                     h->tok, h->arg_v, h->arg_i, h->pre_pos, h->pre_slot, h->err, h->stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -871,6 +931,7 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
     h->eps = c->eps;
     h->qn = h->H * h->hd, h->kn = h->KH * h->hd, h->nqkv = h->qn + 2 * h->kn;
     h->max_batch = max_batch, h->slots = slots;
+    h->Bp = (max_batch + 7) / 8 * 8;
     rc = jl_moe_create(c, max_batch, &h->moe);
     if (rc) {
         delete h;
@@ -901,6 +962,8 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
         {(void**)&h->qkv, (size_t)max_batch * h->nqkv * 4},
         {(void**)&h->att, (size_t)max_batch * h->qn * 4},
         {(void**)&h->scores, (size_t)max_batch * h->H * h->maxT * 4},
+        {(void**)&h->tT, max_batch >= 16 ? (size_t)d * h->Bp * 4 : 0},
+        {(void**)&h->attT, max_batch >= 16 ? (size_t)h->qn * h->Bp * 4 : 0},
         {(void**)&h->logits, (size_t)max_batch * V * 4},
         {(void**)&h->tok, (size_t)max_batch * 4},
         {(void**)&h->arg_v, (size_t)max_batch * kArgParts * 4},
@@ -1043,6 +1106,10 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err;
     aa.sqn = attn_sqn(h->qk_type, h->H, h->KH, h->hd);
     aa.nslots = h->slots;
+    // column-major copies of the matvec inputs for the register-tiled kernel (B >= 16)
+    float* tT = B >= 16 ? h->tT : nullptr;
+    aa.attT = B >= 16 ? h->attT : nullptr;
+    aa.Bp = h->Bp;
     // attention work split: score blocks (group, sequence, position split) and
     // value blocks (head, sequence, dimension slice), about two blocks per SM
     const qk_layout qkl(h->qk_type, h->H, h->KH, h->hd);
@@ -1060,7 +1127,14 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
         return ds;
     };
     int hpb = gsz, dslices = pick_slices(h->KH * B, sms);
-    auto pv_bytes = [&](int hp, int ds) { return ((size_t)hp * maxT4 + 2 * kPvTile * (h->hd / ds)) * sizeof(float); };
+    auto pv_bytes = [&](int hp, int ds) {
+        return ((size_t)hp * maxT4 + (size_t)kPvRing * kPvTile * (h->hd / ds)) * sizeof(float);
+    };
+    // all of a block's V rows in shared memory when they fit (small batches:
+    // one wait instead of a barrier per tile)
+    auto pv_whole_bytes = [&](int hp, int ds) {
+        return ((size_t)hp * maxT4 + (size_t)maxT4 * (h->hd / ds)) * sizeof(float);
+    };
     if (gsz > 8 || 8 % gsz || h->KH * B * dslices < sms || hpb * (h->hd / dslices) / 2 > kPvItems * kPvThreads ||
         pv_bytes(hpb, dslices) > 200 * 1024) {
         hpb = 1;
@@ -1068,16 +1142,17 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     }
     const int pv_items = (hpb * (h->hd / dslices) / 2 + kPvThreads - 1) / kPvThreads;
     const int dw = h->hd / dslices;
-    const size_t pv_smem = pv_bytes(hpb, dslices);
+    const int pv_whole = pv_whole_bytes(hpb, dslices) <= 100 * 1024;
+    const size_t pv_smem = pv_whole ? pv_whole_bytes(hpb, dslices) : pv_bytes(hpb, dslices);
     if (qk_smem > 200 * 1024 || pv_smem > 200 * 1024) return JL_ERR_INVALID;
     for (int l = 0; l < h->L; l++) {
         // norm1 (adding the previous layer's MoE output to the residual)
         rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)(l ? h->h2 : nullptr),
-                    (const uint16_t*)(h->norm1 + (size_t)l * d), h->eps, d, h->t);
+                    (const uint16_t*)(h->norm1 + (size_t)l * d), h->eps, d, h->t, tT, h->Bp);
         if (!rc && l > 0) rc = snap(l - 1, 6, h->h, d);
         if (!rc) rc = snap(l, 0, h->t, d);
         if (!rc)
-            rc = launch_mv<uint16_t>(h->wqkv + (size_t)l * h->nqkv * d, h->t, h->nqkv, d, B,
+            rc = launch_mv<uint16_t>(h->wqkv + (size_t)l * h->nqkv * d, h->t, tT, h->Bp, h->nqkv, d, B,
                                      h->bias ? h->bqkv + (size_t)l * h->nqkv : nullptr, h->qkv, sms, s);
         if (!rc) {
             aa.l = l;
@@ -1092,15 +1167,17 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
             if (!rc) {
                 auto kern = pv_items <= 1 ? k_attn_pv<1> : pv_items <= 2 ? k_attn_pv<2> : k_attn_pv<4>;
                 rc = launch(kern, dim3(h->H / hpb, B, dslices), dim3(kPvThreads), pv_smem, s, aa,
-                            (const float*)h->scores, hpb, dw);
+                            (const float*)h->scores, hpb, dw, pv_whole);
             }
         }
-        if (!rc) rc = launch_mv<uint16_t>(h->wo + (size_t)l * d * h->qn, h->att, d, h->qn, B, nullptr, h->h2, sms, s);
+        if (!rc)
+            rc = launch_mv<uint16_t>(h->wo + (size_t)l * d * h->qn, h->att, aa.attT, h->Bp, d, h->qn, B, nullptr, h->h2,
+                                     sms, s);
         if (!rc) rc = snap(l, 1, h->h2, d);
         // norm2 (adding the attention output to the residual), then the MoE layer
         if (!rc)
             rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)h->h2,
-                        (const uint16_t*)(h->norm2 + (size_t)l * d), h->eps, d, h->t);
+                        (const uint16_t*)(h->norm2 + (size_t)l * d), h->eps, d, h->t, (float*)nullptr, h->Bp);
         if (!rc) rc = snap(l, 2, h->h, d);
         if (!rc) rc = snap(l, 3, h->t, d);
         if (!rc) {
@@ -1113,13 +1190,13 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
         if (rc) return rc;
     }
     rc = launch(k_rms, dim3(B), dim3(kNormThreads), nsm, s, h->h, (const float*)h->h2, (const uint16_t*)h->fnorm,
-                h->eps, d, h->t);
+                h->eps, d, h->t, tT, h->Bp);
     if (!rc) rc = snap(h->L - 1, 6, h->h, d);
     if (rc) return rc;
     if (logits || tok) {
         const int nb = prefill ? 1 : B;
         const float* tx = prefill ? h->t + (size_t)(B - 1) * d : h->t;
-        rc = launch_mv<float>(h->lm, tx, h->V, d, nb, nullptr, h->logits, sms, s);
+        rc = launch_mv<float>(h->lm, tx, prefill ? nullptr : tT, h->Bp, h->V, d, nb, nullptr, h->logits, sms, s);
         if (!rc && tok)
             rc = launch(k_argmax_part, dim3(kArgParts, nb), dim3(256), 0, s, (const float*)h->logits, h->V,
                         h->arg_v, h->arg_i);
@@ -1369,7 +1446,8 @@ int dropin_step(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* po
         cudaFreeAsync(dbg_d, e->st);
     }
     if (!rc && logits)
-        rc = launch_mv<float>(h->lm, h->t, h->V, c->d, B, nullptr, h->logits, h->moe->sm_count, e->st);
+        rc = launch_mv<float>(h->lm, h->t, B >= 16 ? h->tT : nullptr, h->Bp, h->V, c->d, B, nullptr, h->logits,
+                              h->moe->sm_count, e->st);
     if (rc) return rc;
     // the new K/V row of every layer back into the caller's caches
     for (int b = 0; b < B; b++)

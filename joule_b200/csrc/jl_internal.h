@@ -127,11 +127,12 @@ enum {
 int jl_device_once(int key, int (*setup)());
 
 // Decode-step matvecs for B >= 16 tokens (jl_mm.cu): the reference's 8-lane
-// FMA order, register-tiled; W in the chunked lane-major layout (jl_mv.cuh).
+// FMA order, register-tiled; W in the chunked lane-major layout (jl_mv.cuh),
+// the tokens column-major xT [K][Bp] (Bp a multiple of 4, >= B).
 bool jl_mm_ok(int N, int K, int B);
 template <typename WT>
-int jl_launch_mm(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
-                 cudaStream_t s);
+int jl_launch_mm(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,
+                 int sm_count, cudaStream_t s);
 
 // Fingerprint of the host weights a (cfg, W) pair points at: leading bytes of
 // the router rows and of the first and last expert records, the expert

@@ -6,9 +6,11 @@
 // At these batch sizes the work is FP32-FMA bound (the order forbids tensor
 // cores), so the kernel is register-tiled like an SGEMM: block = BN rows x BT
 // tokens; warp j is lane j of the reference's accumulator, and its thread
-// (rg, tg) holds RN x RT chains (rows rg*RN + r, tokens tg + 8q): per 8-column
-// step it reads RN weights (RN/4 16-byte shared loads) and RT token values
-// and issues RN*RT FMAs. Each block reads its weight rows once.
+// (rg, tg) holds RN x RT chains (rows rg*RN + r, tokens tg*RT + q): per
+// 8-column step it reads RN weights and RT token values (RN/4 and RT/4 16-byte
+// shared loads) and issues RN*RT FMAs. Each block reads its weight rows once.
+// The token rows come column-major ([K][Bp], written by the producer kernel
+// beside its row-major output), so a step's RT tokens are contiguous.
 //
 // Stages of 64 columns flow through a ring of 3 to 6 slots of 16-byte cp.async copies:
 // the weight rows (the chunked lane-major layout of jl_mv.cuh, so a block's
@@ -25,8 +27,10 @@
 namespace jl {
 
 constexpr int kMmThreads = 256;
-constexpr int kMmXStride = 68;  // floats per staged token row (64 + 4: 16-byte rows, spread banks)
-constexpr size_t kMmSmemCap = 110 * 1024;  // two blocks per SM
+constexpr int kMmXPad = 4;  // floats of padding per staged column (16-byte rows)
+// shared memory per block: three blocks per SM for the shapes whose registers
+// allow three (RN x RT <= 16), two for the others
+constexpr size_t kMmSmemCap3 = 72 * 1024, kMmSmemCap2 = 110 * 1024;
 
 template <typename WT, int RN, int RT>
 struct mm_shape {
@@ -34,12 +38,14 @@ struct mm_shape {
     static constexpr int U = mv_traits<WT>::U;
     static constexpr int CPS = 8 / U;                 // weight chunks per 64-column stage
     static constexpr int WSS = BN + 4;                // fp32 weight row stride [step][lane][row]
-    static constexpr int X_F = BT * kMmXStride;       // floats per token stage
+    static constexpr int XS = BT + kMmXPad;           // floats per staged column of tokens
+    static constexpr int X_F = 64 * XS;               // floats per token stage [64 columns][XS]
     static constexpr int WR_B = CPS * BN * 8 * 16;    // raw weight bytes per stage
     static constexpr int WS_F = 8 * 8 * WSS;          // floats per widened weight stage
-    // ring depth: as many 64-column stages as fit two blocks per SM (3 to 6)
+    // ring depth: as many 64-column stages as fit the blocks per SM (3 to 6)
     static constexpr size_t stage_bytes = (size_t)X_F * 4 + WR_B;
-    static constexpr int NS_fit = (int)((kMmSmemCap - (size_t)2 * WS_F * 4) / stage_bytes);
+    static constexpr size_t cap = RN * RT <= 16 ? kMmSmemCap3 : kMmSmemCap2;
+    static constexpr int NS_fit = (int)((cap - (size_t)2 * WS_F * 4) / stage_bytes);
     static constexpr int NS = NS_fit < 3 ? 3 : NS_fit > 6 ? 6 : NS_fit;
     static constexpr size_t ring_bytes = (size_t)NS * stage_bytes + (size_t)2 * WS_F * 4;
     static constexpr size_t red_bytes = (size_t)8 * BT * (BN + 1) * 4;
@@ -64,13 +70,13 @@ __device__ __forceinline__ void widen(uint4 v, float* dst, int stride, float) { 
 }
 
 template <typename WT, int RN, int RT>
-__global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, const float* __restrict__ x, int N,
-                                                      int K, int B, const float* __restrict__ bias,
+__global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, const float* __restrict__ xT, int Bp,
+                                                      int N, int K, int B, const float* __restrict__ bias,
                                                       float* __restrict__ out) {
     using S = mm_shape<WT, RN, RT>;
-    constexpr int BN = S::BN, BT = S::BT, U = S::U, CPS = S::CPS, WSS = S::WSS, NS = S::NS;
+    constexpr int BN = S::BN, BT = S::BT, U = S::U, CPS = S::CPS, WSS = S::WSS, NS = S::NS, XS = S::XS;
     extern __shared__ __align__(16) float sm[];
-    float* xr = sm;                                                      // [NS][BT][kMmXStride]
+    float* xr = sm;                                                      // [NS][64][XS]
     uint8_t* wr = reinterpret_cast<uint8_t*>(sm + NS * S::X_F);         // [NS][CPS][BN][8][U] raw
     float* ws = reinterpret_cast<float*>(wr + NS * S::WR_B);            // [2][8 steps][8 lanes][WSS]
     const int tid = threadIdx.x, j = tid >> 5, lane = tid & 31, rg = lane >> 3, tg = lane & 7;
@@ -86,11 +92,11 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
                 cp_async16(dst + p * 16, W + (size_t)(st * CPS + cc) * cstride + (size_t)(n0 * 8) * U + (size_t)p % (BN * 8) * U);
         }
     };
-    auto issue_x = [&](int st) {  // the token rows' 64 columns of this stage
+    auto issue_x = [&](int st) {  // this stage's 64 columns of the token tile, 4 tokens per copy
         float* dst = xr + (st % NS) * S::X_F;
-        for (int p = tid; p < BT * 16; p += kMmThreads) {
-            const int t = p >> 4, c = (p & 15) * 4;
-            if (t0 + t < B) cp_async16(dst + t * kMmXStride + c, x + (size_t)(t0 + t) * K + st * 64 + c);
+        for (int p = tid; p < 64 * (BT / 4); p += kMmThreads) {
+            const int c = p / (BT / 4), q4 = (p % (BT / 4)) * 4;
+            if (t0 + q4 < B) cp_async16(dst + c * XS + q4, xT + (size_t)(st * 64 + c) * Bp + t0 + q4);
         }
     };
     auto widen_stage = [&](int st) {  // raw weights of stage st -> ws[st & 1][s][j][row]
@@ -132,7 +138,7 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
         cp_async_commit();
         if (st + 1 < nst) widen_stage(st + 1);
         const float* wsb = ws + (st & 1) * S::WS_F + j * WSS + rg * RN;
-        const float* xb = xr + (st % NS) * S::X_F + tg * kMmXStride + j;
+        const float* xb = xr + (st % NS) * S::X_F + j * XS + tg * RT;
 #pragma unroll
         for (int s = 0; s < 8; s++) {
             float w[RN], xv[RT];
@@ -144,8 +150,23 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
                 w[4 * r4 + 2] = v.z;
                 w[4 * r4 + 3] = v.w;
             }
+            if constexpr (RT % 4 == 0) {
 #pragma unroll
-            for (int q = 0; q < RT; q++) xv[q] = xb[q * 8 * kMmXStride + s * 8];
+                for (int q4 = 0; q4 < RT / 4; q4++) {
+                    const float4 v = *reinterpret_cast<const float4*>(xb + s * 8 * XS + q4 * 4);
+                    xv[4 * q4] = v.x;
+                    xv[4 * q4 + 1] = v.y;
+                    xv[4 * q4 + 2] = v.z;
+                    xv[4 * q4 + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int q2 = 0; q2 < RT / 2; q2++) {
+                    const float2 v = *reinterpret_cast<const float2*>(xb + s * 8 * XS + q2 * 2);
+                    xv[2 * q2] = v.x;
+                    xv[2 * q2 + 1] = v.y;
+                }
+            }
 #pragma unroll
             for (int r = 0; r < RN; r++)
 #pragma unroll
@@ -158,7 +179,7 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
 #pragma unroll
     for (int r = 0; r < RN; r++)
 #pragma unroll
-        for (int q = 0; q < RT; q++) red[(j * BT + tg + 8 * q) * (BN + 1) + rg * RN + r] = acc[r][q];
+        for (int q = 0; q < RT; q++) red[(j * BT + tg * RT + q) * (BN + 1) + rg * RN + r] = acc[r][q];
     __syncthreads();
     for (int o = tid; o < BN * BT; o += kMmThreads) {
         const int r = o % BN, t = o / BN;
@@ -173,10 +194,11 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
 }
 
 template <typename WT, int RN, int RT>
-int launch_mm_shape(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, cudaStream_t s) {
+int launch_mm_shape(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,
+                    cudaStream_t s) {
     using S = mm_shape<WT, RN, RT>;
     const dim3 grid((N + S::BN - 1) / S::BN, (B + S::BT - 1) / S::BT);
-    return launch(k_mm<WT, RN, RT>, grid, dim3(kMmThreads), S::smem, s, W, x, N, K, B, bias, out);
+    return launch(k_mm<WT, RN, RT>, grid, dim3(kMmThreads), S::smem, s, W, xT, Bp, N, K, B, bias, out);
 }
 
 template <typename WT, int RN, int RT>
@@ -210,26 +232,27 @@ bool jl_mm_ok(int N, int K, int B) { return B >= 16 && K % 64 == 0 && N >= 1; }
 // projection-sized N, 16-row tiles (more blocks) except at long K, where the
 // per-block work is large anyway.
 template <typename WT>
-int jl_launch_mm(const WT* W, const float* x, int N, int K, int B, const float* bias, float* out, int sm_count,
-                 cudaStream_t s) {
+int jl_launch_mm(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,
+                 int sm_count, cudaStream_t s) {
     using namespace jl;
-    if (!jl_mm_ok(N, K, B)) return JL_ERR_INVALID;
+    if (!jl_mm_ok(N, K, B) || Bp % 4 || Bp < B) return JL_ERR_INVALID;
     const int rc = jl_device_once(sizeof(WT) == 2 ? kOnceMmBf16 : kOnceMmF32, [] { return mm_attrs_for<WT>(); });
     if (rc) return rc;
     const long rows32 = (N + 31) / 32;
     if (rows32 >= 8L * sm_count) {  // lm_head-sized
-        if (B <= 16) return launch_mm_shape<WT, 8, 2>(W, x, N, K, B, bias, out, s);
-        if (B <= 32) return launch_mm_shape<WT, 8, 4>(W, x, N, K, B, bias, out, s);
-        return launch_mm_shape<WT, 8, 8>(W, x, N, K, B, bias, out, s);
+        if (B <= 16) return launch_mm_shape<WT, 8, 2>(W, xT, Bp, N, K, B, bias, out, s);
+        if (B <= 32) return launch_mm_shape<WT, 8, 4>(W, xT, Bp, N, K, B, bias, out, s);
+        return launch_mm_shape<WT, 8, 8>(W, xT, Bp, N, K, B, bias, out, s);
     }
-    if (B <= 16) return launch_mm_shape<WT, 4, 2>(W, x, N, K, B, bias, out, s);
+    if (B <= 16) return launch_mm_shape<WT, 4, 2>(W, xT, Bp, N, K, B, bias, out, s);
     if (K >= 4096) {
-        if (B <= 32) return launch_mm_shape<WT, 8, 2>(W, x, N, K, B, bias, out, s);
-        return launch_mm_shape<WT, 8, 4>(W, x, N, K, B, bias, out, s);
+        if (B <= 32) return launch_mm_shape<WT, 8, 2>(W, xT, Bp, N, K, B, bias, out, s);
+        return launch_mm_shape<WT, 8, 4>(W, xT, Bp, N, K, B, bias, out, s);
     }
-    return launch_mm_shape<WT, 4, 4>(W, x, N, K, B, bias, out, s);
+    return launch_mm_shape<WT, 4, 4>(W, xT, Bp, N, K, B, bias, out, s);
 }
 
-template int jl_launch_mm<uint16_t>(const uint16_t*, const float*, int, int, int, const float*, float*, int,
+template int jl_launch_mm<uint16_t>(const uint16_t*, const float*, int, int, int, int, const float*, float*, int,
                                     cudaStream_t);
-template int jl_launch_mm<float>(const float*, const float*, int, int, int, const float*, float*, int, cudaStream_t);
+template int jl_launch_mm<float>(const float*, const float*, int, int, int, int, const float*, float*, int,
+                                 cudaStream_t);
