@@ -315,7 +315,7 @@ constexpr int kQkRing = 3;    // K tiles in the ring (two in flight while one is
 constexpr int kPvThreads = 256;
 constexpr int kPvTile = 16;   // positions per V tile
 constexpr int kPvRing = 8;    // V tiles in the ring (seven in flight while one is used)
-constexpr int kPvItems = 4;   // (head, dimension pair) items per thread at most (NI of k_attn_pv)
+constexpr int kPvItems = 4;   // (head, four dimensions) items per thread at most (NI of k_attn_pv)
 
 // Shared-memory layout of k_attn_qk (floats): q [gsz][hd + 4], k [hd],
 // v [hd], squares, inverse norms [gsz + 1] (padded to 4), two K tiles
@@ -554,34 +554,38 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
     __syncthreads();
     const float sum = stat[hh];
     for (int t = sub; t < T; t += nsub) p[t] = __fdiv_rn(p[t], sum);
-    // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229): items (head, pair of
+    // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229): items (head, four
     // dimensions), NI per thread, their chains interleaved
-    const int np = dw / 2, items = hpb * np;
+    const int nq = dw / 4, items = hpb * nq;  // items: (head, four consecutive dimensions)
     int ih[NI], ii[NI];
-    float ox[NI], oy[NI];
+    float4 o[NI];  // the item's four chains, scalar products and sums (a packed fp32-pair
+                   // multiply and add measured different bits from the reference here)
 #pragma unroll
     for (int k = 0; k < NI; k++) {
         const int it = min(tid + k * kPvThreads, items - 1);
-        ih[k] = it / np;
-        ii[k] = it - ih[k] * np;
-        ox[k] = oy[k] = 0.0f;
+        ih[k] = it / nq;
+        ii[k] = it - ih[k] * nq;
+        o[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     const bool live = tid < items;  // the last item's thread set is complete (items <= NI * threads)
+    auto rows = [&](const float* vbuf, int t0, int nt) {
+#pragma unroll 4
+        for (int r = 0; r < nt; r++) {
+#pragma unroll
+            for (int k = 0; k < NI; k++) {
+                const float pp = p_s[ih[k] * maxT4 + t0 + r];
+                const float4 v = *reinterpret_cast<const float4*>(vbuf + r * dw + 4 * ii[k]);
+                o[k].x = __fadd_rn(o[k].x, __fmul_rn(pp, v.x));
+                o[k].y = __fadd_rn(o[k].y, __fmul_rn(pp, v.y));
+                o[k].z = __fadd_rn(o[k].z, __fmul_rn(pp, v.z));
+                o[k].w = __fadd_rn(o[k].w, __fmul_rn(pp, v.w));
+            }
+        }
+    };
     if (whole) {  // one wait, then the chains over every row without a barrier
         cp_async_wait<0>();
         __syncthreads();
-        if (live) {
-#pragma unroll 4
-            for (int r = 0; r < T; r++) {
-#pragma unroll
-                for (int k = 0; k < NI; k++) {
-                    const float pp = p_s[ih[k] * maxT4 + r];
-                    const float2 v = *reinterpret_cast<const float2*>(vt0 + r * dw + 2 * ii[k]);
-                    ox[k] = __fadd_rn(ox[k], __fmul_rn(pp, v.x));
-                    oy[k] = __fadd_rn(oy[k], __fmul_rn(pp, v.y));
-                }
-            }
-        }
+        if (live) rows(vt0, 0, T);
     }
     for (int j = 0; j < (whole ? 0 : ntiles); j++) {
         const int t0 = j * kPvTile, nt = min(kPvTile, T - t0);
@@ -591,28 +595,19 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
         else cp_async_commit();
         cp_async_wait<kPvRing - 1>();
         __syncthreads();
-        if (live) {
-#pragma unroll 4
-            for (int r = 0; r < nt; r++) {
-#pragma unroll
-                for (int k = 0; k < NI; k++) {
-                    const float pp = p_s[ih[k] * maxT4 + t0 + r];
-                    const float2 v = *reinterpret_cast<const float2*>(buf + r * dw + 2 * ii[k]);
-                    ox[k] = __fadd_rn(ox[k], __fmul_rn(pp, v.x));
-                    oy[k] = __fadd_rn(oy[k], __fmul_rn(pp, v.y));
-                }
-            }
-        }
+        if (live) rows(buf, t0, nt);
         __syncthreads();
     }
 #pragma unroll
     for (int k = 0; k < NI; k++)
         if (tid + k * kPvThreads < items) {
-            const int col = (h0 + ih[k]) * hd + z * dw + 2 * ii[k];
-            *reinterpret_cast<float2*>(a.att + (size_t)b * qn + col) = make_float2(ox[k], oy[k]);
+            const int col = (h0 + ih[k]) * hd + z * dw + 4 * ii[k];
+            *reinterpret_cast<float4*>(a.att + (size_t)b * qn + col) = o[k];
             if (a.attT) {
-                a.attT[(size_t)col * a.Bp + b] = ox[k];
-                a.attT[(size_t)(col + 1) * a.Bp + b] = oy[k];
+                a.attT[(size_t)col * a.Bp + b] = o[k].x;
+                a.attT[(size_t)(col + 1) * a.Bp + b] = o[k].y;
+                a.attT[(size_t)(col + 2) * a.Bp + b] = o[k].z;
+                a.attT[(size_t)(col + 3) * a.Bp + b] = o[k].w;
             }
         }
 }
@@ -1135,12 +1130,12 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     auto pv_whole_bytes = [&](int hp, int ds) {
         return ((size_t)hp * maxT4 + (size_t)maxT4 * (h->hd / ds)) * sizeof(float);
     };
-    if (gsz > 8 || 8 % gsz || h->KH * B * dslices < sms || hpb * (h->hd / dslices) / 2 > kPvItems * kPvThreads ||
+    if (gsz > 8 || 8 % gsz || h->KH * B * dslices < sms || hpb * (h->hd / dslices) / 4 > kPvItems * kPvThreads ||
         pv_bytes(hpb, dslices) > 200 * 1024) {
         hpb = 1;
         dslices = pick_slices(h->H * B, 2 * sms);
     }
-    const int pv_items = (hpb * (h->hd / dslices) / 2 + kPvThreads - 1) / kPvThreads;
+    const int pv_items = (hpb * (h->hd / dslices) / 4 + kPvThreads - 1) / kPvThreads;
     const int dw = h->hd / dslices;
     const int pv_whole = pv_whole_bytes(hpb, dslices) <= 100 * 1024;
     const size_t pv_smem = pv_whole ? pv_whole_bytes(hpb, dslices) : pv_bytes(hpb, dslices);
