@@ -40,7 +40,8 @@ def test_clock_summary_without_a_record():
 
 
 def test_traffic_lookup_reads_the_committed_summary():
-    assert bench.traffic_from_profiles("k_expert_tc<false>", 64) == 229172736.0
+    assert bench.traffic_from_profiles("k_expert_tc<false>", 64) == 232533504.0
+    assert bench.traffic_from_profiles("k_gateup_gemv", 1) == 13398016.0
     assert bench.traffic_from_profiles("k_expert_tc<false>", 63) is None
 
 
