@@ -6,7 +6,7 @@
 // At these batch sizes the work is FP32-FMA bound (the order forbids tensor
 // cores), so the kernel is register-tiled like an SGEMM: block = BN rows x BT
 // tokens; warp j is lane j of the reference's accumulator, and its thread
-// (rg, tg) holds RN x RT chains (rows rg*RN + r, tokens tg*RT + q): per
+// (rg, tg) holds RN x RT chains (rows rg*RN + r, tokens mm_token(tg, q)): per
 // 8-column step it reads RN weights and RT token values (RN/4 and RT/4 16-byte
 // shared loads) and issues RN*RT FMAs. Each block reads its weight rows once.
 // The token rows come column-major ([K][Bp], written by the producer kernel
@@ -51,6 +51,14 @@ struct mm_shape {
     static constexpr size_t red_bytes = (size_t)8 * BT * (BN + 1) * 4;
     static constexpr size_t smem = ring_bytes > red_bytes ? ring_bytes : red_bytes;
 };
+
+// Token (within the block's tile) of chain q of thread tg: runs of four
+// consecutive tokens per lane, the lanes' runs side by side (tile tokens
+// 4 tg .. 4 tg + 3, then 32 + 4 tg .., ...), so a warp's 16-byte loads of one
+// run cover 128 contiguous bytes; two per lane when RT = 2.
+__host__ __device__ constexpr int mm_token(int tg, int q, int RT) {
+    return RT >= 4 ? (q / 4) * 32 + 4 * tg + q % 4 : RT * tg + q;
+}
 
 __device__ __forceinline__ void widen(uint4 v, float* dst, int stride, uint16_t) {  // 8 bf16 -> rows of dst
     dst[0] = __uint_as_float(v.x << 16);
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
         cp_async_commit();
         if (st + 1 < nst) widen_stage(st + 1);
         const float* wsb = ws + (st & 1) * S::WS_F + j * WSS + rg * RN;
-        const float* xb = xr + (st % NS) * S::X_F + j * XS + tg * RT;
+        const float* xb = xr + (st % NS) * S::X_F + j * XS + (RT >= 4 ? 4 : RT) * tg;
 #pragma unroll
         for (int s = 0; s < 8; s++) {
             float w[RN], xv[RT];
@@ -153,7 +161,7 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
             if constexpr (RT % 4 == 0) {
 #pragma unroll
                 for (int q4 = 0; q4 < RT / 4; q4++) {
-                    const float4 v = *reinterpret_cast<const float4*>(xb + s * 8 * XS + q4 * 4);
+                    const float4 v = *reinterpret_cast<const float4*>(xb + s * 8 * XS + q4 * 32);
                     xv[4 * q4] = v.x;
                     xv[4 * q4 + 1] = v.y;
                     xv[4 * q4 + 2] = v.z;
@@ -179,7 +187,7 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
 #pragma unroll
     for (int r = 0; r < RN; r++)
 #pragma unroll
-        for (int q = 0; q < RT; q++) red[(j * BT + tg * RT + q) * (BN + 1) + rg * RN + r] = acc[r][q];
+        for (int q = 0; q < RT; q++) red[(j * BT + mm_token(tg, q, RT)) * (BN + 1) + rg * RN + r] = acc[r][q];
     __syncthreads();
     for (int o = tid; o < BN * BT; o += kMmThreads) {
         const int r = o % BN, t = o / BN;
