@@ -92,28 +92,53 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
     const int nst = K / 64;
     const size_t cstride = (size_t)N * 8 * U;  // elements per chunk of W'
 
+    // Per-thread copy and widen assignments are the same at every stage: their
+    // offsets are computed once (the stage adds a constant).
+    constexpr int PW = CPS * BN * 8;            // 16-byte weight pieces per stage
+    constexpr int KW = (PW + kMmThreads - 1) / kMmThreads;
+    constexpr int PX = 64 * (BT / 4);           // 16-byte token pieces per stage
+    constexpr int KX = (PX + kMmThreads - 1) / kMmThreads;
+    // element offsets (32-bit: a stage adds CPS * N * 8U for the weights, 64 Bp
+    // for the tokens, both far below 2^31 here)
+    const WT* wbase = W + (size_t)(n0 * 8) * U;
+    const float* xbase = xT + t0;
+    int wsrc[KW], wst[KW], xsrc[KX], xdst[KX];  // wst: widened offset (floats), -1: no piece
+    unsigned wlive = 0, xlive = 0;               // bit k: piece k exists and is in range
+#pragma unroll
+    for (int k = 0; k < KW; k++) {
+        const int p = tid + k * kMmThreads;
+        const int cc = p / (BN * 8), r = (p >> 3) % BN, jj = p & 7;
+        if (p < PW && n0 + r < N) wlive |= 1u << k;
+        wsrc[k] = cc * (int)cstride + (p % (BN * 8)) * U;
+        wst[k] = p < PW ? ((cc * U) * 8 + jj) * WSS + r : -1;
+    }
+#pragma unroll
+    for (int k = 0; k < KX; k++) {
+        const int p = tid + k * kMmThreads;
+        const int c = p / (BT / 4), q4 = (p % (BT / 4)) * 4;
+        if (p < PX && t0 + q4 < B) xlive |= 1u << k;
+        xsrc[k] = c * Bp + q4;
+        xdst[k] = c * XS + q4;
+    }
+    const int wstep = CPS * (int)cstride, xstep = 64 * Bp;
     auto issue_w = [&](int st) {  // this stage's weight rows: CPS runs of BN * 128 bytes
         uint8_t* dst = wr + (st % NS) * S::WR_B;
-        for (int p = tid; p < CPS * BN * 8; p += kMmThreads) {
-            const int cc = p / (BN * 8), r = (p >> 3) % BN;
-            if (n0 + r < N)
-                cp_async16(dst + p * 16, W + (size_t)(st * CPS + cc) * cstride + (size_t)(n0 * 8) * U + (size_t)p % (BN * 8) * U);
-        }
+#pragma unroll
+        for (int k = 0; k < KW; k++)
+            if ((wlive >> k) & 1u) cp_async16(dst + (tid + k * kMmThreads) * 16, wbase + wsrc[k] + st * wstep);
     };
     auto issue_x = [&](int st) {  // this stage's 64 columns of the token tile, 4 tokens per copy
         float* dst = xr + (st % NS) * S::X_F;
-        for (int p = tid; p < 64 * (BT / 4); p += kMmThreads) {
-            const int c = p / (BT / 4), q4 = (p % (BT / 4)) * 4;
-            if (t0 + q4 < B) cp_async16(dst + c * XS + q4, xT + (size_t)(st * 64 + c) * Bp + t0 + q4);
-        }
+#pragma unroll
+        for (int k = 0; k < KX; k++)
+            if ((xlive >> k) & 1u) cp_async16(dst + xdst[k], xbase + xsrc[k] + st * xstep);
     };
     auto widen_stage = [&](int st) {  // raw weights of stage st -> ws[st & 1][s][j][row]
         const uint4* src = reinterpret_cast<const uint4*>(wr + (st % NS) * S::WR_B);
         float* dst = ws + (st & 1) * S::WS_F;
-        for (int p = tid; p < CPS * BN * 8; p += kMmThreads) {
-            const int cc = p / (BN * 8), r = (p >> 3) % BN, jj = p & 7;
-            widen(src[p], dst + ((cc * U) * 8 + jj) * WSS + r, 8 * WSS, WT());
-        }
+#pragma unroll
+        for (int k = 0; k < KW; k++)
+            if (wst[k] >= 0) widen(src[tid + k * kMmThreads], dst + wst[k], 8 * WSS, WT());
     };
 
     // weights do not depend on the previous kernel: their first NS - 1 stages
@@ -228,7 +253,8 @@ int mm_attrs_for() {
 
 }  // namespace jl
 
-bool jl_mm_ok(int N, int K, int B) { return B >= 16 && K % 64 == 0 && N >= 1; }
+// (the kernel's per-thread copy offsets are 32-bit: the matrix stays below 2^31 elements)
+bool jl_mm_ok(int N, int K, int B) { return B >= 16 && K % 64 == 0 && N >= 1 && (long long)N * K < (1ll << 31); }
 
 // Tile choice (BN x BT = 4 RN x 8 RT), from timings of every shape on the
 // decode step's matrices on a B200 (QKV 5120 x 2048, o_proj 2048 x 4096,
@@ -243,7 +269,7 @@ template <typename WT>
 int jl_launch_mm(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,
                  int sm_count, cudaStream_t s) {
     using namespace jl;
-    if (!jl_mm_ok(N, K, B) || Bp % 4 || Bp < B) return JL_ERR_INVALID;
+    if (!jl_mm_ok(N, K, B) || Bp % 4 || Bp < B || (long long)K * Bp >= (1ll << 31)) return JL_ERR_INVALID;
     const int rc = jl_device_once(sizeof(WT) == 2 ? kOnceMmBf16 : kOnceMmF32, [] { return mm_attrs_for<WT>(); });
     if (rc) return rc;
     const long rows32 = (N + 31) / 32;
