@@ -286,6 +286,7 @@ struct attn_args {
     int sqn;                 // floats per squares buffer of k_kv_append: max(qn, kn) for whole-vector norms, else hd
     float eps;
     int* err;
+    float* qr;               // [B][H][hd] q after QK-norm and RoPE (register-tiled attention)
 };
 
 // Squares of v[0..n) into sq (n % 4 == 0, 16-byte aligned), loads batched.
@@ -309,6 +310,92 @@ __device__ __forceinline__ void squares(const float* __restrict__ v, int n, floa
     }
 }
 
+// Sum of squares of v[0..n) in index order by the calling thread (n % 4 == 0,
+// v 16-byte aligned): each square rounded, then added (decode_kernel.c:1181).
+__device__ __forceinline__ float chain_sumsq(const float* v, int n) {
+    float s = 0.0f;
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+#pragma unroll 8
+    for (int i = 0; i < n / 4; i++) {
+        const float4 q = v4[i];
+        s = __fadd_rn(s, __fmul_rn(q.x, q.x));
+        s = __fadd_rn(s, __fmul_rn(q.y, q.y));
+        s = __fadd_rn(s, __fmul_rn(q.z, q.z));
+        s = __fadd_rn(s, __fmul_rn(q.w, q.w));
+    }
+    return s;
+}
+
+// The score kernels' prologue for KV group g of sequence b at position pos:
+// the group's q heads into q_s [gsz][qs], the k and v rows into k_s, v_s
+// [hd], then QK-norm and RoPE of q_s and k_s (decode_kernel.c:1162-1199).
+// The rows and this position's RoPE tables (cs_s, sn_s [hd]) arrive as one
+// batch of 16-byte copies with a single wait (the caller's earlier copy
+// groups complete with it). sq holds the squares of the whole-vector norm
+// (qk_type 2; qn + kn floats, each part padded to 4), inv gsz + 1 floats.
+// Every thread of the block calls it; it ends with a barrier.
+__device__ void qk_prepare(const attn_args& a, int g, int b, int pos, float* q_s, int qs, float* k_s, float* v_s,
+                           float* cs_s, float* sn_s, float* sq, float* inv) {
+    const int hd = a.hd, qn = a.H * hd, kn = a.KH * hd, gsz = a.H / a.KH, h0 = g * gsz, tid = threadIdx.x;
+    const int c4 = hd / 4;
+    const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
+    for (int r = 0; r < gsz + 4; r++) {  // q rows, k, v, cos, sin (all 16-byte aligned: hd % 4 == 0)
+        float* dst = r < gsz ? q_s + r * qs : r == gsz ? k_s : r == gsz + 1 ? v_s : r == gsz + 2 ? cs_s : sn_s;
+        const float* src = r < gsz         ? row + (h0 + r) * hd
+                           : r == gsz      ? row + qn + g * hd
+                           : r == gsz + 1  ? row + qn + kn + g * hd
+                           : r == gsz + 2  ? a.cosb + (size_t)pos * hd
+                                           : a.sinb + (size_t)pos * hd;
+        for (int c = tid; c < c4; c += blockDim.x) cp_async16(dst + 4 * c, src + 4 * c);
+    }
+    cp_async_commit();
+    if (a.qk_type == 2) {  // whole vectors q [qn], k [kn] (decode_kernel.c:1162-1174)
+        const int qn4 = (qn + 3) / 4 * 4;
+        squares(row, qn, sq);
+        squares(row + qn, kn, sq + qn4);
+        cp_async_wait<0>();
+        __syncthreads();
+        if (tid == 0) inv[0] = rms_inv(chain_sum(sq, qn), qn, a.eps);
+        if (tid == (blockDim.x > 32 ? 32 : 1)) inv[1] = rms_inv(chain_sum(sq + qn4, kn), kn, a.eps);
+        __syncthreads();
+        for (int c = tid; c < hd; c += blockDim.x) {
+            for (int hh = 0; hh < gsz; hh++) {
+                float* q = q_s + hh * qs + c;
+                *q = __fmul_rn(__fmul_rn(*q, inv[0]), bf16_to_f32(a.qnw[(h0 + hh) * hd + c]));
+            }
+            k_s[c] = __fmul_rn(__fmul_rn(k_s[c], inv[1]), bf16_to_f32(a.knw[g * hd + c]));
+        }
+    } else {
+        cp_async_wait<0>();
+        __syncthreads();
+        if (a.qk_type == 1) {  // per head, weights [hd] (decode_kernel.c:1180-1193)
+            if (tid <= gsz) inv[tid] = rms_inv(chain_sumsq(tid < gsz ? q_s + tid * qs : k_s, hd), hd, a.eps);
+            __syncthreads();
+            for (int c = tid; c < hd; c += blockDim.x) {
+                const float wq = bf16_to_f32(a.qnw[c]);
+                for (int hh = 0; hh < gsz; hh++) {
+                    float* q = q_s + hh * qs + c;
+                    *q = __fmul_rn(__fmul_rn(*q, inv[hh]), wq);
+                }
+                k_s[c] = __fmul_rn(__fmul_rn(k_s[c], inv[gsz]), bf16_to_f32(a.knw[c]));
+            }
+        }
+    }
+    __syncthreads();
+    // RoPE, rotate-half (decode_kernel.c:259-266, 1195-1199); each item owns its pair
+    const int half = hd / 2;
+    for (int i = tid; i < half; i += blockDim.x) {
+        const float cs = cs_s[i], sn = sn_s[i];
+        for (int hh = 0; hh <= gsz; hh++) {
+            float* v = hh < gsz ? q_s + hh * qs : k_s;
+            const float x0 = v[i], x1 = v[i + half];
+            v[i] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            v[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        }
+    }
+    __syncthreads();
+}
+
 constexpr int kQkThreads = 256;
 constexpr int kQkTile = 64;   // positions per K tile
 constexpr int kQkRing = 3;    // K tiles in the ring (two in flight while one is used)
@@ -318,15 +405,15 @@ constexpr int kPvRing = 8;    // V tiles in the ring (seven in flight while one 
 constexpr int kPvItems = 4;   // (head, four dimensions) items per thread at most (NI of k_attn_pv)
 
 // Shared-memory layout of k_attn_qk (floats): q [gsz][hd + 4], k [hd],
-// v [hd], squares, inverse norms [gsz + 1] (padded to 4), two K tiles
-// [kQkTile][hd + 4] x kQkRing.
+// v [hd], cos [hd], sin [hd], squares (whole-vector QK-norm only), inverse norms [gsz + 1]
+// (padded to 4), K tiles [kQkTile][hd + 4] x kQkRing.
 struct qk_layout {
     int qs, sq, inv, tiles, total;
     __host__ __device__ qk_layout(int qk_type, int H, int KH, int hd) {
         const int gsz = H / KH, qrow = hd + 4;
         qs = qrow;
-        sq = gsz * qrow + 2 * hd;
-        const int nsq = qk_type == 2 ? (H * hd + 3) / 4 * 4 + (KH * hd + 3) / 4 * 4 : (gsz + 1) * hd;
+        sq = gsz * qrow + 4 * hd;
+        const int nsq = qk_type == 2 ? (H * hd + 3) / 4 * 4 + (KH * hd + 3) / 4 * 4 : 0;
         inv = sq + (nsq + 3) / 4 * 4;
         tiles = inv + (gsz + 4) / 4 * 4;
         total = tiles + kQkRing * kQkTile * qrow;
@@ -342,6 +429,8 @@ __global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __re
     float* q_s = sm;                 // [gsz][QS]
     float* k_s = sm + gsz * QS;      // [hd]
     float* v_s = k_s + hd;           // [hd]
+    float* cs_s = v_s + hd;          // [hd]
+    float* sn_s = cs_s + hd;         // [hd]
     float* sq = sm + lay.sq;
     float* inv = sm + lay.inv;
     float* tb0 = sm + lay.tiles;     // tile j at tb0 + (j % kQkRing) * kQkTile * KP
@@ -378,56 +467,7 @@ __global__ void __launch_bounds__(kQkThreads) k_attn_qk(attn_args a, float* __re
         if (jt < ntiles) issue_k(t_lo + jt * kQkTile, tb0 + jt * kQkTile * KP);
         else cp_async_commit();
     }
-    const float* row = a.qkv + (size_t)b * (qn + 2 * kn);
-    for (int i = tid; i < gsz * hd; i += blockDim.x) q_s[(i / hd) * QS + i % hd] = row[h0 * hd + i];
-    for (int i = tid; i < hd; i += blockDim.x) {
-        k_s[i] = row[qn + g * hd + i];
-        v_s[i] = row[qn + kn + g * hd + i];
-    }
-    // QK-norm
-    if (a.qk_type == 2) {  // whole vectors q [qn], k [kn] (decode_kernel.c:1162-1174)
-        const int qn4 = (qn + 3) / 4 * 4;
-        squares(row, qn, sq);
-        squares(row + qn, kn, sq + qn4);
-        __syncthreads();
-        if (tid == 0) inv[0] = rms_inv(chain_sum(sq, qn), qn, a.eps);
-        if (tid == 32) inv[1] = rms_inv(chain_sum(sq + qn4, kn), kn, a.eps);
-        __syncthreads();
-        for (int i = tid; i < gsz * hd; i += blockDim.x) {
-            float* q = q_s + (i / hd) * QS + i % hd;
-            *q = __fmul_rn(__fmul_rn(*q, inv[0]), bf16_to_f32(a.qnw[h0 * hd + i]));
-        }
-        for (int i = tid; i < hd; i += blockDim.x)
-            k_s[i] = __fmul_rn(__fmul_rn(k_s[i], inv[1]), bf16_to_f32(a.knw[g * hd + i]));
-    } else if (a.qk_type == 1) {  // per head, weights [hd] (decode_kernel.c:1180-1193)
-        __syncthreads();
-        for (int i = tid; i < (gsz + 1) * hd; i += blockDim.x) {
-            const int hh = i / hd, c = i - hh * hd;
-            const float v = hh < gsz ? q_s[hh * QS + c] : k_s[c];
-            sq[i] = __fmul_rn(v, v);
-        }
-        __syncthreads();
-        if (tid <= gsz) inv[tid] = rms_inv(chain_sum(sq + tid * hd, hd), hd, a.eps);
-        __syncthreads();
-        for (int i = tid; i < gsz * hd; i += blockDim.x) {
-            float* q = q_s + (i / hd) * QS + i % hd;
-            *q = __fmul_rn(__fmul_rn(*q, inv[i / hd]), bf16_to_f32(a.qnw[i % hd]));
-        }
-        for (int i = tid; i < hd; i += blockDim.x)
-            k_s[i] = __fmul_rn(__fmul_rn(k_s[i], inv[gsz]), bf16_to_f32(a.knw[i]));
-    }
-    __syncthreads();
-    // RoPE, rotate-half (decode_kernel.c:259-266, 1195-1199); each item owns its pair
-    const int half = hd / 2;
-    for (int it = tid; it < (gsz + 1) * half; it += blockDim.x) {
-        const int hh = it / half, i = it - hh * half;
-        float* v = hh < gsz ? q_s + hh * QS : k_s;
-        const float cs = a.cosb[(size_t)pos * hd + i], sn = a.sinb[(size_t)pos * hd + i];
-        const float x0 = v[i], x1 = v[i + half];
-        v[i] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-        v[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-    }
-    __syncthreads();
+    qk_prepare(a, g, b, pos, q_s, QS, k_s, v_s, cs_s, sn_s, sq, inv);
     if (!a.from_cache && split == 0) {        // KV append (decode_kernel.c:1200-1205)
         for (int i = tid; i < hd; i += blockDim.x) {
             a.kc[cache_off + (size_t)pos * kn + g * hd + i] = k_s[i];
@@ -610,6 +650,291 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
                 a.attT[(size_t)(col + 3) * a.Bp + b] = o[k].w;
             }
         }
+}
+
+// ---------------------------------------------------------------------------
+// Register-tiled attention for KV groups of an even number of heads and head
+// dimensions 64 or 128 (the decode step at batches of 16 and more), in three
+// launches: the same chains in the same order as k_attn_qk / k_attn_pv, each
+// thread running 8 of them, so one shared-memory load feeds several chains
+// and the loops unroll at compile time.
+//
+// k_qk_prep, block (KV group g, row b): the prologue once per (group, row):
+// QK-norm and RoPE of the group's q heads, written to qr [B][H][hd], and of
+// the k row, which goes into the cache at positions[b] with the v row
+// (decode_kernel.c:1162-1205). The score kernel then reads q from qr and
+// every K row from the cache.
+//
+// k_attn_qk_t<HD, PPT>, block (KV group g, sequence b, split p): the block's
+// positions are split p of ceil(T / PT) even splits of [0, T) (PT = 32 PPT);
+// their K rows of the group arrive whole in shared memory, one bulk copy per
+// row on one mbarrier. Thread (head pair hp, position lane pq) owns heads 2hp,
+// 2hp + 1 against positions pq, pq + 32, ... (2 x PPT chains): a 4-column
+// step loads 2 q and PPT k float4s for 8 PPT products and sums.
+//
+// k_attn_pv_t<HD>, block (KV group g, sequence b, dimension slice z of dw):
+// the softmax of the group's heads from their staged score rows (per head the
+// max, p_t = expf_fast(s_t - max), their sum in t order by one thread,
+// p_t /= sum; decode_kernel.c:1219-1221), then thread (head h, dimension
+// quad dq) runs the 4 chains att[i] = 0 + p_0 v_0[i] + ... in t order of
+// dimensions z dw + 4 dq .. + 3. V rows [t][dw] stream through a ring of
+// kPvRingT tiles of kPvRowsT rows; per 4 rows a thread loads a p float4 (p
+// rows padded to ps = 4 mod 32 floats, so the heads' rows sit in distinct
+// banks) and 4 v float4s for 16 products and sums. The block is rounded up
+// to whole warps; the extra threads only copy.
+__global__ void __launch_bounds__(kAttnThreads) k_qk_prep(attn_args a) {
+    extern __shared__ __align__(16) float sm[];
+    const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int hd = a.hd, kn = a.KH * hd, gsz = a.H / a.KH, QS = hd + 4;
+    float* q_s = sm;              // [gsz][QS]
+    float* k_s = q_s + gsz * QS;  // [hd]
+    float* v_s = k_s + hd;        // [hd]
+    float* cs_s = v_s + hd;       // [hd]
+    float* sn_s = cs_s + hd;      // [hd]
+    float* inv = sn_s + hd;       // [gsz + 1], padded to 4
+    float* sq = inv + (gsz + 4) / 4 * 4;
+    griddep_wait();
+    griddep_launch_dependents();
+    const int pos = a.positions[b];
+    const int slot = a.slots[b];
+    if (pos < 0 || pos >= a.maxT || slot < 0 || slot >= a.nslots) {
+        if (tid == 0) atomicOr(a.err, kErrPosition);
+        return;
+    }
+    qk_prepare(a, g, b, pos, q_s, QS, k_s, v_s, cs_s, sn_s, sq, inv);
+    float* dst = a.qr + ((size_t)b * a.H + g * gsz) * hd;
+    for (int hh = 0; hh < gsz; hh++)
+        for (int c = tid; c < hd / 4; c += blockDim.x)
+            reinterpret_cast<float4*>(dst + hh * hd)[c] = reinterpret_cast<const float4*>(q_s + hh * QS)[c];
+    const size_t off = (((size_t)slot * a.L + a.l) * a.maxT + pos) * kn + g * hd;
+    for (int i = tid; i < hd; i += blockDim.x) {
+        a.kc[off + i] = k_s[i];
+        a.vc[off + i] = v_s[i];
+    }
+}
+
+size_t qk_prep_smem(int qk_type, int H, int KH, int hd) {
+    const int gsz = H / KH;
+    return ((size_t)gsz * (hd + 4) + 4 * hd + (gsz + 4) / 4 * 4 +
+            (qk_type == 2 ? (H * hd + 3) / 4 * 4 + (KH * hd + 3) / 4 * 4 : 0)) * sizeof(float);
+}
+
+// Shared memory of k_attn_qk_t (floats): the K rows [PT][HD + 4], then q
+// [gsz][HD + 4] (rows padded by 16 bytes: the eight rows a warp reads at once
+// fall in distinct banks).
+template <int HD, int PPT>
+struct qk_t_layout {
+    static constexpr int PT = 32 * PPT, KS = HD + 4;
+    static size_t bytes(int gsz) { return (size_t)(PT + gsz) * KS * sizeof(float); }
+};
+
+template <int HD, int PPT>
+__global__ void __launch_bounds__(256) k_attn_qk_t(attn_args a, float* __restrict__ scores) {
+    using LY = qk_t_layout<HD, PPT>;
+    constexpr int PT = LY::PT, KS = LY::KS;
+    extern __shared__ __align__(16) float sm[];
+    __shared__ __align__(8) uint64_t bar;
+    const int g = blockIdx.x, b = blockIdx.y, split = blockIdx.z, tid = threadIdx.x;
+    const int gsz = a.H / a.KH, nhp = gsz / 2, h0 = g * gsz, kn = a.KH * HD;
+    const int hp = tid % nhp, pq = tid / nhp;
+    float* kt = sm;              // [PT][KS]
+    float* q_s = sm + PT * KS;   // [gsz][KS]
+    // Positions and slots are inputs of the step, written before its first
+    // kernel: they, and the K rows of earlier steps, are read before the
+    // dependent-grid wait, so the rows stream in while k_qk_prep runs. The
+    // row it appends (and every row, for a prefill chunk) and q come after.
+    const int pos = a.positions[b];
+    const int slot = a.slots[b];
+    if (pos < 0 || pos >= a.maxT || slot < 0 || slot >= a.nslots) return;  // k_qk_prep flags it
+    const int T = pos + 1, ns = (T + PT - 1) / PT, tpb = (T + ns - 1) / ns, t_lo = split * tpb;
+    if (split >= ns || t_lo >= T) return;
+    const int n = min(T - t_lo, tpb);
+    const int early = a.from_cache ? 0 : split == ns - 1 ? n - 1 : n;  // rows loaded before the wait
+    const float* K = a.kc + ((size_t)slot * a.L + a.l) * a.maxT * kn + (size_t)t_lo * kn + g * HD;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        mbar_expect_tx(&bar, (uint32_t)((n + gsz) * HD * sizeof(float)));
+    }
+    __syncthreads();
+    for (int r = tid; r < early; r += blockDim.x) bulk_g2s(kt + r * KS, K + (size_t)r * kn, HD * sizeof(float), &bar);
+    griddep_wait();
+    griddep_launch_dependents();
+    for (int r = early + tid; r < n; r += blockDim.x)
+        bulk_g2s(kt + r * KS, K + (size_t)r * kn, HD * sizeof(float), &bar);
+    const float* qsrc = a.qr + ((size_t)b * a.H + h0) * HD;
+    for (int r = tid; r < gsz; r += blockDim.x) bulk_g2s(q_s + r * KS, qsrc + r * HD, HD * sizeof(float), &bar);
+    if (!mbar_wait_bounded(&bar, 0, a.err)) return;
+    // scores (decode_kernel.c:1212-1218)
+    float acc[2][PPT];
+#pragma unroll
+    for (int i = 0; i < PPT; i++) acc[0][i] = acc[1][i] = 0.0f;
+    const float* qa = q_s + 2 * hp * KS;
+    const float* qb = qa + KS;
+    const float* kb = kt + pq * KS;
+#pragma unroll 8
+    for (int c = 0; c < HD / 4; c++) {
+        const float4 x = *reinterpret_cast<const float4*>(qa + 4 * c);
+        const float4 y = *reinterpret_cast<const float4*>(qb + 4 * c);
+        float4 u[PPT];
+#pragma unroll
+        for (int i = 0; i < PPT; i++) u[i] = *reinterpret_cast<const float4*>(kb + 32 * i * KS + 4 * c);
+#pragma unroll
+        for (int i = 0; i < PPT; i++) {
+            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.x, u[i].x));
+            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.x, u[i].x));
+        }
+#pragma unroll
+        for (int i = 0; i < PPT; i++) {
+            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.y, u[i].y));
+            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.y, u[i].y));
+        }
+#pragma unroll
+        for (int i = 0; i < PPT; i++) {
+            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.z, u[i].z));
+            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.z, u[i].z));
+        }
+#pragma unroll
+        for (int i = 0; i < PPT; i++) {
+            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.w, u[i].w));
+            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.w, u[i].w));
+        }
+    }
+    const float scale = sqrtf_fast((float)HD);
+    float* out = scores + ((size_t)b * a.H + h0 + 2 * hp) * a.maxT + t_lo;
+#pragma unroll
+    for (int i = 0; i < PPT; i++) {
+        const int t = pq + 32 * i;
+        if (t < n) {
+            out[t] = __fdiv_rn(acc[0][i], scale);
+            out[a.maxT + t] = __fdiv_rn(acc[1][i], scale);
+        }
+    }
+}
+
+constexpr int kPvRowsT = 32;
+constexpr int kPvRingT = 4;
+
+__device__ __forceinline__ void pv_step(float4& o, float p, const float4& v) {
+    o.x = __fadd_rn(o.x, __fmul_rn(p, v.x));
+    o.y = __fadd_rn(o.y, __fmul_rn(p, v.y));
+    o.z = __fadd_rn(o.z, __fmul_rn(p, v.z));
+    o.w = __fadd_rn(o.w, __fmul_rn(p, v.w));
+}
+
+// four rows r .. r + 3 of a V tile into the thread's four chains
+__device__ __forceinline__ void pv_rows4(float4& o, const float* p, const float* vb, int dw) {
+    const float4 pp = *reinterpret_cast<const float4*>(p);
+    const float4 v0 = *reinterpret_cast<const float4*>(vb);
+    const float4 v1 = *reinterpret_cast<const float4*>(vb + dw);
+    const float4 v2 = *reinterpret_cast<const float4*>(vb + 2 * dw);
+    const float4 v3 = *reinterpret_cast<const float4*>(vb + 3 * dw);
+    pv_step(o, pp.x, v0);
+    pv_step(o, pp.y, v1);
+    pv_step(o, pp.z, v2);
+    pv_step(o, pp.w, v3);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __restrict__ scores, int dw, int ps) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float stat[16];
+    const int g = blockIdx.x, b = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int gsz = a.H / a.KH, h0 = g * gsz, qn = a.H * HD, kn = a.KH * HD;
+    const int hh0 = tid % gsz, dq = tid / gsz, nq = dw / 4;  // the thread's head and dimension quad
+    const bool live = dq < nq;
+    float* p_s = sm;            // [gsz][ps]
+    float* vt = sm + gsz * ps;  // [kPvRingT][kPvRowsT][dw]
+    // Positions and slots are inputs of the step and the V rows are in the
+    // cache once k_attn_qk_t runs (k_qk_prep appended this step's rows and
+    // k_attn_qk_t waited for it before releasing this kernel): the ring's
+    // first tiles go out before the dependent-grid wait, the scores after it.
+    const int pos = a.positions[b];
+    const int slot = a.slots[b];
+    if (pos < 0 || pos >= a.maxT || slot < 0 || slot >= a.nslots) return;  // k_qk_prep flags it
+    const int T = pos + 1, T4 = (T + 3) / 4 * 4;
+    const float* V = a.vc + ((size_t)slot * a.L + a.l) * a.maxT * kn + g * HD + z * dw;
+    const int ntiles = (T + kPvRowsT - 1) / kPvRowsT;
+    // tile copies: thread (rows vr0, vr0 + rstep, ..., 16-byte column vc), fixed per thread
+    const int rstep = blockDim.x / nq, vr0 = tid / nq, vc = 4 * (tid - vr0 * nq);
+    auto issue_v = [&](int j) {  // tile j into slot j % kPvRingT
+        const int t0 = j * kPvRowsT, nt = min(kPvRowsT, T - t0);
+        float* buf = vt + (j % kPvRingT) * kPvRowsT * dw + vc;
+        const float* src = V + (size_t)t0 * kn + vc;
+        for (int r = vr0; r < nt; r += rstep) cp_async16(buf + r * dw, src + (size_t)r * kn);
+    };
+    for (int j = 0; j < kPvRingT - 1; j++) {
+        if (j < ntiles) issue_v(j);
+        cp_async_commit();
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    // the group's score rows (16-byte pieces when the rows are 16-byte aligned)
+    const float* src = scores + ((size_t)b * a.H + h0) * a.maxT;
+    if ((a.maxT & 3) == 0) {
+        for (int hh = 0; hh < gsz; hh++)
+            for (int c = tid; c < T4 / 4; c += blockDim.x) cp_async16(p_s + hh * ps + 4 * c, src + (size_t)hh * a.maxT + 4 * c);
+    } else {
+        for (int hh = 0; hh < gsz; hh++)
+            for (int t = tid; t < T; t += blockDim.x) cp_async4(p_s + hh * ps + t, src + (size_t)hh * a.maxT + t);
+    }
+    cp_async_commit();
+    // softmax (decode_kernel.c:1219-1221): per head the max, p_t = expf_fast(s_t - max), their sum
+    // in t order by one thread, p_t /= sum
+    cp_async_wait<0>();  // the scores (the newest group) have landed, and the ring's first tiles
+    __syncthreads();
+    for (int hh = warp; hh < gsz; hh += nwarps) {
+        float* p = p_s + hh * ps;
+        float mx = -1e30f;
+        for (int t = lane; t < T; t += 32) {
+            const float v = p[t];
+            if (v > mx) mx = v;
+        }
+        if (lane < T4 - T) p[T + lane] = 0.0f;  // pads are +0 for the sum
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int t = lane; t < T; t += 32) p[t] = expf_fast(__fsub_rn(p[t], mx));
+    }
+    __syncthreads();
+    if (tid < gsz) stat[tid] = chain_sum(p_s + tid * ps, T4);  // sequential over t (decode_kernel.c:1220)
+    __syncthreads();
+    for (int hh = 0; hh < gsz; hh++) {
+        const float sum = stat[hh];
+        for (int t = tid; t < T; t += blockDim.x) p_s[hh * ps + t] = __fdiv_rn(p_s[hh * ps + t], sum);
+    }
+    // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229)
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float* pa = p_s + hh0 * ps;
+    for (int j = 0; j < ntiles; j++) {
+        const int t0 = j * kPvRowsT, nt = min(kPvRowsT, T - t0);
+        const int jn = j + kPvRingT - 1;  // refills the slot tile j - 1 used
+        if (jn < ntiles) issue_v(jn);
+        cp_async_commit();
+        cp_async_wait<kPvRingT - 1>();
+        __syncthreads();
+        const float* vb = vt + (j % kPvRingT) * kPvRowsT * dw + 4 * dq;
+        if (live) {
+            if (nt == kPvRowsT) {
+#pragma unroll
+                for (int r = 0; r < kPvRowsT; r += 4) pv_rows4(o, pa + t0 + r, vb + r * dw, dw);
+            } else {
+                int r = 0;
+                for (; r + 4 <= nt; r += 4) pv_rows4(o, pa + t0 + r, vb + r * dw, dw);
+                for (; r < nt; r++) pv_step(o, pa[t0 + r], *reinterpret_cast<const float4*>(vb + r * dw));
+            }
+        }
+        __syncthreads();
+    }
+    if (!live) return;
+    const int col = (h0 + hh0) * HD + z * dw + 4 * dq;
+    *reinterpret_cast<float4*>(a.att + (size_t)b * qn + col) = o;
+    if (a.attT) {
+        a.attT[(size_t)col * a.Bp + b] = o.x;
+        a.attT[(size_t)(col + 1) * a.Bp + b] = o.y;
+        a.attT[(size_t)(col + 2) * a.Bp + b] = o.z;
+        a.attT[(size_t)(col + 3) * a.Bp + b] = o.w;
+    }
 }
 
 // K/V append for a batch of positions of one or more sequences (batched
@@ -800,6 +1125,7 @@ struct jl_dec {
     float* attT;       // [qn, Bp]
     int Bp;            // max_batch rounded up to 8
     float* scores;     // [max_batch, H, maxT] attention scores
+    float* qr;         // [max_batch, qn] prepared q of the register-tiled attention
     float* logits;     // [max_batch, V]
     int* tok;          // [max_batch]
     float* arg_v;      // [max_batch][kArgParts] argmax partials
@@ -830,8 +1156,52 @@ int dec_attrs() {
         JL_CUDA(cudaFuncSetAttribute(k_attn_pv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         JL_CUDA(cudaFuncSetAttribute(k_attn_pv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         JL_CUDA(cudaFuncSetAttribute(k_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_qk_t<64, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_qk_t<128, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_pv_t<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_attn_pv_t<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+        JL_CUDA(cudaFuncSetAttribute(k_qk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
         return JL_OK;
     });
+}
+
+// The register-tiled attention of one layer (head dims 64 and 128, even
+// group sizes up to 16): k_qk_prep (which also appends the K/V rows), then
+// k_attn_qk_t with 4 positions per thread, then k_attn_pv_t with one head per
+// thread (4 chains) and the head dimension cut into slices of at least 32
+// until there is about one value block per SM and at most 256 threads a
+// block. Timed at B = 16 and 64 on the Qwen3 shape, 2 and 4 positions per
+// score thread and 1 and 2 heads per value thread all took within 3 % of one
+// another (latency-bound, about 50 % issue efficiency); the chosen pair was
+// the fastest at B = 16.
+bool attn_tiled_ok(int hd, int gsz) { return (hd == 64 || hd == 128) && gsz % 2 == 0 && gsz <= 16; }
+
+template <int HD, int PPT>
+int launch_qk_t(const jl::attn_args& aa, float* scores, int B, cudaStream_t s) {
+    using namespace jl;
+    using LY = qk_t_layout<HD, PPT>;
+    const int gsz = aa.H / aa.KH;
+    const size_t smem = LY::bytes(gsz);
+    if (smem > 200 * 1024) return JL_ERR_INVALID;
+    return launch(k_attn_qk_t<HD, PPT>, dim3(aa.KH, B, (aa.maxT + LY::PT - 1) / LY::PT), dim3(16 * gsz), smem, s, aa,
+                  scores);
+}
+
+template <int HD>
+int launch_attn_t(const jl::attn_args& aa, float* scores, int B, int sms, cudaStream_t s) {
+    using namespace jl;
+    const int gsz = aa.H / aa.KH, ps = (aa.maxT + 31) / 32 * 32 + 4;
+    int rc = launch(k_qk_prep, dim3(aa.KH, B), dim3(kAttnThreads), qk_prep_smem(aa.qk_type, aa.H, aa.KH, HD), s, aa);
+    if (!rc) rc = launch_qk_t<HD, 4>(aa, scores, B, s);
+    if (rc) return rc;
+    int ds = 1;
+    while (ds < 4 && HD / (2 * ds) >= 32 && (aa.KH * B * ds < sms || gsz * (HD / ds / 4) > 256)) ds *= 2;
+    const int dw = HD / ds;
+    const int threads = (gsz * (dw / 4) + 31) / 32 * 32;
+    if (threads > 256) return JL_ERR_INVALID;
+    const size_t smem = ((size_t)gsz * ps + (size_t)kPvRingT * kPvRowsT * dw) * sizeof(float);
+    if (smem > 200 * 1024) return JL_ERR_INVALID;
+    return launch(k_attn_pv_t<HD>, dim3(aa.KH, B, ds), dim3(threads), smem, s, aa, (const float*)scores, dw, ps);
 }
 
 // Row tiles per block: one for a single token group (the most blocks), more
@@ -895,8 +1265,8 @@ extern "C" int jl_dec_destroy(jl_dec* h) {
     if (!h) return JL_OK;
     if (h->moe) jl_moe_destroy(h->moe);
     void* ptrs[] = {h->embed, h->norm1, h->norm2, h->fnorm, h->qnw, h->knw, h->wqkv, h->wo, h->bqkv, h->lm,
-                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->tT, h->attT, h->scores, h->logits,
-                    h->tok, h->arg_v, h->arg_i, h->pre_pos, h->pre_slot, h->err, h->stage};
+                    h->cosb, h->sinb, h->kc, h->vc, h->h, h->t, h->h2, h->qkv, h->att, h->tT, h->attT, h->scores, h->qr,
+                    h->logits, h->tok, h->arg_v, h->arg_i, h->pre_pos, h->pre_slot, h->err, h->stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete h;
@@ -957,6 +1327,7 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
         {(void**)&h->qkv, (size_t)max_batch * h->nqkv * 4},
         {(void**)&h->att, (size_t)max_batch * h->qn * 4},
         {(void**)&h->scores, (size_t)max_batch * h->H * h->maxT * 4},
+        {(void**)&h->qr, (size_t)max_batch * h->qn * 4},
         {(void**)&h->tT, max_batch >= 16 ? (size_t)d * h->Bp * 4 : 0},
         {(void**)&h->attT, max_batch >= 16 ? (size_t)h->qn * h->Bp * 4 : 0},
         {(void**)&h->logits, (size_t)max_batch * V * 4},
@@ -1098,7 +1469,7 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     attn_args aa;
     aa.qkv = h->qkv, aa.att = h->att, aa.positions = positions, aa.slots = slots, aa.kc = h->kc, aa.vc = h->vc;
     aa.cosb = h->cosb, aa.sinb = h->sinb, aa.L = h->L, aa.H = h->H, aa.KH = h->KH, aa.hd = h->hd, aa.maxT = h->maxT;
-    aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err;
+    aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err, aa.qr = h->qr;
     aa.sqn = attn_sqn(h->qk_type, h->H, h->KH, h->hd);
     aa.nslots = h->slots;
     // column-major copies of the matvec inputs for the register-tiled kernel (B >= 16)
@@ -1116,6 +1487,8 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     // (V read once per group), else single heads; slices of the head
     // dimension (multiples of 4 floats) up to 4 per head
     const int gsz = h->H / h->KH, maxT4 = (h->maxT + 3) / 4 * 4;
+    // the register-tiled kernels at batches of 16 and more
+    const bool attn_t = B >= 16 && attn_tiled_ok(h->hd, gsz);
     auto pick_slices = [&](int units, int target) {
         int ds = 1;
         while (ds < 4 && units * ds < target && h->hd % (8 * ds) == 0) ds *= 2;
@@ -1155,11 +1528,14 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
             aa.qnw = h->qk_type ? h->qnw + l * qs : nullptr;
             aa.knw = h->qk_type ? h->knw + l * ks : nullptr;
             aa.from_cache = prefill;
-            if (prefill)
+            if (prefill && !attn_t)
                 rc = launch(k_kv_append, dim3(h->KH, B), dim3(kAttnThreads), (size_t)(128 + aa.sqn) * sizeof(float),
                             s, aa);
-            if (!rc) rc = launch(k_attn_qk, dim3(h->KH, B, splits), dim3(kQkThreads), qk_smem, s, aa, h->scores, tp);
-            if (!rc) {
+            if (!rc && attn_t)
+                rc = h->hd == 64 ? launch_attn_t<64>(aa, h->scores, B, sms, s)
+                                 : launch_attn_t<128>(aa, h->scores, B, sms, s);
+            else if (!rc) rc = launch(k_attn_qk, dim3(h->KH, B, splits), dim3(kQkThreads), qk_smem, s, aa, h->scores, tp);
+            if (!rc && !attn_t) {
                 auto kern = pv_items <= 1 ? k_attn_pv<1> : pv_items <= 2 ? k_attn_pv<2> : k_attn_pv<4>;
                 rc = launch(kern, dim3(h->H / hpb, B, dslices), dim3(kPvThreads), pv_smem, s, aa,
                             (const float*)h->scores, hpb, dw, pv_whole);

@@ -15,6 +15,12 @@ Shapes: d = 512, heads of 64 with GQA 8: 32 q / 4 kv heads (qn 2048) or 64 /
 they take the matvec kernel through its tile shapes: lm_head (fp32) 32 x 16,
 32 x 32, 32 x 64 (large V) and 16 x 32 (small V); projections (bf16) 16 x 16,
 16 x 32, 32 x 16 and 32 x 32.
+
+The register-tiled attention kernels (k_attn_qk_t / k_attn_pv_t) run at these
+batches for head dims 64 and 128 and even group sizes; the last three cases
+take them through head dim 128 with contexts up to 600 (five position splits,
+value slices of 32 dims), groups of 16 heads with the whole-vector QK-norm,
+and groups of 2 without QK-norm but with a QKV bias.
 """
 from __future__ import annotations
 
@@ -35,18 +41,20 @@ class _DevArray:
                                          "version": 2}
 
 
-def _shape(V: int, H: int, KH: int):
+def _shape(V: int, H: int, KH: int, hd: int = 64, qk: int = 1, bias: int = 0, maxT: int = 160):
     from oracle.decode import DecodeShape
-    return DecodeShape("qwen3b", 2, 512, H, KH, 64, 8, 2, 128, V, 160, 1, 0, 1, 1e-6, 1e6)
+    return DecodeShape("qwen3b", 2, 512, H, KH, hd, 8, 2, 128, V, maxT, qk, bias, 1, 1e-6, 1e6)
 
 
-@pytest.mark.parametrize("B,V,H,KH", [(16, 40960, 32, 4), (32, 40960, 64, 8), (40, 4096, 32, 4),
-                                      (64, 40960, 64, 8)])
-def test_batched_step_bit_identical_to_restatement(B, V, H, KH):
+@pytest.mark.parametrize("B,V,H,KH,hd,qk,bias,maxT", [
+    (16, 40960, 32, 4, 64, 1, 0, 160), (32, 40960, 64, 8, 64, 1, 0, 160), (40, 4096, 32, 4, 64, 1, 0, 160),
+    (64, 40960, 64, 8, 64, 1, 0, 160), (24, 4096, 16, 2, 128, 1, 0, 600), (20, 4096, 32, 2, 64, 2, 0, 160),
+    (16, 4096, 8, 4, 128, 0, 1, 160)])
+def test_batched_step_bit_identical_to_restatement(B, V, H, KH, hd, qk, bias, maxT):
     from oracle.decode import RestatedDecoder, _Caches, embed, make_model
     from test_decode_gpu import _structs
     from joule_b200.native import check, get_dll
-    s = _shape(V, H, KH)
+    s = _shape(V, H, KH, hd, qk, bias, maxT)
     model = make_model(s, seed=41)
     rng = np.random.default_rng(7 + B)
     positions = np.array([(5 + 37 * b) % (s.maxT - 2) for b in range(B)], np.int32)
@@ -99,3 +107,39 @@ def test_batched_step_bit_identical_to_restatement(B, V, H, KH):
     bad = np.argwhere(got != ref)
     assert bad.size == 0, f"{len(bad)} logits differ, first at {bad[:4].tolist()}"
     assert np.array_equal(tok.cpu().numpy(), np.argmax(ref, axis=1).astype(np.int32))
+
+
+@pytest.mark.parametrize("hd,H,KH", [(64, 32, 4), (128, 16, 2)])
+def test_prefill_chunks_bit_identical_to_restatement(hd, H, KH):
+    """jl_dec_prefill of a 41-token prompt in chunks of 16 rows (the
+    register-tiled attention: a chunk's K/V rows all go into the cache before
+    any of its rows' scores) gives the restatement's last-token logits, one
+    position at a time, bit for bit."""
+    from oracle.decode import RestatedDecoder, make_model, prefill
+    from test_decode_gpu import _structs
+    from joule_b200.native import check, get_dll
+    s = _shape(4096, H, KH, hd)
+    model = make_model(s, seed=43)
+    prompt = np.random.default_rng(11).integers(0, s.V, 41).astype(np.int32)
+    lib = get_dll()
+    cfg, W, tables = _structs(model)
+    h = ctypes.c_void_p()
+    check(lib.jl_dec_create(ctypes.byref(cfg), ctypes.byref(W), 16, 16, 0, ctypes.byref(h)), "jl_dec_create")
+    try:
+        moe = ctypes.c_void_p()
+        check(lib.jl_dec_moe(h, ctypes.byref(moe)), "jl_dec_moe")
+        check(lib.jl_moe_set_path(moe, 1), "jl_moe_set_path")  # exact
+        stream = torch.cuda.current_stream().cuda_stream
+        p = torch.from_numpy(prompt).cuda()
+        logits = torch.empty(s.V, device="cuda")
+        tok = torch.empty(1, dtype=torch.int32, device="cuda")
+        check(lib.jl_dec_prefill(h, 3, p.data_ptr(), p.numel(), 0, logits.data_ptr(), tok.data_ptr(), stream),
+              "jl_dec_prefill")
+        torch.cuda.synchronize()
+        check(lib.jl_dec_check(h, stream), "jl_dec_check")
+        got = logits.cpu().numpy()
+    finally:
+        lib.jl_dec_destroy(h)
+    ref = prefill(RestatedDecoder(model), prompt.tolist())
+    bad = np.argwhere(got != ref)
+    assert bad.size == 0, f"{len(bad)} logits differ, first at {bad[:4].tolist()}"
