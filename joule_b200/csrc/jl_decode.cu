@@ -682,6 +682,14 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
 // rows padded to ps = 4 mod 32 floats, so the heads' rows sit in distinct
 // banks) and 4 v float4s for 16 products and sums. The block is rounded up
 // to whole warps; the extra threads only copy.
+// Chain steps o += a * b for two chains at once: each product by the scalar
+// multiply, the two sums by one packed add (each lane rounds as the scalar add
+// does). A packed multiply feeding a packed add directly is not used: the
+// assembler fuses that pair into a packed FMA (one rounding instead of two).
+__device__ __forceinline__ float2 add_prod2(float2 o, float a0, float b0, float a1, float b1) {
+    return __fadd2_rn(o, make_float2(__fmul_rn(a0, b0), __fmul_rn(a1, b1)));
+}
+
 __global__ void __launch_bounds__(kAttnThreads) k_qk_prep(attn_args a) {
     extern __shared__ __align__(16) float sm[];
     const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
@@ -765,10 +773,10 @@ __global__ void __launch_bounds__(256) k_attn_qk_t(attn_args a, float* __restric
     const float* qsrc = a.qr + ((size_t)b * a.H + h0) * HD;
     for (int r = tid; r < gsz; r += blockDim.x) bulk_g2s(q_s + r * KS, qsrc + r * HD, HD * sizeof(float), &bar);
     if (!mbar_wait_bounded(&bar, 0, a.err)) return;
-    // scores (decode_kernel.c:1212-1218)
-    float acc[2][PPT];
+    // scores (decode_kernel.c:1212-1218): acc[i] = the chains of heads 2hp, 2hp + 1 at position pq + 32 i
+    float2 acc[PPT];
 #pragma unroll
-    for (int i = 0; i < PPT; i++) acc[0][i] = acc[1][i] = 0.0f;
+    for (int i = 0; i < PPT; i++) acc[i] = make_float2(0.0f, 0.0f);
     const float* qa = q_s + 2 * hp * KS;
     const float* qb = qa + KS;
     const float* kb = kt + pq * KS;
@@ -780,25 +788,13 @@ __global__ void __launch_bounds__(256) k_attn_qk_t(attn_args a, float* __restric
 #pragma unroll
         for (int i = 0; i < PPT; i++) u[i] = *reinterpret_cast<const float4*>(kb + 32 * i * KS + 4 * c);
 #pragma unroll
-        for (int i = 0; i < PPT; i++) {
-            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.x, u[i].x));
-            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.x, u[i].x));
-        }
+        for (int i = 0; i < PPT; i++) acc[i] = add_prod2(acc[i], x.x, u[i].x, y.x, u[i].x);
 #pragma unroll
-        for (int i = 0; i < PPT; i++) {
-            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.y, u[i].y));
-            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.y, u[i].y));
-        }
+        for (int i = 0; i < PPT; i++) acc[i] = add_prod2(acc[i], x.y, u[i].y, y.y, u[i].y);
 #pragma unroll
-        for (int i = 0; i < PPT; i++) {
-            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.z, u[i].z));
-            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.z, u[i].z));
-        }
+        for (int i = 0; i < PPT; i++) acc[i] = add_prod2(acc[i], x.z, u[i].z, y.z, u[i].z);
 #pragma unroll
-        for (int i = 0; i < PPT; i++) {
-            acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(x.w, u[i].w));
-            acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(y.w, u[i].w));
-        }
+        for (int i = 0; i < PPT; i++) acc[i] = add_prod2(acc[i], x.w, u[i].w, y.w, u[i].w);
     }
     const float scale = sqrtf_fast((float)HD);
     float* out = scores + ((size_t)b * a.H + h0 + 2 * hp) * a.maxT + t_lo;
@@ -806,8 +802,8 @@ __global__ void __launch_bounds__(256) k_attn_qk_t(attn_args a, float* __restric
     for (int i = 0; i < PPT; i++) {
         const int t = pq + 32 * i;
         if (t < n) {
-            out[t] = __fdiv_rn(acc[0][i], scale);
-            out[a.maxT + t] = __fdiv_rn(acc[1][i], scale);
+            out[t] = __fdiv_rn(acc[i].x, scale);
+            out[a.maxT + t] = __fdiv_rn(acc[i].y, scale);
         }
     }
 }
@@ -815,28 +811,33 @@ __global__ void __launch_bounds__(256) k_attn_qk_t(attn_args a, float* __restric
 constexpr int kPvRowsT = 32;
 constexpr int kPvRingT = 4;
 
-__device__ __forceinline__ void pv_step(float4& o, float p, const float4& v) {
-    o.x = __fadd_rn(o.x, __fmul_rn(p, v.x));
-    o.y = __fadd_rn(o.y, __fmul_rn(p, v.y));
-    o.z = __fadd_rn(o.z, __fmul_rn(p, v.z));
-    o.w = __fadd_rn(o.w, __fmul_rn(p, v.w));
+__device__ __forceinline__ void pv_step(float2& oxy, float2& ozw, float p, const float4& v) {
+    oxy = add_prod2(oxy, p, v.x, p, v.y);
+    ozw = add_prod2(ozw, p, v.z, p, v.w);
 }
 
 // four rows r .. r + 3 of a V tile into the thread's four chains
-__device__ __forceinline__ void pv_rows4(float4& o, const float* p, const float* vb, int dw) {
+__device__ __forceinline__ void pv_rows4(float2& oxy, float2& ozw, const float* p, const float* vb, int dw) {
     const float4 pp = *reinterpret_cast<const float4*>(p);
-    const float4 v0 = *reinterpret_cast<const float4*>(vb);
-    const float4 v1 = *reinterpret_cast<const float4*>(vb + dw);
-    const float4 v2 = *reinterpret_cast<const float4*>(vb + 2 * dw);
-    const float4 v3 = *reinterpret_cast<const float4*>(vb + 3 * dw);
-    pv_step(o, pp.x, v0);
-    pv_step(o, pp.y, v1);
-    pv_step(o, pp.z, v2);
-    pv_step(o, pp.w, v3);
+    pv_step(oxy, ozw, pp.x, *reinterpret_cast<const float4*>(vb));
+    pv_step(oxy, ozw, pp.y, *reinterpret_cast<const float4*>(vb + dw));
+    pv_step(oxy, ozw, pp.z, *reinterpret_cast<const float4*>(vb + 2 * dw));
+    pv_step(oxy, ozw, pp.w, *reinterpret_cast<const float4*>(vb + 3 * dw));
 }
 
+// Shared memory of k_attn_pv_t (floats): scores, then probabilities, [gsz][ps]
+// (ps = 4 mod 32: the heads' rows in distinct banks), then the V ring.
+struct pv_t_layout {
+    int ps, vt, total;
+    __host__ __device__ pv_t_layout(int gsz, int maxT, int dw) {
+        ps = (maxT + 31) / 32 * 32 + 4;
+        vt = gsz * ps;
+        total = vt + kPvRingT * kPvRowsT * dw;
+    }
+};
+
 template <int HD>
-__global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __restrict__ scores, int dw, int ps) {
+__global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __restrict__ scores, int dw) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float stat[16];
     const int g = blockIdx.x, b = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
@@ -844,8 +845,10 @@ __global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __r
     const int gsz = a.H / a.KH, h0 = g * gsz, qn = a.H * HD, kn = a.KH * HD;
     const int hh0 = tid % gsz, dq = tid / gsz, nq = dw / 4;  // the thread's head and dimension quad
     const bool live = dq < nq;
-    float* p_s = sm;            // [gsz][ps]
-    float* vt = sm + gsz * ps;  // [kPvRingT][kPvRowsT][dw]
+    const pv_t_layout lay(gsz, a.maxT, dw);
+    const int ps = lay.ps;
+    float* s_s = sm;           // [gsz][ps]
+    float* vt = sm + lay.vt;   // [kPvRingT][kPvRowsT][dw]
     // Positions and slots are inputs of the step and the V rows are in the
     // cache once k_attn_qk_t runs (k_qk_prep appended this step's rows and
     // k_attn_qk_t waited for it before releasing this kernel): the ring's
@@ -874,10 +877,10 @@ __global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __r
     const float* src = scores + ((size_t)b * a.H + h0) * a.maxT;
     if ((a.maxT & 3) == 0) {
         for (int hh = 0; hh < gsz; hh++)
-            for (int c = tid; c < T4 / 4; c += blockDim.x) cp_async16(p_s + hh * ps + 4 * c, src + (size_t)hh * a.maxT + 4 * c);
+            for (int c = tid; c < T4 / 4; c += blockDim.x) cp_async16(s_s + hh * ps + 4 * c, src + (size_t)hh * a.maxT + 4 * c);
     } else {
         for (int hh = 0; hh < gsz; hh++)
-            for (int t = tid; t < T; t += blockDim.x) cp_async4(p_s + hh * ps + t, src + (size_t)hh * a.maxT + t);
+            for (int t = tid; t < T; t += blockDim.x) cp_async4(s_s + hh * ps + t, src + (size_t)hh * a.maxT + t);
     }
     cp_async_commit();
     // softmax (decode_kernel.c:1219-1221): per head the max, p_t = expf_fast(s_t - max), their sum
@@ -885,7 +888,7 @@ __global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __r
     cp_async_wait<0>();  // the scores (the newest group) have landed, and the ring's first tiles
     __syncthreads();
     for (int hh = warp; hh < gsz; hh += nwarps) {
-        float* p = p_s + hh * ps;
+        float* p = s_s + hh * ps;
         float mx = -1e30f;
         for (int t = lane; t < T; t += 32) {
             const float v = p[t];
@@ -897,15 +900,15 @@ __global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __r
         for (int t = lane; t < T; t += 32) p[t] = expf_fast(__fsub_rn(p[t], mx));
     }
     __syncthreads();
-    if (tid < gsz) stat[tid] = chain_sum(p_s + tid * ps, T4);  // sequential over t (decode_kernel.c:1220)
+    if (tid < gsz) stat[tid] = chain_sum(s_s + tid * ps, T4);  // sequential over t (decode_kernel.c:1220)
     __syncthreads();
     for (int hh = 0; hh < gsz; hh++) {
         const float sum = stat[hh];
-        for (int t = tid; t < T; t += blockDim.x) p_s[hh * ps + t] = __fdiv_rn(p_s[hh * ps + t], sum);
+        for (int t = tid; t < T; t += blockDim.x) s_s[hh * ps + t] = __fdiv_rn(s_s[hh * ps + t], sum);
     }
     // att[i] = 0 + p_0 v_0[i] + p_1 v_1[i] + ... (decode_kernel.c:1222-1229)
-    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const float* pa = p_s + hh0 * ps;
+    float2 oxy = make_float2(0.0f, 0.0f), ozw = oxy;
+    const float* pa = s_s + hh0 * ps;
     for (int j = 0; j < ntiles; j++) {
         const int t0 = j * kPvRowsT, nt = min(kPvRowsT, T - t0);
         const int jn = j + kPvRingT - 1;  // refills the slot tile j - 1 used
@@ -917,23 +920,23 @@ __global__ void __launch_bounds__(256) k_attn_pv_t(attn_args a, const float* __r
         if (live) {
             if (nt == kPvRowsT) {
 #pragma unroll
-                for (int r = 0; r < kPvRowsT; r += 4) pv_rows4(o, pa + t0 + r, vb + r * dw, dw);
+                for (int r = 0; r < kPvRowsT; r += 4) pv_rows4(oxy, ozw, pa + t0 + r, vb + r * dw, dw);
             } else {
                 int r = 0;
-                for (; r + 4 <= nt; r += 4) pv_rows4(o, pa + t0 + r, vb + r * dw, dw);
-                for (; r < nt; r++) pv_step(o, pa[t0 + r], *reinterpret_cast<const float4*>(vb + r * dw));
+                for (; r + 4 <= nt; r += 4) pv_rows4(oxy, ozw, pa + t0 + r, vb + r * dw, dw);
+                for (; r < nt; r++) pv_step(oxy, ozw, pa[t0 + r], *reinterpret_cast<const float4*>(vb + r * dw));
             }
         }
         __syncthreads();
     }
     if (!live) return;
     const int col = (h0 + hh0) * HD + z * dw + 4 * dq;
-    *reinterpret_cast<float4*>(a.att + (size_t)b * qn + col) = o;
+    *reinterpret_cast<float4*>(a.att + (size_t)b * qn + col) = make_float4(oxy.x, oxy.y, ozw.x, ozw.y);
     if (a.attT) {
-        a.attT[(size_t)col * a.Bp + b] = o.x;
-        a.attT[(size_t)(col + 1) * a.Bp + b] = o.y;
-        a.attT[(size_t)(col + 2) * a.Bp + b] = o.z;
-        a.attT[(size_t)(col + 3) * a.Bp + b] = o.w;
+        a.attT[(size_t)col * a.Bp + b] = oxy.x;
+        a.attT[(size_t)(col + 1) * a.Bp + b] = oxy.y;
+        a.attT[(size_t)(col + 2) * a.Bp + b] = ozw.x;
+        a.attT[(size_t)(col + 3) * a.Bp + b] = ozw.y;
     }
 }
 
@@ -1190,7 +1193,7 @@ int launch_qk_t(const jl::attn_args& aa, float* scores, int B, cudaStream_t s) {
 template <int HD>
 int launch_attn_t(const jl::attn_args& aa, float* scores, int B, int sms, cudaStream_t s) {
     using namespace jl;
-    const int gsz = aa.H / aa.KH, ps = (aa.maxT + 31) / 32 * 32 + 4;
+    const int gsz = aa.H / aa.KH;
     int rc = launch(k_qk_prep, dim3(aa.KH, B), dim3(kAttnThreads), qk_prep_smem(aa.qk_type, aa.H, aa.KH, HD), s, aa);
     if (!rc) rc = launch_qk_t<HD, 4>(aa, scores, B, s);
     if (rc) return rc;
@@ -1199,9 +1202,9 @@ int launch_attn_t(const jl::attn_args& aa, float* scores, int B, int sms, cudaSt
     const int dw = HD / ds;
     const int threads = (gsz * (dw / 4) + 31) / 32 * 32;
     if (threads > 256) return JL_ERR_INVALID;
-    const size_t smem = ((size_t)gsz * ps + (size_t)kPvRingT * kPvRowsT * dw) * sizeof(float);
+    const size_t smem = (size_t)pv_t_layout(gsz, aa.maxT, dw).total * sizeof(float);
     if (smem > 200 * 1024) return JL_ERR_INVALID;
-    return launch(k_attn_pv_t<HD>, dim3(aa.KH, B, ds), dim3(threads), smem, s, aa, (const float*)scores, dw, ps);
+    return launch(k_attn_pv_t<HD>, dim3(aa.KH, B, ds), dim3(threads), smem, s, aa, (const float*)scores, dw);
 }
 
 // Row tiles per block: one for a single token group (the most blocks), more

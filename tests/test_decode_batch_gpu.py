@@ -46,11 +46,15 @@ def _shape(V: int, H: int, KH: int, hd: int = 64, qk: int = 1, bias: int = 0, ma
     return DecodeShape("qwen3b", 2, 512, H, KH, hd, 8, 2, 128, V, maxT, qk, bias, 1, 1e-6, 1e6)
 
 
-@pytest.mark.parametrize("B,V,H,KH,hd,qk,bias,maxT", [
-    (16, 40960, 32, 4, 64, 1, 0, 160), (32, 40960, 64, 8, 64, 1, 0, 160), (40, 4096, 32, 4, 64, 1, 0, 160),
-    (64, 40960, 64, 8, 64, 1, 0, 160), (24, 4096, 16, 2, 128, 1, 0, 600), (20, 4096, 32, 2, 64, 2, 0, 160),
-    (16, 4096, 8, 4, 128, 0, 1, 160)])
-def test_batched_step_bit_identical_to_restatement(B, V, H, KH, hd, qk, bias, maxT):
+@pytest.mark.parametrize("B,V,H,KH,hd,qk,bias,maxT,kv_scale", [
+    (16, 40960, 32, 4, 64, 1, 0, 160, 1), (32, 40960, 64, 8, 64, 1, 0, 160, 1), (40, 4096, 32, 4, 64, 1, 0, 160, 1),
+    (64, 40960, 64, 8, 64, 1, 0, 160, 1), (24, 4096, 16, 2, 128, 1, 0, 600, 1), (20, 4096, 32, 2, 64, 2, 0, 160, 1),
+    (16, 4096, 8, 4, 128, 0, 1, 160, 1), (16, 4096, 32, 4, 128, 1, 0, 300, 30)])
+def test_batched_step_bit_identical_to_restatement(B, V, H, KH, hd, qk, bias, maxT, kv_scale):
+    """kv_scale 30: cached rows of standard deviation 30, so scores spread by
+    hundreds and the softmax's small probabilities underflow to subnormals
+    (and zero); some cached K and V entries are subnormal themselves. The
+    products and sums of those must round as the reference's do."""
     from oracle.decode import RestatedDecoder, _Caches, embed, make_model
     from test_decode_gpu import _structs
     from joule_b200.native import check, get_dll
@@ -63,8 +67,12 @@ def test_batched_step_bit_identical_to_restatement(B, V, H, KH, hd, qk, bias, ma
     caches = _Caches(s, B)
     for b in range(B):
         for l in range(s.L):
-            caches.k[b * s.L + l][: positions[b]] = rng.standard_normal((positions[b], kn), np.float32)
-            caches.v[b * s.L + l][: positions[b]] = rng.standard_normal((positions[b], kn), np.float32)
+            for c in (caches.k[b * s.L + l], caches.v[b * s.L + l]):
+                rows = rng.standard_normal((positions[b], kn), np.float32) * np.float32(kv_scale)
+                if kv_scale != 1:
+                    tiny = rng.random(rows.shape) < 0.01
+                    rows[tiny] = rng.standard_normal(int(tiny.sum())).astype(np.float32) * np.float32(1e-39)
+                c[: positions[b]] = rows
     x = embed(model, tokens)
 
     lib = get_dll()
