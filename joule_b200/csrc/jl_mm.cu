@@ -8,7 +8,8 @@
 // tokens; warp j is lane j of the reference's accumulator, and its thread
 // (rg, tg) holds RN x RT chains (rows rg*RN + r, tokens mm_token(tg, q)): per
 // 8-column step it reads RN weights and RT token values (RN/4 and RT/4 16-byte
-// shared loads) and issues RN*RT FMAs. Each block reads its weight rows once.
+// shared loads) and issues RN*RT/2 packed fp32-pair FMAs (each lane rounds as
+// fmaf; the pairs are 2 x 2 blocks of chains, diagonal and anti-diagonal). Each block reads its weight rows once.
 // The token rows come column-major ([K][Bp], written by the producer kernel
 // beside its row-major output), so a step's RT tokens are contiguous.
 //
@@ -78,7 +79,7 @@ __device__ __forceinline__ void widen(uint4 v, float* dst, int stride, float) { 
 }
 
 template <typename WT, int RN, int RT>
-__global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, const float* __restrict__ xT, int Bp,
+__global__ void __launch_bounds__(kMmThreads, RN * RT <= 16 ? 3 : 2) k_mm(const WT* __restrict__ W, const float* __restrict__ xT, int Bp,
                                                       int N, int K, int B, const float* __restrict__ bias,
                                                       float* __restrict__ out) {
     using S = mm_shape<WT, RN, RT>;
@@ -155,11 +156,15 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
     __syncthreads();
     widen_stage(0);
 
-    float acc[RN][RT];
+    // chains in 2 x 2 blocks (rows 2i, 2i+1; tokens 2k, 2k+1), two packed FMAs
+    // per block and step: dg[i][k] = {(2i, 2k), (2i+1, 2k+1)} takes the weight
+    // pair times the token pair, an[i][k] = {(2i, 2k+1), (2i+1, 2k)} the weight
+    // pair times the swapped token pair. Each lane is fmaf(w, x, acc).
+    float2 dg[RN / 2][RT / 2], an[RN / 2][RT / 2];
 #pragma unroll
-    for (int r = 0; r < RN; r++)
+    for (int i = 0; i < RN / 2; i++)
 #pragma unroll
-        for (int q = 0; q < RT; q++) acc[r][q] = 0.0f;
+        for (int k = 0; k < RT / 2; k++) dg[i][k] = an[i][k] = make_float2(0.0f, 0.0f);
 
     for (int st = 0; st < nst; st++) {
         cp_async_wait<NS - 3>();  // this thread's copies up to stage st + 1 have landed
@@ -201,11 +206,27 @@ __global__ void __launch_bounds__(kMmThreads, 2) k_mm(const WT* __restrict__ W, 
                 }
             }
 #pragma unroll
-            for (int r = 0; r < RN; r++)
+            for (int k = 0; k < RT / 2; k++) {
+                const float2 xp = make_float2(xv[2 * k], xv[2 * k + 1]), xs = make_float2(xv[2 * k + 1], xv[2 * k]);
 #pragma unroll
-                for (int q = 0; q < RT; q++) acc[r][q] = __fmaf_rn(w[r], xv[q], acc[r][q]);
+                for (int i = 0; i < RN / 2; i++) {
+                    const float2 wp = make_float2(w[2 * i], w[2 * i + 1]);
+                    dg[i][k] = __ffma2_rn(wp, xp, dg[i][k]);
+                    an[i][k] = __ffma2_rn(wp, xs, an[i][k]);
+                }
+            }
         }
     }
+    float acc[RN][RT];
+#pragma unroll
+    for (int i = 0; i < RN / 2; i++)
+#pragma unroll
+        for (int k = 0; k < RT / 2; k++) {
+            acc[2 * i][2 * k] = dg[i][k].x;
+            acc[2 * i + 1][2 * k + 1] = dg[i][k].y;
+            acc[2 * i][2 * k + 1] = an[i][k].x;
+            acc[2 * i + 1][2 * k] = an[i][k].y;
+        }
     cp_async_wait<0>();
     __syncthreads();  // the ring is free: it becomes the lanes' reduction area [j][token][row]
     float* red = sm;
