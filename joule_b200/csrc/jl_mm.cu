@@ -49,7 +49,11 @@ struct mm_shape {
     static constexpr int NS_fit = (int)((cap - (size_t)2 * WS_F * 4) / stage_bytes);
     static constexpr int NS = NS_fit < 3 ? 3 : NS_fit > 6 ? 6 : NS_fit;
     static constexpr size_t ring_bytes = (size_t)NS * stage_bytes + (size_t)2 * WS_F * 4;
-    static constexpr size_t red_bytes = (size_t)8 * BT * (BN + 1) * 4;
+    // lanes' sums [j][token][row]: rows in 4 groups of RN + 1 (one pad float
+    // each), tokens RS = 4 (RN + 1) + 1 floats apart, so a warp's 32 stores
+    // (8 token runs x 4 row groups) fall in distinct banks
+    static constexpr int RS = 4 * (RN + 1) + 1;
+    static constexpr size_t red_bytes = (size_t)8 * BT * RS * 4;
     static constexpr size_t smem = ring_bytes > red_bytes ? ring_bytes : red_bytes;
 };
 
@@ -233,14 +237,14 @@ __global__ void __launch_bounds__(kMmThreads, RN * RT <= 16 ? 3 : 2) k_mm(const 
 #pragma unroll
     for (int r = 0; r < RN; r++)
 #pragma unroll
-        for (int q = 0; q < RT; q++) red[(j * BT + mm_token(tg, q, RT)) * (BN + 1) + rg * RN + r] = acc[r][q];
+        for (int q = 0; q < RT; q++) red[(j * BT + mm_token(tg, q, RT)) * S::RS + rg * (RN + 1) + r] = acc[r][q];
     __syncthreads();
     for (int o = tid; o < BN * BT; o += kMmThreads) {
         const int r = o % BN, t = o / BN;
         if (n0 + r >= N || t0 + t >= B) continue;
         float l[8];
 #pragma unroll
-        for (int jj = 0; jj < 8; jj++) l[jj] = red[(jj * BT + t) * (BN + 1) + r];
+        for (int jj = 0; jj < 8; jj++) l[jj] = red[(jj * BT + t) * S::RS + (r / RN) * (RN + 1) + r % RN];
         float v = hsum8(l);
         if (bias) v = __fadd_rn(v, bias[n0 + r]);
         out[(size_t)(t0 + t) * N + n0 + r] = v;
