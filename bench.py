@@ -979,7 +979,7 @@ def decode_headline(a, line, fd):
                               "experts of 48 layers vs 126 MB L2",
                            parallelism="single GPU"),
                e2e=head["e2e"], clocks=fd.get("clocks"),
-               gpu_launches=(L * (6 + moe_launches) + 5) * a.steps,
+               gpu_launches=(L * (dense_launches(a.batch) + moe_launches) + 5) * a.steps,
                full_decode=fd)
     for k in ("roofline", "microbench"):
         if k in line:
@@ -1011,6 +1011,13 @@ def dtype_of(B):
 
 def gateup_kernel(B):
     return "k_gateup_gemv" if path_of(B) == "gemv" else "k_expert_tc<false>"
+
+
+def dense_launches(B):
+    # per layer outside the MoE layer: two norms, QKV, o_proj and the attention:
+    # k_attn_qk + k_attn_pv below B = 16, k_qk_prep + k_attn_qk_t + k_attn_pv_t from 16
+    # (the Qwen3 shape: head dim 128, groups of 8 heads)
+    return 4 + (3 if B >= 16 else 2)
 
 
 def launches_per_step(B):
