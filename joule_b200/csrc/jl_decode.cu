@@ -1210,7 +1210,7 @@ int launch_attn_t(const jl::attn_args& aa, float* scores, int B, int sms, cudaSt
 // Row tiles per block: one for a single token group (the most blocks), more
 // when the token rows are staged per block for several groups.
 // x: [B][K] row-major; xT: the same as a column-major [K][Bp] copy (the
-// register-tiled kernel at B >= 16 reads that one).
+// register-tiled kernel at B >= kMmMinB reads that one).
 template <typename WT>
 int launch_mv(const WT* W, const float* x, const float* xT, int Bp, int N, int K, int B, const float* bias,
               float* out, int sm_count, cudaStream_t s) {
@@ -1331,8 +1331,8 @@ extern "C" int jl_dec_create(const KernelCfg* c, const KernelW* W, int max_batch
         {(void**)&h->att, (size_t)max_batch * h->qn * 4},
         {(void**)&h->scores, (size_t)max_batch * h->H * h->maxT * 4},
         {(void**)&h->qr, (size_t)max_batch * h->qn * 4},
-        {(void**)&h->tT, max_batch >= 16 ? (size_t)d * h->Bp * 4 : 0},
-        {(void**)&h->attT, max_batch >= 16 ? (size_t)h->qn * h->Bp * 4 : 0},
+        {(void**)&h->tT, max_batch >= kMmMinB ? (size_t)d * h->Bp * 4 : 0},
+        {(void**)&h->attT, max_batch >= kMmMinB ? (size_t)h->qn * h->Bp * 4 : 0},
         {(void**)&h->logits, (size_t)max_batch * V * 4},
         {(void**)&h->tok, (size_t)max_batch * 4},
         {(void**)&h->arg_v, (size_t)max_batch * kArgParts * 4},
@@ -1475,9 +1475,9 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     aa.qk_type = h->qk_type, aa.eps = h->eps, aa.err = h->err, aa.qr = h->qr;
     aa.sqn = attn_sqn(h->qk_type, h->H, h->KH, h->hd);
     aa.nslots = h->slots;
-    // column-major copies of the matvec inputs for the register-tiled kernel (B >= 16)
-    float* tT = B >= 16 ? h->tT : nullptr;
-    aa.attT = B >= 16 ? h->attT : nullptr;
+    // column-major copies of the matvec inputs for the register-tiled kernel (B >= kMmMinB)
+    float* tT = B >= kMmMinB ? h->tT : nullptr;
+    aa.attT = B >= kMmMinB ? h->attT : nullptr;
     aa.Bp = h->Bp;
     // attention work split: score blocks (group, sequence, position split) and
     // value blocks (head, sequence, dimension slice), about two blocks per SM
@@ -1820,7 +1820,7 @@ int dropin_step(const KernelCfg* c, const KernelW* W, KVCache* kv, const int* po
         cudaFreeAsync(dbg_d, e->st);
     }
     if (!rc && logits)
-        rc = launch_mv<float>(h->lm, h->t, B >= 16 ? h->tT : nullptr, h->Bp, h->V, c->d, B, nullptr, h->logits,
+        rc = launch_mv<float>(h->lm, h->t, B >= kMmMinB ? h->tT : nullptr, h->Bp, h->V, c->d, B, nullptr, h->logits,
                               h->moe->sm_count, e->st);
     if (rc) return rc;
     // the new K/V row of every layer back into the caller's caches

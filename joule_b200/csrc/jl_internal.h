@@ -126,9 +126,12 @@ enum {
 };
 int jl_device_once(int key, int (*setup)());
 
-// Decode-step matvecs for B >= 16 tokens (jl_mm.cu): the reference's 8-lane
-// FMA order, register-tiled; W in the chunked lane-major layout (jl_mv.cuh),
-// the tokens column-major xT [K][Bp] (Bp a multiple of 4, >= B).
+// Decode-step matvecs for B >= kMmMinB tokens (jl_mm.cu): the reference's
+// 8-lane FMA order, register-tiled; W in the chunked lane-major layout
+// (jl_mv.cuh), the tokens column-major xT [K][Bp] (Bp a multiple of 4, >= B).
+// Below 16 tokens the 16-token tiles run part empty, still faster than the
+// small-batch kernel from 8 tokens (B = 8: lm_head 379 us against 572 us).
+constexpr int kMmMinB = 8;
 bool jl_mm_ok(int N, int K, int B);
 template <typename WT>
 int jl_launch_mm(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,

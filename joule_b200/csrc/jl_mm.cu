@@ -1,4 +1,4 @@
-// Matvecs of the decode step for batches of 16 tokens and more (QKV, o_proj,
+// Matvecs of the decode step for batches of 8 tokens and more (QKV, o_proj,
 // lm_head): out[b][n] = hsum8_j( chain over s of fma(W[n][8s + j], x[b][8s + j]) )
 // (+ bias[n]), the reference's 8-lane FMA order (decode_kernel.c:693-718,
 // 969-995) with the AVX tree at the end, bit for bit.
@@ -279,7 +279,7 @@ int mm_attrs_for() {
 }  // namespace jl
 
 // (the kernel's per-thread copy offsets are 32-bit: the matrix stays below 2^31 elements)
-bool jl_mm_ok(int N, int K, int B) { return B >= 16 && K % 64 == 0 && N >= 1 && (long long)N * K < (1ll << 31); }
+bool jl_mm_ok(int N, int K, int B) { return B >= kMmMinB && K % 64 == 0 && N >= 1 && (long long)N * K < (1ll << 31); }
 
 // Tile choice (BN x BT = 4 RN x 8 RT), from timings of every shape on the
 // decode step's matrices on a B200 (QKV 5120 x 2048, o_proj 2048 x 4096,

@@ -1,8 +1,9 @@
 """Large-batch decode steps on the GPU against the C restatement of the
 reference's decode step (needs a GPU).
 
-At B >= 16 the step's matvecs (QKV, o_proj, lm_head) run on the register-tiled
-kernel (jl_mm.cu) and attention reads long, ragged contexts. One step of B
+At B >= 8 the step's matvecs (QKV, o_proj, lm_head) run on the register-tiled
+kernel (jl_mm.cu; below 16 tokens its 16-token tiles run part empty) and
+attention reads long, ragged contexts. One step of B
 sequences, each at its own position with a KV cache pre-filled with seeded
 values (the same rows in the oracle's caches and in the library's slots), must
 give the restatement's logits bit for bit (MoE on its exact path), and the
@@ -49,7 +50,8 @@ def _shape(V: int, H: int, KH: int, hd: int = 64, qk: int = 1, bias: int = 0, ma
 @pytest.mark.parametrize("B,V,H,KH,hd,qk,bias,maxT,kv_scale", [
     (16, 40960, 32, 4, 64, 1, 0, 160, 1), (32, 40960, 64, 8, 64, 1, 0, 160, 1), (40, 4096, 32, 4, 64, 1, 0, 160, 1),
     (64, 40960, 64, 8, 64, 1, 0, 160, 1), (24, 4096, 16, 2, 128, 1, 0, 600, 1), (20, 4096, 32, 2, 64, 2, 0, 160, 1),
-    (16, 4096, 8, 4, 128, 0, 1, 160, 1), (16, 4096, 32, 4, 128, 1, 0, 300, 30)])
+    (16, 4096, 8, 4, 128, 0, 1, 160, 1), (16, 4096, 32, 4, 128, 1, 0, 300, 30), (8, 40960, 32, 4, 64, 1, 0, 160, 1),
+    (12, 4096, 16, 2, 128, 1, 0, 300, 1)])
 def test_batched_step_bit_identical_to_restatement(B, V, H, KH, hd, qk, bias, maxT, kv_scale):
     """kv_scale 30: cached rows of standard deviation 30, so scores spread by
     hundreds and the softmax's small probabilities underflow to subnormals
