@@ -1215,7 +1215,8 @@ template <typename WT>
 int launch_mv(const WT* W, const float* x, const float* xT, int Bp, int N, int K, int B, const float* bias,
               float* out, int sm_count, cudaStream_t s) {
     using namespace jl;
-    if (jl_mm_ok(N, K, B)) {
+    const bool big = (size_t)N * K * sizeof(WT) > ((size_t)64 << 20);  // beyond the L2 prefetch below
+    if (jl_mm_ok(N, K, B, big ? kMmMinB : 16)) {
         if (!xT) return JL_ERR_INVALID;
         return jl_launch_mm<WT>(W, xT, Bp, N, K, B, bias, out, sm_count, s);
     }

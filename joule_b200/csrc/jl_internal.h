@@ -126,13 +126,16 @@ enum {
 };
 int jl_device_once(int key, int (*setup)());
 
-// Decode-step matvecs for B >= kMmMinB tokens (jl_mm.cu): the reference's
-// 8-lane FMA order, register-tiled; W in the chunked lane-major layout
+// Decode-step matvecs on the register-tiled kernel (jl_mm.cu): the
+// reference's 8-lane FMA order; W in the chunked lane-major layout
 // (jl_mv.cuh), the tokens column-major xT [K][Bp] (Bp a multiple of 4, >= B).
-// Below 16 tokens the 16-token tiles run part empty, still faster than the
-// small-batch kernel from 8 tokens (B = 8: lm_head 379 us against 572 us).
+// From 16 tokens for every matrix; from kMmMinB tokens (its 16-token tiles
+// part empty) for matrices too large for the small-batch kernel's L2
+// prefetch (> 64 MB, the lm_head): at B = 8 the lm_head takes 379 us there
+// against 572 us, while the prefetched projections are faster on the
+// small-batch kernel inside the decode step's graph.
 constexpr int kMmMinB = 8;
-bool jl_mm_ok(int N, int K, int B);
+bool jl_mm_ok(int N, int K, int B, int min_b);
 template <typename WT>
 int jl_launch_mm(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,
                  int sm_count, cudaStream_t s);

@@ -1,4 +1,4 @@
-// Matvecs of the decode step for batches of 8 tokens and more (QKV, o_proj,
+// Matvecs of the decode step for batches of 16 tokens and more (QKV, o_proj,
 // lm_head): out[b][n] = hsum8_j( chain over s of fma(W[n][8s + j], x[b][8s + j]) )
 // (+ bias[n]), the reference's 8-lane FMA order (decode_kernel.c:693-718,
 // 969-995) with the AVX tree at the end, bit for bit.
@@ -279,7 +279,9 @@ int mm_attrs_for() {
 }  // namespace jl
 
 // (the kernel's per-thread copy offsets are 32-bit: the matrix stays below 2^31 elements)
-bool jl_mm_ok(int N, int K, int B) { return B >= kMmMinB && K % 64 == 0 && N >= 1 && (long long)N * K < (1ll << 31); }
+bool jl_mm_ok(int N, int K, int B, int min_b) {
+    return B >= min_b && B >= kMmMinB && K % 64 == 0 && N >= 1 && (long long)N * K < (1ll << 31);
+}
 
 // Tile choice (BN x BT = 4 RN x 8 RT), from timings of every shape on the
 // decode step's matrices on a B200 (QKV 5120 x 2048, o_proj 2048 x 4096,
@@ -294,7 +296,7 @@ template <typename WT>
 int jl_launch_mm(const WT* W, const float* xT, int Bp, int N, int K, int B, const float* bias, float* out,
                  int sm_count, cudaStream_t s) {
     using namespace jl;
-    if (!jl_mm_ok(N, K, B) || Bp % 4 || Bp < B || (long long)K * Bp >= (1ll << 31)) return JL_ERR_INVALID;
+    if (!jl_mm_ok(N, K, B, kMmMinB) || Bp % 4 || Bp < B || (long long)K * Bp >= (1ll << 31)) return JL_ERR_INVALID;
     const int rc = jl_device_once(sizeof(WT) == 2 ? kOnceMmBf16 : kOnceMmF32, [] { return mm_attrs_for<WT>(); });
     if (rc) return rc;
     const long rows32 = (N + 31) / 32;
