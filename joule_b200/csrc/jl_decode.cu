@@ -656,8 +656,9 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
 // Register-tiled attention for KV groups of an even number of heads and head
 // dimensions 64 or 128 (the decode step at batches of 16 and more), in three
 // launches: the same chains in the same order as k_attn_qk / k_attn_pv, each
-// thread running 8 of them, so one shared-memory load feeds several chains
-// and the loops unroll at compile time.
+// thread running several of them (8 scores, 4 values), so one shared-memory
+// load feeds several chains and the loops unroll at compile time; two
+// chains' sums share one packed add (add_prod2).
 //
 // k_qk_prep, block (KV group g, row b): the prologue once per (group, row):
 // QK-norm and RoPE of the group's q heads, written to qr [B][H][hd], and of
@@ -682,6 +683,7 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(attn_args a, const float
 // rows padded to ps = 4 mod 32 floats, so the heads' rows sit in distinct
 // banks) and 4 v float4s for 16 products and sums. The block is rounded up
 // to whole warps; the extra threads only copy.
+
 // Chain steps o += a * b for two chains at once: each product by the scalar
 // multiply, the two sums by one packed add (each lane rounds as the scalar add
 // does). A packed multiply feeding a packed add directly is not used: the
