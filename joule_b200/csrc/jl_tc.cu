@@ -407,8 +407,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
     long long* tr = (blockIdx.x == 0) ? ws.trace : nullptr;
     const int tk = is_down ? kTraceDown : kTraceGateup;
     trace_point(tr, tk, 0);
-    griddep_wait();
-    griddep_launch_dependents();
+    // Only the activation producer reads the previous kernel's output (the
+    // token tiles of k_tc_permute, or gate/up's activations for down) and
+    // waits for it. The tile list is the dispatch step's, two or three
+    // launches back and complete once the previous kernel runs (it waited
+    // for its own predecessor before releasing this grid), so the weights
+    // stream and dequantise meanwhile.
     const int n_items = *ws.tc_ntiles * MT;
     if ((int)blockIdx.x >= n_items) return;
     const int my_items = (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
@@ -491,6 +495,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else if (warp == kWAct) {
         // ---------------- activation producer: stage = kb K steps of one item's tile
+        griddep_wait();
+        griddep_launch_dependents();
         if (lane == 0) {
             int G = 0;
             bool ok = true;
