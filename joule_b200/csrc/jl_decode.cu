@@ -1493,8 +1493,10 @@ static int dec_step(jl_dec* h, const int* slots, const int* positions, const flo
     // (V read once per group), else single heads; slices of the head
     // dimension (multiples of 4 floats) up to 4 per head
     const int gsz = h->H / h->KH, maxT4 = (h->maxT + 3) / 4 * 4;
-    // the register-tiled kernels at batches of 16 and more
-    const bool attn_t = B >= 16 && attn_tiled_ok(h->hd, gsz);
+    // the register-tiled kernels at batches of 16 and more, for contexts whose
+    // score rows fit the value kernel's shared memory (longer ones take k_attn_pv)
+    const bool attn_t = B >= 16 && attn_tiled_ok(h->hd, gsz) &&
+                        (size_t)pv_t_layout(gsz, h->maxT, h->hd).total * sizeof(float) <= 200 * 1024;
     auto pick_slices = [&](int units, int target) {
         int ds = 1;
         while (ds < 4 && units * ds < target && h->hd % (8 * ds) == 0) ds *= 2;

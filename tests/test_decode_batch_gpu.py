@@ -18,10 +18,12 @@ they take the matvec kernel through its tile shapes: lm_head (fp32) 32 x 16,
 16 x 32, 32 x 16 and 32 x 32.
 
 The register-tiled attention kernels (k_attn_qk_t / k_attn_pv_t) run at these
-batches for head dims 64 and 128 and even group sizes; the last three cases
-take them through head dim 128 with contexts up to 600 (five position splits,
-value slices of 32 dims), groups of 16 heads with the whole-vector QK-norm,
-and groups of 2 without QK-norm but with a QKV bias.
+batches for head dims 64 and 128 and even group sizes; further cases take them
+through head dim 128 with contexts up to 600 (five position splits, value
+slices of 32 dims), groups of 16 heads with the whole-vector QK-norm, and
+groups of 2 without QK-norm but with a QKV bias. Contexts whose score rows do
+not fit the tiled value kernel's shared memory (groups of 16 at maxT 3000)
+fall back to k_attn_qk / k_attn_pv at B = 16.
 """
 from __future__ import annotations
 
@@ -51,7 +53,7 @@ def _shape(V: int, H: int, KH: int, hd: int = 64, qk: int = 1, bias: int = 0, ma
     (16, 40960, 32, 4, 64, 1, 0, 160, 1), (32, 40960, 64, 8, 64, 1, 0, 160, 1), (40, 4096, 32, 4, 64, 1, 0, 160, 1),
     (64, 40960, 64, 8, 64, 1, 0, 160, 1), (24, 4096, 16, 2, 128, 1, 0, 600, 1), (20, 4096, 32, 2, 64, 2, 0, 160, 1),
     (16, 4096, 8, 4, 128, 0, 1, 160, 1), (16, 4096, 32, 4, 128, 1, 0, 300, 30), (8, 40960, 32, 4, 64, 1, 0, 160, 1),
-    (12, 4096, 16, 2, 128, 1, 0, 300, 1)])
+    (12, 4096, 16, 2, 128, 1, 0, 300, 1), (16, 4096, 32, 2, 64, 1, 0, 3000, 1)])
 def test_batched_step_bit_identical_to_restatement(B, V, H, KH, hd, qk, bias, maxT, kv_scale):
     """kv_scale 30: cached rows of standard deviation 30, so scores spread by
     hundreds and the softmax's small probabilities underflow to subnormals
