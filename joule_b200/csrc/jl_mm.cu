@@ -1,5 +1,5 @@
 // Matvecs of the decode step for batches of 16 tokens and more (QKV, o_proj,
-// lm_head): out[b][n] = hsum8_j( chain over s of fma(W[n][8s + j], x[b][8s + j]) )
+// lm_head; the lm_head from 8 tokens, see jl_mm_ok in jl_internal.h): out[b][n] = hsum8_j( chain over s of fma(W[n][8s + j], x[b][8s + j]) )
 // (+ bias[n]), the reference's 8-lane FMA order (decode_kernel.c:693-718,
 // 969-995) with the AVX tree at the end, bit for bit.
 //
